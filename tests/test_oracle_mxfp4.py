@@ -1,0 +1,61 @@
+"""CPU checks of the oracle's MXFP4 decode (MXD:29-67, MXO:65-91).
+
+compressed-tensors (the library MXD:70-112 checks against) is not installed,
+so the decode is pinned by the E2M1 table, the sign-bit rule for nibble 8
+(-0.0, MXO:65-75), the low-nibble-first packing order (MXD:14-20) and the
+exact power-of-two scale for every byte the format allows.
+"""
+
+import numpy as np
+
+from oracle import lmoe_oracle as O
+
+
+def test_e2m1_table_and_negative_zero():
+  packed = np.array([[0x10, 0x32, 0x54, 0x76, 0x98, 0xBA, 0xDC, 0xFE]], np.uint8)
+  scale = np.array([[127, 127]], np.uint8)[:, :1].repeat(1, 1)
+  out = O.dequantize_mxfp4(packed, np.array([[127]], np.uint8))
+  assert out.shape == (1, 16)
+  expect = [0, .5, 1, 1.5, 2, 3, 4, 6, -0.0, -.5, -1, -1.5, -2, -3, -4, -6]
+  assert out[0].tolist() == expect
+  assert np.signbit(out[0, 8]) and not np.signbit(out[0, 0])
+  del scale
+
+
+def test_low_nibble_is_even_k():
+  packed = np.array([[0x2F]], np.uint8)  # low nibble 0xF (-6), high 0x2 (1.0)
+  out = O.dequantize_mxfp4(np.repeat(packed, 16, axis=1), np.array([[127]], np.uint8))
+  assert out[0, 0] == -6.0 and out[0, 1] == 1.0
+
+
+def test_scale_is_exact_power_of_two():
+  codes = np.full((1, 16), 0x22, np.uint8)  # every element 1.0
+  for s in range(1, 255):
+    out = O.dequantize_mxfp4(codes, np.array([[s]], np.uint8))
+    assert np.all(out == np.float32(2.0) ** (s - 127)), s
+
+
+def test_group_size_32_blocks():
+  rng = np.random.default_rng(0)
+  packed = rng.integers(0, 256, (4, 64), dtype=np.uint8)
+  scale = rng.integers(120, 130, (4, 4), dtype=np.uint8)
+  out = O.dequantize_mxfp4(packed, scale)
+  base = O.dequantize_mxfp4(packed, np.full_like(scale, 127))
+  for b in range(4):
+    f = (2.0 ** (scale[:, b].astype(np.float64) - 127))[:, None]
+    assert np.array_equal(out[:, b * 32:(b + 1) * 32], (base[:, b * 32:(b + 1) * 32] * f).astype(np.float32))
+
+
+def test_mxfp4_ragged_dot_matches_dense_loop():
+  rng = np.random.default_rng(1)
+  g, n, k = 3, 16, 64
+  packed = rng.integers(0, 256, (g, n, k // 2), dtype=np.uint8)
+  scale = rng.integers(121, 130, (g, n, k // 32), dtype=np.uint8)
+  gs = np.array([5, 0, 7], np.int32)
+  lhs = rng.standard_normal((14, k)).astype(np.float32)
+  out = O.mxfp4_ragged_dot(lhs, packed, scale, gs, dtype="fp32")
+  w0 = O.dequantize_mxfp4(packed[0], scale[0])
+  w2 = O.dequantize_mxfp4(packed[2], scale[2])
+  assert np.allclose(out[:5], lhs[:5] @ w0.T, atol=1e-5)
+  assert np.allclose(out[5:12], lhs[5:12] @ w2.T, atol=1e-5)
+  assert np.all(out[12:] == 0)
