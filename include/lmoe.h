@@ -1,0 +1,169 @@
+/*
+ * lmoe.h -- C ABI of the B200 (sm_100a) LatentMoE expert path.
+ *
+ * Drop-in boundary for the reference's JAX-facing operators
+ * (Yog-Sothothftgn/tokamax-tpu-kernel-lab, paths below relative to its root).
+ * Every entry point:
+ *   - takes plain device pointers, sizes and a CUDA stream (`stream` is a
+ *     cudaStream_t passed as void*; NULL = the legacy default stream);
+ *   - is stream-ordered and asynchronous, allocates nothing and never
+ *     synchronises the host (group sizes live in device memory and are read
+ *     only on the device);
+ *   - returns LMOE_OK or a host-detected error code;
+ *   - optionally records a device-detected error (group sizes that exceed the
+ *     row count, a bounded wait that timed out) in `dev_status`, a device
+ *     int32 the caller zeroes and reads back when it chooses (may be NULL).
+ * Layouts are row-major.  bf16 = IEEE bfloat16 stored as uint16.
+ */
+#ifndef LMOE_H_
+#define LMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LMOE_API __attribute__((visibility("default")))
+#else
+#define LMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LMOE_OK = 0,
+  LMOE_BAD_SHAPE = 1,      /* sizes out of range / inconsistent */
+  LMOE_UNSUPPORTED = 2,    /* alignment or divisibility the kernels need */
+  LMOE_LAUNCH_FAILED = 3,  /* CUDA launch or tensor-map encode failed */
+  LMOE_DEVICE_BOUNDS = 4,  /* (dev_status) group sizes invalid on the device */
+  LMOE_WAIT_TIMEOUT = 5    /* (dev_status) a bounded device wait gave up */
+};
+
+enum { LMOE_RHS_GKN = 0, LMOE_RHS_GNK = 1 };
+enum { LMOE_ROUTER_SIGMOID = 0, LMOE_ROUTER_SOFTMAX = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+LMOE_API int lmoe_version(void);
+
+/* Grouped matmul, bf16 in, f32 accumulate (tcgen05), bf16 or f32 out.
+ *   out[r] = lhs[r] @ rhs[g]  for r in group g's contiguous row range; rows at or
+ *   past sum(group_sizes) are written as zero.
+ * lhs (m, k); rhs (g, k, n) [LMOE_RHS_GKN] or (g, n, k) [LMOE_RHS_GNK];
+ * group_sizes (g,) int32 device; out (m, n).  k, n multiples of 8.
+ * Replaces tokamax.ragged_dot(lhs, rhs, group_sizes, implementation=...)
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:358-369, 604-607). */
+LMOE_API int lmoe_ragged_dot_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
+                         int64_t m, int64_t k, int64_t n, int64_t num_groups, int rhs_layout,
+                         int out_f32, int32_t* dev_status, void* stream);
+
+/* Same semantics in IEEE float32 on the CUDA cores (f32 compute dtype).
+ * Replaces ragged_dot with f32 operands (the reference's f32 configs,
+ * 05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:383-406). */
+LMOE_API int lmoe_ragged_dot_f32(const float* lhs, const float* rhs, const int32_t* group_sizes, float* out,
+                        int64_t m, int64_t k, int64_t n, int64_t num_groups, int rhs_layout,
+                        int32_t* dev_status, void* stream);
+
+/* Dense f32 GEMM on the CUDA cores with an optional fused f32 residual add:
+ *   out = lhs @ rhs (+ addend).  The f32 form of lmoe_gemm_bf16 below. */
+LMOE_API int lmoe_gemm_f32(const float* lhs, const float* rhs, const float* addend, float* out,
+                           int64_t m, int64_t k, int64_t n, int rhs_layout, int32_t* dev_status,
+                           void* stream);
+
+/* Dense bf16 GEMM with a fused bf16 residual add:
+ *   out = bf16(bf16(lhs @ rhs) + addend)       (addend may equal nothing: pass NULL
+ *   for a plain bf16(lhs @ rhs)).  rhs layout as above with g = 1.
+ * Replaces `up + shared_out` after `normed @ up_proj` / `... @ shared_down`
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:422-435). */
+LMOE_API int lmoe_gemm_bf16(const void* lhs, const void* rhs, const void* addend, void* out, int64_t m,
+                   int64_t k, int64_t n, int rhs_layout, int out_f32, int32_t* dev_status,
+                   void* stream);
+
+/* Fused gate/up grouped matmul + SiTU-GLU epilogue, bf16 out (m, intermediate).
+ * w_gateup is the plain concatenation [gate | up] along N:
+ *   (g, k, 2*intermediate) [LMOE_RHS_GKN] or (g, 2*intermediate, k) [LMOE_RHS_GNK].
+ * round_gate_up = 1 rounds gate/up to bf16 before the activation (the unfused
+ * reference's convention); 0 applies it to the f32 accumulator (tokamax fuse_act).
+ * Replaces PallasMosaicTpuV2RaggedDot()(..., fuse_gateup_activation="situ:b:lb")
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:610-723) and the
+ * dense own kernel (05_ragged_dot_on_tpu/own_gateup_situ_pallas_kernel.py:79-199). */
+LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const int32_t* group_sizes,
+                          void* out, int64_t m, int64_t k, int64_t intermediate,
+                          int64_t num_groups, int rhs_layout, float beta, float linear_beta,
+                          int round_gate_up, int32_t* dev_status, void* stream);
+
+/* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).
+ * gate/up rows have pitch ld_in elements; bf16 = 1 for bf16 I/O, 0 for f32.
+ * Replaces _situ_and_mul (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:296-310). */
+LMOE_API int lmoe_situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
+                      int64_t intermediate, float beta, float linear_beta, int bf16, void* stream);
+
+/* Router epilogue from f32 logits (T, E): sigmoid (or softmax), + bias for
+ * selection only, top-k descending with ties to the lower expert id, gather of
+ * the un-biased scores, renormalise (sum + 1e-20) when k > 1 and renormalize,
+ * times routed_scaling_factor.  topk_idx (T, k) int32, topk_w (T, k) f32.
+ * E <= 1024, k <= 32.  bias may be NULL.
+ * Replaces the gate of latent_moe_forward
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:347-356, 601-631). */
+LMOE_API int lmoe_router_topk(const float* logits, const float* bias, int64_t num_tokens,
+                     int64_t num_experts, int64_t top_k, int activation, int renormalize,
+                     float routed_scaling_factor, int32_t* topk_idx, float* topk_w, void* stream);
+
+/* Workspace bytes lmoe_dispatch needs for max(num_tokens*top_k, m_out) entries. */
+LMOE_API size_t lmoe_dispatch_workspace_size(int64_t num_entries, int64_t num_local_experts);
+
+/* Dispatch metadata: stable counting sort of the flattened (token, slot)
+ * entries by local expert id.  Entries whose expert is outside
+ * [expert_start, expert_start + num_local_experts) (and padding entries up to
+ * m_out) sort after every real entry; the first m_out sorted positions are kept
+ * (tail drop on overflow).
+ *   full dropless dispatch:   expert_start 0, num_local_experts E, m_out T*k, pad_bucket 0
+ *                             -> order = argsort(flat_ids, stable), group_sizes = bincount
+ *                             (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:370-378)
+ *   shard, capacity padded:   m_out = m_padded, pad_bucket 1 -> group_sizes has
+ *                             num_local_experts + 1 entries, the last one the
+ *                             padding bucket (kimi_k3_latent_moe_reference.py:754-877)
+ * Outputs (device; NULL to skip where marked optional):
+ *   order[m_out]        (optional) flat entry index at each sorted position
+ *   token_idx[m_out]    source token, -1 for padding positions
+ *   weight[m_out]       (optional) topk_w of the entry, 0 for padding
+ *   slot_pos[T*k]       (optional) sorted position of each entry, -1 if not kept
+ *   group_sizes[...]    kept count per local expert (+ padding bucket)
+ *   per_expert_counts   (optional) kept count per local expert
+ *   valid[m_out]        (optional) 1 for real rows, 0 for padding
+ * topk_w may be NULL (weights then read as 0).  num_local_experts <= 2048. */
+LMOE_API int lmoe_dispatch(const int32_t* topk_idx, const float* topk_w, int64_t num_tokens,
+                  int64_t top_k, int64_t expert_start, int64_t num_local_experts, int64_t m_out,
+                  int pad_bucket, int32_t* order, int32_t* token_idx, float* weight,
+                  int32_t* slot_pos, int32_t* group_sizes, int32_t* per_expert_counts,
+                  uint8_t* valid, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Row gather: out[p] = token_idx[p] >= 0 ? x[token_idx[p]] : 0, rows of row_bytes
+ * (a multiple of 16).  Replaces `x[sorted_token_idx]` / `where(valid, x[idx], 0)`
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:372-374, 867-868). */
+LMOE_API int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out,
+                     int64_t rows, int64_t row_bytes, void* stream);
+
+/* Weighted combine + RMSNorm:
+ *   routed[t] = dtype(sum_s expert_out[slot_pos[t*k+s]] * topk_w[t,s])   (f32, slot order)
+ *   normed[t] = dtype(dtype(routed[t] / sqrt(mean(routed[t]^2) + eps)) * norm_scale)
+ * slot_pos < 0 contributes nothing.  routed_out / normed_out may be NULL.
+ * Replaces kimi_k3_latent_moe_reference.py:413-419 and _rms_norm (286-293). */
+LMOE_API int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
+                         const void* norm_scale, int64_t num_tokens, int64_t top_k,
+                         int64_t latent, float eps, int bf16, void* routed_out, void* normed_out,
+                         void* stream);
+
+/* Scatter-add combine of one expert shard:
+ *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0
+ * Replaces _combine_shard_contribution
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:1113-1141). */
+LMOE_API int lmoe_combine_scatter_add(const void* shard_out, const int32_t* padded_token_idx,
+                             const float* padded_combine_weight, void* routed_out, int64_t rows,
+                             int64_t latent, int64_t num_tokens, int bf16, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LMOE_H_ */

@@ -1,0 +1,49 @@
+"""CPU checks of the C-ABI library: it loads, and it exports exactly the entry
+points include/lmoe.h declares (no compute calls -- there is no GPU here)."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "lmoe.h"
+
+
+def declared_symbols() -> list[str]:
+  text = HEADER.read_text()
+  return sorted(set(re.findall(r"LMOE_API\s+\w+\s+(lmoe_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+  syms = declared_symbols()
+  assert "lmoe_ragged_dot_bf16" in syms and "lmoe_dispatch" in syms
+  assert len(syms) >= 12
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+  from tokamax_tpu_kernel_lab_b200 import _native
+  if not _native.LIB_PATH.exists():
+    pytest.fail(f"{_native.LIB_PATH} is not built")
+  lib = ctypes.CDLL(str(_native.LIB_PATH))
+  for name in declared_symbols():
+    assert hasattr(lib, name), f"{name} declared in lmoe.h but not exported"
+
+
+def test_ctypes_signatures_cover_the_header():
+  from tokamax_tpu_kernel_lab_b200 import _native
+  assert sorted(_native.SIGNATURES) == declared_symbols()
+
+
+def test_version_call_needs_no_gpu():
+  from tokamax_tpu_kernel_lab_b200 import _native
+  assert _native.load().lmoe_version() >= 100
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+  from tokamax_tpu_kernel_lab_b200 import _native
+  monkeypatch.setattr(_native, "LIB_PATH", tmp_path / "absent.so")
+  monkeypatch.setattr(_native, "_lib", None)
+  with pytest.raises(_native.NativeLibraryMissing):
+    _native.load()

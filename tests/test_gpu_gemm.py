@@ -1,0 +1,174 @@
+"""GPU parity: tensor-core grouped GEMM (ragged_dot), fused gate/up SiTU-GLU,
+dense GEMM with residual add, f32 CUDA-core path -- all through the C ABI,
+checked against the CPU oracle."""
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lmoe_oracle as O
+from tests.gpu_util import (DISTRIBUTIONS, assert_bf16_close, distribution_sizes, to_dev, to_np,
+                            zipf_group_sizes)
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lm():
+  import tokamax_tpu_kernel_lab_b200 as lm
+  lm.load_native()
+  return lm
+
+
+def _rand(rng, *shape, scale=1.0):
+  return (rng.standard_normal(shape, dtype=np.float32) * np.float32(scale))
+
+
+def _ragged_case(lm, rng, m, k, n, gs, layout, extra_rows=0):
+  g = len(gs)
+  lhs = O.bf16_round(_rand(rng, m + extra_rows, k, scale=1 / np.sqrt(k)))
+  rhs = O.bf16_round(_rand(rng, g, k, n, scale=1 / np.sqrt(k)))
+  ref = O.ragged_dot(lhs, rhs, gs, dtype="fp32")
+  rhs_dev = rhs if layout == "gkn" else np.ascontiguousarray(rhs.transpose(0, 2, 1))
+  out = lm.ragged_dot(to_dev(lhs), to_dev(rhs_dev), torch.from_numpy(gs).cuda(),
+                      rhs_layout=layout)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  return ref, to_np(out)
+
+
+@pytest.mark.parametrize("layout", ["gkn", "gnk"])
+@pytest.mark.parametrize("dist", DISTRIBUTIONS)
+def test_ragged_dot_distributions(lm, layout, dist):
+  """benchmark_harness.py:156-205 distributions, small shape (m 512, k 256, n 384, g 4)."""
+  rng = np.random.default_rng(zlib.crc32(f"{layout}/{dist}".encode()))
+  gs = distribution_sizes(dist, 512, 4, rng)
+  ref, got = _ragged_case(lm, rng, 512, 256, 384, gs, layout)
+  assert_bf16_close(ref, got, f"{layout}/{dist}")
+
+
+@pytest.mark.parametrize("layout", ["gkn", "gnk"])
+@pytest.mark.parametrize("m,k,n,g", [(1, 64, 128, 1), (300, 200, 136, 7), (2048, 512, 512, 8),
+                                     (1000, 1024, 1024, 16)])
+def test_ragged_dot_shapes(lm, layout, m, k, n, g):
+  """Ragged boundaries mid-tile, K and N tails, single row."""
+  rng = np.random.default_rng(m * 7 + k)
+  gs = rng.multinomial(m, np.full(g, 1.0 / g)).astype(np.int32)
+  ref, got = _ragged_case(lm, rng, m, k, n, gs, layout)
+  assert_bf16_close(ref, got, f"{layout} {m}x{k}x{n} g{g}")
+
+
+def test_ragged_dot_rows_past_sum_are_zero(lm):
+  rng = np.random.default_rng(3)
+  gs = np.array([100, 0, 37], np.int32)
+  ref, got = _ragged_case(lm, rng, 137, 128, 256, gs, "gkn", extra_rows=91)
+  assert np.all(got[137:] == 0)
+  assert_bf16_close(ref, got)
+
+
+def test_ragged_dot_f32_output(lm):
+  rng = np.random.default_rng(4)
+  gs = np.array([70, 130, 56], np.int32)
+  lhs = O.bf16_round(_rand(rng, 256, 256))
+  rhs = O.bf16_round(_rand(rng, 3, 256, 128))
+  ref = O.ragged_dot(lhs, rhs, gs, dtype="fp32")
+  out = lm.ragged_dot(to_dev(lhs), to_dev(rhs), torch.from_numpy(gs).cuda(),
+                      preferred_element_type=torch.float32)
+  # bf16 products are exact in f32; only the accumulation order differs
+  assert np.abs(to_np(out) - ref).max() <= 1e-4 * np.abs(ref).max()
+
+
+def test_ragged_dot_config2_full_size(lm):
+  """Benchmark configuration 2: lhs (8192, 2048), rhs (128, 2048, 1536) bf16,
+  Zipf(1.1) group sizes with empty groups; values N(0,1)/sqrt(K)."""
+  rng = np.random.default_rng(1)
+  m, k, n, g = 8192, 2048, 1536, 128
+  gs = zipf_group_sizes(rng, m, g)
+  assert (gs == 0).any()
+  ref, got = _ragged_case(lm, rng, m, k, n, gs, "gkn")
+  assert_bf16_close(ref, got, "config 2")
+
+
+def test_ragged_dot_f32_kernel(lm):
+  rng = np.random.default_rng(5)
+  gs = np.array([5, 0, 60, 35], np.int32)
+  lhs = _rand(rng, 110, 96)
+  rhs = _rand(rng, 4, 96, 72)
+  for layout in ("gkn", "gnk"):
+    r = rhs if layout == "gkn" else np.ascontiguousarray(rhs.transpose(0, 2, 1))
+    out = lm.ragged_dot(torch.from_numpy(lhs).cuda(), torch.from_numpy(r).cuda(),
+                        torch.from_numpy(gs).cuda(), rhs_layout=layout)
+    ref = O.ragged_dot(lhs, rhs, gs, dtype="fp32")
+    assert np.allclose(to_np(out), ref, atol=1e-5, rtol=1e-5)
+    assert np.all(to_np(out)[100:] == 0)
+
+
+@pytest.mark.parametrize("layout", ["gkn", "gnk"])
+@pytest.mark.parametrize("round_gate_up", [True, False])
+def test_fused_gateup_situ(lm, layout, round_gate_up):
+  rng = np.random.default_rng(6)
+  m, k, inter, g = 1500, 512, 384, 6
+  gs = rng.multinomial(m - 20, np.full(g, 1.0 / g)).astype(np.int32)
+  lhs = O.bf16_round(_rand(rng, m, k))
+  wg = O.bf16_round(_rand(rng, g, k, inter, scale=0.05))
+  wu = O.bf16_round(_rand(rng, g, k, inter, scale=0.05))
+  fused = np.concatenate([wg, wu], axis=-1)
+  ref = O.fused_gateup_situ(lhs, fused, gs, inter, 4.0, 25.0, dtype="fp32",
+                            round_gate_up=round_gate_up)
+  w_dev = fused if layout == "gkn" else np.ascontiguousarray(fused.transpose(0, 2, 1))
+  out = lm.fused_gateup_situ(to_dev(lhs), to_dev(w_dev), torch.from_numpy(gs).cuda(),
+                             round_gate_up=round_gate_up, rhs_layout=layout)
+  got = to_np(out)
+  assert np.all(got[gs.sum():] == 0)
+  assert_bf16_close(ref, got, f"situ {layout} round={round_gate_up}")
+
+
+def test_fused_gateup_matches_unfused_kernels(lm):
+  """Fused vs unfused: ragged_dot(gate), ragged_dot(up), situ_and_mul; with the
+  bf16-round convention the two are bit-identical."""
+  rng = np.random.default_rng(7)
+  m, k, inter, g = 640, 256, 256, 5
+  gs = rng.multinomial(m, np.full(g, 1.0 / g)).astype(np.int32)
+  lhs = to_dev(_rand(rng, m, k))
+  wg = to_dev(_rand(rng, g, k, inter, scale=0.05))
+  wu = to_dev(_rand(rng, g, k, inter, scale=0.05))
+  gsd = torch.from_numpy(gs).cuda()
+  gate = lm.ragged_dot(lhs, wg, gsd)
+  up = lm.ragged_dot(lhs, wu, gsd)
+  unfused = lm.situ_and_mul(gate, up)
+  fused = lm.fused_gateup_situ(lhs, lm.prefuse_gateup_weights(wg, wu), gsd)
+  assert torch.equal(unfused, fused)
+
+
+def test_dense_gemm_residual_add(lm):
+  rng = np.random.default_rng(8)
+  a = O.bf16_round(_rand(rng, 333, 512))
+  w = O.bf16_round(_rand(rng, 512, 264, scale=0.05))
+  add = O.bf16_round(_rand(rng, 333, 264))
+  ref = O.bf16_round(O.bf16_round(a @ w) + add)
+  out = lm.gemm(to_dev(a), to_dev(np.ascontiguousarray(w.T)), addend=to_dev(add))
+  assert_bf16_close(ref, to_np(out), "gemm+add")
+
+
+def test_device_status_reports_oversized_groups(lm):
+  """group sizes summing past M are rejected on the device (no out-of-bounds
+  access): the status word records LMOE_DEVICE_BOUNDS."""
+  lhs = torch.zeros(64, 64, dtype=torch.bfloat16, device="cuda")
+  rhs = torch.zeros(2, 64, 64, dtype=torch.bfloat16, device="cuda")
+  gs = torch.tensor([60, 60], dtype=torch.int32, device="cuda")
+  lm.ragged_dot(lhs, rhs, gs)
+  with pytest.raises(RuntimeError, match="status 4"):
+    lm.check_device_status()
+  lm.check_device_status()  # reset by the previous check
+
+
+def test_unsupported_shapes_raise(lm):
+  lhs = torch.zeros(16, 20, dtype=torch.bfloat16, device="cuda")
+  rhs = torch.zeros(1, 20, 16, dtype=torch.bfloat16, device="cuda")
+  with pytest.raises(NotImplementedError):
+    lm.ragged_dot(lhs, rhs, torch.tensor([16], dtype=torch.int32, device="cuda"))
+  with pytest.raises(NotImplementedError):
+    lm.ragged_dot(lhs, rhs, torch.tensor([16], dtype=torch.int32, device="cuda"),
+                  implementation="mosaic_tpu_v2")

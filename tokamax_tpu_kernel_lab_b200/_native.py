@@ -1,0 +1,96 @@
+"""ctypes binding of the in-tree C ABI (`include/lmoe.h`, `liblmoe_b200.so`).
+
+There is no fallback: if the shared library is missing or fails to load, every
+operator raises `NativeLibraryMissing`.  Build it with
+`python -m tokamax_tpu_kernel_lab_b200.build`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+LIB_PATH = pathlib.Path(__file__).resolve().with_name("liblmoe_b200.so")
+
+LMOE_OK = 0
+LMOE_BAD_SHAPE = 1
+LMOE_UNSUPPORTED = 2
+LMOE_LAUNCH_FAILED = 3
+LMOE_DEVICE_BOUNDS = 4
+LMOE_WAIT_TIMEOUT = 5
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/lmoe.h one to one
+SIGNATURES = {
+    "lmoe_version": (_i32, []),
+    "lmoe_ragged_dot_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p]),
+    "lmoe_ragged_dot_f32": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p]),
+    "lmoe_gemm_f32": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _p]),
+    "lmoe_gemm_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p, _p]),
+    "lmoe_gateup_situ_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _f32,
+                                     _i32, _p, _p]),
+    "lmoe_situ_and_mul": (_i32, [_p, _p, _i64, _p, _i64, _i64, _f32, _f32, _i32, _p]),
+    "lmoe_router_topk": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
+    "lmoe_dispatch_workspace_size": (_sz, [_i64, _i64]),
+    "lmoe_dispatch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p,
+                             _p, _p, _sz, _p]),
+    "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _p]),
+    "lmoe_combine_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p, _p, _p]),
+    "lmoe_combine_scatter_add": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]),
+}
+
+
+class NativeLibraryMissing(RuntimeError):
+  pass
+
+
+class LmoeError(RuntimeError):
+  def __init__(self, name: str, code: int):
+    super().__init__(f"{name} failed with status {code}")
+    self.code = code
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+  """Load liblmoe_b200.so (once) and attach the C signatures."""
+  global _lib
+  with _lock:
+    if _lib is not None:
+      return _lib
+    if not LIB_PATH.exists():
+      raise NativeLibraryMissing(
+          f"{LIB_PATH} not found; build it with `python -m tokamax_tpu_kernel_lab_b200.build`")
+    try:
+      lib = ctypes.CDLL(str(LIB_PATH))
+    except OSError as e:  # pragma: no cover
+      raise NativeLibraryMissing(f"cannot load {LIB_PATH}: {e}") from e
+    for name, (res, args) in SIGNATURES.items():
+      fn = getattr(lib, name)
+      fn.restype = res
+      fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def call(name: str, *args) -> int:
+  """Invoke an entry point; raise on a non-OK host status.
+
+  LMOE_UNSUPPORTED maps to NotImplementedError (the reference's error class for
+  shapes an implementation does not support), LMOE_BAD_SHAPE to ValueError."""
+  rc = getattr(load(), name)(*args)
+  if rc == LMOE_OK:
+    return rc
+  if rc == LMOE_UNSUPPORTED:
+    raise NotImplementedError(f"{name}: unsupported shape or alignment (status {rc})")
+  if rc == LMOE_BAD_SHAPE:
+    raise ValueError(f"{name}: invalid shape (status {rc})")
+  raise LmoeError(name, rc)

@@ -1,0 +1,551 @@
+// Persistent grouped GEMM (ragged_dot) on sm_100a tensor cores.
+//
+//   out[r, :] = lhs[r, :] @ rhs[g(r)]        r in [off_g, off_g + group_sizes[g])
+//
+// Semantics follow `tokamax.ragged_dot(lhs, rhs, group_sizes)` as the reference
+// calls it (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:358-369),
+// i.e. the per-expert loop of kimi_k3_latent_moe_reference.py:383-406: groups
+// are contiguous row ranges in order, rows at or past sum(group_sizes) are
+// zero.  group_sizes lives in device memory and is read only on the device
+// (no host synchronisation).
+//
+// Design (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile (128 rows x 64 K, bf16, 128B swizzle) and
+//               B tile (BN x 64 K) per pipeline stage, completion on an mbarrier.
+//   warp 1      TMEM owner and UMMA issuer: tcgen05.mma kind::f16, M=128, N=BN,
+//               K=16 per instruction, f32 accumulator in TMEM, two accumulator
+//               buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
+//   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp owns one
+//               32-lane quarter of TMEM), fused activation, predicated stores of
+//               the rows that belong to the tile's group.
+// The tile schedule (group -> row offset, group -> first tile) is an in-CTA
+// prefix sum over group_sizes; tiles are (group, m-tile, n-tile) with n
+// fastest and are dealt round-robin to the persistent CTAs.  Empty groups own
+// no tiles, so their weights are never read.
+//
+// Epilogues:
+//   EPI_BF16      out = bf16(acc)
+//   EPI_F32       out = acc (f32)
+//   EPI_BF16_ADD  out = bf16(bf16(acc) + addend)    (residual add, bf16 rounding of each op)
+//   EPI_SITU      B tile = [gate cols | up cols] of a fused (G, 2I, K) / (G, K, 2I)
+//                 weight; out = bf16(situ(g, u)) with g, u = acc (rounded to bf16
+//                 first when round_gate_up, the convention of
+//                 kimi_k3_latent_moe_reference.py:296-310 / own_gateup_situ_pallas_kernel.py:116-125)
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "lmoe_internal.h"
+#include "ptx.cuh"
+
+namespace lmoe {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+constexpr int kMaxGroups = 2048;
+
+enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_BF16_ADD = 2, EPI_SITU = 3 };
+
+struct GemmArgs {
+  const int32_t* group_sizes;  // nullptr: a single group of M rows
+  int32_t* status;
+  void* out;
+  const __nv_bfloat16* addend;  // EPI_BF16_ADD
+  int64_t ldo;                  // output row pitch, elements
+  int64_t ld_add;               // addend row pitch, elements
+  int M, N, K, G;               // N = output columns (EPI_SITU: the intermediate size I)
+  int n_tiles;                  // ceil(N / output tile width)
+  int up_offset;                // EPI_SITU: row/col offset of the up half in the fused weight
+  float beta, linear_beta;
+  int round_gate_up;
+  int zero_tail;
+};
+
+template <int BN, int STAGES, bool B_MN, int EPI>
+struct GemmCfg {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kOutTileN = (EPI == EPI_SITU) ? BN / 2 : BN;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kGemmThreads * 4;
+  static constexpr int kBarBytes = 8 * (2 * STAGES + 5) + 16;
+  static constexpr size_t kSmem = 1024 + size_t(STAGES) * kStageBytes + kSchedBytes + kBarBytes;
+  static_assert(BN % 64 == 0 && BN <= 256, "BN");
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
+};
+
+// In-CTA schedule: row_off[g] = sum(gs[:g]), tile_start[g] = sum(tiles[:g]).
+// Returns the total tile count, or -1 when group_sizes is invalid.
+__device__ int build_schedule(const GemmArgs& a, int32_t* row_off, int32_t* tile_start,
+                              int32_t* scan_rows, int32_t* scan_tiles) {
+  const int G = a.G;
+  const int nthr = blockDim.x;
+  const int per = (G + nthr - 1) / nthr;
+  const int g0 = min(G, threadIdx.x * per);
+  const int g1 = min(G, g0 + per);
+  long long rows = 0, tiles = 0;
+  int bad = 0;
+  for (int g = g0; g < g1; ++g) {
+    const int s = a.group_sizes ? __ldg(a.group_sizes + g) : a.M;
+    if (s < 0) bad = 1;
+    const int ss = max(s, 0);
+    rows += ss;
+    tiles += static_cast<long long>((ss + kBM - 1) / kBM) * a.n_tiles;
+  }
+  scan_rows[threadIdx.x] = bad ? -1 : static_cast<int32_t>(min(rows, (long long)INT32_MAX));
+  scan_tiles[threadIdx.x] = static_cast<int32_t>(min(tiles, (long long)INT32_MAX));
+  __syncthreads();
+  __shared__ int s_total;
+  if (threadIdx.x == 0) {
+    long long r = 0, t = 0;
+    int invalid = 0;
+    for (int i = 0; i < nthr; ++i) {
+      const int rr = scan_rows[i];
+      const int tt = scan_tiles[i];
+      if (rr < 0) invalid = 1;
+      scan_rows[i] = static_cast<int32_t>(r);
+      scan_tiles[i] = static_cast<int32_t>(t);
+      r += max(rr, 0);
+      t += tt;
+    }
+    if (invalid || r > a.M || t > INT32_MAX) {
+      record_status(a.status, kDeviceBounds);
+      s_total = -1;
+    } else {
+      s_total = static_cast<int>(t);
+      row_off[G] = static_cast<int32_t>(r);
+      tile_start[G] = static_cast<int32_t>(t);
+    }
+  }
+  __syncthreads();
+  if (s_total >= 0) {
+    int r = scan_rows[threadIdx.x];
+    int t = scan_tiles[threadIdx.x];
+    for (int g = g0; g < g1; ++g) {
+      row_off[g] = r;
+      tile_start[g] = t;
+      const int s = a.group_sizes ? __ldg(a.group_sizes + g) : a.M;
+      r += s;
+      t += ((s + kBM - 1) / kBM) * a.n_tiles;
+    }
+  }
+  __syncthreads();
+  return s_total;
+}
+
+// last g with tile_start[g] <= t (groups with no tiles are skipped naturally)
+__device__ __forceinline__ int find_group(const int32_t* tile_start, int G, int t) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+struct TileCoord {
+  int g, m_tile, n_tile, row0, row_end;
+};
+
+__device__ __forceinline__ TileCoord decode_tile(const int32_t* tile_start, const int32_t* row_off,
+                                                 int G, int n_tiles, int t) {
+  TileCoord c;
+  c.g = find_group(tile_start, G, t);
+  const int local = t - tile_start[c.g];
+  c.m_tile = local / n_tiles;
+  c.n_tile = local - c.m_tile * n_tiles;
+  c.row0 = row_off[c.g] + c.m_tile * kBM;
+  c.row_end = row_off[c.g + 1];
+  return c;
+}
+
+__device__ __forceinline__ float situ_f(float g, float u, float beta, float lbeta) {
+  const float sig = 1.0f / (1.0f + expf(-g));
+  const float sg = (beta * tanhf(g / beta)) * sig;
+  const float bu = lbeta * tanhf(u / lbeta);
+  return sg * bu;
+}
+
+template <int BN, int STAGES, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using C = GemmCfg<BN, STAGES, B_MN, EPI>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  int32_t* row_off = reinterpret_cast<int32_t*>(smem + STAGES * C::kStageBytes);
+  int32_t* tile_start = row_off + (kMaxGroups + 1);
+  int32_t* scan_rows = tile_start + (kMaxGroups + 1);
+  int32_t* scan_tiles = scan_rows + kGemmThreads;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(scan_tiles + kGemmThreads);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = args.G;
+
+  if (threadIdx.x == 0) *abort_flag = 0;
+  const int total = build_schedule(args, row_off, tile_start, scan_rows, scan_tiles);
+  if (total < 0) return;  // uniform across the CTA; nothing allocated yet
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(tfull + b), 1);
+      mbar_init(smem_u32(tempty + b), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (args.K + kBK - 1) / kBK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0, last_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const TileCoord tc = decode_tile(tile_start, row_off, G, args.n_tiles, t);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(full + stage);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          const uint32_t a_dst = smem_u32(stages + stage * C::kStageBytes);
+          const uint32_t b_dst = a_dst + C::kABytes;
+          tma_load_2d(a_dst, &tmA, fb, kb * kBK, tc.row0);
+          // B tile: two halves of BN/2 output columns each
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int nbase;
+            if (EPI == EPI_SITU) {
+              nbase = (h == 0 ? 0 : args.up_offset) + tc.n_tile * (BN / 2);
+            } else {
+              nbase = tc.n_tile * BN + h * (BN / 2);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 128; ++c) {
+                tma_load_3d(b_dst + (h * (BN / 128) + c) * (kBK * 128), &tmB, fb, nbase + c * 64,
+                            kb * kBK, tc.g);
+              }
+            } else {
+              tma_load_3d(b_dst + h * (BN / 2) * 128, &tmB, fb, kb * kBK, nbase, tc.g);
+            }
+          }
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // abort: let every copy already issued land before the CTA retires
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) mbar_drain(smem_u32(full + s), (last_parity >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, B_MN);
+      uint32_t stage = 0, phase = 0;
+      uint32_t acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        if (!mbar_wait(smem_u32(tempty + acc), acc_phase ^ 1u, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stages + stage * C::kStageBytes);
+          const uint32_t b_addr = a_addr + C::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, kBK * 128, 1024)
+                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(empty + stage));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(tfull + acc));
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        // abort: wait for every UMMA already issued before TMEM is released
+        umma_commit(smem_u32(drain));
+        mbar_drain(smem_u32(drain), 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint32_t acc = 0, acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const TileCoord tc = decode_tile(tile_start, row_off, G, args.n_tiles, t);
+      if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.status)) break;
+      tc_fence_after();
+      const int r = tc.row0 + q * 32 + lane;
+      const bool valid = r < tc.row_end;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if (EPI == EPI_SITU) {
+#pragma unroll 1
+        for (int c = 0; c < (BN / 2) / 32; ++c) {
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, gv);
+          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, uv);
+          tmem_ld_wait();
+          const int col0 = tc.n_tile * (BN / 2) + c * 32;
+          if (valid && col0 < args.N) {
+            __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.out) + r * args.ldo + col0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              if (col0 + j * 8 < args.N) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float o[2];
+#pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    float g = __uint_as_float(gv[j * 8 + e * 2 + h]);
+                    float u = __uint_as_float(uv[j * 8 + e * 2 + h]);
+                    if (args.round_gate_up) {
+                      g = bf16_round_f(g);
+                      u = bf16_round_f(u);
+                    }
+                    o[h] = situ_f(g, u, args.beta, args.linear_beta);
+                  }
+                  pk[e] = pack_bf16x2(o[0], o[1]);
+                }
+                *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          tmem_ld_wait();
+          const int col0 = tc.n_tile * BN + c * 32;
+          if (valid && col0 < args.N) {
+            if (EPI == EPI_F32) {
+              float* orow = reinterpret_cast<float*>(args.out) + r * args.ldo + col0;
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (col0 + j * 4 < args.N)
+                  *reinterpret_cast<uint4*>(orow + j * 4) =
+                      make_uint4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+            } else {
+              __nv_bfloat16* orow =
+                  reinterpret_cast<__nv_bfloat16*>(args.out) + r * args.ldo + col0;
+              const __nv_bfloat16* arow =
+                  (EPI == EPI_BF16_ADD) ? args.addend + r * args.ld_add + col0 : nullptr;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                if (col0 + j * 8 < args.N) {
+                  uint32_t pk[4];
+                  if (EPI == EPI_BF16_ADD) {
+                    const uint4 av = *reinterpret_cast<const uint4*>(arow + j * 8);
+                    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const __nv_bfloat162 ab = *reinterpret_cast<const __nv_bfloat162*>(&aw[e]);
+                      const float x0 = bf16_round_f(__uint_as_float(v[j * 8 + e * 2]));
+                      const float x1 = bf16_round_f(__uint_as_float(v[j * 8 + e * 2 + 1]));
+                      pk[e] = pack_bf16x2(x0 + __low2float(ab), x1 + __high2float(ab));
+                    }
+                  } else {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                      pk[e] = pack_bf16x2(__uint_as_float(v[j * 8 + e * 2]),
+                                          __uint_as_float(v[j * 8 + e * 2 + 1]));
+                  }
+                  *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(tempty + acc));
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    // rows at or past sum(group_sizes) are zero (ragged_dot semantics)
+    if (args.zero_tail) {
+      const int esize = (EPI == EPI_F32) ? 4 : 2;
+      const int64_t row_bytes = static_cast<int64_t>(args.N) * esize;
+      const int64_t chunks_per_row = row_bytes / 16;
+      const int64_t first = row_off[G];
+      const int64_t n_chunks = (args.M - first) * chunks_per_row;
+      const int64_t pitch = args.ldo * esize;
+      const int etid = threadIdx.x - 64;
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * 128 + etid; i < n_chunks;
+           i += static_cast<int64_t>(gridDim.x) * 128) {
+        const int64_t rr = first + i / chunks_per_row;
+        const int64_t cc = i % chunks_per_row;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(args.out) + rr * pitch + cc * 16) =
+            make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// --------------------------------------------------------------------------- host side
+
+namespace {
+
+template <int BN, int STAGES, bool B_MN, int EPI>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int max_tiles,
+                cudaStream_t stream) {
+  using C = GemmCfg<BN, STAGES, B_MN, EPI>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, B_MN, EPI>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static uint64_t configured = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(configured & (1ull << dev))) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(C::kSmem)) != cudaSuccess)
+        return kLaunchFailed;
+      configured |= 1ull << dev;
+    }
+  }
+  const int sms = num_sms(dev);
+  const int grid = max(1, min(sms, max_tiles));
+  kern<<<grid, kGemmThreads, C::kSmem, stream>>>(ta, tb, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+constexpr int kStagesBN256 = 4;
+
+template <int EPI>
+int dispatch_layout(bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                    int max_tiles, cudaStream_t s) {
+  if (b_mn) return launch_gemm<256, kStagesBN256, true, EPI>(ta, tb, a, max_tiles, s);
+  return launch_gemm<256, kStagesBN256, false, EPI>(ta, tb, a, max_tiles, s);
+}
+
+}  // namespace
+
+// rhs_layout: 0 = (G, K, N) ("gkn", N contiguous, the reference's layout);
+//             1 = (G, N, K) ("gnk", K contiguous, torch nn.Linear layout)
+int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
+                      int64_t M, int64_t K, int64_t N_out, int64_t G, int rhs_layout, int epi,
+                      const void* addend, int64_t ld_add, int64_t up_offset, float beta,
+                      float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
+                      cudaStream_t stream) {
+  if (M < 0 || K <= 0 || N_out <= 0 || G <= 0 || G > kMaxGroups) return kBadShape;
+  if (M >= (1ll << 31) || K >= (1ll << 31) || N_out >= (1ll << 31)) return kBadShape;
+  if (rhs_layout != 0 && rhs_layout != 1) return kBadShape;
+  if (K % 8 != 0 || N_out % 8 != 0) return kUnsupported;  // 16-byte TMA strides / vector stores
+  if (M == 0) return kOk;
+  if ((reinterpret_cast<uintptr_t>(lhs) | reinterpret_cast<uintptr_t>(rhs) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return kUnsupported;
+  if (epi == EPI_BF16_ADD && (addend == nullptr || (reinterpret_cast<uintptr_t>(addend) & 15) ||
+                              ld_add % 8 != 0))
+    return kUnsupported;
+  const bool b_mn = rhs_layout == 0;
+  // width of the weight's N axis (the fused [gate|up] weight is 2I wide)
+  const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
+  if (epi == EPI_SITU && (up_offset != N_out)) return kBadShape;
+
+  CUtensorMap ta, tb;
+  if (!encode_tmap_bf16_2d(&ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                           static_cast<uint64_t>(K) * 2, kBK, kBM))
+    return kLaunchFailed;
+  if (b_mn) {
+    // dims {N, K, G}, box {64, 64, 1}
+    if (!encode_tmap_bf16_3d(&tb, rhs, n_weight, K, G, n_weight * 2, n_weight * K * 2, 64, kBK))
+      return kLaunchFailed;
+  } else {
+    // dims {K, N, G}, box {64, 128, 1}
+    if (!encode_tmap_bf16_3d(&tb, rhs, K, n_weight, G, K * 2, n_weight * K * 2, kBK, 128))
+      return kLaunchFailed;
+  }
+  GemmArgs a{};
+  a.group_sizes = group_sizes;
+  a.status = status;
+  a.out = out;
+  a.addend = static_cast<const __nv_bfloat16*>(addend);
+  a.ldo = N_out;
+  a.ld_add = ld_add;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N_out);
+  a.K = static_cast<int>(K);
+  a.G = static_cast<int>(G);
+  const int out_tile = (epi == EPI_SITU) ? 128 : 256;
+  a.n_tiles = static_cast<int>((N_out + out_tile - 1) / out_tile);
+  a.up_offset = static_cast<int>(up_offset);
+  a.beta = beta;
+  a.linear_beta = linear_beta;
+  a.round_gate_up = round_gate_up;
+  a.zero_tail = zero_tail;
+  if (group_sizes == nullptr) a.G = 1;
+  const int64_t max_tiles64 = ((M + kBM - 1) / kBM + a.G) * a.n_tiles;
+  const int max_tiles = static_cast<int>(std::min<int64_t>(max_tiles64, 1 << 30));
+  switch (epi) {
+    case EPI_BF16: return dispatch_layout<EPI_BF16>(b_mn, ta, tb, a, max_tiles, stream);
+    case EPI_F32: return dispatch_layout<EPI_F32>(b_mn, ta, tb, a, max_tiles, stream);
+    case EPI_BF16_ADD: return dispatch_layout<EPI_BF16_ADD>(b_mn, ta, tb, a, max_tiles, stream);
+    case EPI_SITU: return dispatch_layout<EPI_SITU>(b_mn, ta, tb, a, max_tiles, stream);
+    default: return kBadShape;
+  }
+}
+
+}  // namespace lmoe

@@ -1,0 +1,69 @@
+// Internal host-side declarations shared by the CUDA translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace lmoe {
+
+int num_sms(int device);
+
+// Tensor maps for bf16 tiles with 128-byte swizzle (box inner extent = 64
+// elements = 128 bytes).  Out-of-range elements read as zero.
+bool encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                         uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+bool encode_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                         uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                         uint32_t box1);
+// Tensor map for raw bytes (uint8), no swizzle, 3D.
+bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                       uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                       uint32_t box1);
+
+int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
+                      int64_t M, int64_t K, int64_t N_out, int64_t G, int rhs_layout, int epi,
+                      const void* addend, int64_t ld_add, int64_t up_offset, float beta,
+                      float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
+                      cudaStream_t stream);
+
+inline int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int simt_grouped_gemm_f32(const float* lhs, const float* rhs, const int32_t* group_sizes,
+                          float* out, const float* addend, int64_t M, int64_t K, int64_t N,
+                          int64_t G, int rhs_layout, int zero_tail, int32_t* status,
+                          cudaStream_t stream);
+int router_topk(const float* logits, const float* bias, int64_t T, int64_t E, int64_t k,
+                int activation, int renormalize, float rsf, int32_t* topk_idx, float* topk_w,
+                cudaStream_t stream);
+
+// Dispatch outputs (device pointers; optional ones may be null).
+struct DispatchOut {
+  int32_t* order;              // [m_out] entry index at each sorted position
+  int32_t* token_idx;          // [m_out] source token, -1 for padding
+  float* weight;               // [m_out] combine weight, 0 for padding
+  int32_t* slot_pos;           // [S]     sorted position of entry i, -1 if not kept
+  int32_t* group_sizes;        // [num_keys (+1 with the padding bucket)]
+  int32_t* per_expert_counts;  // [num_keys]
+  uint8_t* valid;              // [m_out]
+};
+size_t dispatch_workspace_bytes(int64_t n_ext, int64_t num_keys);
+int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64_t top_k,
+                  int64_t start, int64_t num_keys, int64_t m_out, int pad_bucket, DispatchOut o,
+                  void* workspace, size_t ws_bytes, cudaStream_t stream);
+int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
+                int64_t row_bytes, cudaStream_t stream);
+int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
+                    const void* norm_scale, int64_t T, int64_t k, int64_t L, float eps, int bf16,
+                    void* routed_out, void* normed_out, cudaStream_t stream);
+int scatter_add(const void* shard_out, const int32_t* idx, const float* w, void* routed,
+                int64_t rows, int64_t L, int64_t T, int bf16, cudaStream_t stream);
+int situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
+                 int64_t I, float beta, float lbeta, int bf16, cudaStream_t stream);
+
+}  // namespace lmoe

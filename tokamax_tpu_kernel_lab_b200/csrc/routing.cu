@@ -1,0 +1,577 @@
+// Router top-k, dispatch (stable counting sort + capacity padding + row
+// gather), weighted combine + RMSNorm, scatter-add combine and the unfused
+// SiTU-GLU activation.  All HBM-bound integer/byte work: warp-level
+// primitives, 16-byte vector accesses, no tensor cores.
+//
+// Reference semantics (paths relative to the reference project):
+//   router        05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:347-356
+//   dispatch      kimi_k3_latent_moe_reference.py:370-378 (full) and
+//                 kimi_k3_latent_moe_reference.py:754-877 (shard, capacity padded)
+//   combine       kimi_k3_latent_moe_reference.py:413-416, 286-293 (RMSNorm)
+//   scatter-add   kimi_k3_latent_moe_reference.py:1113-1141
+//   SiTU-GLU      kimi_k3_latent_moe_reference.py:296-310
+#include <cuda_bf16.h>
+
+#include <cfloat>
+
+#include "lmoe_internal.h"
+#include "ptx.cuh"
+
+namespace lmoe {
+
+// =========================================================================== router
+// One warp per token.  Lane l holds experts e = l + 32*j, j < PER.
+// Selection = top-k of scores_for_choice (descending, ties -> lower expert id,
+// the `jax.lax.top_k` rule); weights = un-biased scores of the winners,
+// renormalised in slot order, times routed_scaling_factor.
+template <int PER>
+__global__ void __launch_bounds__(256) router_topk_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
+    int activation, int renormalize, float rsf, int32_t* __restrict__ topk_idx,
+    float* __restrict__ topk_w) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* row = logits + static_cast<int64_t>(warp) * E;
+  float sc[PER], key[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = lane + 32 * j;
+    sc[j] = (e < E) ? row[e] : -FLT_MAX;
+  }
+  if (activation == 0) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = 1.0f / (1.0f + expf(-sc[j]));
+  } else {
+    float m = -FLT_MAX;
+#pragma unroll
+    for (int j = 0; j < PER; ++j)
+      if (lane + 32 * j < E) m = fmaxf(m, sc[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      sc[j] = (lane + 32 * j < E) ? expf(sc[j] - m) : 0.f;
+      s += sc[j];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = sc[j] / s;
+  }
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = lane + 32 * j;
+    key[j] = (e < E) ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
+  }
+  float wsum = 0.f;
+  float my_w = 0.f;
+  int my_idx = 0;
+  for (int s = 0; s < k; ++s) {
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && (key[j] > bv || (key[j] == bv && e < bi))) {
+        bv = key[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    // owner lane takes the winner out and broadcasts its un-biased score
+    float wv = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      if (lane + 32 * j == bi) {
+        wv = sc[j];
+        key[j] = -FLT_MAX;
+      }
+    }
+    wv = __shfl_sync(0xffffffffu, wv, bi & 31);
+    wsum += wv;
+    if (lane == s) {
+      my_w = wv;
+      my_idx = bi;
+    }
+  }
+  if (lane < k) {
+    float w = my_w;
+    if (k > 1 && renormalize) w = w / (wsum + 1e-20f);
+    w = w * rsf;
+    topk_idx[static_cast<int64_t>(warp) * k + lane] = my_idx;
+    topk_w[static_cast<int64_t>(warp) * k + lane] = w;
+  }
+}
+
+int router_topk(const float* logits, const float* bias, int64_t T, int64_t E, int64_t k,
+                int activation, int renormalize, float rsf, int32_t* topk_idx, float* topk_w,
+                cudaStream_t stream) {
+  if (T < 0 || E <= 0 || E > 1024 || k <= 0 || k > 32 || k > E) return kBadShape;
+  if (activation != 0 && activation != 1) return kBadShape;
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const int blocks = static_cast<int>((T * 32 + threads - 1) / threads);
+  const int per = static_cast<int>((E + 31) / 32);
+#define LMOE_ROUTER(P)                                                                      \
+  router_topk_kernel<P><<<blocks, threads, 0, stream>>>(logits, bias, (int)T, (int)E, (int)k, \
+                                                         activation, renormalize, rsf,        \
+                                                         topk_idx, topk_w)
+  if (per <= 2) LMOE_ROUTER(2);
+  else if (per <= 4) LMOE_ROUTER(4);
+  else if (per <= 8) LMOE_ROUTER(8);
+  else if (per <= 16) LMOE_ROUTER(16);
+  else if (per <= 28) LMOE_ROUTER(28);
+  else LMOE_ROUTER(32);
+#undef LMOE_ROUTER
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+// =========================================================================== dispatch
+// Stable counting sort of the (token, slot) entries by key:
+//   key(i) = flat_ids[i] - start   if the id is in [start, start + num_keys)
+//          = num_keys (sentinel)   otherwise, and for the padding entries
+//                                   i >= T*k that fill the sort up to m_padded
+// Position of entry i = bin_start[key] + (#entries of the same key in earlier
+// chunks) + (#entries of the same key earlier in its chunk); the first
+// m_padded positions are kept (tail drop on overflow).
+constexpr int kDispThreads = 256;
+constexpr int kDispItems = 8;                                // entries per thread
+constexpr int kDispChunk = kDispThreads * kDispItems;        // entries per block
+constexpr int kMaxBins = 2049;                               // num_keys + 1
+
+struct DispatchWs {
+  int32_t* counts;  // [bins][nchunks]  per-chunk counts, then per-chunk exclusive prefix
+  int32_t* totals;  // [bins]
+  int32_t* rank;    // [n_ext]          rank of the entry within its chunk and key
+};
+
+__device__ __forceinline__ int entry_key(const int32_t* flat_ids, int64_t i, int64_t S, int start,
+                                         int num_keys) {
+  if (i >= S) return num_keys;
+  const int id = flat_ids[i];
+  const int local = id - start;
+  return (local >= 0 && local < num_keys) ? local : num_keys;
+}
+
+// Kernel 1: per-chunk histogram and stable in-chunk ranks.  Each warp owns a
+// contiguous run of 32*kDispItems entries, processed 32 at a time in order;
+// __match_any_sync finds equal keys inside a 32-entry round.
+__global__ void __launch_bounds__(kDispThreads) dispatch_rank_kernel(
+    const int32_t* __restrict__ flat_ids, int64_t S, int64_t n_ext, int start, int num_keys,
+    int nchunks, DispatchWs ws) {
+  extern __shared__ uint16_t whist[];  // [8 warps][bins]
+  const int bins = num_keys + 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 8 * bins; i += blockDim.x) whist[i] = 0;
+  __syncthreads();
+  uint16_t* h = whist + warp * bins;
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kDispChunk + warp * 32 * kDispItems;
+  int keys[kDispItems];
+  int ranks[kDispItems];
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int it = 0; it < kDispItems; ++it) {
+    const int64_t i = base + it * 32 + lane;
+    const bool live = i < n_ext;
+    const int key = live ? entry_key(flat_ids, i, S, start, num_keys) : -1 - lane;  // dead lanes unique
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int before = __popc(peers & lt);
+    const int leader = __ffs(peers) - 1;
+    int r = 0;
+    if (live) r = h[key] + before;
+    __syncwarp();
+    if (live && lane == leader) h[key] = static_cast<uint16_t>(h[key] + __popc(peers));
+    __syncwarp();
+    keys[it] = key;
+    ranks[it] = r;
+  }
+  __syncthreads();
+  // exclusive prefix over the 8 warps for every bin; chunk total to global
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) {
+    int run = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int c = whist[w * bins + b];
+      whist[w * bins + b] = static_cast<uint16_t>(run);
+      run += c;
+    }
+    ws.counts[static_cast<int64_t>(b) * nchunks + blockIdx.x] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < kDispItems; ++it) {
+    const int64_t i = base + it * 32 + lane;
+    if (i < n_ext) ws.rank[i] = whist[warp * bins + keys[it]] + ranks[it];
+  }
+}
+
+// Kernel 2: one warp per bin: exclusive prefix of its per-chunk counts, total.
+__global__ void dispatch_bin_scan_kernel(int bins, int nchunks, DispatchWs ws) {
+  const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (b >= bins) return;
+  int32_t* row = ws.counts + static_cast<int64_t>(b) * nchunks;
+  int carry = 0;
+  for (int c0 = 0; c0 < nchunks; c0 += 32) {
+    const int c = c0 + lane;
+    const int v = (c < nchunks) ? row[c] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (c < nchunks) row[c] = carry + incl - v;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) ws.totals[b] = carry;
+}
+
+
+
+// Kernel 3: every block rebuilds the bin starts (exclusive scan of the totals)
+// in shared memory, then scatters its chunk's entries.  Block 0 also writes
+// group_sizes (kept counts after the m_out cap, plus the padding bucket).
+__global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
+    const int32_t* __restrict__ flat_ids, const float* __restrict__ flat_w, int64_t S,
+    int64_t n_ext, int start, int num_keys, int top_k, int64_t m_out, int pad_bucket, int nchunks,
+    DispatchWs ws, DispatchOut o) {
+  __shared__ int bin_start[kMaxBins + 1];
+  __shared__ int warp_sums[kDispThreads / 32];
+  const int bins = num_keys + 1;
+  // block-wide exclusive scan of totals[0..bins)
+  const int per = (bins + kDispThreads - 1) / kDispThreads;
+  const int b0 = min(bins, static_cast<int>(threadIdx.x) * per), b1 = min(bins, b0 + per);
+  int local = 0;
+  for (int b = b0; b < b1; ++b) local += ws.totals[b];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  int wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += warp_sums[w];
+  int run = wbase + incl - local;
+  for (int b = b0; b < b1; ++b) {
+    bin_start[b] = run;
+    run += ws.totals[b];
+  }
+  if (threadIdx.x == kDispThreads - 1) bin_start[bins] = run;
+  __syncthreads();
+
+  if (blockIdx.x == 0) {
+    int kept_local = 0;
+    for (int b = threadIdx.x; b < num_keys; b += blockDim.x) {
+      const int64_t s0 = bin_start[b];
+      const int64_t room = m_out - s0;
+      const int64_t tb = ws.totals[b];
+      const int64_t kept = room <= 0 ? 0 : (tb < room ? tb : room);
+      o.group_sizes[b] = static_cast<int32_t>(kept);
+      if (o.per_expert_counts) o.per_expert_counts[b] = static_cast<int32_t>(kept);
+      kept_local += static_cast<int>(kept);
+    }
+    if (pad_bucket) {
+      // padding bucket = m_out - sum(kept): reduce kept_local over the block
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) kept_local += __shfl_xor_sync(0xffffffffu, kept_local, off);
+      __syncthreads();
+      if (lane == 0) warp_sums[warp] = kept_local;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int tot = 0;
+        for (int w = 0; w < kDispThreads / 32; ++w) tot += warp_sums[w];
+        o.group_sizes[num_keys] = static_cast<int32_t>(m_out - tot);
+      }
+    }
+  }
+
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kDispChunk;
+  for (int it = 0; it < kDispItems; ++it) {
+    const int64_t i = base + it * kDispThreads + threadIdx.x;
+    if (i >= n_ext) break;
+    const int key = entry_key(flat_ids, i, S, start, num_keys);
+    const int64_t pos = static_cast<int64_t>(bin_start[key]) +
+                        ws.counts[static_cast<int64_t>(key) * nchunks + blockIdx.x] + ws.rank[i];
+    const bool in_range = pos < m_out;
+    if (i < S && o.slot_pos) o.slot_pos[i] = (in_range && key < num_keys) ? static_cast<int32_t>(pos) : -1;
+    if (!in_range) continue;
+    const bool valid = key < num_keys;
+    if (o.order) o.order[pos] = static_cast<int32_t>(i);
+    o.token_idx[pos] = valid ? static_cast<int32_t>(i / top_k) : -1;
+    if (o.weight) o.weight[pos] = (valid && flat_w) ? flat_w[i] : 0.f;
+    if (o.valid) o.valid[pos] = valid ? 1 : 0;
+  }
+}
+
+// Kernel 4: row gather, one warp per output row, 16-byte vectors.
+//   out[p, :] = token_idx[p] >= 0 ? x[token_idx[p], :] : 0
+__global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restrict__ x,
+                                                          const int32_t* __restrict__ token_idx,
+                                                          uint4* __restrict__ out, int64_t rows,
+                                                          int vec_per_row, int64_t x_rows) {
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t p = warp; p < rows; p += nwarps) {
+    const int t = token_idx[p];
+    uint4* dst = out + p * vec_per_row;
+    if (t >= 0 && t < x_rows) {
+      const uint4* src = x + static_cast<int64_t>(t) * vec_per_row;
+      int v = lane;
+      for (; v + 96 < vec_per_row; v += 128) {
+        const uint4 a = __ldg(src + v), b = __ldg(src + v + 32), c = __ldg(src + v + 64),
+                    d = __ldg(src + v + 96);
+        dst[v] = a;
+        dst[v + 32] = b;
+        dst[v + 64] = c;
+        dst[v + 96] = d;
+      }
+      for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
+    } else {
+      for (int v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+size_t dispatch_workspace_bytes(int64_t n_ext, int64_t num_keys) {
+  const int64_t nchunks = (n_ext + kDispChunk - 1) / kDispChunk;
+  const int64_t bins = num_keys + 1;
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  return static_cast<size_t>(al(bins * nchunks * 4) + al(bins * 4) + al(n_ext * 4));
+}
+
+int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64_t top_k,
+                  int64_t start, int64_t num_keys, int64_t m_out, int pad_bucket, DispatchOut o,
+                  void* workspace, size_t ws_bytes, cudaStream_t stream) {
+  if (S < 0 || top_k <= 0 || num_keys <= 0 || num_keys + 1 > kMaxBins || m_out < 0)
+    return kBadShape;
+  if (S >= (1ll << 31) || m_out >= (1ll << 31)) return kBadShape;
+  const int64_t n_ext = std::max<int64_t>(S, m_out);
+  if (ws_bytes < dispatch_workspace_bytes(n_ext, num_keys) || (n_ext > 0 && workspace == nullptr))
+    return kBadShape;
+  if (n_ext == 0) {
+    // no entries: every group is empty
+    if (cudaMemsetAsync(o.group_sizes, 0, (num_keys + (pad_bucket ? 1 : 0)) * 4, stream) != cudaSuccess)
+      return kLaunchFailed;
+    if (o.per_expert_counts && cudaMemsetAsync(o.per_expert_counts, 0, num_keys * 4, stream) != cudaSuccess)
+      return kLaunchFailed;
+    return kOk;
+  }
+  const int nchunks = static_cast<int>((n_ext + kDispChunk - 1) / kDispChunk);
+  const int bins = static_cast<int>(num_keys + 1);
+  auto al = [](int64_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* p = static_cast<uint8_t*>(workspace);
+  DispatchWs ws;
+  ws.counts = reinterpret_cast<int32_t*>(p);
+  p += al(static_cast<int64_t>(bins) * nchunks * 4);
+  ws.totals = reinterpret_cast<int32_t*>(p);
+  p += al(bins * 4);
+  ws.rank = reinterpret_cast<int32_t*>(p);
+  const size_t sh = static_cast<size_t>(8) * bins * sizeof(uint16_t);
+  if (sh > 48 * 1024) {
+    if (cudaFuncSetAttribute(dispatch_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sh)) != cudaSuccess)
+      return kLaunchFailed;
+  }
+  dispatch_rank_kernel<<<nchunks, kDispThreads, sh, stream>>>(flat_ids, S, n_ext,
+                                                              static_cast<int>(start),
+                                                              static_cast<int>(num_keys), nchunks, ws);
+  dispatch_bin_scan_kernel<<<(bins * 32 + 255) / 256, 256, 0, stream>>>(bins, nchunks, ws);
+  dispatch_scatter_kernel<<<nchunks, kDispThreads, 0, stream>>>(
+      flat_ids, flat_w, S, n_ext, static_cast<int>(start), static_cast<int>(num_keys),
+      static_cast<int>(top_k), m_out, pad_bucket, nchunks, ws, o);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
+                int64_t row_bytes, cudaStream_t stream) {
+  if (rows < 0 || row_bytes <= 0 || row_bytes % 16 != 0) return kBadShape;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return kUnsupported;
+  if (rows == 0) return kOk;
+  const int threads = 256;
+  const int64_t want = (rows * 32 + threads - 1) / threads;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms(current_device())) * 16));
+  gather_rows_kernel<<<blocks, threads, 0, stream>>>(static_cast<const uint4*>(x), token_idx,
+                                                     static_cast<uint4*>(out), rows,
+                                                     static_cast<int>(row_bytes / 16), x_rows);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+// =========================================================================== combine
+// routed[t] = bf16( sum_s out[slot_pos[t*k+s]] * w[t,s] )   (f32, slot order)
+// normed[t] = bf16( bf16(routed * 1/sqrt(mean(routed^2) + eps)) * scale )
+// One block per token; L elements staged in shared memory as f32.
+template <bool BF16_IO>
+__global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
+    const void* __restrict__ expert_out, const int32_t* __restrict__ slot_pos,
+    const float* __restrict__ topk_w, const void* __restrict__ norm_scale, int T, int k, int L,
+    float eps, void* __restrict__ routed_out, void* __restrict__ normed_out) {
+  extern __shared__ float racc[];
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < L; c += blockDim.x) racc[c] = 0.f;
+  // no barrier needed: each thread owns the same columns in every loop below
+  for (int s = 0; s < k; ++s) {
+    const int p = slot_pos[static_cast<int64_t>(t) * k + s];
+    const float w = topk_w[static_cast<int64_t>(t) * k + s];
+    if (p < 0) continue;
+    if (BF16_IO) {
+      const __nv_bfloat16* row = static_cast<const __nv_bfloat16*>(expert_out) + static_cast<int64_t>(p) * L;
+      for (int c = threadIdx.x; c < L; c += blockDim.x)
+        racc[c] = __fadd_rn(racc[c], __fmul_rn(__bfloat162float(row[c]), w));
+    } else {
+      const float* row = static_cast<const float*>(expert_out) + static_cast<int64_t>(p) * L;
+      for (int c = threadIdx.x; c < L; c += blockDim.x)
+        racc[c] = __fadd_rn(racc[c], __fmul_rn(row[c], w));
+    }
+  }
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < L; c += blockDim.x) {
+    float v = racc[c];
+    if (BF16_IO) v = bf16_round_f(v);
+    racc[c] = v;
+    ss += v * v;
+    if (routed_out) {
+      if (BF16_IO)
+        static_cast<__nv_bfloat16*>(routed_out)[static_cast<int64_t>(t) * L + c] = __float2bfloat16_rn(v);
+      else
+        static_cast<float*>(routed_out)[static_cast<int64_t>(t) * L + c] = v;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = (threadIdx.x < (blockDim.x >> 5)) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float var = red[0] / static_cast<float>(L);
+  const float inv = 1.0f / sqrtf(var + eps);
+  if (normed_out) {
+    for (int c = threadIdx.x; c < L; c += blockDim.x) {
+      float n = racc[c] * inv;
+      if (BF16_IO) {
+        n = bf16_round_f(n);
+        const float sc = __bfloat162float(static_cast<const __nv_bfloat16*>(norm_scale)[c]);
+        static_cast<__nv_bfloat16*>(normed_out)[static_cast<int64_t>(t) * L + c] = __float2bfloat16_rn(n * sc);
+      } else {
+        const float sc = static_cast<const float*>(norm_scale)[c];
+        static_cast<float*>(normed_out)[static_cast<int64_t>(t) * L + c] = n * sc;
+      }
+    }
+  }
+}
+
+int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
+                    const void* norm_scale, int64_t T, int64_t k, int64_t L, float eps, int bf16,
+                    void* routed_out, void* normed_out, cudaStream_t stream) {
+  if (T < 0 || k <= 0 || L <= 0 || L > 12288) return kBadShape;  // L f32 values in 48 KB smem
+  if (T == 0) return kOk;
+  const size_t sh = static_cast<size_t>(L) * sizeof(float);
+  if (bf16)
+    combine_rmsnorm_kernel<true><<<static_cast<int>(T), 256, sh, stream>>>(
+        expert_out, slot_pos, topk_w, norm_scale, (int)T, (int)k, (int)L, eps, routed_out, normed_out);
+  else
+    combine_rmsnorm_kernel<false><<<static_cast<int>(T), 256, sh, stream>>>(
+        expert_out, slot_pos, topk_w, norm_scale, (int)T, (int)k, (int)L, eps, routed_out, normed_out);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+// =========================================================================== scatter-add
+// routed[idx[p], :] += dtype(shard_out[p, :] * w[p])  for every padded row p
+// with idx[p] >= 0 (idx == -1 rows carry weight 0 by construction).
+// One warp per row, bf16x2 atomics (f32 atomics for the f32 variant).
+template <bool BF16_IO>
+__global__ void __launch_bounds__(256) scatter_add_kernel(const void* __restrict__ shard_out,
+                                                          const int32_t* __restrict__ idx,
+                                                          const float* __restrict__ w,
+                                                          void* routed, int64_t rows, int L, int T) {
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const int t = idx[warp];
+  const float wv = w[warp];
+  if (t < 0 || t >= T || wv == 0.f) return;
+  if (BF16_IO) {
+    const __nv_bfloat162* src =
+        reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(shard_out) + warp * L);
+    __nv_bfloat162* dst =
+        reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(routed) + static_cast<int64_t>(t) * L);
+    for (int c = lane; c < L / 2; c += 32) {
+      const float2 v = __bfloat1622float2(src[c]);
+      atomicAdd(dst + c, __floats2bfloat162_rn(v.x * wv, v.y * wv));
+    }
+  } else {
+    const float* src = static_cast<const float*>(shard_out) + warp * L;
+    float* dst = static_cast<float*>(routed) + static_cast<int64_t>(t) * L;
+    for (int c = lane; c < L; c += 32) atomicAdd(dst + c, src[c] * wv);
+  }
+}
+
+int scatter_add(const void* shard_out, const int32_t* idx, const float* w, void* routed,
+                int64_t rows, int64_t L, int64_t T, int bf16, cudaStream_t stream) {
+  if (rows < 0 || L <= 0 || T < 0 || (bf16 && L % 2)) return kBadShape;
+  if (rows == 0) return kOk;
+  const int blocks = static_cast<int>((rows * 32 + 255) / 256);
+  if (bf16)
+    scatter_add_kernel<true><<<blocks, 256, 0, stream>>>(shard_out, idx, w, routed, rows, (int)L, (int)T);
+  else
+    scatter_add_kernel<false><<<blocks, 256, 0, stream>>>(shard_out, idx, w, routed, rows, (int)L, (int)T);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+// =========================================================================== SiTU-GLU
+// out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)), f32 math.
+// gate/up may be two arrays or the two halves of one fused [gate|up] row.
+template <bool BF16_IO>
+__global__ void situ_kernel(const void* __restrict__ gate, const void* __restrict__ up,
+                            int64_t ld_in, void* __restrict__ out, int64_t rows, int64_t I,
+                            float beta, float lbeta) {
+  const int64_t n = rows * I;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / I, c = i - r * I;
+    float g, u;
+    if (BF16_IO) {
+      g = __bfloat162float(static_cast<const __nv_bfloat16*>(gate)[r * ld_in + c]);
+      u = __bfloat162float(static_cast<const __nv_bfloat16*>(up)[r * ld_in + c]);
+    } else {
+      g = static_cast<const float*>(gate)[r * ld_in + c];
+      u = static_cast<const float*>(up)[r * ld_in + c];
+    }
+    const float sig = 1.0f / (1.0f + expf(-g));
+    const float v = ((beta * tanhf(g / beta)) * sig) * (lbeta * tanhf(u / lbeta));
+    if (BF16_IO) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(out)[i] = v;
+  }
+}
+
+int situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
+                 int64_t I, float beta, float lbeta, int bf16, cudaStream_t stream) {
+  if (rows < 0 || I <= 0 || ld_in < I) return kBadShape;
+  if (rows == 0) return kOk;
+  const int blocks = static_cast<int>(std::min<int64_t>((rows * I + 255) / 256, 148 * 32));
+  if (bf16) situ_kernel<true><<<blocks, 256, 0, stream>>>(gate, up, ld_in, out, rows, I, beta, lbeta);
+  else situ_kernel<false><<<blocks, 256, 0, stream>>>(gate, up, ld_in, out, rows, I, beta, lbeta);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace lmoe

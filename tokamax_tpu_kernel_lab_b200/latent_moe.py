@@ -1,0 +1,235 @@
+"""LatentMoE layer forward on B200: the model-level drop-in for
+`latent_moe_forward` (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:330-435)
+and `latent_moe_forward_ragged_dot` (kimi_k3_latent_moe_ragged_dot.py:317-391).
+
+Weights arrive in the reference's (in, out) layout (`LatentMoEWeights`,
+kimi_k3_latent_moe_reference.py:217-252) and are re-laid out ONCE by
+`prepare_weights` into the K-major forms the kernels stream (the analogue of
+the reference's one-time `prefuse_gateup_weights`, kimi_k3_latent_moe_ragged_dot.py:610-641):
+
+  router      (E, d)          bf16/f32    logits = h @ W^T in f32
+  down        (L, d)          x = h @ W_down
+  expert_gu   (E, 2I, L)      [gate | up] rows, one fused grouped GEMM + SiTU-GLU
+  expert_down (E, L, I)
+  up          (d, L)
+  shared_gu   (2*Is, d)       [gate | up] of the shared expert (one dense group)
+  shared_down (d, Is)
+
+bf16 forward, in stream order (11 launches, no host synchronisation):
+  1 logits      tensor-core GEMM, f32 out          (exact bf16 products, f32 sums)
+  2 top-k       router_topk                         (sigmoid, bias for selection only)
+  3 x           tensor-core GEMM (down-projection)
+  4-6 dispatch  stable counting sort by expert      (order, slot_pos, group_sizes)
+  7 gather      sorted rows of x
+  8 gate/up     grouped GEMM + fused SiTU-GLU epilogue
+  9 down        grouped GEMM
+  10 combine    f32 weighted sum in slot order + RMSNorm
+  11 up-proj    GEMM;  12 shared gate/up GEMM + SiTU;  13 shared down GEMM + residual add
+The f32 forward runs the same steps on the f32 CUDA-core kernels.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+
+import torch
+
+from . import ops
+
+
+@dataclasses.dataclass(frozen=True)
+class LatentMoEConfig:
+  """kimi_k3_latent_moe_reference.py:156-171."""
+
+  hidden_size: int
+  latent_size: int
+  intermediate_size: int
+  num_experts: int
+  top_k: int
+  num_shared_experts: int
+  moe_renormalize: bool = True
+  routed_scaling_factor: float = 1.0
+  rms_norm_eps: float = 1e-5
+  activation_situ_beta: float = 4.0
+  activation_situ_linear_beta: float = 25.0
+
+
+def toy_config() -> LatentMoEConfig:
+  """kimi_k3_latent_moe_reference.py:174-188."""
+  return LatentMoEConfig(64, 32, 48, 8, 2, 1)
+
+
+def kimi_k3_config() -> LatentMoEConfig:
+  """kimi_k3_latent_moe_reference.py:191-208."""
+  return LatentMoEConfig(7168, 3584, 3072, 896, 16, 2)
+
+
+def reduced_cpu_config() -> LatentMoEConfig:
+  """Configuration 1 of the benchmark plan: d 512 -> L 256, 64 experts, I 512, top-8."""
+  return LatentMoEConfig(512, 256, 512, 64, 8, 1)
+
+
+def full_layer_config() -> LatentMoEConfig:
+  """Configuration 5: d 7168, L 2048, 896 experts, I 1024, top-16, 2 shared."""
+  return LatentMoEConfig(7168, 2048, 1024, 896, 16, 2)
+
+
+@dataclasses.dataclass
+class LatentMoEWeights:
+  """kimi_k3_latent_moe_reference.py:217-252, (in, out) layout, torch tensors."""
+
+  router_weight: torch.Tensor  # (d, E)
+  e_score_correction_bias: torch.Tensor  # (E,)
+  down_proj: torch.Tensor  # (d, L)
+  up_proj: torch.Tensor  # (L, d)
+  expert_gate: torch.Tensor  # (E, L, I)
+  expert_up: torch.Tensor  # (E, L, I)
+  expert_down: torch.Tensor  # (E, I, L)
+  norm_scale: torch.Tensor  # (L,)
+  shared_gate: torch.Tensor  # (d, I*ns)
+  shared_up: torch.Tensor  # (d, I*ns)
+  shared_down: torch.Tensor  # (I*ns, d)
+
+
+def init_weights(config: LatentMoEConfig, seed: int = 0, dtype: torch.dtype = torch.bfloat16,
+                 device: str | torch.device = "cuda", bias_std: float = 0.0) -> LatentMoEWeights:
+  """N(0, 0.02^2) weights (the distribution of kimi_k3_latent_moe_reference.py:255-283),
+  drawn on the device from a seeded generator; optional N(0, bias_std^2)
+  router bias for the skewed-load configurations."""
+  gen = torch.Generator(device=device)
+  gen.manual_seed(seed)
+  c = config
+  si = c.intermediate_size * c.num_shared_experts
+
+  def normal(*shape):
+    return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * 0.02).to(dtype)
+
+  bias = torch.zeros(c.num_experts, device=device, dtype=torch.float32)
+  if bias_std > 0:
+    bias = torch.randn(c.num_experts, generator=gen, device=device) * bias_std
+  return LatentMoEWeights(
+      router_weight=normal(c.hidden_size, c.num_experts),
+      e_score_correction_bias=bias.to(dtype),
+      down_proj=normal(c.hidden_size, c.latent_size),
+      up_proj=normal(c.latent_size, c.hidden_size),
+      expert_gate=normal(c.num_experts, c.latent_size, c.intermediate_size),
+      expert_up=normal(c.num_experts, c.latent_size, c.intermediate_size),
+      expert_down=normal(c.num_experts, c.intermediate_size, c.latent_size),
+      norm_scale=torch.ones(c.latent_size, device=device, dtype=dtype),
+      shared_gate=normal(c.hidden_size, si),
+      shared_up=normal(c.hidden_size, si),
+      shared_down=normal(si, c.hidden_size),
+  )
+
+
+@dataclasses.dataclass
+class PreparedWeights:
+  """Kernel layouts (see the module docstring)."""
+
+  dtype: torch.dtype
+  router: torch.Tensor
+  bias: torch.Tensor  # f32
+  down: torch.Tensor
+  up: torch.Tensor
+  expert_gu: torch.Tensor | None
+  expert_gate: torch.Tensor | None  # f32 path keeps gate and up apart (G, I, L)
+  expert_up: torch.Tensor | None
+  expert_down: torch.Tensor
+  norm_scale: torch.Tensor
+  shared_gu: torch.Tensor | None
+  shared_gate: torch.Tensor | None
+  shared_up: torch.Tensor | None
+  shared_down: torch.Tensor
+
+
+def _t(w: torch.Tensor) -> torch.Tensor:
+  return w.transpose(-1, -2).contiguous()
+
+
+def prepare_weights(w: LatentMoEWeights, dtype: torch.dtype | None = None) -> PreparedWeights:
+  """One-time re-layout of (in, out) weights into the K-major kernel layouts."""
+  dtype = dtype or w.down_proj.dtype
+  cv = lambda a: a.to(dtype)
+  bf16 = dtype == torch.bfloat16
+  return PreparedWeights(
+      dtype=dtype,
+      router=_t(cv(w.router_weight)),
+      bias=w.e_score_correction_bias.float().contiguous(),
+      down=_t(cv(w.down_proj)),
+      up=_t(cv(w.up_proj)),
+      expert_gu=_t(torch.cat([cv(w.expert_gate), cv(w.expert_up)], dim=-1)) if bf16 else None,
+      expert_gate=None if bf16 else _t(cv(w.expert_gate)),
+      expert_up=None if bf16 else _t(cv(w.expert_up)),
+      expert_down=_t(cv(w.expert_down)),
+      norm_scale=cv(w.norm_scale).contiguous(),
+      shared_gu=_t(torch.cat([cv(w.shared_gate), cv(w.shared_up)], dim=-1)) if bf16 else None,
+      shared_gate=None if bf16 else _t(cv(w.shared_gate)),
+      shared_up=None if bf16 else _t(cv(w.shared_up)),
+      shared_down=_t(cv(w.shared_down)),
+  )
+
+
+def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoEConfig, *,
+                       router_activation: str = "sigmoid",
+                       return_intermediates: bool = False):
+  """The 8-step LatentMoE forward (kimi_k3_latent_moe_reference.py:330-435).
+  `weights` is a LatentMoEWeights (prepared on the fly) or PreparedWeights."""
+  pw = weights if isinstance(weights, PreparedWeights) else prepare_weights(weights)
+  h = hidden_states.to(pw.dtype).contiguous()
+  c = config
+  t = h.shape[0]
+  inter = {}
+  logits = ops.router_logits(h, pw.router)
+  topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
+                                     routed_scaling_factor=c.routed_scaling_factor,
+                                     activation=router_activation)
+  x = _dense(h, pw.down)
+  d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
+  sorted_tokens = ops.gather_rows(x, d.token_idx)
+  beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
+  if pw.dtype == torch.bfloat16:
+    act = ops.fused_gateup_situ(sorted_tokens, pw.expert_gu, d.group_sizes, beta=beta,
+                                linear_beta=lbeta, round_gate_up=True, rhs_layout="gnk")
+  else:
+    gate = ops.ragged_dot(sorted_tokens, pw.expert_gate, d.group_sizes, rhs_layout="gnk")
+    up = ops.ragged_dot(sorted_tokens, pw.expert_up, d.group_sizes, rhs_layout="gnk")
+    act = ops.situ_and_mul(gate, up, beta, lbeta)
+  down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
+  routed, normed = ops.combine_rmsnorm(down, d.slot_pos, topk_w, pw.norm_scale, c.rms_norm_eps,
+                                       want_routed=True)
+  upo = _dense(normed, pw.up)
+  if pw.dtype == torch.bfloat16:
+    shared_act = ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
+                                       round_gate_up=True, rhs_layout="gnk")
+  else:
+    shared_act = ops.situ_and_mul(_dense(h, pw.shared_gate), _dense(h, pw.shared_up), beta, lbeta)
+  final = _dense(shared_act, pw.shared_down, addend=upo)
+  if return_intermediates:
+    inter.update(router_logits=logits, topk_indices=topk_idx, topk_weights=topk_w,
+                 latent_projection=x, sorted_token_indices=d.order, group_sizes=d.group_sizes,
+                 situ_output=act, expert_down_output=down, routed_output_after_combine=routed,
+                 normalized_output=normed, up_projection_output=upo, final_output=final,
+                 slot_pos=d.slot_pos)
+    return final, inter
+  return final
+
+
+def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None):
+  """a @ W^T for W given (N, K); bf16 on the tensor cores, f32 on the CUDA cores."""
+  if a.dtype == torch.float32:
+    from . import _native
+    m, k = a.shape
+    n = w_nk.shape[0]
+    out = torch.empty(m, n, dtype=torch.float32, device=a.device)
+    _native.call("lmoe_gemm_f32", a.contiguous().data_ptr(), w_nk.data_ptr(),
+                 None if addend is None else addend.contiguous().data_ptr(), out.data_ptr(), m, k,
+                 n, 1, ops.device_status(a.device).data_ptr(), ops._stream())
+    return out
+  return ops.gemm(a, w_nk, addend=addend, rhs_layout="nk")
+
+
+def latent_moe_forward_ragged_dot(hidden_states, weights, config, implementation=None):
+  """kimi_k3_latent_moe_ragged_dot.py:317-391: same forward, routed FFN as
+  ragged_dot calls (here always the sm_100a kernels)."""
+  ops._check_impl(implementation)
+  return latent_moe_forward(hidden_states, weights, config)

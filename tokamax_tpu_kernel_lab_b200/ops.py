@@ -1,0 +1,345 @@
+"""Operator API of the LatentMoE expert path on B200 -- the drop-in for the
+reference's JAX-facing operators.  Tensors are torch CUDA tensors (torch is
+used only for device memory and the current stream); every computation runs
+in the sm_100a kernels of `liblmoe_b200.so` through the C ABI.
+
+Reference interfaces mirrored (paths relative to the reference project):
+  ragged_dot                  tokamax.ragged_dot(lhs, rhs, group_sizes, implementation=...)
+                              as called at 05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:358-369
+  prefuse_gateup_weights      kimi_k3_latent_moe_ragged_dot.py:610-641
+  fused_gateup_situ           PallasMosaicTpuV2RaggedDot()(..., fuse_gateup_activation="situ:b:lb")
+                              kimi_k3_latent_moe_ragged_dot.py:644-723
+  situ_and_mul                kimi_k3_latent_moe_reference.py:296-310
+  router_gate                 kimi_k3_latent_moe_reference.py:347-356 / 601-631
+  filter_and_pad_to_shard_jittable   kimi_k3_latent_moe_reference.py:754-877
+  combine_shard_contribution  kimi_k3_latent_moe_reference.py:1113-1141
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+import torch
+
+from . import _native
+
+_SUPPORTED_IMPLEMENTATIONS = (None, "sm100", "b200")
+_status_buffers: dict[int, torch.Tensor] = {}
+
+
+def _stream() -> int:
+  return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+  return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor) -> None:
+  for t in ts:
+    if t is not None and not t.is_cuda:
+      raise ValueError("all operands must be CUDA tensors (there is no CPU path)")
+
+
+def device_status(device: torch.device | int | None = None) -> torch.Tensor:
+  """The per-device int32 word kernels record device-side errors into."""
+  idx = torch.cuda.current_device() if device is None else torch.device("cuda", device).index \
+      if isinstance(device, int) else (device.index if device.index is not None
+                                       else torch.cuda.current_device())
+  buf = _status_buffers.get(idx)
+  if buf is None:
+    buf = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+    _status_buffers[idx] = buf
+  return buf
+
+
+def check_device_status(device=None, reset: bool = True) -> None:
+  """Synchronise and raise if a kernel recorded a device-side error."""
+  buf = device_status(device)
+  code = int(buf.item())
+  if code != 0:
+    if reset:
+      buf.zero_()
+    raise _native.LmoeError("device status", code)
+
+
+def _check_impl(implementation):
+  if implementation not in _SUPPORTED_IMPLEMENTATIONS:
+    raise NotImplementedError(
+        f"implementation={implementation!r}: this build has one implementation, the sm_100a kernels")
+
+
+# ----------------------------------------------------------------------------- GEMMs
+
+
+def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, *,
+               implementation: str | None = None, precision=None,
+               preferred_element_type: torch.dtype | None = None, rhs_layout: str = "gkn",
+               out: torch.Tensor | None = None) -> torch.Tensor:
+  """out[r] = lhs[r] @ rhs[g] for the rows r of group g; rows past
+  sum(group_sizes) are zero.  lhs (M, K); rhs (G, K, N) ("gkn", the reference's
+  layout) or (G, N, K) ("gnk"); group_sizes (G,) int32 on the device.
+
+  bf16 operands run on the tensor cores (f32 accumulate, bf16 or f32 out);
+  f32 operands run the f32 CUDA-core kernel."""
+  _check_impl(implementation)
+  del precision
+  _need_cuda(lhs, rhs, group_sizes)
+  if lhs.dim() != 2 or rhs.dim() != 3:
+    raise ValueError("lhs must be (M, K) and rhs (G, K, N) / (G, N, K)")
+  layout = {"gkn": 0, "gnk": 1}[rhs_layout]
+  m, k = lhs.shape
+  g = rhs.shape[0]
+  n = rhs.shape[2] if layout == 0 else rhs.shape[1]
+  kk = rhs.shape[1] if layout == 0 else rhs.shape[2]
+  if kk != k or group_sizes.shape != (g,):
+    raise ValueError(f"shape mismatch lhs {tuple(lhs.shape)} rhs {tuple(rhs.shape)} "
+                     f"group_sizes {tuple(group_sizes.shape)}")
+  gs = group_sizes if group_sizes.dtype == torch.int32 else group_sizes.to(torch.int32)
+  lhs, rhs, gs = lhs.contiguous(), rhs.contiguous(), gs.contiguous()
+  status = device_status(lhs.device)
+  if lhs.dtype == torch.float32:
+    if rhs.dtype != torch.float32:
+      raise ValueError("f32 lhs needs f32 rhs")
+    res = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=lhs.device)
+    _native.call("lmoe_ragged_dot_f32", _ptr(lhs), _ptr(rhs), _ptr(gs), _ptr(res), m, k, n, g,
+                 layout, _ptr(status), _stream())
+    return res
+  if lhs.dtype != torch.bfloat16 or rhs.dtype != torch.bfloat16:
+    raise NotImplementedError(f"dtypes {lhs.dtype}/{rhs.dtype}: bf16 or f32 operands only")
+  out_dtype = preferred_element_type or torch.bfloat16
+  if out_dtype not in (torch.bfloat16, torch.float32):
+    raise NotImplementedError(f"preferred_element_type={out_dtype}")
+  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  _native.call("lmoe_ragged_dot_bf16", _ptr(lhs), _ptr(rhs), _ptr(gs), _ptr(res), m, k, n, g,
+               layout, int(out_dtype == torch.float32), _ptr(status), _stream())
+  return res
+
+
+def gemm(lhs: torch.Tensor, rhs: torch.Tensor, *, addend: torch.Tensor | None = None,
+         rhs_layout: str = "nk", out_dtype: torch.dtype = torch.bfloat16,
+         out: torch.Tensor | None = None) -> torch.Tensor:
+  """Dense bf16 GEMM (one group of the tensor-core kernel):
+  out = bf16(bf16(lhs @ W) + addend) with W given as (N, K) ("nk") or (K, N) ("kn")."""
+  _need_cuda(lhs, rhs, addend)
+  layout = {"kn": 0, "nk": 1}[rhs_layout]
+  m, k = lhs.shape
+  n = rhs.shape[1] if layout == 0 else rhs.shape[0]
+  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  _native.call("lmoe_gemm_bf16", _ptr(lhs), _ptr(rhs), _ptr(addend), _ptr(res), m, k, n, layout,
+               int(out_dtype == torch.float32), _ptr(device_status(lhs.device)), _stream())
+  return res
+
+
+def prefuse_gateup_weights(expert_gate: torch.Tensor, expert_up: torch.Tensor,
+                           layout: str = "gkn") -> torch.Tensor:
+  """[gate | up] concatenated along N, plain, not interleaved
+  (kimi_k3_latent_moe_ragged_dot.py:610-641).  Done once per weight set.
+  Inputs are (G, K, I); "gnk" returns the (G, 2I, K) K-major form the
+  kernels read fastest."""
+  fused = torch.cat([expert_gate, expert_up], dim=-1)
+  if layout == "gnk":
+    fused = fused.transpose(-1, -2).contiguous()
+  return fused
+
+
+def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: torch.Tensor | None,
+                      *, beta: float = 4.0, linear_beta: float = 25.0, round_gate_up: bool = True,
+                      rhs_layout: str = "gkn", out: torch.Tensor | None = None) -> torch.Tensor:
+  """SiTU-GLU(lhs @ gate_g, lhs @ up_g) from ONE grouped matmul against the
+  fused [gate | up] weight.  `group_sizes=None` means one dense group
+  (the shared expert).  Returns (M, I) bf16."""
+  _need_cuda(lhs, w_gateup, group_sizes)
+  layout = {"gkn": 0, "gnk": 1}[rhs_layout]
+  w = w_gateup if w_gateup.dim() == 3 else w_gateup.unsqueeze(0)
+  m, k = lhs.shape
+  two_i = w.shape[2] if layout == 0 else w.shape[1]
+  inter = two_i // 2
+  g = w.shape[0]
+  if group_sizes is not None and group_sizes.shape != (g,):
+    raise ValueError("group_sizes must have one entry per weight group")
+  gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
+  res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
+  _native.call("lmoe_gateup_situ_bf16", _ptr(lhs.contiguous()), _ptr(w.contiguous()), _ptr(gs),
+               _ptr(res), m, k, inter, g, layout, float(beta), float(linear_beta),
+               int(round_gate_up), _ptr(device_status(lhs.device)), _stream())
+  return res
+
+
+def parse_fused_activation(spec: str) -> tuple[float, float]:
+  """"situ:<beta>:<linear_beta>" (kimi_k3_latent_moe_ragged_dot.py:718)."""
+  parts = spec.split(":")
+  if len(parts) != 3 or parts[0] != "situ":
+    raise NotImplementedError(f"fused activation {spec!r}")
+  return float(parts[1]), float(parts[2])
+
+
+def situ_and_mul(gate: torch.Tensor, up: torch.Tensor, beta: float = 4.0,
+                 linear_beta: float = 25.0) -> torch.Tensor:
+  """Elementwise SiTU-GLU in f32, cast back to the input dtype."""
+  _need_cuda(gate, up)
+  if gate.shape != up.shape or gate.dtype != up.dtype:
+    raise ValueError("gate/up mismatch")
+  g2, u2 = gate.reshape(-1, gate.shape[-1]).contiguous(), up.reshape(-1, up.shape[-1]).contiguous()
+  out = torch.empty_like(g2)
+  _native.call("lmoe_situ_and_mul", _ptr(g2), _ptr(u2), g2.shape[1], _ptr(out), g2.shape[0],
+               g2.shape[1], float(beta), float(linear_beta), int(gate.dtype == torch.bfloat16),
+               _stream())
+  return out.reshape(gate.shape)
+
+
+# ----------------------------------------------------------------------------- routing
+
+
+def router_topk(logits: torch.Tensor, bias: torch.Tensor | None, top_k: int, *,
+                renormalize: bool = True, routed_scaling_factor: float = 1.0,
+                activation: str = "sigmoid") -> tuple[torch.Tensor, torch.Tensor]:
+  """Gate math of kimi_k3_latent_moe_reference.py:348-356 from f32 logits:
+  returns (topk_idx int32 (T, k), topk_weight f32 (T, k))."""
+  _need_cuda(logits, bias)
+  logits = logits.float().contiguous()
+  t, e = logits.shape
+  b = None if bias is None else bias.float().contiguous()
+  idx = torch.empty(t, top_k, dtype=torch.int32, device=logits.device)
+  w = torch.empty(t, top_k, dtype=torch.float32, device=logits.device)
+  act = {"sigmoid": 0, "softmax": 1}[activation]
+  _native.call("lmoe_router_topk", _ptr(logits), _ptr(b), t, e, top_k, act, int(renormalize),
+               float(routed_scaling_factor), _ptr(idx), _ptr(w), _stream())
+  return idx, w
+
+
+def router_logits(hidden_states: torch.Tensor, router_weight_nk: torch.Tensor) -> torch.Tensor:
+  """f32 logits = h @ W_router.  bf16 h and W: tensor cores, exact bf16
+  products, f32 accumulation.  f32 h and W: the f32 CUDA-core kernel.
+  `router_weight_nk` is (E, d)."""
+  if hidden_states.dtype == torch.float32:
+    gs = torch.tensor([hidden_states.shape[0]], dtype=torch.int32, device=hidden_states.device)
+    return ragged_dot(hidden_states, router_weight_nk.unsqueeze(0), gs, rhs_layout="gnk")
+  return gemm(hidden_states, router_weight_nk, rhs_layout="nk", out_dtype=torch.float32)
+
+
+def router_gate(hidden_states, router_weight_nk, bias, top_k, *, renormalize=True,
+                routed_scaling_factor=1.0, activation="sigmoid"):
+  """(topk_idx, topk_weight f32) on the original hidden states."""
+  logits = router_logits(hidden_states, router_weight_nk)
+  return router_topk(logits, bias, top_k, renormalize=renormalize,
+                     routed_scaling_factor=routed_scaling_factor, activation=activation)
+
+
+@dataclasses.dataclass
+class Dispatch:
+  """Device outputs of the dispatch kernels."""
+
+  order: torch.Tensor | None       # (m_out,) flat (token*k+slot) entry at each sorted position
+  token_idx: torch.Tensor          # (m_out,) source token, -1 for padding
+  weight: torch.Tensor | None      # (m_out,) f32 combine weight, 0 for padding
+  slot_pos: torch.Tensor | None    # (T*k,) sorted position of each entry, -1 if not kept
+  group_sizes: torch.Tensor        # (E_local [+1],) int32
+  per_expert_counts: torch.Tensor | None
+  valid: torch.Tensor | None       # (m_out,) bool
+
+
+def dispatch_workspace_size(num_entries: int, num_local_experts: int) -> int:
+  return int(_native.load().lmoe_dispatch_workspace_size(num_entries, num_local_experts))
+
+
+def dispatch(topk_idx: torch.Tensor, topk_weight: torch.Tensor | None, num_local_experts: int, *,
+             expert_start: int = 0, m_out: int | None = None, pad_bucket: bool = False,
+             want_order: bool = True, want_slot_pos: bool = True, want_valid: bool = False,
+             workspace: torch.Tensor | None = None) -> Dispatch:
+  """Stable counting sort of the (token, slot) entries by local expert id
+  (argsort + bincount of kimi_k3_latent_moe_reference.py:370-378; with
+  expert_start / m_out / pad_bucket the shard form of 754-877)."""
+  _need_cuda(topk_idx, topk_weight)
+  t, k = topk_idx.shape
+  s = t * k
+  m_out = s if m_out is None else int(m_out)
+  dev = topk_idx.device
+  ids = topk_idx.to(torch.int32).contiguous()
+  w = None if topk_weight is None else topk_weight.float().contiguous()
+  n_ext = max(s, m_out)
+  ws_bytes = dispatch_workspace_size(n_ext, num_local_experts)
+  if workspace is None or workspace.numel() < ws_bytes:
+    workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+  i32 = lambda n: torch.empty(n, dtype=torch.int32, device=dev)
+  res = Dispatch(
+      order=i32(m_out) if want_order else None,
+      token_idx=i32(m_out),
+      weight=torch.empty(m_out, dtype=torch.float32, device=dev) if w is not None else None,
+      slot_pos=i32(s) if want_slot_pos else None,
+      group_sizes=i32(num_local_experts + (1 if pad_bucket else 0)),
+      per_expert_counts=i32(num_local_experts) if pad_bucket else None,
+      valid=torch.empty(m_out, dtype=torch.uint8, device=dev) if want_valid else None,
+  )
+  _native.call("lmoe_dispatch", _ptr(ids), _ptr(w), t, k, expert_start, num_local_experts, m_out,
+               int(pad_bucket), _ptr(res.order), _ptr(res.token_idx), _ptr(res.weight),
+               _ptr(res.slot_pos), _ptr(res.group_sizes), _ptr(res.per_expert_counts),
+               _ptr(res.valid), _ptr(workspace), workspace.numel(), _stream())
+  if res.valid is not None:
+    res.valid = res.valid.view(torch.bool)
+  return res
+
+
+def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | None = None):
+  """out[p] = x[token_idx[p]] (zero where token_idx < 0)."""
+  _need_cuda(x, token_idx)
+  x = x.contiguous()
+  rows = token_idx.shape[0]
+  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=x.dtype, device=x.device)
+  _native.call("lmoe_gather_rows", _ptr(x), x.shape[0], _ptr(token_idx.to(torch.int32)),
+               _ptr(res), rows, x.shape[1] * x.element_size(), _stream())
+  return res
+
+
+def shard_m_padded(num_tokens, top_k, num_experts, local_num_experts, capacity_factor, tile_size):
+  """kimi_k3_latent_moe_reference.py:825-826."""
+  expected_total = num_tokens * top_k * local_num_experts / num_experts
+  v = math.ceil(expected_total * capacity_factor)
+  return -(-v // tile_size) * tile_size
+
+
+def filter_and_pad_to_shard_jittable(topk_idx, topk_weight, x, num_experts, top_k,
+                                     local_expert_start, local_num_experts,
+                                     capacity_factor=2.0, tile_size=128):
+  """Static-shape shard dispatch (kimi_k3_latent_moe_reference.py:754-877).
+  Returns (sorted_tokens, group_sizes, valid_mask, per_expert_counts,
+  padded_token_idx, padded_combine_weight)."""
+  t = topk_idx.shape[0]
+  m_padded = shard_m_padded(t, top_k, num_experts, local_num_experts, capacity_factor, tile_size)
+  d = dispatch(topk_idx, topk_weight, local_num_experts, expert_start=local_expert_start,
+               m_out=m_padded, pad_bucket=True, want_order=False, want_slot_pos=False,
+               want_valid=True)
+  sorted_tokens = gather_rows(x, d.token_idx)
+  return sorted_tokens, d.group_sizes, d.valid, d.per_expert_counts, d.token_idx, d.weight
+
+
+def combine_rmsnorm(expert_out: torch.Tensor, slot_pos: torch.Tensor, topk_weight: torch.Tensor,
+                    norm_scale: torch.Tensor, eps: float, *, want_routed: bool = False):
+  """routed = dtype(sum_s out[slot_pos] * w) (f32, slot order) and its RMSNorm.
+  Returns normed, or (routed, normed) with want_routed."""
+  _need_cuda(expert_out, slot_pos, topk_weight, norm_scale)
+  t, k = topk_weight.shape
+  L = expert_out.shape[1]
+  bf16 = expert_out.dtype == torch.bfloat16
+  normed = torch.empty(t, L, dtype=expert_out.dtype, device=expert_out.device)
+  routed = torch.empty_like(normed) if want_routed else None
+  _native.call("lmoe_combine_rmsnorm", _ptr(expert_out.contiguous()), _ptr(slot_pos),
+               _ptr(topk_weight.float().contiguous()), _ptr(norm_scale.to(expert_out.dtype)),
+               t, k, L, float(eps), int(bf16), _ptr(routed), _ptr(normed), _stream())
+  return (routed, normed) if want_routed else normed
+
+
+def combine_shard_contribution(routed_out: torch.Tensor, shard_out: torch.Tensor,
+                               padded_token_idx: torch.Tensor,
+                               padded_combine_weight: torch.Tensor) -> torch.Tensor:
+  """routed_out.at[idx].add((shard_out * w).astype(routed_out.dtype)) as a
+  scatter-add kernel (in place on a copy of routed_out, which is returned)."""
+  _need_cuda(routed_out, shard_out, padded_token_idx, padded_combine_weight)
+  out = routed_out.clone()
+  rows, L = shard_out.shape
+  _native.call("lmoe_combine_scatter_add", _ptr(shard_out.to(out.dtype).contiguous()),
+               _ptr(padded_token_idx.to(torch.int32).contiguous()),
+               _ptr(padded_combine_weight.float().contiguous()), _ptr(out), rows, L,
+               out.shape[0], int(out.dtype == torch.bfloat16), _stream())
+  return out
