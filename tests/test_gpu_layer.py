@@ -1,0 +1,124 @@
+"""GPU parity of the whole LatentMoE layer through the C ABI:
+- the reference's six golden bundles (official PyTorch block) stage by stage,
+- the reduced-scale configuration 1 (f32 and bf16) against the CPU oracle,
+- a skewed bf16 layer at a larger scale against the oracle,
+- bit-level properties at full size: determinism and batch invariance."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lmoe_oracle as O
+from tests.golden import NAMES, load
+from tests.gpu_util import assert_bf16_close, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lm():
+  import tokamax_tpu_kernel_lab_b200 as lm
+  lm.load_native()
+  return lm
+
+
+def _cfg(lm, c):
+  return lm.LatentMoEConfig(c.hidden_size, c.latent_size, c.intermediate_size, c.num_experts,
+                            c.top_k, c.num_shared_experts, c.moe_renormalize,
+                            c.routed_scaling_factor, c.rms_norm_eps, c.activation_situ_beta,
+                            c.activation_situ_linear_beta)
+
+
+def _torch_weights(lm, w: O.Weights, dtype):
+  f = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda().to(dtype)
+  return lm.LatentMoEWeights(**{k: f(getattr(w, k)) for k in (
+      "router_weight", "e_score_correction_bias", "down_proj", "up_proj", "expert_gate",
+      "expert_up", "expert_down", "norm_scale", "shared_gate", "shared_up", "shared_down")})
+
+
+def _run(lm, h, w, cfg, dtype):
+  tdt = torch.bfloat16 if dtype == "bf16" else torch.float32
+  tw = _torch_weights(lm, w, tdt)
+  hd = torch.from_numpy(np.ascontiguousarray(h, np.float32)).cuda().to(tdt)
+  final, inter = lm.latent_moe_forward(hd, tw, _cfg(lm, cfg), return_intermediates=True)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  return final, inter
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_golden_bundle_through_gpu(lm, name):
+  g = load(name)
+  c = g["config"]
+  cfg = O.LatentMoEConfig(c["hidden_size"], c["routed_expert_hidden_size"],
+                          c["moe_intermediate_size"], c["num_experts"],
+                          c["num_experts_per_token"], c["num_shared_experts"])
+  w = O.Weights(**g["weights"])
+  final, inter = _run(lm, g["hidden_states"], w, cfg, g["dtype"])
+  out = g["outputs"]
+  # routing: group sizes and canonicalised indices exact
+  assert np.array_equal(inter["group_sizes"].cpu().numpy(), out["group_sizes"])
+  gi = np.sort(out["topk_indices"], axis=-1)
+  ji = np.sort(inter["topk_indices"].cpu().numpy(), axis=-1)
+  assert np.array_equal(gi, ji)
+  golden_final = out["final_output"].reshape(final.shape)
+  if g["dtype"] == "fp32":
+    assert np.allclose(to_np(final), golden_final, atol=1e-4, rtol=1e-3)
+    assert np.allclose(to_np(inter["router_logits"]), out["router_logits"], atol=1e-5)
+  else:
+    assert_bf16_close(golden_final, to_np(final), name)
+    assert_bf16_close(out["normalized_output"], to_np(inter["normalized_output"]), name,
+                      max_abs=3.2e-2, rel=2e-2)
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_reduced_config1(lm, dtype):
+  """Configuration 1: T=128 (2 x 64), d 512 -> L 256, 64 experts, I 512, top-8,
+  N(0,1) inputs, N(0, 0.02^2) weights, seed 0."""
+  cfg = O.LatentMoEConfig(512, 256, 512, 64, 8, 1)
+  w = O.init_weights_np(cfg, 0, dtype=dtype)
+  h = O.to_dtype(np.random.default_rng(0).standard_normal((128, 512), dtype=np.float32), dtype)
+  ref, rinter = O.latent_moe_forward(h, w, cfg, dtype=dtype, return_intermediates=True)
+  final, inter = _run(lm, h, w, cfg, dtype)
+  assert np.array_equal(np.sort(inter["topk_indices"].cpu().numpy(), -1),
+                        np.sort(rinter["topk_indices"], -1))
+  assert np.array_equal(inter["group_sizes"].cpu().numpy(), rinter["group_sizes"])
+  assert np.array_equal(inter["sorted_token_indices"].cpu().numpy(),
+                        rinter["sorted_token_indices"])
+  if dtype == "fp32":
+    assert np.allclose(to_np(final), ref, atol=1e-4, rtol=1e-3)
+  else:
+    assert_bf16_close(ref, to_np(final), "config1 bf16")
+
+
+def test_skewed_bf16_layer(lm):
+  """A scaled-down configuration 3/5 layer (bf16, per-expert router bias
+  N(0, 0.5^2) for skewed load, empty experts) against the bf16-emulating oracle;
+  tokens whose top-k set differs on a near-tie are excluded and counted."""
+  cfg = O.LatentMoEConfig(1024, 512, 256, 128, 8, 2)
+  w = O.init_weights_np(cfg, 2, dtype="bf16", bias_std=0.5)
+  h = O.bf16_round(np.random.default_rng(2).standard_normal((768, 1024), dtype=np.float32))
+  ref, rinter = O.latent_moe_forward(h, w, cfg, dtype="bf16", return_intermediates=True)
+  final, inter = _run(lm, h, w, cfg, "bf16")
+  same = np.all(np.sort(inter["topk_indices"].cpu().numpy(), -1) ==
+                np.sort(rinter["topk_indices"], -1), axis=1)
+  assert same.mean() >= 0.995
+  assert (rinter["group_sizes"] == 0).any() or rinter["group_sizes"].max() > 3 * 768 * 8 / 128
+  assert_bf16_close(ref[same], to_np(final)[same], "skewed layer")
+
+
+def test_layer_is_deterministic_and_batch_invariant(lm):
+  """Two runs are bit-identical, and the first half of the tokens gives the
+  same bits whether run alone or inside the full batch (per-row GEMM results
+  do not depend on the tile a row lands in; the combine is in slot order)."""
+  cfg = lm.LatentMoEConfig(2048, 1024, 512, 256, 16, 2)
+  w = lm.init_weights(cfg, seed=3, bias_std=0.5)
+  pw = lm.prepare_weights(w)
+  gen = torch.Generator(device="cuda").manual_seed(3)
+  h = torch.randn(2048, 2048, generator=gen, device="cuda").to(torch.bfloat16)
+  a = lm.latent_moe_forward(h, pw, cfg)
+  b = lm.latent_moe_forward(h, pw, cfg)
+  half = lm.latent_moe_forward(h[:1024].contiguous(), pw, cfg)
+  torch.cuda.synchronize()
+  assert torch.equal(a, b)
+  assert torch.equal(a[:1024], half)

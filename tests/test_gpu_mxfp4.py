@@ -1,0 +1,125 @@
+"""GPU parity of the MXFP4 grouped matmul (weights packed in HBM, expanded to
+bf16 per tile in shared memory, tensor-core MMA) against the dequant-then-matmul
+oracle (05_ragged_dot_on_tpu/mxfp4_dequant.py:29-67), and of the MXFP4 layer."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lmoe_oracle as O
+from tests.gpu_util import assert_bf16_close, assert_gemm_close, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def lm():
+  import tokamax_tpu_kernel_lab_b200 as lm
+  lm.load_native()
+  return lm
+
+
+def _mx(rng, g, n, k, lo=121, hi=129):
+  packed = rng.integers(0, 256, (g, n, k // 2), dtype=np.uint8)
+  scale = rng.integers(lo, hi + 1, (g, n, k // 32), dtype=np.uint8)
+  return packed, scale
+
+
+def _dev_mx(lm, packed, scale):
+  return lm.MXFP4Weights(torch.from_numpy(packed).cuda(), torch.from_numpy(scale).cuda())
+
+
+def test_in_kernel_dequant_is_bit_exact(lm):
+  """lhs = identity rows, f32 output: out[k, n] = dequant(W)[n, k] exactly
+  (e2m1 x 2^e is exact in bf16 and one product per output is nonzero).
+  Scale bytes span 1..200 (0 decodes to 2^-127, checked separately)."""
+  rng = np.random.default_rng(0)
+  k, n = 256, 384
+  packed, scale = _mx(rng, 1, n, k, lo=1, hi=200)
+  scale[0, 0, 0] = 0
+  lhs = np.eye(k, dtype=np.float32)
+  out = lm.mxfp4_ragged_dot(to_dev(lhs), _dev_mx(lm, packed, scale),
+                            torch.tensor([k], dtype=torch.int32, device="cuda"),
+                            preferred_element_type=torch.float32)
+  ref = O.dequantize_mxfp4(packed[0], scale[0]).T
+  assert np.array_equal(to_np(out), ref)
+
+
+@pytest.mark.parametrize("m,k,n,g", [(700, 256, 256, 3), (2048, 1024, 512, 16), (1, 64, 128, 2)])
+def test_mxfp4_ragged_dot(lm, m, k, n, g):
+  rng = np.random.default_rng(m + k + n)
+  packed, scale = _mx(rng, g, n, k)
+  gs = rng.multinomial(m, np.full(g, 1.0 / g)).astype(np.int32)
+  lhs = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
+  ref = O.mxfp4_ragged_dot(lhs, packed, scale, gs, dtype="fp32")
+  out = lm.mxfp4_ragged_dot(to_dev(lhs), _dev_mx(lm, packed, scale), torch.from_numpy(gs).cuda())
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  scale_ref = float(np.abs(ref).max()) or 1.0
+  # compare on a unit scale (outputs here are O(100)): the MXFP4 bar is 1e-2 relative
+  assert_gemm_close(ref / scale_ref, to_np(out) / scale_ref, f"mxfp4 {m}x{k}x{n}")
+
+
+def test_mxfp4_config4_full_size(lm):
+  """Benchmark configuration 4: weights (128, K=4096, N=2048) with e2m1 codes
+  uniform over all 16 and scale exponents uniform in [-6, 2]; x (16384, 4096)
+  bf16 N(0,1); uniform-random group sizes summing to 16384."""
+  rng = np.random.default_rng(3)
+  g, k, n, m = 128, 4096, 2048, 16384
+  packed, scale = _mx(rng, g, n, k, lo=121, hi=129)
+  gs = rng.multinomial(m, np.full(g, 1.0 / g)).astype(np.int32)
+  lhs = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
+  ref = O.mxfp4_ragged_dot(lhs, packed, scale, gs, dtype="fp32")
+  out = lm.mxfp4_ragged_dot(to_dev(lhs), _dev_mx(lm, packed, scale), torch.from_numpy(gs).cuda())
+  s = float(np.abs(ref).max())
+  rep = assert_gemm_close(ref / s, to_np(out) / s, "config 4")
+  assert rep["normwise_rel"] <= 1e-2
+
+
+@pytest.mark.parametrize("round_gate_up", [True, False])
+def test_mxfp4_fused_gateup_situ(lm, round_gate_up):
+  rng = np.random.default_rng(9)
+  m, k, inter, g = 1200, 512, 256, 5
+  packed, scale = _mx(rng, g, 2 * inter, k, lo=120, hi=121)  # weights rms ~0.02
+  gs = rng.multinomial(m - 17, np.full(g, 1.0 / g)).astype(np.int32)
+  lhs = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
+  lazy = O.LazyMXFP4Experts(packed, scale)
+  ref = O.fused_gateup_situ(lhs, lazy, gs, inter, 4.0, 25.0, dtype="bf16",
+                            round_gate_up=round_gate_up, out_dtype="fp32")
+  out = lm.mxfp4_fused_gateup_situ(to_dev(lhs), _dev_mx(lm, packed, scale),
+                                   torch.from_numpy(gs).cuda(), round_gate_up=round_gate_up)
+  got = to_np(out)
+  assert np.all(got[gs.sum():] == 0)
+  assert_bf16_close(ref, got, f"mxfp4 situ round={round_gate_up}")
+
+
+def test_mxfp4_layer_matches_oracle(lm):
+  """A LatentMoE layer with MXFP4 routed experts (the configuration-5 format,
+  scaled down) against the dequant-then-forward oracle."""
+  cfg = lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+  pw = lm.init_prepared_mxfp4(cfg, seed=5, bias_std=0.5)
+  gen = torch.Generator(device="cuda").manual_seed(5)
+  h = torch.randn(384, 1024, generator=gen, device="cuda").to(torch.bfloat16)
+  final, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  I = cfg.intermediate_size
+  si = I * cfg.num_shared_experts
+  npf = lambda t: t.float().cpu().numpy()
+  gu_p, gu_s = pw.expert_gu_mx.packed.cpu().numpy(), pw.expert_gu_mx.scale.cpu().numpy()
+  dn_p, dn_s = pw.expert_down_mx.packed.cpu().numpy(), pw.expert_down_mx.scale.cpu().numpy()
+  w = O.Weights(
+      router_weight=npf(pw.router).T, e_score_correction_bias=npf(pw.bias),
+      down_proj=npf(pw.down).T, up_proj=npf(pw.up).T,
+      expert_gate=O.LazyMXFP4Experts(gu_p, gu_s, 0, I),
+      expert_up=O.LazyMXFP4Experts(gu_p, gu_s, I, 2 * I),
+      expert_down=O.LazyMXFP4Experts(dn_p, dn_s),
+      norm_scale=npf(pw.norm_scale),
+      shared_gate=npf(pw.shared_gu)[:si].T, shared_up=npf(pw.shared_gu)[si:].T,
+      shared_down=npf(pw.shared_down).T)
+  ocfg = O.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+  ref, rinter = O.latent_moe_forward(npf(h), w, ocfg, dtype="bf16", return_intermediates=True)
+  same = np.all(np.sort(inter["topk_indices"].cpu().numpy(), -1) ==
+                np.sort(rinter["topk_indices"], -1), axis=1)
+  assert same.mean() >= 0.99
+  assert_bf16_close(ref[same], to_np(final)[same], "mxfp4 layer")

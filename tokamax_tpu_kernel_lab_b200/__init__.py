@@ -4,12 +4,12 @@ operator API (tokamax `ragged_dot`, fused gate/up, `latent_moe_forward`)."""
 
 from ._native import LIB_PATH, NativeLibraryMissing, load as load_native
 from .latent_moe import (LatentMoEConfig, LatentMoEWeights, PreparedWeights, full_layer_config,
-                         init_weights, kimi_k3_config, latent_moe_forward,
-                         latent_moe_forward_ragged_dot, prepare_weights, reduced_cpu_config,
-                         toy_config)
-from .ops import (Dispatch, check_device_status, combine_rmsnorm, combine_shard_contribution,
+                         init_prepared_mxfp4, init_weights, kimi_k3_config, latent_moe_forward,
+                         latent_moe_forward_ragged_dot, prepare_weights, random_mxfp4,
+                         reduced_cpu_config, toy_config)
+from .ops import (Dispatch, MXFP4Weights, check_device_status, combine_rmsnorm, combine_shard_contribution,
                   dispatch, filter_and_pad_to_shard_jittable, fused_gateup_situ, gather_rows, gemm,
-                  parse_fused_activation, prefuse_gateup_weights, ragged_dot, router_gate,
+                  mxfp4_fused_gateup_situ, mxfp4_ragged_dot, parse_fused_activation, prefuse_gateup_weights, ragged_dot, router_gate,
                   router_logits, router_topk, situ_and_mul)
 
 __all__ = [
@@ -20,5 +20,6 @@ __all__ = [
     "combine_shard_contribution", "dispatch", "filter_and_pad_to_shard_jittable",
     "fused_gateup_situ", "gather_rows", "gemm", "parse_fused_activation",
     "prefuse_gateup_weights", "ragged_dot", "router_gate", "router_logits", "router_topk",
-    "situ_and_mul",
+    "situ_and_mul", "MXFP4Weights", "mxfp4_ragged_dot", "mxfp4_fused_gateup_situ",
+    "init_prepared_mxfp4", "random_mxfp4",
 ]

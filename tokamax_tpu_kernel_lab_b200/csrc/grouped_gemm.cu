@@ -9,15 +9,24 @@
 // zero.  group_sizes lives in device memory and is read only on the device
 // (no host synchronisation).
 //
-// Design (one CTA per SM, 192 threads):
+// Design (one CTA per SM):
 //   warp 0      TMA producer: A tile (128 rows x 64 K, bf16, 128B swizzle) and
-//               B tile (BN x 64 K) per pipeline stage, completion on an mbarrier.
+//               the B operand of the stage, completion on an mbarrier.
 //   warp 1      TMEM owner and UMMA issuer: tcgen05.mma kind::f16, M=128, N=BN,
 //               K=16 per instruction, f32 accumulator in TMEM, two accumulator
 //               buffers so the epilogue of tile i overlaps the MMAs of tile i+1.
 //   warps 2-5   epilogue: tcgen05.ld of the accumulator (each warp owns one
 //               32-lane quarter of TMEM), fused activation, predicated stores of
 //               the rows that belong to the tile's group.
+//   warps 6-13  (MXFP4 weights only) dequant: expand the packed e2m1 codes the
+//               TMA brought into shared memory, times their E8M0 block scale,
+//               into the swizzled bf16 operand layout the UMMA reads.  The
+//               weights stay packed in HBM (4.25 bits per weight read).
+// B operand formats:
+//   B_KMAJOR   bf16 (G, N, K)          one TMA box per half tile
+//   B_NMAJOR   bf16 (G, K, N)          the reference's layout; MN-major UMMA operand
+//   B_MXFP4    u8 (G, N, K/2) codes (low nibble = even k) + u8 (G, N, K/32) E8M0
+//              scales (the checkpoint's (out, in) layout, 05_ragged_dot_on_tpu/mxfp4_dequant.py:29-67)
 // The tile schedule (group -> row offset, group -> first tile) is an in-CTA
 // prefix sum over group_sizes; tiles are (group, m-tile, n-tile) with n
 // fastest and are dealt round-robin to the persistent CTAs.  Empty groups own
@@ -27,9 +36,9 @@
 //   EPI_BF16      out = bf16(acc)
 //   EPI_F32       out = acc (f32)
 //   EPI_BF16_ADD  out = bf16(bf16(acc) + addend)    (residual add, bf16 rounding of each op)
-//   EPI_SITU      B tile = [gate cols | up cols] of a fused (G, 2I, K) / (G, K, 2I)
-//                 weight; out = bf16(situ(g, u)) with g, u = acc (rounded to bf16
-//                 first when round_gate_up, the convention of
+//   EPI_SITU      B tile = [gate cols | up cols] of a fused [gate | up] weight;
+//                 out = bf16(situ(g, u)) with g, u = acc (rounded to bf16 first
+//                 when round_gate_up, the convention of
 //                 kimi_k3_latent_moe_reference.py:296-310 / own_gateup_situ_pallas_kernel.py:116-125)
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -43,38 +52,43 @@ namespace lmoe {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
 constexpr int kMaxGroups = 2048;
 
 enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_BF16_ADD = 2, EPI_SITU = 3 };
+enum BFmt { B_KMAJOR = 0, B_NMAJOR = 1, B_MXFP4 = 2 };
 
 struct GemmArgs {
   const int32_t* group_sizes;  // nullptr: a single group of M rows
   int32_t* status;
   void* out;
   const __nv_bfloat16* addend;  // EPI_BF16_ADD
+  const uint8_t* scales;        // B_MXFP4: (G, n_weight, K/32) E8M0 bytes
   int64_t ldo;                  // output row pitch, elements
   int64_t ld_add;               // addend row pitch, elements
   int M, N, K, G;               // N = output columns (EPI_SITU: the intermediate size I)
   int n_tiles;                  // ceil(N / output tile width)
   int up_offset;                // EPI_SITU: row/col offset of the up half in the fused weight
+  int n_weight;                 // rows (N extent) of one group's weight
   float beta, linear_beta;
   int round_gate_up;
   int zero_tail;
 };
 
-template <int BN, int STAGES, bool B_MN, int EPI>
+template <int BN, int STAGES, int BF, int EPI>
 struct GemmCfg {
+  static constexpr int kThreads = (BF == B_MXFP4) ? 448 : 192;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kOutTileN = (EPI == EPI_SITU) ? BN / 2 : BN;
+  static constexpr int kPackedBytes = (BF == B_MXFP4) ? BN * (kBK / 2) : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kGemmThreads * 4;
-  static constexpr int kBarBytes = 8 * (2 * STAGES + 5) + 16;
+  static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kThreads * 4;
+  static constexpr int kBarBytes = 8 * (3 * STAGES + 5) + 16;
   static constexpr size_t kSmem = 1024 + size_t(STAGES) * kStageBytes + kSchedBytes + kBarBytes;
-  static_assert(BN % 64 == 0 && BN <= 256, "BN");
+  static_assert(BN % 128 == 0 && BN <= 256, "BN");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for SW128");
+  static_assert(kSmem <= 232448, "shared memory");
 };
 
 // In-CTA schedule: row_off[g] = sum(gs[:g]), tile_start[g] = sum(tiles[:g]).
@@ -84,7 +98,7 @@ __device__ int build_schedule(const GemmArgs& a, int32_t* row_off, int32_t* tile
   const int G = a.G;
   const int nthr = blockDim.x;
   const int per = (G + nthr - 1) / nthr;
-  const int g0 = min(G, threadIdx.x * per);
+  const int g0 = min(G, static_cast<int>(threadIdx.x) * per);
   const int g1 = min(G, g0 + per);
   long long rows = 0, tiles = 0;
   int bad = 0;
@@ -162,6 +176,13 @@ __device__ __forceinline__ TileCoord decode_tile(const int32_t* tile_start, cons
   return c;
 }
 
+// first weight row (N index) of half h of the B tile
+template <int BN, int EPI>
+__device__ __forceinline__ int b_half_base(const GemmArgs& a, int n_tile, int h) {
+  if (EPI == EPI_SITU) return (h == 0 ? 0 : a.up_offset) + n_tile * (BN / 2);
+  return n_tile * BN + h * (BN / 2);
+}
+
 __device__ __forceinline__ float situ_f(float g, float u, float beta, float lbeta) {
   const float sig = 1.0f / (1.0f + expf(-g));
   const float sg = (beta * tanhf(g / beta)) * sig;
@@ -169,11 +190,49 @@ __device__ __forceinline__ float situ_f(float g, float u, float beta, float lbet
   return sg * bu;
 }
 
-template <int BN, int STAGES, bool B_MN, int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
+// 8 e2m1 codes (one u32, low nibble first) -> 8 bf16 (uint4), times 2^(s-127).
+// Magnitudes {0, .5, 1, 1.5, 2, 3, 4, 6} are looked up bytewise with prmt
+// (high and low byte tables), the code's bit 3 becomes the bf16 sign bit (so
+// code 8 gives -0.0), and the power-of-two scale is one exact bf16x2 multiply.
+__device__ __forceinline__ uint4 dequant_e2m1x8(uint32_t x, __nv_bfloat162 scale2) {
+  const uint32_t sel = x & 0x77777777u;
+  const uint32_t kHi0 = 0x3F3F3F00u, kHi1 = 0x40404040u;
+  const uint32_t kLo0 = 0xC0800000u, kLo1 = 0xC0804000u;
+  const uint32_t hi_a = prmt(kHi0, kHi1, sel & 0xFFFFu), hi_b = prmt(kHi0, kHi1, sel >> 16);
+  const uint32_t lo_a = prmt(kLo0, kLo1, sel & 0xFFFFu), lo_b = prmt(kLo0, kLo1, sel >> 16);
+  uint32_t w0 = prmt(lo_a, hi_a, 0x5140u), w1 = prmt(lo_a, hi_a, 0x7362u);
+  uint32_t w2 = prmt(lo_b, hi_b, 0x5140u), w3 = prmt(lo_b, hi_b, 0x7362u);
+  w0 |= ((x << 12) & 0x00008000u) | ((x << 24) & 0x80000000u);
+  w1 |= ((x << 4) & 0x00008000u) | ((x << 16) & 0x80000000u);
+  w2 |= ((x >> 4) & 0x00008000u) | ((x << 8) & 0x80000000u);
+  w3 |= ((x >> 12) & 0x00008000u) | (x & 0x80000000u);
+  uint32_t r[4] = {w0, w1, w2, w3};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&r[i]);
+    v = __hmul2(v, scale2);
+    r[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// bf16 bit pattern of 2^(s-127) for an E8M0 byte s (s = 0 -> 2^-127, subnormal)
+__device__ __forceinline__ uint32_t e8m0_to_bf16_bits(uint32_t s) {
+  return s == 0 ? 0x0040u : (s << 7);
+}
+
+template <int BN, int STAGES, int BF, int EPI>
+__global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using C = GemmCfg<BN, STAGES, B_MN, EPI>;
+  using C = GemmCfg<BN, STAGES, BF, EPI>;
+  constexpr bool kMx = BF == B_MXFP4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -181,11 +240,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   int32_t* row_off = reinterpret_cast<int32_t*>(smem + STAGES * C::kStageBytes);
   int32_t* tile_start = row_off + (kMaxGroups + 1);
   int32_t* scan_rows = tile_start + (kMaxGroups + 1);
-  int32_t* scan_tiles = scan_rows + kGemmThreads;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(scan_tiles + kGemmThreads);
+  int32_t* scan_tiles = scan_rows + C::kThreads;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(scan_tiles + C::kThreads);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* bready = bars + 2 * STAGES;
+  uint64_t* tfull = bars + 3 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -203,6 +263,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(full + s), 1);
       mbar_init(smem_u32(empty + s), 1);
+      mbar_init(smem_u32(bready + s), 8);  // one arrival per dequant warp
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(tfull + b), 1);
@@ -236,27 +297,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           const uint32_t fb = smem_u32(full + stage);
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          mbar_arrive_expect_tx(fb, C::kABytes + (kMx ? C::kPackedBytes : C::kBBytes));
           const uint32_t a_dst = smem_u32(stages + stage * C::kStageBytes);
           const uint32_t b_dst = a_dst + C::kABytes;
+          const uint32_t p_dst = b_dst + C::kBBytes;
           tma_load_2d(a_dst, &tmA, fb, kb * kBK, tc.row0);
-          // B tile: two halves of BN/2 output columns each
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            int nbase;
-            if (EPI == EPI_SITU) {
-              nbase = (h == 0 ? 0 : args.up_offset) + tc.n_tile * (BN / 2);
-            } else {
-              nbase = tc.n_tile * BN + h * (BN / 2);
-            }
-            if (B_MN) {
+            const int nbase = b_half_base<BN, EPI>(args, tc.n_tile, h);
+            if (BF == B_NMAJOR) {
 #pragma unroll
-              for (int c = 0; c < BN / 128; ++c) {
+              for (int c = 0; c < BN / 128; ++c)
                 tma_load_3d(b_dst + (h * (BN / 128) + c) * (kBK * 128), &tmB, fb, nbase + c * 64,
                             kb * kBK, tc.g);
-              }
-            } else {
+            } else if (BF == B_KMAJOR) {
               tma_load_3d(b_dst + h * (BN / 2) * 128, &tmB, fb, kb * kBK, nbase, tc.g);
+            } else {
+              tma_load_3d(p_dst + h * (BN / 2) * (kBK / 2), &tmB, fb, kb * (kBK / 2), nbase, tc.g);
             }
           }
           issued |= 1u << stage;
@@ -276,7 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, B_MN);
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, BF == B_NMAJOR);
       uint32_t stage = 0, phase = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
@@ -288,7 +345,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status)) {
+          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status) ||
+              (kMx && !mbar_wait(smem_u32(bready + stage), phase, abort_flag, args.status))) {
             ok = false;
             break;
           }
@@ -298,8 +356,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + k * 2048, kBK * 128, 1024)
-                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = (BF == B_NMAJOR)
+                                       ? smem_desc_sw128(b_addr + k * 2048, kBK * 128, 1024)
+                                       : smem_desc_sw128(b_addr + k * 32, 16, 1024);
             umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(empty + stage));
@@ -319,7 +378,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_drain(smem_u32(drain), 0);
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint32_t acc = 0, acc_phase = 0;
@@ -433,6 +492,51 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             make_uint4(0, 0, 0, 0);
       }
     }
+  } else if (kMx) {
+    // ------------------------------------------------------------ MXFP4 dequant
+    // thread i of the 256 dequant threads expands row i of the B tile: 64 K
+    // elements = 8 chunks of 8 bf16, written at the 128B-swizzled position
+    // (chunk c of row r lands in 16-byte slot c ^ (r & 7)).
+    const int r = threadIdx.x - 192;
+    const int h = r / (BN / 2);
+    const int kgroups = args.K / 32;
+    uint32_t stage = 0, phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const TileCoord tc = decode_tile(tile_start, row_off, G, args.n_tiles, t);
+      const int n_row = b_half_base<BN, EPI>(args, tc.n_tile, h) + (r % (BN / 2));
+      const bool row_in = n_row < args.n_weight;
+      const uint8_t* srow = args.scales + (static_cast<int64_t>(tc.g) * args.n_weight + n_row) * kgroups;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        // scale bytes for this row's two 32-element blocks (read before the wait)
+        uint32_t s01 = 0x7F7Fu;
+        if (row_in) s01 = __ldg(reinterpret_cast<const uint16_t*>(srow + kb * 2));
+        if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = stages + stage * C::kStageBytes;
+        const uint4* prow = reinterpret_cast<const uint4*>(st + C::kABytes + C::kBBytes + r * (kBK / 2));
+        const uint4 p0 = prow[0], p1 = prow[1];
+        const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const uint32_t b0 = e8m0_to_bf16_bits(s01 & 0xFFu), b1 = e8m0_to_bf16_bits(s01 >> 8);
+        const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
+        uint8_t* brow = st + C::kABytes + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t sc = c < 4 ? sc0 : sc1;
+          const uint4 v = dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sc));
+          *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(bready + stage));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -447,11 +551,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 namespace {
 
-template <int BN, int STAGES, bool B_MN, int EPI>
+template <int BN, int STAGES, int BF, int EPI>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int max_tiles,
                 cudaStream_t stream) {
-  using C = GemmCfg<BN, STAGES, B_MN, EPI>;
-  auto kern = grouped_gemm_kernel<BN, STAGES, B_MN, EPI>;
+  using C = GemmCfg<BN, STAGES, BF, EPI>;
+  auto kern = grouped_gemm_kernel<BN, STAGES, BF, EPI>;
   int dev = 0;
   cudaGetDevice(&dev);
   static std::mutex mu;
@@ -467,17 +571,76 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
   }
   const int sms = num_sms(dev);
   const int grid = max(1, min(sms, max_tiles));
-  kern<<<grid, kGemmThreads, C::kSmem, stream>>>(ta, tb, a);
+  kern<<<grid, C::kThreads, C::kSmem, stream>>>(ta, tb, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
-constexpr int kStagesBN256 = 4;
+constexpr int kStagesBf16 = 4;
+constexpr int kStagesMx = 3;
 
 template <int EPI>
-int dispatch_layout(bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                     int max_tiles, cudaStream_t s) {
-  if (b_mn) return launch_gemm<256, kStagesBN256, true, EPI>(ta, tb, a, max_tiles, s);
-  return launch_gemm<256, kStagesBN256, false, EPI>(ta, tb, a, max_tiles, s);
+  switch (bf) {
+    case B_NMAJOR: return launch_gemm<256, kStagesBf16, B_NMAJOR, EPI>(ta, tb, a, max_tiles, s);
+    case B_KMAJOR: return launch_gemm<256, kStagesBf16, B_KMAJOR, EPI>(ta, tb, a, max_tiles, s);
+    default: return launch_gemm<256, kStagesMx, B_MXFP4, EPI>(ta, tb, a, max_tiles, s);
+  }
+}
+
+int launch_epi(int epi, int bf, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+               int max_tiles, cudaStream_t stream) {
+  switch (epi) {
+    case EPI_BF16: return dispatch_format<EPI_BF16>(bf, ta, tb, a, max_tiles, stream);
+    case EPI_F32: return dispatch_format<EPI_F32>(bf, ta, tb, a, max_tiles, stream);
+    case EPI_BF16_ADD: return dispatch_format<EPI_BF16_ADD>(bf, ta, tb, a, max_tiles, stream);
+    case EPI_SITU: return dispatch_format<EPI_SITU>(bf, ta, tb, a, max_tiles, stream);
+    default: return kBadShape;
+  }
+}
+
+int common_checks(const void* lhs, const void* out, int64_t M, int64_t K, int64_t N_out, int64_t G,
+                  int epi, const void* addend, int64_t ld_add, int64_t up_offset) {
+  if (M < 0 || K <= 0 || N_out <= 0 || G <= 0 || G > kMaxGroups) return kBadShape;
+  if (M >= (1ll << 31) || K >= (1ll << 31) || N_out >= (1ll << 31)) return kBadShape;
+  if (K % 8 != 0 || N_out % 8 != 0) return kUnsupported;  // 16-byte TMA strides / vector stores
+  if ((reinterpret_cast<uintptr_t>(lhs) | reinterpret_cast<uintptr_t>(out)) & 15) return kUnsupported;
+  if (epi == EPI_BF16_ADD && (addend == nullptr || (reinterpret_cast<uintptr_t>(addend) & 15) ||
+                              ld_add % 8 != 0))
+    return kUnsupported;
+  if (epi == EPI_SITU && up_offset != N_out) return kBadShape;
+  return kOk;
+}
+
+GemmArgs make_args(const int32_t* group_sizes, void* out, const void* addend, int64_t ld_add,
+                   int64_t M, int64_t K, int64_t N_out, int64_t G, int epi, int64_t up_offset,
+                   int64_t n_weight, float beta, float linear_beta, int round_gate_up,
+                   int zero_tail, int32_t* status) {
+  GemmArgs a{};
+  a.group_sizes = group_sizes;
+  a.status = status;
+  a.out = out;
+  a.addend = static_cast<const __nv_bfloat16*>(addend);
+  a.ldo = N_out;
+  a.ld_add = ld_add;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N_out);
+  a.K = static_cast<int>(K);
+  a.G = group_sizes == nullptr ? 1 : static_cast<int>(G);
+  const int out_tile = (epi == EPI_SITU) ? 128 : 256;
+  a.n_tiles = static_cast<int>((N_out + out_tile - 1) / out_tile);
+  a.up_offset = static_cast<int>(up_offset);
+  a.n_weight = static_cast<int>(n_weight);
+  a.beta = beta;
+  a.linear_beta = linear_beta;
+  a.round_gate_up = round_gate_up;
+  a.zero_tail = zero_tail;
+  return a;
+}
+
+int max_tiles_of(const GemmArgs& a) {
+  const int64_t t = ((static_cast<int64_t>(a.M) + kBM - 1) / kBM + a.G) * a.n_tiles;
+  return static_cast<int>(std::min<int64_t>(t, 1 << 30));
 }
 
 }  // namespace
@@ -489,22 +652,14 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
                       const void* addend, int64_t ld_add, int64_t up_offset, float beta,
                       float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
                       cudaStream_t stream) {
-  if (M < 0 || K <= 0 || N_out <= 0 || G <= 0 || G > kMaxGroups) return kBadShape;
-  if (M >= (1ll << 31) || K >= (1ll << 31) || N_out >= (1ll << 31)) return kBadShape;
   if (rhs_layout != 0 && rhs_layout != 1) return kBadShape;
-  if (K % 8 != 0 || N_out % 8 != 0) return kUnsupported;  // 16-byte TMA strides / vector stores
+  int rc = common_checks(lhs, out, M, K, N_out, G, epi, addend, ld_add, up_offset);
+  if (rc != kOk) return rc;
+  if (reinterpret_cast<uintptr_t>(rhs) & 15) return kUnsupported;
   if (M == 0) return kOk;
-  if ((reinterpret_cast<uintptr_t>(lhs) | reinterpret_cast<uintptr_t>(rhs) |
-       reinterpret_cast<uintptr_t>(out)) & 15)
-    return kUnsupported;
-  if (epi == EPI_BF16_ADD && (addend == nullptr || (reinterpret_cast<uintptr_t>(addend) & 15) ||
-                              ld_add % 8 != 0))
-    return kUnsupported;
   const bool b_mn = rhs_layout == 0;
   // width of the weight's N axis (the fused [gate|up] weight is 2I wide)
   const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
-  if (epi == EPI_SITU && (up_offset != N_out)) return kBadShape;
-
   CUtensorMap ta, tb;
   if (!encode_tmap_bf16_2d(&ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
                            static_cast<uint64_t>(K) * 2, kBK, kBM))
@@ -518,34 +673,36 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
     if (!encode_tmap_bf16_3d(&tb, rhs, K, n_weight, G, K * 2, n_weight * K * 2, kBK, 128))
       return kLaunchFailed;
   }
-  GemmArgs a{};
-  a.group_sizes = group_sizes;
-  a.status = status;
-  a.out = out;
-  a.addend = static_cast<const __nv_bfloat16*>(addend);
-  a.ldo = N_out;
-  a.ld_add = ld_add;
-  a.M = static_cast<int>(M);
-  a.N = static_cast<int>(N_out);
-  a.K = static_cast<int>(K);
-  a.G = static_cast<int>(G);
-  const int out_tile = (epi == EPI_SITU) ? 128 : 256;
-  a.n_tiles = static_cast<int>((N_out + out_tile - 1) / out_tile);
-  a.up_offset = static_cast<int>(up_offset);
-  a.beta = beta;
-  a.linear_beta = linear_beta;
-  a.round_gate_up = round_gate_up;
-  a.zero_tail = zero_tail;
-  if (group_sizes == nullptr) a.G = 1;
-  const int64_t max_tiles64 = ((M + kBM - 1) / kBM + a.G) * a.n_tiles;
-  const int max_tiles = static_cast<int>(std::min<int64_t>(max_tiles64, 1 << 30));
-  switch (epi) {
-    case EPI_BF16: return dispatch_layout<EPI_BF16>(b_mn, ta, tb, a, max_tiles, stream);
-    case EPI_F32: return dispatch_layout<EPI_F32>(b_mn, ta, tb, a, max_tiles, stream);
-    case EPI_BF16_ADD: return dispatch_layout<EPI_BF16_ADD>(b_mn, ta, tb, a, max_tiles, stream);
-    case EPI_SITU: return dispatch_layout<EPI_SITU>(b_mn, ta, tb, a, max_tiles, stream);
-    default: return kBadShape;
-  }
+  const GemmArgs a = make_args(group_sizes, out, addend, ld_add, M, K, N_out, G, epi, up_offset,
+                               n_weight, beta, linear_beta, round_gate_up, zero_tail, status);
+  return launch_epi(epi, b_mn ? B_NMAJOR : B_KMAJOR, ta, tb, a, max_tiles_of(a), stream);
+}
+
+// MXFP4 weights: packed (G, n_weight, K/2) u8, scales (G, n_weight, K/32) u8.
+int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
+                       const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N_out,
+                       int64_t G, int epi, int64_t up_offset, float beta, float linear_beta,
+                       int round_gate_up, int zero_tail, int32_t* status, cudaStream_t stream) {
+  int rc = common_checks(lhs, out, M, K, N_out, G, epi, nullptr, 0, up_offset);
+  if (rc != kOk) return rc;
+  if (epi == EPI_BF16_ADD) return kUnsupported;
+  if (K % 64 != 0) return kUnsupported;  // whole 32-element scale blocks per 64-wide K step
+  if (reinterpret_cast<uintptr_t>(packed) & 15 || scales == nullptr ||
+      (reinterpret_cast<uintptr_t>(scales) & 1))
+    return kUnsupported;
+  if (M == 0) return kOk;
+  const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
+  CUtensorMap ta, tb;
+  if (!encode_tmap_bf16_2d(&ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                           static_cast<uint64_t>(K) * 2, kBK, kBM))
+    return kLaunchFailed;
+  // dims {K/2 bytes, N, G}, box {32 bytes = 64 codes, 128 rows, 1}
+  if (!encode_tmap_u8_3d(&tb, packed, K / 2, n_weight, G, K / 2, n_weight * (K / 2), kBK / 2, 128))
+    return kLaunchFailed;
+  GemmArgs a = make_args(group_sizes, out, nullptr, 0, M, K, N_out, G, epi, up_offset, n_weight,
+                         beta, linear_beta, round_gate_up, zero_tail, status);
+  a.scales = static_cast<const uint8_t*>(scales);
+  return launch_epi(epi, B_MXFP4, ta, tb, a, max_tiles_of(a), stream);
 }
 
 }  // namespace lmoe

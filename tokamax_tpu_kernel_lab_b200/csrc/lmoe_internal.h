@@ -28,6 +28,11 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
                       float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
                       cudaStream_t stream);
 
+int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
+                       const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N_out,
+                       int64_t G, int epi, int64_t up_offset, float beta, float linear_beta,
+                       int round_gate_up, int zero_tail, int32_t* status, cudaStream_t stream);
+
 inline int current_device() {
   int d = 0;
   cudaGetDevice(&d);

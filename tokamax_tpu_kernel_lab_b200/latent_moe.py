@@ -92,10 +92,12 @@ class LatentMoEWeights:
 
 
 def init_weights(config: LatentMoEConfig, seed: int = 0, dtype: torch.dtype = torch.bfloat16,
-                 device: str | torch.device = "cuda", bias_std: float = 0.0) -> LatentMoEWeights:
+                 device: str | torch.device = "cuda", bias_std: float = 0.0,
+                 experts: bool = True) -> LatentMoEWeights:
   """N(0, 0.02^2) weights (the distribution of kimi_k3_latent_moe_reference.py:255-283),
   drawn on the device from a seeded generator; optional N(0, bias_std^2)
-  router bias for the skewed-load configurations."""
+  router bias for the skewed-load configurations.  experts=False leaves the
+  routed-expert tensors out (None), for MXFP4 experts supplied separately."""
   gen = torch.Generator(device=device)
   gen.manual_seed(seed)
   c = config
@@ -107,14 +109,15 @@ def init_weights(config: LatentMoEConfig, seed: int = 0, dtype: torch.dtype = to
   bias = torch.zeros(c.num_experts, device=device, dtype=torch.float32)
   if bias_std > 0:
     bias = torch.randn(c.num_experts, generator=gen, device=device) * bias_std
+  ex = (lambda *s: normal(*s)) if experts else (lambda *s: None)
   return LatentMoEWeights(
       router_weight=normal(c.hidden_size, c.num_experts),
       e_score_correction_bias=bias.to(dtype),
       down_proj=normal(c.hidden_size, c.latent_size),
       up_proj=normal(c.latent_size, c.hidden_size),
-      expert_gate=normal(c.num_experts, c.latent_size, c.intermediate_size),
-      expert_up=normal(c.num_experts, c.latent_size, c.intermediate_size),
-      expert_down=normal(c.num_experts, c.intermediate_size, c.latent_size),
+      expert_gate=ex(c.num_experts, c.latent_size, c.intermediate_size),
+      expert_up=ex(c.num_experts, c.latent_size, c.intermediate_size),
+      expert_down=ex(c.num_experts, c.intermediate_size, c.latent_size),
       norm_scale=torch.ones(c.latent_size, device=device, dtype=dtype),
       shared_gate=normal(c.hidden_size, si),
       shared_up=normal(c.hidden_size, si),
@@ -124,7 +127,8 @@ def init_weights(config: LatentMoEConfig, seed: int = 0, dtype: torch.dtype = to
 
 @dataclasses.dataclass
 class PreparedWeights:
-  """Kernel layouts (see the module docstring)."""
+  """Kernel layouts (see the module docstring).  Routed experts are either
+  bf16/f32 tensors or MXFP4 (`expert_gu_mx`, `expert_down_mx`)."""
 
   dtype: torch.dtype
   router: torch.Tensor
@@ -134,12 +138,54 @@ class PreparedWeights:
   expert_gu: torch.Tensor | None
   expert_gate: torch.Tensor | None  # f32 path keeps gate and up apart (G, I, L)
   expert_up: torch.Tensor | None
-  expert_down: torch.Tensor
+  expert_down: torch.Tensor | None
   norm_scale: torch.Tensor
   shared_gu: torch.Tensor | None
   shared_gate: torch.Tensor | None
   shared_up: torch.Tensor | None
   shared_down: torch.Tensor
+  expert_gu_mx: ops.MXFP4Weights | None = None     # (E, 2I, L/2) codes: [w1 gate | w3 up]
+  expert_down_mx: ops.MXFP4Weights | None = None   # (E, L, I/2) codes: w2
+
+
+def random_mxfp4(num_experts: int, n: int, k: int, seed: int, device="cuda",
+                 scale_exp=(-8, -6)) -> ops.MXFP4Weights:
+  """Seeded synthetic MXFP4 weights: e2m1 codes uniform over all 16 values and
+  E8M0 scales with unbiased exponent uniform in [scale_exp[0], scale_exp[1]]
+  ((-8, -6) gives weights of rms ~0.02, the N(0, 0.02^2) scale of the dense
+  weights; (-6, 2) is benchmark configuration 4)."""
+  gen = torch.Generator(device=device)
+  gen.manual_seed(seed)
+  packed = torch.randint(0, 256, (num_experts, n, k // 2), generator=gen, device=device,
+                         dtype=torch.int32).to(torch.uint8)
+  scale = torch.randint(127 + scale_exp[0], 127 + scale_exp[1] + 1, (num_experts, n, k // 32),
+                        generator=gen, device=device, dtype=torch.int32).to(torch.uint8)
+  return ops.MXFP4Weights(packed, scale)
+
+
+def init_prepared_mxfp4(config: LatentMoEConfig, seed: int = 0, device="cuda",
+                        bias_std: float = 0.5, expert_start: int = 0,
+                        num_local_experts: int | None = None) -> PreparedWeights:
+  """bf16 dense weights (N(0, 0.02^2)) plus MXFP4 routed experts, directly in
+  the kernel layouts.  With expert_start / num_local_experts only that
+  contiguous expert range is materialised (expert parallelism); the experts
+  are drawn per global index so every rank sees the same global weights."""
+  c = config
+  e_loc = c.num_experts if num_local_experts is None else num_local_experts
+  dense = init_weights(dataclasses.replace(c, num_experts=c.num_experts), seed=seed,
+                       dtype=torch.bfloat16, device=device, bias_std=bias_std, experts=False)
+  pw = prepare_weights(dense, torch.bfloat16)
+  gus, downs = [], []
+  for e in range(expert_start, expert_start + e_loc):
+    gus.append(random_mxfp4(1, 2 * c.intermediate_size, c.latent_size, seed * 100003 + 2 * e + 1,
+                            device))
+    downs.append(random_mxfp4(1, c.latent_size, c.intermediate_size, seed * 100003 + 2 * e + 2,
+                              device))
+  pw.expert_gu_mx = ops.MXFP4Weights(torch.cat([w.packed for w in gus]),
+                                     torch.cat([w.scale for w in gus]))
+  pw.expert_down_mx = ops.MXFP4Weights(torch.cat([w.packed for w in downs]),
+                                       torch.cat([w.scale for w in downs]))
+  return pw
 
 
 def _t(w: torch.Tensor) -> torch.Tensor:
@@ -151,16 +197,18 @@ def prepare_weights(w: LatentMoEWeights, dtype: torch.dtype | None = None) -> Pr
   dtype = dtype or w.down_proj.dtype
   cv = lambda a: a.to(dtype)
   bf16 = dtype == torch.bfloat16
+  has_ex = w.expert_gate is not None
   return PreparedWeights(
       dtype=dtype,
       router=_t(cv(w.router_weight)),
       bias=w.e_score_correction_bias.float().contiguous(),
       down=_t(cv(w.down_proj)),
       up=_t(cv(w.up_proj)),
-      expert_gu=_t(torch.cat([cv(w.expert_gate), cv(w.expert_up)], dim=-1)) if bf16 else None,
-      expert_gate=None if bf16 else _t(cv(w.expert_gate)),
-      expert_up=None if bf16 else _t(cv(w.expert_up)),
-      expert_down=_t(cv(w.expert_down)),
+      expert_gu=_t(torch.cat([cv(w.expert_gate), cv(w.expert_up)], dim=-1))
+      if bf16 and has_ex else None,
+      expert_gate=None if bf16 or not has_ex else _t(cv(w.expert_gate)),
+      expert_up=None if bf16 or not has_ex else _t(cv(w.expert_up)),
+      expert_down=_t(cv(w.expert_down)) if has_ex else None,
       norm_scale=cv(w.norm_scale).contiguous(),
       shared_gu=_t(torch.cat([cv(w.shared_gate), cv(w.shared_up)], dim=-1)) if bf16 else None,
       shared_gate=None if bf16 else _t(cv(w.shared_gate)),
@@ -187,14 +235,19 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
   sorted_tokens = ops.gather_rows(x, d.token_idx)
   beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
-  if pw.dtype == torch.bfloat16:
+  if pw.expert_gu_mx is not None:
+    act = ops.mxfp4_fused_gateup_situ(sorted_tokens, pw.expert_gu_mx, d.group_sizes, beta=beta,
+                                      linear_beta=lbeta, round_gate_up=True)
+    down = ops.mxfp4_ragged_dot(act, pw.expert_down_mx, d.group_sizes)
+  elif pw.dtype == torch.bfloat16:
     act = ops.fused_gateup_situ(sorted_tokens, pw.expert_gu, d.group_sizes, beta=beta,
                                 linear_beta=lbeta, round_gate_up=True, rhs_layout="gnk")
+    down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
   else:
     gate = ops.ragged_dot(sorted_tokens, pw.expert_gate, d.group_sizes, rhs_layout="gnk")
     up = ops.ragged_dot(sorted_tokens, pw.expert_up, d.group_sizes, rhs_layout="gnk")
     act = ops.situ_and_mul(gate, up, beta, lbeta)
-  down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
+    down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
   routed, normed = ops.combine_rmsnorm(down, d.slot_pos, topk_w, pw.norm_scale, c.rms_norm_eps,
                                        want_routed=True)
   upo = _dense(normed, pw.up)

@@ -167,6 +167,58 @@ def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: to
   return res
 
 
+@dataclasses.dataclass
+class MXFP4Weights:
+  """MXFP4 expert weights in the checkpoint's (out, in) layout:
+  `packed` (G, N, K/2) uint8 e2m1 codes, low nibble = even k;
+  `scale` (G, N, K/32) uint8 E8M0 exponents (2^(s-127)).
+  (05_ragged_dot_on_tpu/mxfp4_dequant.py:14-20, README.md:303-318)."""
+
+  packed: torch.Tensor
+  scale: torch.Tensor
+
+  @property
+  def shape(self):
+    g, n, kh = self.packed.shape
+    return g, n, kh * 2
+
+
+def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tensor, *,
+                     preferred_element_type: torch.dtype | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+  """lhs (M, K) bf16 @ dequant(w[g])^T per group -> (M, N); the weights stay
+  packed in HBM and are expanded tile by tile in shared memory."""
+  _need_cuda(lhs, w.packed, w.scale, group_sizes)
+  g, n, k = w.shape
+  m = lhs.shape[0]
+  if lhs.shape[1] != k or w.scale.shape != (g, n, k // 32):
+    raise ValueError("MXFP4 shape mismatch")
+  out_dtype = preferred_element_type or torch.bfloat16
+  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  _native.call("lmoe_mxfp4_ragged_dot", _ptr(lhs.contiguous()), _ptr(w.packed), _ptr(w.scale),
+               _ptr(group_sizes.to(torch.int32).contiguous()), _ptr(res), m, k, n, g,
+               int(out_dtype == torch.float32), _ptr(device_status(lhs.device)), _stream())
+  return res
+
+
+def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
+                            group_sizes: torch.Tensor | None, *, beta: float = 4.0,
+                            linear_beta: float = 25.0, round_gate_up: bool = True,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+  """SiTU-GLU of one grouped matmul against MXFP4 [gate rows | up rows]."""
+  _need_cuda(lhs, w_gateup.packed, w_gateup.scale, group_sizes)
+  g, two_i, k = w_gateup.shape
+  inter = two_i // 2
+  m = lhs.shape[0]
+  gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
+  res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
+  _native.call("lmoe_mxfp4_gateup_situ", _ptr(lhs.contiguous()), _ptr(w_gateup.packed),
+               _ptr(w_gateup.scale), _ptr(gs), _ptr(res), m, k, inter, g, float(beta),
+               float(linear_beta), int(round_gate_up), _ptr(device_status(lhs.device)),
+               _stream())
+  return res
+
+
 def parse_fused_activation(spec: str) -> tuple[float, float]:
   """"situ:<beta>:<linear_beta>" (kimi_k3_latent_moe_ragged_dot.py:718)."""
   parts = spec.split(":")
