@@ -178,6 +178,18 @@ LMOE_API int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_po
                          int64_t latent, float eps, int bf16, void* routed_out, void* normed_out,
                          void* stream);
 
+/* Expert-parallel receive-side reordering.  After the payload all-to-all the
+ * rows are grouped by source rank, each source block ordered by local expert;
+ * recv_counts (world, num_local_experts) int32 device holds the per-(source,
+ * expert) row counts.  Writes em_src[p] (received row feeding expert-major
+ * position p), its inverse sm_src[q], and group_sizes (num_local_experts) for
+ * the grouped GEMMs.  rows_cap bounds the number of rows written.
+ * No counterpart in the reference, which only simulates expert shards in one
+ * process (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:1531-1674). */
+LMOE_API int lmoe_ep_reorder(const int32_t* recv_counts, int64_t world, int64_t num_local_experts,
+                             int64_t rows_cap, int32_t* em_src, int32_t* sm_src,
+                             int32_t* group_sizes, void* stream);
+
 /* Scatter-add combine of one expert shard:
  *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0
  * Replaces _combine_shard_contribution

@@ -46,7 +46,12 @@ SIGNATURES = {
     "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _p]),
     "lmoe_combine_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p, _p, _p]),
     "lmoe_combine_scatter_add": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]),
+    "lmoe_ep_reorder": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
 }
+
+# kernels launched by one call of each entry point (for the bench's launch count)
+KERNELS_PER_CALL = {"lmoe_dispatch": 3}
+launch_count = 0
 
 
 class NativeLibraryMissing(RuntimeError):
@@ -89,8 +94,10 @@ def call(name: str, *args) -> int:
 
   LMOE_UNSUPPORTED maps to NotImplementedError (the reference's error class for
   shapes an implementation does not support), LMOE_BAD_SHAPE to ValueError."""
+  global launch_count
   rc = getattr(load(), name)(*args)
   if rc == LMOE_OK:
+    launch_count += KERNELS_PER_CALL.get(name, 1)
     return rc
   if rc == LMOE_UNSUPPORTED:
     raise NotImplementedError(f"{name}: unsupported shape or alignment (status {rc})")

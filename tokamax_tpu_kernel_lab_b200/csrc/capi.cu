@@ -119,6 +119,13 @@ int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const 
                                eps, bf16, routed_out, normed_out, S(stream));
 }
 
+int lmoe_ep_reorder(const int32_t* recv_counts, int64_t world, int64_t num_local_experts,
+                    int64_t rows_cap, int32_t* em_src, int32_t* sm_src, int32_t* group_sizes,
+                    void* stream) {
+  return lmoe::ep_reorder(recv_counts, world, num_local_experts, rows_cap, em_src, sm_src,
+                          group_sizes, S(stream));
+}
+
 int lmoe_combine_scatter_add(const void* shard_out, const int32_t* padded_token_idx,
                              const float* padded_combine_weight, void* routed_out, int64_t rows,
                              int64_t latent, int64_t num_tokens, int bf16, void* stream) {

@@ -68,6 +68,8 @@ int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float
                     void* routed_out, void* normed_out, cudaStream_t stream);
 int scatter_add(const void* shard_out, const int32_t* idx, const float* w, void* routed,
                 int64_t rows, int64_t L, int64_t T, int bf16, cudaStream_t stream);
+int ep_reorder(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t rows_cap,
+               int32_t* em_src, int32_t* sm_src, int32_t* group_sizes, cudaStream_t stream);
 int situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
                  int64_t I, float beta, float lbeta, int bf16, cudaStream_t stream);
 

@@ -538,6 +538,73 @@ int scatter_add(const void* shard_out, const int32_t* idx, const float* w, void*
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
+// =========================================================================== EP reorder
+// Expert-parallel receive side.  Rows arrive from the all-to-all grouped by
+// source rank, and within a source block ordered by local expert (the sender's
+// dispatch sorts by global expert id).  For recv_counts[s][e] (rows source s
+// sent for local expert e):
+//   em_src[p] = q   expert-major position p takes received row q
+//   sm_src[q] = p   (inverse) expert-major row that returns to received row q
+//   group_sizes[e] = sum_s recv_counts[s][e]
+// Expert-major order is (expert, source, arrival), so each expert's rows keep
+// their source-rank order and the grouped GEMM sees one contiguous group per
+// local expert.
+constexpr int kMaxEpBlocks = 4096;  // world * local experts
+
+__global__ void __launch_bounds__(256) ep_reorder_kernel(const int32_t* __restrict__ recv_counts,
+                                                         int world, int n_local, int64_t rows_cap,
+                                                         int32_t* __restrict__ em_src,
+                                                         int32_t* __restrict__ sm_src,
+                                                         int32_t* __restrict__ group_sizes) {
+  __shared__ int src_off[kMaxEpBlocks + 1];  // block (s, e) start in source-major order
+  __shared__ int exp_off[kMaxEpBlocks];      // block (s, e) start in expert-major order
+  const int nb = world * n_local;
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int i = 0; i < nb; ++i) {
+      src_off[i] = run;
+      run += recv_counts[i];
+    }
+    src_off[nb] = run;
+    run = 0;
+    for (int e = 0; e < n_local; ++e)
+      for (int s = 0; s < world; ++s) {
+        exp_off[s * n_local + e] = run;
+        run += recv_counts[s * n_local + e];
+      }
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e < n_local; e += blockDim.x) {
+      int t = 0;
+      for (int s = 0; s < world; ++s) t += recv_counts[s * n_local + e];
+      group_sizes[e] = t;
+    }
+  }
+  const int64_t total = min<int64_t>(src_off[nb], rows_cap);
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < total;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int lo = 0, hi = nb - 1;  // last block with src_off <= q (empty blocks skipped)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (src_off[mid] <= q) lo = mid; else hi = mid - 1;
+    }
+    const int64_t p = exp_off[lo] + (q - src_off[lo]);
+    em_src[p] = static_cast<int32_t>(q);
+    sm_src[q] = static_cast<int32_t>(p);
+  }
+}
+
+int ep_reorder(const int32_t* recv_counts, int64_t world, int64_t n_local, int64_t rows_cap,
+               int32_t* em_src, int32_t* sm_src, int32_t* group_sizes, cudaStream_t stream) {
+  if (world <= 0 || n_local <= 0 || world * n_local > kMaxEpBlocks || rows_cap < 0)
+    return kBadShape;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((rows_cap + 255) / 256, 1024)));
+  ep_reorder_kernel<<<blocks, 256, 0, stream>>>(recv_counts, (int)world, (int)n_local, rows_cap,
+                                                em_src, sm_src, group_sizes);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
 // =========================================================================== SiTU-GLU
 // out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)), f32 math.
 // gate/up may be two arrays or the two halves of one fused [gate|up] row.
