@@ -581,7 +581,8 @@ __global__ void __launch_bounds__(256) ep_reorder_kernel(const int32_t* __restri
       group_sizes[e] = t;
     }
   }
-  const int64_t total = min<int64_t>(src_off[nb], rows_cap);
+  const int64_t received = src_off[nb];
+  const int64_t total = received < rows_cap ? received : rows_cap;
   for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < total;
        q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     int lo = 0, hi = nb - 1;  // last block with src_off <= q (empty blocks skipped)
