@@ -37,7 +37,8 @@ enum {
   LMOE_UNSUPPORTED = 2,    /* alignment or divisibility the kernels need */
   LMOE_LAUNCH_FAILED = 3,  /* CUDA launch or tensor-map encode failed */
   LMOE_DEVICE_BOUNDS = 4,  /* (dev_status) group sizes invalid on the device */
-  LMOE_WAIT_TIMEOUT = 5    /* (dev_status) a bounded device wait gave up */
+  LMOE_WAIT_TIMEOUT = 5,   /* (dev_status) a bounded device wait gave up */
+  LMOE_SCRATCH_TOO_SMALL = 6 /* request exceeds the library's built-in scratch */
 };
 
 enum { LMOE_RHS_GKN = 0, LMOE_RHS_GNK = 1 };
@@ -161,6 +162,25 @@ LMOE_API int lmoe_dispatch(const int32_t* topk_idx, const float* topk_w, int64_t
                   int pad_bucket, int32_t* order, int32_t* token_idx, float* weight,
                   int32_t* slot_pos, int32_t* group_sizes, int32_t* per_expert_counts,
                   uint8_t* valid, void* workspace, size_t workspace_bytes, void* stream);
+
+/* lmoe_dispatch without a workspace argument, for callers that cannot allocate
+ * device memory where they dispatch (a framework that owns the whole memory
+ * pool, or a latency-critical loop that must not call cudaMalloc, which can
+ * block on the device).  Same arguments and outputs as lmoe_dispatch minus the
+ * workspace; the scratch is a fixed ~2.1 MB array inside the library, one per
+ * device, resident until the process exits.  Limit: max(num_tokens*top_k, m_out)
+ * <= 262144 and num_local_experts <= 2048, else LMOE_SCRATCH_TOO_SMALL with no
+ * launch.  All calls on a device share the array: calls that overlap on the
+ * GPU race and must be ordered.  The first call on each device looks up the
+ * array's address; make it before any stream capture.
+ * No counterpart in the reference. */
+LMOE_API int lmoe_dispatch_static_scratch(const int32_t* topk_idx, const float* topk_w,
+                                          int64_t num_tokens, int64_t top_k,
+                                          int64_t expert_start, int64_t num_local_experts,
+                                          int64_t m_out, int pad_bucket, int32_t* order,
+                                          int32_t* token_idx, float* weight, int32_t* slot_pos,
+                                          int32_t* group_sizes, int32_t* per_expert_counts,
+                                          uint8_t* valid, void* stream);
 
 /* Row gather: out[p] = token_idx[p] >= 0 ? x[token_idx[p]] : 0, rows of row_bytes
  * (a multiple of 16).  Replaces `x[sorted_token_idx]` / `where(valid, x[idx], 0)`
