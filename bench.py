@@ -346,7 +346,10 @@ def main():
     gs = torch.full((n_local,), rows // n_local, dtype=torch.int32, device=dev)
     gs[0] += rows - int(gs.sum().item())
     xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(torch.bfloat16)
-  act = torch.empty(rows, cfg.intermediate_size, dtype=torch.bfloat16, device=dev)
+  f16 = pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok
+  if f16:  # the forward feeds this kernel f16-carried bf16 rows
+    xs = xs.to(torch.float16)
+  act = torch.empty(rows, cfg.intermediate_size, dtype=xs.dtype, device=dev)
   for _ in range(2):
     ops.mxfp4_fused_gateup_situ(xs, pw.expert_gu_mx, gs, out=act)
   torch.cuda.synchronize()

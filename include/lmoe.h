@@ -100,22 +100,29 @@ LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const 
  * accumulation.  Result = lhs @ dequant(w)^T, exactly the dequant-then-matmul
  * of 05_ragged_dot_on_tpu/mxfp4_dequant.py:29-67 (code 8 = -0.0, scale byte 0 =
  * 2^-127).  k a multiple of 64, n a multiple of 8; bf16 or f32 out.
+ * lhs_f16 = 1: lhs holds f16 (bf16 values carried in f16, e.g. from
+ * lmoe_gather_rows with convert = 1); the codes are then expanded with the
+ * hardware e2m1 -> f16 conversion and the MMA runs on f16 operands, which needs
+ * every scale byte in [104, 140] (weights of magnitude 2^-23 .. 2^13 x 6).
  * Replaces the MXFP4 dequant matmul
  * (05_ragged_dot_on_tpu/mxfp4_online_dequant_matmul_pallas.py:120-157). */
 LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
                                    const void* weight_scale, const int32_t* group_sizes, void* out,
                                    int64_t m, int64_t k, int64_t n, int64_t num_groups,
-                                   int out_f32, int32_t* dev_status, void* stream);
+                                   int lhs_f16, int out_f32, int32_t* dev_status, void* stream);
 
 /* Fused gate/up + SiTU-GLU against MXFP4 weights: the packed rows are
  * [gate (intermediate rows) | up (intermediate rows)] per group, i.e.
  * (g, 2*intermediate, k/2) codes and (g, 2*intermediate, k/32) scales (the
- * checkpoint's w1 and w3 stacked).  group_sizes NULL = one dense group. */
+ * checkpoint's w1 and w3 stacked).  group_sizes NULL = one dense group.
+ * lhs_f16 as above; out_f16 = 1 stores the bf16-rounded activation as f16
+ * (the lhs of a following lhs_f16 down-projection). */
 LMOE_API int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed,
                                     const void* weight_scale, const int32_t* group_sizes,
                                     void* out, int64_t m, int64_t k, int64_t intermediate,
                                     int64_t num_groups, float beta, float linear_beta,
-                                    int round_gate_up, int32_t* dev_status, void* stream);
+                                    int round_gate_up, int lhs_f16, int out_f16,
+                                    int32_t* dev_status, void* stream);
 
 /* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).
  * gate/up rows have pitch ld_in elements; bf16 = 1 for bf16 I/O, 0 for f32.
@@ -183,10 +190,12 @@ LMOE_API int lmoe_dispatch_static_scratch(const int32_t* topk_idx, const float* 
                                           uint8_t* valid, void* stream);
 
 /* Row gather: out[p] = token_idx[p] >= 0 ? x[token_idx[p]] : 0, rows of row_bytes
- * (a multiple of 16).  Replaces `x[sorted_token_idx]` / `where(valid, x[idx], 0)`
+ * (a multiple of 16).  convert = 1 reads bf16 rows and writes them as f16
+ * (exact in f16's normal range), the lhs_f16 form of the MXFP4 kernels.
+ * Replaces `x[sorted_token_idx]` / `where(valid, x[idx], 0)`
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:372-374, 867-868). */
 LMOE_API int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out,
-                     int64_t rows, int64_t row_bytes, void* stream);
+                              int64_t rows, int64_t row_bytes, int convert, void* stream);
 
 /* Weighted combine + RMSNorm:
  *   routed[t] = dtype(sum_s expert_out[slot_pos[t*k+s]] * topk_w[t,s])   (f32, slot order)

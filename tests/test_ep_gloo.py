@@ -58,6 +58,9 @@ class OracleBackend:
     out[ok] = x.numpy()[idx[ok]]
     return torch.from_numpy(out)
 
+  def gather_send(self, x, index):
+    return self.gather(x, index)
+
   def reorder(self, recv_counts, world, n_local, rows):
     cnt = recv_counts.numpy().reshape(world, n_local)
     src_off = np.concatenate([[0], np.cumsum(cnt.reshape(-1))])[:-1].reshape(world, n_local)

@@ -45,14 +45,42 @@ def test_in_kernel_dequant_is_bit_exact(lm):
   assert np.array_equal(to_np(out), ref)
 
 
+def test_f16_operand_dequant_is_bit_exact(lm):
+  """The f16-operand kernel (hardware e2m1 -> f16 expansion, f16 x f16 UMMA)
+  reproduces dequant(W) exactly for every scale byte in its range [104, 140]."""
+  rng = np.random.default_rng(10)
+  k, n = 256, 256
+  packed, scale = _mx(rng, 1, n, k, lo=104, hi=140)
+  scale[0, 0, :2] = (104, 140)
+  lhs = torch.eye(k, dtype=torch.float16, device="cuda")
+  w = _dev_mx(lm, packed, scale)
+  assert w.f16_operand_ok
+  out = lm.mxfp4_ragged_dot(lhs, w, torch.tensor([k], dtype=torch.int32, device="cuda"),
+                            preferred_element_type=torch.float32)
+  ref = O.dequantize_mxfp4(packed[0], scale[0]).T
+  assert np.array_equal(to_np(out), ref)
+
+
+def test_f16_operand_rejects_out_of_range_scales(lm):
+  rng = np.random.default_rng(11)
+  packed, scale = _mx(rng, 1, 128, 64, lo=141, hi=150)
+  w = _dev_mx(lm, packed, scale)
+  assert not w.f16_operand_ok
+  with pytest.raises(NotImplementedError):
+    lm.mxfp4_ragged_dot(torch.zeros(4, 64, dtype=torch.float16, device="cuda"), w,
+                        torch.tensor([4], dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("lhs_dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("m,k,n,g", [(700, 256, 256, 3), (2048, 1024, 512, 16), (1, 64, 128, 2)])
-def test_mxfp4_ragged_dot(lm, m, k, n, g):
+def test_mxfp4_ragged_dot(lm, m, k, n, g, lhs_dtype):
   rng = np.random.default_rng(m + k + n)
   packed, scale = _mx(rng, g, n, k)
   gs = rng.multinomial(m, np.full(g, 1.0 / g)).astype(np.int32)
   lhs = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32))
   ref = O.mxfp4_ragged_dot(lhs, packed, scale, gs, dtype="fp32")
-  out = lm.mxfp4_ragged_dot(to_dev(lhs), _dev_mx(lm, packed, scale), torch.from_numpy(gs).cuda())
+  out = lm.mxfp4_ragged_dot(to_dev(lhs).to(lhs_dtype), _dev_mx(lm, packed, scale),
+                            torch.from_numpy(gs).cuda())
   torch.cuda.synchronize()
   lm.check_device_status()
   scale_ref = float(np.abs(ref).max()) or 1.0
@@ -76,8 +104,9 @@ def test_mxfp4_config4_full_size(lm):
   assert rep["normwise_rel"] <= 1e-2
 
 
+@pytest.mark.parametrize("f16", [False, True])
 @pytest.mark.parametrize("round_gate_up", [True, False])
-def test_mxfp4_fused_gateup_situ(lm, round_gate_up):
+def test_mxfp4_fused_gateup_situ(lm, round_gate_up, f16):
   rng = np.random.default_rng(9)
   m, k, inter, g = 1200, 512, 256, 5
   packed, scale = _mx(rng, g, 2 * inter, k, lo=120, hi=121)  # weights rms ~0.02
@@ -86,9 +115,14 @@ def test_mxfp4_fused_gateup_situ(lm, round_gate_up):
   lazy = O.LazyMXFP4Experts(packed, scale)
   ref = O.fused_gateup_situ(lhs, lazy, gs, inter, 4.0, 25.0, dtype="bf16",
                             round_gate_up=round_gate_up, out_dtype="fp32")
-  out = lm.mxfp4_fused_gateup_situ(to_dev(lhs), _dev_mx(lm, packed, scale),
-                                   torch.from_numpy(gs).cuda(), round_gate_up=round_gate_up)
+  dt = torch.float16 if f16 else torch.bfloat16
+  out = lm.mxfp4_fused_gateup_situ(to_dev(lhs).to(dt), _dev_mx(lm, packed, scale),
+                                   torch.from_numpy(gs).cuda(), round_gate_up=round_gate_up,
+                                   out_dtype=dt)
+  assert out.dtype == dt
   got = to_np(out)
+  # the f16 output carries the bf16-rounded activation exactly
+  assert np.array_equal(O.bf16_round(got), got)
   assert np.all(got[gs.sum():] == 0)
   assert_bf16_close(ref, got, f"mxfp4 situ round={round_gate_up}")
 

@@ -58,21 +58,23 @@ int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const int32_t* 
 
 int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed, const void* weight_scale,
                           const int32_t* group_sizes, void* out, int64_t m, int64_t k, int64_t n,
-                          int64_t num_groups, int out_f32, int32_t* dev_status, void* stream) {
+                          int64_t num_groups, int lhs_f16, int out_f32, int32_t* dev_status,
+                          void* stream) {
   if (group_sizes == nullptr) return LMOE_BAD_SHAPE;
   return lmoe::grouped_gemm_mxfp4(lhs, weight_packed, weight_scale, group_sizes, out, m, k, n,
                                   num_groups, out_f32 ? kEpiF32 : kEpiBf16, 0, 0.f, 0.f, 0, 1,
-                                  dev_status, S(stream));
+                                  lhs_f16, 0, dev_status, S(stream));
 }
 
 int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed, const void* weight_scale,
                            const int32_t* group_sizes, void* out, int64_t m, int64_t k,
                            int64_t intermediate, int64_t num_groups, float beta, float linear_beta,
-                           int round_gate_up, int32_t* dev_status, void* stream) {
+                           int round_gate_up, int lhs_f16, int out_f16, int32_t* dev_status,
+                           void* stream) {
   return lmoe::grouped_gemm_mxfp4(lhs, weight_packed, weight_scale, group_sizes, out, m, k,
                                   intermediate, group_sizes ? num_groups : 1, kEpiSitu,
                                   intermediate, beta, linear_beta, round_gate_up,
-                                  group_sizes ? 1 : 0, dev_status, S(stream));
+                                  group_sizes ? 1 : 0, lhs_f16, out_f16, dev_status, S(stream));
 }
 
 int lmoe_situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
@@ -107,8 +109,8 @@ int lmoe_dispatch(const int32_t* topk_idx, const float* topk_w, int64_t num_toke
 }
 
 int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out,
-                     int64_t rows, int64_t row_bytes, void* stream) {
-  return lmoe::gather_rows(x, x_rows, token_idx, out, rows, row_bytes, S(stream));
+                     int64_t rows, int64_t row_bytes, int convert, void* stream) {
+  return lmoe::gather_rows(x, x_rows, token_idx, out, rows, row_bytes, convert, S(stream));
 }
 
 int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,

@@ -55,7 +55,14 @@ constexpr int kBK = 64;
 constexpr int kMaxGroups = 2048;
 
 enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_BF16_ADD = 2, EPI_SITU = 3 };
-enum BFmt { B_KMAJOR = 0, B_NMAJOR = 1, B_MXFP4 = 2 };
+// B_MXFP4F16: the same packed MXFP4 weights, but the activations arrive as f16
+// (bf16 values, which convert to f16 exactly in f16's normal range) and the
+// codes are expanded with the hardware e2m1x2 -> f16x2 conversion; the UMMA
+// runs kind::f16 with f16 operands.  The f16 scale 2^(s-127) and every scaled
+// code stay exact for scale bytes in [104, 140] (the caller checks the range).
+enum BFmt { B_KMAJOR = 0, B_NMAJOR = 1, B_MXFP4 = 2, B_MXFP4F16 = 3 };
+
+__host__ __device__ constexpr bool is_mx(int bf) { return bf == B_MXFP4 || bf == B_MXFP4F16; }
 
 struct GemmArgs {
   const int32_t* group_sizes;  // nullptr: a single group of M rows
@@ -69,17 +76,18 @@ struct GemmArgs {
   int n_tiles;                  // ceil(N / output tile width)
   int up_offset;                // EPI_SITU: row/col offset of the up half in the fused weight
   int n_weight;                 // rows (N extent) of one group's weight
-  float beta, linear_beta;
+  float beta, linear_beta, inv_beta, inv_linear_beta;
   int round_gate_up;
   int zero_tail;
+  int out_f16;  // EPI_BF16 / EPI_SITU: store the bf16-rounded value as f16
 };
 
 template <int BN, int STAGES, int BF, int EPI>
 struct GemmCfg {
-  static constexpr int kThreads = (BF == B_MXFP4) ? 448 : 192;
+  static constexpr int kThreads = is_mx(BF) ? 448 : 192;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kPackedBytes = (BF == B_MXFP4) ? BN * (kBK / 2) : 0;
+  static constexpr int kPackedBytes = is_mx(BF) ? BN * (kBK / 2) : 0;
   static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kThreads * 4;
@@ -183,12 +191,6 @@ __device__ __forceinline__ int b_half_base(const GemmArgs& a, int n_tile, int h)
   return n_tile * BN + h * (BN / 2);
 }
 
-__device__ __forceinline__ float situ_f(float g, float u, float beta, float lbeta) {
-  const float sig = 1.0f / (1.0f + expf(-g));
-  const float sg = (beta * tanhf(g / beta)) * sig;
-  const float bu = lbeta * tanhf(u / lbeta);
-  return sg * bu;
-}
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
@@ -227,12 +229,42 @@ __device__ __forceinline__ uint32_t e8m0_to_bf16_bits(uint32_t s) {
   return s == 0 ? 0x0040u : (s << 7);
 }
 
+// f16 bit pattern of 2^(s-127), exact for s in [103, 142] (subnormal below 113)
+__device__ __forceinline__ uint32_t e8m0_to_f16_bits(uint32_t s) {
+  const int e = static_cast<int>(s) - 127;
+  return e >= -14 ? static_cast<uint32_t>(e + 15) << 10 : 1u << (e + 24);
+}
+
+// 8 e2m1 codes -> 8 f16 (uint4) with the hardware conversion (low nibble ->
+// low half), times the f16x2 scale (an exact power of two).
+__device__ __forceinline__ uint4 dequant_e2m1x8_f16(uint32_t x, uint32_t scale2) {
+  uint32_t r[4];
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+      : "r"(x));
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(r[i]) : "r"(scale2));
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// bf16-rounded value stored as f16 (exact for |v| in f16's normal range)
+__device__ __forceinline__ uint32_t pack_f16x2_of_bf16(float lo, float hi) {
+  const __half2 v = __floats2half2_rn(bf16_round_f(lo), bf16_round_f(hi));
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 template <int BN, int STAGES, int BF, int EPI>
 __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using C = GemmCfg<BN, STAGES, BF, EPI>;
-  constexpr bool kMx = BF == B_MXFP4;
+  constexpr bool kMx = is_mx(BF);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -333,7 +365,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, BF == B_NMAJOR);
+      constexpr uint32_t idesc = (BF == B_MXFP4F16) ? idesc_f16_f32(kBM, BN, false)
+                                                    : idesc_bf16_f32(kBM, BN, BF == B_NMAJOR);
       uint32_t stage = 0, phase = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
@@ -414,9 +447,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                       g = bf16_round_f(g);
                       u = bf16_round_f(u);
                     }
-                    o[h] = situ_f(g, u, args.beta, args.linear_beta);
+                    o[h] = situ_fast(g, u, args.beta, args.inv_beta, args.linear_beta, args.inv_linear_beta);
                   }
-                  pk[e] = pack_bf16x2(o[0], o[1]);
+                  pk[e] = args.out_f16 ? pack_f16x2_of_bf16(o[0], o[1]) : pack_bf16x2(o[0], o[1]);
                 }
                 *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
@@ -459,9 +492,11 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                     }
                   } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                      pk[e] = pack_bf16x2(__uint_as_float(v[j * 8 + e * 2]),
-                                          __uint_as_float(v[j * 8 + e * 2 + 1]));
+                    for (int e = 0; e < 4; ++e) {
+                      const float x0 = __uint_as_float(v[j * 8 + e * 2]);
+                      const float x1 = __uint_as_float(v[j * 8 + e * 2 + 1]);
+                      pk[e] = args.out_f16 ? pack_f16x2_of_bf16(x0, x1) : pack_bf16x2(x0, x1);
+                    }
                   }
                   *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
@@ -519,14 +554,24 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
         const uint4* prow = reinterpret_cast<const uint4*>(st + C::kABytes + C::kBBytes + r * (kBK / 2));
         const uint4 p0 = prow[0], p1 = prow[1];
         const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        const uint32_t b0 = e8m0_to_bf16_bits(s01 & 0xFFu), b1 = e8m0_to_bf16_bits(s01 >> 8);
-        const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
         uint8_t* brow = st + C::kABytes + r * 128;
+        if (BF == B_MXFP4F16) {
+          const uint32_t b0 = e8m0_to_f16_bits(s01 & 0xFFu), b1 = e8m0_to_f16_bits(s01 >> 8);
+          const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t sc = c < 4 ? sc0 : sc1;
-          const uint4 v = dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sc));
-          *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+          for (int c = 0; c < 8; ++c) {
+            const uint4 v = dequant_e2m1x8_f16(words[c], c < 4 ? sc0 : sc1);
+            *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+          }
+        } else {
+          const uint32_t b0 = e8m0_to_bf16_bits(s01 & 0xFFu), b1 = e8m0_to_bf16_bits(s01 >> 8);
+          const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t sc = c < 4 ? sc0 : sc1;
+            const uint4 v = dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sc));
+            *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+          }
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -584,6 +629,7 @@ int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const 
   switch (bf) {
     case B_NMAJOR: return launch_gemm<256, kStagesBf16, B_NMAJOR, EPI>(ta, tb, a, max_tiles, s);
     case B_KMAJOR: return launch_gemm<256, kStagesBf16, B_KMAJOR, EPI>(ta, tb, a, max_tiles, s);
+    case B_MXFP4F16: return launch_gemm<256, kStagesMx, B_MXFP4F16, EPI>(ta, tb, a, max_tiles, s);
     default: return launch_gemm<256, kStagesMx, B_MXFP4, EPI>(ta, tb, a, max_tiles, s);
   }
 }
@@ -633,6 +679,8 @@ GemmArgs make_args(const int32_t* group_sizes, void* out, const void* addend, in
   a.n_weight = static_cast<int>(n_weight);
   a.beta = beta;
   a.linear_beta = linear_beta;
+  a.inv_beta = beta != 0.f ? 1.0f / beta : 0.f;
+  a.inv_linear_beta = linear_beta != 0.f ? 1.0f / linear_beta : 0.f;
   a.round_gate_up = round_gate_up;
   a.zero_tail = zero_tail;
   return a;
@@ -679,13 +727,17 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
 }
 
 // MXFP4 weights: packed (G, n_weight, K/2) u8, scales (G, n_weight, K/32) u8.
+// lhs_f16: lhs holds f16 (bf16 values carried as f16) and the f16 operand path
+// runs (scale bytes must lie in [104, 140]); out_f16: bf16-rounded results are
+// stored as f16 (EPI_BF16 / EPI_SITU).
 int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
                        const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N_out,
                        int64_t G, int epi, int64_t up_offset, float beta, float linear_beta,
-                       int round_gate_up, int zero_tail, int32_t* status, cudaStream_t stream) {
+                       int round_gate_up, int zero_tail, int lhs_f16, int out_f16,
+                       int32_t* status, cudaStream_t stream) {
   int rc = common_checks(lhs, out, M, K, N_out, G, epi, nullptr, 0, up_offset);
   if (rc != kOk) return rc;
-  if (epi == EPI_BF16_ADD) return kUnsupported;
+  if (epi == EPI_BF16_ADD || (out_f16 && epi == EPI_F32)) return kUnsupported;
   if (K % 64 != 0) return kUnsupported;  // whole 32-element scale blocks per 64-wide K step
   if (reinterpret_cast<uintptr_t>(packed) & 15 || scales == nullptr ||
       (reinterpret_cast<uintptr_t>(scales) & 1))
@@ -702,7 +754,8 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
   GemmArgs a = make_args(group_sizes, out, nullptr, 0, M, K, N_out, G, epi, up_offset, n_weight,
                          beta, linear_beta, round_gate_up, zero_tail, status);
   a.scales = static_cast<const uint8_t*>(scales);
-  return launch_epi(epi, B_MXFP4, ta, tb, a, max_tiles_of(a), stream);
+  a.out_f16 = out_f16;
+  return launch_epi(epi, lhs_f16 ? B_MXFP4F16 : B_MXFP4, ta, tb, a, max_tiles_of(a), stream);
 }
 
 }  // namespace lmoe

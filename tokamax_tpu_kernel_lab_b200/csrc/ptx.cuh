@@ -12,6 +12,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #ifndef LMOE_WAIT_TIMEOUT_NS
 #define LMOE_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate wait
@@ -219,6 +220,32 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n, bool b_mn_major) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) |
          ((m >> 4) << 24);
+}
+
+// Same with f16 A and B (A/B format 0).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t m, uint32_t n, bool b_mn_major) {
+  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Hardware tanh (MUFU.TANH; max relative error about 2^-11).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// SiTU-GLU of one (gate, up) pair: beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb),
+// with inv_beta = 1/beta and inv_lbeta = 1/lb precomputed.  tanh on the MUFU
+// unit, sigmoid as 1 / (1 + 2^(-g*log2 e)) with the approximate exp2 and
+// reciprocal; every output is rounded to bf16 afterwards, far coarser than
+// these approximations.  Used by both the fused GEMM epilogue and the
+// standalone SiTU kernel, so the two produce identical bits.
+__device__ __forceinline__ float situ_fast(float g, float u, float beta, float inv_beta,
+                                           float lbeta, float inv_lbeta) {
+  const float sig = __frcp_rn(1.0f + exp2f(-1.4426950408889634f * g));
+  const float sg = (beta * tanh_fast(g * inv_beta)) * sig;
+  const float bu = lbeta * tanh_fast(u * inv_lbeta);
+  return sg * bu;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -317,8 +317,21 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
   }
 }
 
+// 8 bf16 -> 8 f16 (exact for magnitudes in f16's normal range)
+__device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    const __half2 h = __floats2half2_rn(f.x, f.y);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // Kernel 4: row gather, one warp per output row, 16-byte vectors.
-//   out[p, :] = token_idx[p] >= 0 ? x[token_idx[p], :] : 0
+//   out[p, :] = token_idx[p] >= 0 ? x[token_idx[p], :] : 0      (CONVERT: bf16 -> f16)
+template <bool CONVERT>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restrict__ x,
                                                           const int32_t* __restrict__ token_idx,
                                                           uint4* __restrict__ out, int64_t rows,
@@ -326,6 +339,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  auto cv = [](uint4 v) { return CONVERT ? bf16x8_to_f16x8(v) : v; };
   for (int64_t p = warp; p < rows; p += nwarps) {
     const int t = token_idx[p];
     uint4* dst = out + p * vec_per_row;
@@ -335,12 +349,12 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
       for (; v + 96 < vec_per_row; v += 128) {
         const uint4 a = __ldg(src + v), b = __ldg(src + v + 32), c = __ldg(src + v + 64),
                     d = __ldg(src + v + 96);
-        dst[v] = a;
-        dst[v + 32] = b;
-        dst[v + 64] = c;
-        dst[v + 96] = d;
+        dst[v] = cv(a);
+        dst[v + 32] = cv(b);
+        dst[v + 64] = cv(c);
+        dst[v + 96] = cv(d);
       }
-      for (; v < vec_per_row; v += 32) dst[v] = __ldg(src + v);
+      for (; v < vec_per_row; v += 32) dst[v] = cv(__ldg(src + v));
     } else {
       for (int v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
     }
@@ -398,16 +412,22 @@ int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64
 }
 
 int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
-                int64_t row_bytes, cudaStream_t stream) {
+                int64_t row_bytes, int convert, cudaStream_t stream) {
   if (rows < 0 || row_bytes <= 0 || row_bytes % 16 != 0) return kBadShape;
+  if (convert != 0 && convert != 1) return kBadShape;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return kUnsupported;
   if (rows == 0) return kOk;
   const int threads = 256;
   const int64_t want = (rows * 32 + threads - 1) / threads;
   const int blocks = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms(current_device())) * 16));
-  gather_rows_kernel<<<blocks, threads, 0, stream>>>(static_cast<const uint4*>(x), token_idx,
-                                                     static_cast<uint4*>(out), rows,
-                                                     static_cast<int>(row_bytes / 16), x_rows);
+  if (convert)
+    gather_rows_kernel<true><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint4*>(x), token_idx, static_cast<uint4*>(out), rows,
+        static_cast<int>(row_bytes / 16), x_rows);
+  else
+    gather_rows_kernel<false><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint4*>(x), token_idx, static_cast<uint4*>(out), rows,
+        static_cast<int>(row_bytes / 16), x_rows);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
@@ -480,11 +500,114 @@ __global__ void __launch_bounds__(256) combine_rmsnorm_kernel(
   }
 }
 
+// bf16 fast path: one block per token, each thread owns CH chunks of 8
+// consecutive columns (16-byte loads and stores), accumulates the k slot rows
+// in f32 registers in slot order (same arithmetic as the generic kernel), and
+// the RMS statistic is a block reduction of the bf16-rounded routed values.
+template <int CH>
+__global__ void __launch_bounds__(256) combine_rmsnorm_bf16_vec_kernel(
+    const __nv_bfloat16* __restrict__ expert_out, const int32_t* __restrict__ slot_pos,
+    const float* __restrict__ topk_w, const __nv_bfloat16* __restrict__ norm_scale, int k, int L,
+    float eps, __nv_bfloat16* __restrict__ routed_out, __nv_bfloat16* __restrict__ normed_out) {
+  __shared__ float red[8];
+  const int t = blockIdx.x;
+  const int nchunk = L / 8;
+  float acc[CH][8];
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[c][e] = 0.f;
+  for (int s = 0; s < k; ++s) {
+    const int p = __ldg(slot_pos + static_cast<int64_t>(t) * k + s);
+    const float w = __ldg(topk_w + static_cast<int64_t>(t) * k + s);
+    if (p < 0) continue;
+    const uint4* row = reinterpret_cast<const uint4*>(expert_out + static_cast<int64_t>(p) * L);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const int ch = threadIdx.x + c * 256;
+      if (ch < nchunk) {
+        const uint4 v = __ldg(row + ch);
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wv[e]));
+          acc[c][2 * e] = __fadd_rn(acc[c][2 * e], __fmul_rn(f.x, w));
+          acc[c][2 * e + 1] = __fadd_rn(acc[c][2 * e + 1], __fmul_rn(f.y, w));
+        }
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int ch = threadIdx.x + c * 256;
+    if (ch < nchunk) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc[c][e] = bf16_round_f(acc[c][e]);
+        ss += acc[c][e] * acc[c][e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pk[e] = pack_bf16x2(acc[c][2 * e], acc[c][2 * e + 1]);
+      if (routed_out)
+        reinterpret_cast<uint4*>(routed_out + static_cast<int64_t>(t) * L)[ch] =
+            make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = 1.0f / sqrtf(tot / static_cast<float>(L) + eps);
+  if (normed_out == nullptr) return;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int ch = threadIdx.x + c * 256;
+    if (ch < nchunk) {
+      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(norm_scale) + ch);
+      const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 sc = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sw[e]));
+        const float n0 = bf16_round_f(acc[c][2 * e] * inv) * sc.x;
+        const float n1 = bf16_round_f(acc[c][2 * e + 1] * inv) * sc.y;
+        pk[e] = pack_bf16x2(n0, n1);
+      }
+      reinterpret_cast<uint4*>(normed_out + static_cast<int64_t>(t) * L)[ch] =
+          make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  }
+}
+
 int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
                     const void* norm_scale, int64_t T, int64_t k, int64_t L, float eps, int bf16,
                     void* routed_out, void* normed_out, cudaStream_t stream) {
   if (T < 0 || k <= 0 || L <= 0 || L > 12288) return kBadShape;  // L f32 values in 48 KB smem
   if (T == 0) return kOk;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(expert_out) |
+                         reinterpret_cast<uintptr_t>(norm_scale) |
+                         reinterpret_cast<uintptr_t>(routed_out) |
+                         reinterpret_cast<uintptr_t>(normed_out)) & 15) == 0;
+  if (bf16 && aligned && L % 8 == 0 && L <= 8 * 256 * 4) {
+    const int ch = static_cast<int>((L / 8 + 255) / 256);
+    auto eo = static_cast<const __nv_bfloat16*>(expert_out);
+    auto ns = static_cast<const __nv_bfloat16*>(norm_scale);
+    auto ro = static_cast<__nv_bfloat16*>(routed_out);
+    auto no = static_cast<__nv_bfloat16*>(normed_out);
+    const int grid = static_cast<int>(T);
+    if (ch == 1)
+      combine_rmsnorm_bf16_vec_kernel<1><<<grid, 256, 0, stream>>>(eo, slot_pos, topk_w, ns, (int)k, (int)L, eps, ro, no);
+    else if (ch == 2)
+      combine_rmsnorm_bf16_vec_kernel<2><<<grid, 256, 0, stream>>>(eo, slot_pos, topk_w, ns, (int)k, (int)L, eps, ro, no);
+    else
+      combine_rmsnorm_bf16_vec_kernel<4><<<grid, 256, 0, stream>>>(eo, slot_pos, topk_w, ns, (int)k, (int)L, eps, ro, no);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  }
   const size_t sh = static_cast<size_t>(L) * sizeof(float);
   if (bf16)
     combine_rmsnorm_kernel<true><<<static_cast<int>(T), 256, sh, stream>>>(
@@ -625,8 +748,7 @@ __global__ void situ_kernel(const void* __restrict__ gate, const void* __restric
       g = static_cast<const float*>(gate)[r * ld_in + c];
       u = static_cast<const float*>(up)[r * ld_in + c];
     }
-    const float sig = 1.0f / (1.0f + expf(-g));
-    const float v = ((beta * tanhf(g / beta)) * sig) * (lbeta * tanhf(u / lbeta));
+    const float v = situ_fast(g, u, beta, 1.0f / beta, lbeta, 1.0f / lbeta);
     if (BF16_IO) static_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
     else static_cast<float*>(out)[i] = v;
   }

@@ -60,6 +60,13 @@ class GpuBackend:
   def gather(self, x, index):
     return ops.gather_rows(x, index)
 
+  def gather_send(self, x, index):
+    """Rows to send: f16 when the MXFP4 f16-operand kernel will consume them."""
+    pw = self.pw
+    f16 = (pw.expert_gu_mx is not None and pw.expert_gu_mx.f16_operand_ok and
+           pw.expert_down_mx.f16_operand_ok)
+    return ops.gather_rows(x, index, to_f16=f16)
+
   def reorder(self, recv_counts, world, n_local, rows):
     dev = recv_counts.device
     em = torch.empty(max(rows, 1), dtype=torch.int32, device=dev)
@@ -74,7 +81,8 @@ class GpuBackend:
     c, pw = self.cfg, self.pw
     b, lb = c.activation_situ_beta, c.activation_situ_linear_beta
     if pw.expert_gu_mx is not None:
-      act = ops.mxfp4_fused_gateup_situ(xe, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb)
+      act = ops.mxfp4_fused_gateup_situ(xe, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb,
+                                        out_dtype=xe.dtype)
       return ops.mxfp4_ragged_dot(act, pw.expert_down_mx, gs_local)
     act = ops.fused_gateup_situ(xe, pw.expert_gu, gs_local, beta=b, linear_beta=lb,
                                 rhs_layout="gnk")
@@ -109,7 +117,7 @@ def ep_forward(h: torch.Tensor, backend, cfg: LatentMoEConfig, group=None,
   idx, w = backend.route(h)
   x = backend.down(h)
   token_idx, slot_pos, group_sizes = backend.dispatch(idx, w)
-  send = backend.gather(x, token_idx)  # destination-rank-major, expert-sorted
+  send = backend.gather_send(x, token_idx)  # destination-rank-major, expert-sorted
   recv_counts = torch.empty_like(group_sizes)
   dist.all_to_all_single(recv_counts, group_sizes, group=group)
   counts = torch.cat([group_sizes, recv_counts]).cpu().numpy().astype(np.int64)

@@ -233,17 +233,16 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                                      activation=router_activation)
   x = _dense(h, pw.down)
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
-  sorted_tokens = ops.gather_rows(x, d.token_idx)
   beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
   if pw.expert_gu_mx is not None:
-    act = ops.mxfp4_fused_gateup_situ(sorted_tokens, pw.expert_gu_mx, d.group_sizes, beta=beta,
-                                      linear_beta=lbeta, round_gate_up=True)
-    down = ops.mxfp4_ragged_dot(act, pw.expert_down_mx, d.group_sizes)
+    act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c)
   elif pw.dtype == torch.bfloat16:
+    sorted_tokens = ops.gather_rows(x, d.token_idx)
     act = ops.fused_gateup_situ(sorted_tokens, pw.expert_gu, d.group_sizes, beta=beta,
                                 linear_beta=lbeta, round_gate_up=True, rhs_layout="gnk")
     down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
   else:
+    sorted_tokens = ops.gather_rows(x, d.token_idx)
     gate = ops.ragged_dot(sorted_tokens, pw.expert_gate, d.group_sizes, rhs_layout="gnk")
     up = ops.ragged_dot(sorted_tokens, pw.expert_up, d.group_sizes, rhs_layout="gnk")
     act = ops.situ_and_mul(gate, up, beta, lbeta)
@@ -265,6 +264,21 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                  slot_pos=d.slot_pos)
     return final, inter
   return final
+
+
+def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMoEConfig):
+  """Routed-expert FFN on MXFP4 weights: gather, fused gate/up + SiTU-GLU,
+  down.  When every scale byte allows it, the gathered rows and the
+  activation travel as f16 (the same bf16 values, exactly) and the GEMMs use
+  the f16-operand kernel; otherwise the bf16 operand kernel.
+  Returns (activation, down output bf16)."""
+  f16 = pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok
+  rows = ops.gather_rows(x, token_idx, to_f16=f16)
+  act = ops.mxfp4_fused_gateup_situ(rows, pw.expert_gu_mx, group_sizes,
+                                    beta=c.activation_situ_beta,
+                                    linear_beta=c.activation_situ_linear_beta, round_gate_up=True,
+                                    out_dtype=torch.float16 if f16 else torch.bfloat16)
+  return act, ops.mxfp4_ragged_dot(act, pw.expert_down_mx, group_sizes)
 
 
 def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None):

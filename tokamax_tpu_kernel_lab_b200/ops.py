@@ -176,46 +176,69 @@ class MXFP4Weights:
 
   packed: torch.Tensor
   scale: torch.Tensor
+  _f16_ok: bool | None = None
 
   @property
   def shape(self):
     g, n, kh = self.packed.shape
     return g, n, kh * 2
 
+  @property
+  def f16_operand_ok(self) -> bool:
+    """True when every scale byte lies in [104, 140], so the f16-operand
+    kernel (hardware e2m1 -> f16 expansion) represents every weight exactly.
+    Checked once per weight set (weights are static) and cached."""
+    if self._f16_ok is None:
+      lo, hi = torch.aminmax(self.scale)
+      self._f16_ok = bool(int(lo) >= 104 and int(hi) <= 140)
+    return self._f16_ok
+
 
 def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tensor, *,
                      preferred_element_type: torch.dtype | None = None,
                      out: torch.Tensor | None = None) -> torch.Tensor:
-  """lhs (M, K) bf16 @ dequant(w[g])^T per group -> (M, N); the weights stay
-  packed in HBM and are expanded tile by tile in shared memory."""
+  """lhs (M, K) @ dequant(w[g])^T per group -> (M, N); the weights stay
+  packed in HBM and are expanded tile by tile in shared memory.  lhs is bf16,
+  or f16 carrying bf16 values (the f16-operand kernel; needs
+  w.f16_operand_ok)."""
   _need_cuda(lhs, w.packed, w.scale, group_sizes)
   g, n, k = w.shape
   m = lhs.shape[0]
   if lhs.shape[1] != k or w.scale.shape != (g, n, k // 32):
     raise ValueError("MXFP4 shape mismatch")
+  lhs_f16 = lhs.dtype == torch.float16
+  if lhs_f16 and not w.f16_operand_ok:
+    raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
   out_dtype = preferred_element_type or torch.bfloat16
   res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
   _native.call("lmoe_mxfp4_ragged_dot", _ptr(lhs.contiguous()), _ptr(w.packed), _ptr(w.scale),
                _ptr(group_sizes.to(torch.int32).contiguous()), _ptr(res), m, k, n, g,
-               int(out_dtype == torch.float32), _ptr(device_status(lhs.device)), _stream())
+               int(lhs_f16), int(out_dtype == torch.float32), _ptr(device_status(lhs.device)),
+               _stream())
   return res
 
 
 def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
                             group_sizes: torch.Tensor | None, *, beta: float = 4.0,
                             linear_beta: float = 25.0, round_gate_up: bool = True,
+                            out_dtype: torch.dtype = torch.bfloat16,
                             out: torch.Tensor | None = None) -> torch.Tensor:
-  """SiTU-GLU of one grouped matmul against MXFP4 [gate rows | up rows]."""
+  """SiTU-GLU of one grouped matmul against MXFP4 [gate rows | up rows].
+  lhs bf16, or f16 carrying bf16 values; out_dtype=torch.float16 stores the
+  bf16-rounded activation as f16 (the lhs of an f16 down-projection)."""
   _need_cuda(lhs, w_gateup.packed, w_gateup.scale, group_sizes)
   g, two_i, k = w_gateup.shape
   inter = two_i // 2
   m = lhs.shape[0]
+  lhs_f16 = lhs.dtype == torch.float16
+  if lhs_f16 and not w_gateup.f16_operand_ok:
+    raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
   gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
-  res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
+  res = out if out is not None else torch.empty(m, inter, dtype=out_dtype, device=lhs.device)
   _native.call("lmoe_mxfp4_gateup_situ", _ptr(lhs.contiguous()), _ptr(w_gateup.packed),
                _ptr(w_gateup.scale), _ptr(gs), _ptr(res), m, k, inter, g, float(beta),
-               float(linear_beta), int(round_gate_up), _ptr(device_status(lhs.device)),
-               _stream())
+               float(linear_beta), int(round_gate_up), int(lhs_f16),
+               int(res.dtype == torch.float16), _ptr(device_status(lhs.device)), _stream())
   return res
 
 
@@ -333,14 +356,19 @@ def dispatch(topk_idx: torch.Tensor, topk_weight: torch.Tensor | None, num_local
   return res
 
 
-def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | None = None):
-  """out[p] = x[token_idx[p]] (zero where token_idx < 0)."""
+def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | None = None,
+                to_f16: bool = False):
+  """out[p] = x[token_idx[p]] (zero where token_idx < 0); to_f16 converts bf16
+  rows to f16 on the way (exact in f16's normal range)."""
   _need_cuda(x, token_idx)
   x = x.contiguous()
   rows = token_idx.shape[0]
-  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=x.dtype, device=x.device)
+  if to_f16 and x.dtype != torch.bfloat16:
+    raise ValueError("to_f16 converts bf16 rows")
+  dt = torch.float16 if to_f16 else x.dtype
+  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=dt, device=x.device)
   _native.call("lmoe_gather_rows", _ptr(x), x.shape[0], _ptr(token_idx.to(torch.int32)),
-               _ptr(res), rows, x.shape[1] * x.element_size(), _stream())
+               _ptr(res), rows, x.shape[1] * x.element_size(), int(to_f16), _stream())
   return res
 
 
