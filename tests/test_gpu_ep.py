@@ -1,0 +1,69 @@
+"""Expert parallelism on real GPUs (NCCL all-to-all): the concatenated
+per-rank outputs must equal the single-GPU forward of all tokens bit for bit.
+Needs at least 2 GPUs; skipped otherwise."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+  with socket.socket() as s:
+    s.bind(("127.0.0.1", 0))
+    return s.getsockname()[1]
+
+
+def _cfg(lm):
+  return lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+
+
+def _worker(rank, world, port, results):
+  import torch.distributed as dist
+
+  import tokamax_tpu_kernel_lab_b200 as lm
+  from tokamax_tpu_kernel_lab_b200.expert_parallel import EPStats, GpuBackend, ep_forward
+
+  os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+  torch.cuda.set_device(rank)
+  dev = torch.device("cuda", rank)
+  dist.init_process_group("nccl", rank=rank, world_size=world,
+                          timeout=datetime.timedelta(seconds=60), device_id=dev)
+  try:
+    cfg = _cfg(lm)
+    n_local = cfg.num_experts // world
+    pw = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5,
+                                expert_start=rank * n_local, num_local_experts=n_local)
+    gen = torch.Generator(device=dev).manual_seed(21)
+    h = torch.randn(512, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
+    t = h.shape[0] // world
+    stats = EPStats([], [])
+    out = ep_forward(h[rank * t:(rank + 1) * t].contiguous(), GpuBackend(pw, cfg), cfg,
+                     stats=stats)
+    torch.cuda.synchronize()
+    lm.check_device_status()
+    results[rank] = (out.cpu(), stats.send_rows, stats.recv_rows)
+    if rank == 0:
+      full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
+      results["ref"] = lm.latent_moe_forward(h, full, cfg).cpu()
+    dist.barrier()
+  finally:
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_forward_bit_exact_vs_single_gpu(world):
+  if torch.cuda.device_count() < world:
+    pytest.skip(f"needs {world} GPUs")
+  import torch.multiprocessing as mp
+  mgr = mp.get_context("spawn").Manager()
+  results = mgr.dict()
+  mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+  got = torch.cat([results[r][0] for r in range(world)])
+  assert torch.equal(got, results["ref"])
+  assert sum(sum(results[r][1]) for r in range(world)) == 512 * 8

@@ -82,17 +82,24 @@ struct GemmArgs {
   int out_f16;  // EPI_BF16 / EPI_SITU: store the bf16-rounded value as f16
 };
 
+// Shared-memory pipeline.  bf16 B: STAGES load stages of [A | B].  MXFP4 B:
+// STAGES load stages of [A | packed B] (24 KB, so the ring is deep enough to
+// hide TMA latency) and a separate ring of kDStages expanded bf16/f16 B
+// tiles written by the dequant warps.
 template <int BN, int STAGES, int BF, int EPI>
 struct GemmCfg {
   static constexpr int kThreads = is_mx(BF) ? 448 : 192;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kPackedBytes = is_mx(BF) ? BN * (kBK / 2) : 0;
-  static constexpr int kStageBytes = kABytes + kBBytes + kPackedBytes;
+  static constexpr int kStageBytes = kABytes + (is_mx(BF) ? kPackedBytes : kBBytes);
+  static constexpr int kDStages = is_mx(BF) ? 2 : 0;
+  static constexpr int kDAlloc = kDStages > 0 ? kDStages : 1;  // barrier slots
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kThreads * 4;
-  static constexpr int kBarBytes = 8 * (3 * STAGES + 5) + 16;
-  static constexpr size_t kSmem = 1024 + size_t(STAGES) * kStageBytes + kSchedBytes + kBarBytes;
+  static constexpr int kBarBytes = 8 * (2 * STAGES + 2 * kDAlloc + 5) + 16;
+  static constexpr size_t kSmem = 1024 + size_t(STAGES) * kStageBytes +
+                                  size_t(kDStages) * kBBytes + kSchedBytes + kBarBytes;
   static_assert(BN % 128 == 0 && BN <= 256, "BN");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for SW128");
@@ -269,15 +276,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* stages = smem;
-  int32_t* row_off = reinterpret_cast<int32_t*>(smem + STAGES * C::kStageBytes);
+  uint8_t* dstages = smem + STAGES * C::kStageBytes;  // expanded B ring (MXFP4)
+  int32_t* row_off = reinterpret_cast<int32_t*>(dstages + C::kDStages * C::kBBytes);
   int32_t* tile_start = row_off + (kMaxGroups + 1);
   int32_t* scan_rows = tile_start + (kMaxGroups + 1);
   int32_t* scan_tiles = scan_rows + C::kThreads;
   uint64_t* bars = reinterpret_cast<uint64_t*>(scan_tiles + C::kThreads);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
-  uint64_t* bready = bars + 2 * STAGES;
-  uint64_t* tfull = bars + 3 * STAGES;
+  uint64_t* bready = bars + 2 * STAGES;       // expanded B tile ready (dequant -> MMA)
+  uint64_t* bempty = bready + C::kDAlloc;     // expanded B tile consumed (MMA -> dequant)
+  uint64_t* tfull = bempty + C::kDAlloc;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -295,7 +304,10 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(smem_u32(full + s), 1);
       mbar_init(smem_u32(empty + s), 1);
+    }
+    for (int s = 0; s < C::kDAlloc; ++s) {
       mbar_init(smem_u32(bready + s), 8);  // one arrival per dequant warp
+      mbar_init(smem_u32(bempty + s), 1);  // UMMA commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(tfull + b), 1);
@@ -331,8 +343,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           const uint32_t fb = smem_u32(full + stage);
           mbar_arrive_expect_tx(fb, C::kABytes + (kMx ? C::kPackedBytes : C::kBBytes));
           const uint32_t a_dst = smem_u32(stages + stage * C::kStageBytes);
-          const uint32_t b_dst = a_dst + C::kABytes;
-          const uint32_t p_dst = b_dst + C::kBBytes;
+          const uint32_t b_dst = a_dst + C::kABytes;  // bf16 B, or the packed codes (MXFP4)
+          const uint32_t p_dst = b_dst;
           tma_load_2d(a_dst, &tmA, fb, kb * kBK, tc.row0);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -367,7 +379,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = (BF == B_MXFP4F16) ? idesc_f16_f32(kBM, BN, false)
                                                     : idesc_bf16_f32(kBM, BN, BF == B_NMAJOR);
-      uint32_t stage = 0, phase = 0;
+      uint32_t stage = 0, phase = 0, dstage = 0, dphase = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
@@ -379,13 +391,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status) ||
-              (kMx && !mbar_wait(smem_u32(bready + stage), phase, abort_flag, args.status))) {
+              (kMx && !mbar_wait(smem_u32(bready + dstage), dphase, abort_flag, args.status))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(stages + stage * C::kStageBytes);
-          const uint32_t b_addr = a_addr + C::kABytes;
+          const uint32_t b_addr = kMx ? smem_u32(dstages + dstage * C::kBBytes) : a_addr + C::kABytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
@@ -398,6 +410,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
+          }
+          if (kMx) {
+            umma_commit(smem_u32(bempty + dstage));
+            if (++dstage == C::kDAlloc) {
+              dstage = 0;
+              dphase ^= 1u;
+            }
           }
         }
         if (!ok) break;
@@ -535,26 +554,29 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     const int r = threadIdx.x - 192;
     const int h = r / (BN / 2);
     const int kgroups = args.K / 32;
-    uint32_t stage = 0, phase = 0;
+    uint32_t stage = 0, phase = 0, dstage = 0, dphase = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
       const TileCoord tc = decode_tile(tile_start, row_off, G, args.n_tiles, t);
       const int n_row = b_half_base<BN, EPI>(args, tc.n_tile, h) + (r % (BN / 2));
       const bool row_in = n_row < args.n_weight;
-      const uint8_t* srow = args.scales + (static_cast<int64_t>(tc.g) * args.n_weight + n_row) * kgroups;
+      const uint16_t* srow = reinterpret_cast<const uint16_t*>(
+          args.scales + (static_cast<int64_t>(tc.g) * args.n_weight + n_row) * kgroups);
+      // scale bytes of this row's two 32-element blocks, fetched one k step ahead
+      uint32_t s_next = row_in ? __ldg(srow) : 0x7F7Fu;
       for (int kb = 0; kb < num_kb; ++kb) {
-        // scale bytes for this row's two 32-element blocks (read before the wait)
-        uint32_t s01 = 0x7F7Fu;
-        if (row_in) s01 = __ldg(reinterpret_cast<const uint16_t*>(srow + kb * 2));
-        if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status)) {
+        const uint32_t s01 = s_next;
+        if (kb + 1 < num_kb) s_next = row_in ? __ldg(srow + kb + 1) : 0x7F7Fu;
+        if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status) ||
+            !mbar_wait(smem_u32(bempty + dstage), dphase ^ 1u, abort_flag, args.status)) {
           ok = false;
           break;
         }
-        uint8_t* st = stages + stage * C::kStageBytes;
-        const uint4* prow = reinterpret_cast<const uint4*>(st + C::kABytes + C::kBBytes + r * (kBK / 2));
+        const uint8_t* st = stages + stage * C::kStageBytes;
+        const uint4* prow = reinterpret_cast<const uint4*>(st + C::kABytes + r * (kBK / 2));
         const uint4 p0 = prow[0], p1 = prow[1];
         const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        uint8_t* brow = st + C::kABytes + r * 128;
+        uint8_t* brow = dstages + dstage * C::kBBytes + r * 128;
         if (BF == B_MXFP4F16) {
           const uint32_t b0 = e8m0_to_f16_bits(s01 & 0xFFu), b1 = e8m0_to_f16_bits(s01 >> 8);
           const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
@@ -575,10 +597,14 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(bready + stage));
+        if (lane == 0) mbar_arrive(smem_u32(bready + dstage));
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
+        }
+        if (++dstage == C::kDAlloc) {
+          dstage = 0;
+          dphase ^= 1u;
         }
       }
     }
@@ -621,7 +647,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
 }
 
 constexpr int kStagesBf16 = 4;
-constexpr int kStagesMx = 3;
+constexpr int kStagesMx = 5;
 
 template <int EPI>
 int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
