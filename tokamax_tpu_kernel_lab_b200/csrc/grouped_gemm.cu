@@ -562,11 +562,19 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
       const bool row_in = n_row < args.n_weight;
       const uint16_t* srow = reinterpret_cast<const uint16_t*>(
           args.scales + (static_cast<int64_t>(tc.g) * args.n_weight + n_row) * kgroups);
-      // scale bytes of this row's two 32-element blocks, fetched one k step ahead
-      uint32_t s_next = row_in ? __ldg(srow) : 0x7F7Fu;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const uint32_t s01 = s_next;
-        if (kb + 1 < num_kb) s_next = row_in ? __ldg(srow + kb + 1) : 0x7F7Fu;
+      // scale bytes of this row's two 32-element blocks, fetched kPrefetch k steps
+      // ahead (a global load outlives several 512-cycle MMA steps)
+      constexpr int kPrefetch = 4;
+      uint32_t sq[kPrefetch];
+#pragma unroll
+      for (int j = 0; j < kPrefetch; ++j) sq[j] = (row_in && j < num_kb) ? __ldg(srow + j) : 0x7F7Fu;
+      for (int kb0 = 0; kb0 < num_kb && ok; kb0 += kPrefetch)
+#pragma unroll
+      for (int j = 0; j < kPrefetch; ++j) {
+        const int kb = kb0 + j;
+        if (kb >= num_kb) break;
+        const uint32_t s01 = sq[j];
+        if (kb + kPrefetch < num_kb) sq[j] = row_in ? __ldg(srow + kb + kPrefetch) : 0x7F7Fu;
         if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status) ||
             !mbar_wait(smem_u32(bempty + dstage), dphase ^ 1u, abort_flag, args.status)) {
           ok = false;
