@@ -334,21 +334,20 @@ def main():
          "ms_per_step": ms_e2e}
 
   # ---------------------------------------------------------------- dominant kernel
-  # the MXFP4 fused gate/up grouped GEMM on this rank's routed rows, timed alone
+  # the MXFP4 fused gate/up grouped GEMM on this rank's routed rows (already
+  # gathered into expert order, as the forward feeds it), timed alone
+  rows = t_local * cfg.top_k
   if world == 1:
     _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True)
     gs = inter["group_sizes"]
-    rows = t_local * cfg.top_k
-    xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(torch.bfloat16)
+    xs = ops.gather_rows(inter["latent_projection"], inter["token_idx"])
   else:
-    # the expert-major rows this rank receives: use the local share of the routed rows
-    rows = t_local * cfg.top_k
+    # stand-in for the expert-major rows this rank receives: the local share of
+    # the routed rows spread evenly over the local experts
     gs = torch.full((n_local,), rows // n_local, dtype=torch.int32, device=dev)
     gs[0] += rows - int(gs.sum().item())
-    xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(torch.bfloat16)
-  f16 = pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok
-  if f16:  # the forward feeds this kernel f16-carried bf16 rows
-    xs = xs.to(torch.float16)
+    xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(
+        torch.float16 if lm.latent_moe.mxfp4_f16_path(pw) else torch.bfloat16)
   act = torch.empty(rows, cfg.intermediate_size, dtype=xs.dtype, device=dev)
   for _ in range(2):
     ops.mxfp4_fused_gateup_situ(xs, pw.expert_gu_mx, gs, out=act)

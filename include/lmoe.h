@@ -74,6 +74,8 @@ LMOE_API int lmoe_gemm_f32(const float* lhs, const float* rhs, const float* adde
 /* Dense bf16 GEMM with a fused bf16 residual add:
  *   out = bf16(bf16(lhs @ rhs) + addend)       (addend may equal nothing: pass NULL
  *   for a plain bf16(lhs @ rhs)).  rhs layout as above with g = 1.
+ *   out_f32: 0 = bf16 out, 1 = f32 out, 2 = the bf16-rounded result stored as
+ *   f16 (the lhs form of the f16-operand MXFP4 kernels); 1 and 2 need addend NULL.
  * Replaces `up + shared_out` after `normed @ up_proj` / `... @ shared_down`
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:422-435). */
 LMOE_API int lmoe_gemm_bf16(const void* lhs, const void* rhs, const void* addend, void* out, int64_t m,
@@ -85,13 +87,18 @@ LMOE_API int lmoe_gemm_bf16(const void* lhs, const void* rhs, const void* addend
  *   (g, k, 2*intermediate) [LMOE_RHS_GKN] or (g, 2*intermediate, k) [LMOE_RHS_GNK].
  * round_gate_up = 1 rounds gate/up to bf16 before the activation (the unfused
  * reference's convention); 0 applies it to the f32 accumulator (tokamax fuse_act).
+ * lhs_row_index (optional, device int32, m entries): the dispatch gather fused
+ * into the operand load -- logical row r is row lhs_row_index[r] of lhs, which
+ * then has lhs_src_rows rows (index -1 reads as zeros), so the sorted copy of
+ * the tokens is never materialised.  NULL: lhs is read directly (m rows).
  * Replaces PallasMosaicTpuV2RaggedDot()(..., fuse_gateup_activation="situ:b:lb")
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:610-723) and the
  * dense own kernel (05_ragged_dot_on_tpu/own_gateup_situ_pallas_kernel.py:79-199). */
 LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const int32_t* group_sizes,
                           void* out, int64_t m, int64_t k, int64_t intermediate,
                           int64_t num_groups, int rhs_layout, float beta, float linear_beta,
-                          int round_gate_up, int32_t* dev_status, void* stream);
+                          int round_gate_up, const int32_t* lhs_row_index,
+                          int64_t lhs_src_rows, int32_t* dev_status, void* stream);
 
 /* Grouped matmul against MXFP4 weights: e2m1 codes (g, n, k/2) uint8, low nibble
  * = even k, and one E8M0 scale byte per 32-element k block (g, n, k/32) -- the
@@ -116,12 +123,14 @@ LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
  * (g, 2*intermediate, k/2) codes and (g, 2*intermediate, k/32) scales (the
  * checkpoint's w1 and w3 stacked).  group_sizes NULL = one dense group.
  * lhs_f16 as above; out_f16 = 1 stores the bf16-rounded activation as f16
- * (the lhs of a following lhs_f16 down-projection). */
+ * (the lhs of a following lhs_f16 down-projection); lhs_row_index /
+ * lhs_src_rows fuse the dispatch gather as in lmoe_gateup_situ_bf16. */
 LMOE_API int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed,
                                     const void* weight_scale, const int32_t* group_sizes,
                                     void* out, int64_t m, int64_t k, int64_t intermediate,
                                     int64_t num_groups, float beta, float linear_beta,
                                     int round_gate_up, int lhs_f16, int out_f16,
+                                    const int32_t* lhs_row_index, int64_t lhs_src_rows,
                                     int32_t* dev_status, void* stream);
 
 /* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).

@@ -75,6 +75,9 @@ class OracleBackend:
     sm[em] = np.arange(rows, dtype=np.int32)
     return torch.from_numpy(em), torch.from_numpy(sm), torch.from_numpy(cnt.sum(0).astype(np.int32))
 
+  def experts_indexed(self, src, index, gs_local):
+    return self.experts(self.gather(src, index), gs_local)
+
   def experts(self, xe, gs_local):
     c, w = self.cfg, self.w
     sl = slice(self.e0, self.e1)

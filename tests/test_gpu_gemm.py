@@ -173,3 +173,24 @@ def test_unsupported_shapes_raise(lm):
   with pytest.raises(NotImplementedError):
     lm.ragged_dot(lhs, rhs, torch.tensor([16], dtype=torch.int32, device="cuda"),
                   implementation="mosaic_tpu_v2")
+
+
+@pytest.mark.parametrize("layout", ["gkn", "gnk"])
+def test_fused_gateup_with_row_gather(lm, layout):
+  """The dispatch gather fused into the operand load (TMA tile::gather4):
+  logical row r = x[row_index[r]], index -1 = a zero row."""
+  rng = np.random.default_rng(13)
+  t, k, inter, g, m = 300, 256, 256, 4, 1000
+  x = O.bf16_round(_rand(rng, t, k))
+  idx = rng.integers(-1, t, m).astype(np.int32)
+  gs = rng.multinomial(m - 9, np.full(g, 1.0 / g)).astype(np.int32)
+  fused = O.bf16_round(_rand(rng, g, k, 2 * inter, scale=0.02))
+  rows = np.where(idx[:, None] >= 0, x[np.maximum(idx, 0)], 0).astype(np.float32)
+  ref = O.fused_gateup_situ(rows, fused, gs, inter, 4.0, 25.0, dtype="bf16", out_dtype="fp32")
+  w_dev = fused if layout == "gkn" else np.ascontiguousarray(fused.transpose(0, 2, 1))
+  out = lm.fused_gateup_situ(to_dev(x), to_dev(w_dev), torch.from_numpy(gs).cuda(),
+                             rhs_layout=layout, row_index=torch.from_numpy(idx).cuda())
+  direct = lm.fused_gateup_situ(to_dev(rows), to_dev(w_dev), torch.from_numpy(gs).cuda(),
+                                rhs_layout=layout)
+  assert torch.equal(out, direct)  # same rows, same bits
+  assert_bf16_close(ref, to_np(out), f"gather {layout}")

@@ -157,3 +157,24 @@ def test_mxfp4_layer_matches_oracle(lm):
                 np.sort(rinter["topk_indices"], -1), axis=1)
   assert same.mean() >= 0.99
   assert_bf16_close(ref[same], to_np(final)[same], "mxfp4 layer")
+
+
+@pytest.mark.parametrize("f16", [False, True])
+def test_mxfp4_gateup_with_row_gather(lm, f16):
+  rng = np.random.default_rng(14)
+  t, k, inter, g, m = 200, 512, 256, 3, 900
+  packed, scale = _mx(rng, g, 2 * inter, k, lo=120, hi=121)
+  x = O.bf16_round(rng.standard_normal((t, k), dtype=np.float32))
+  idx = rng.integers(-1, t, m).astype(np.int32)
+  gs = rng.multinomial(m - 5, np.full(g, 1.0 / g)).astype(np.int32)
+  rows = np.where(idx[:, None] >= 0, x[np.maximum(idx, 0)], 0).astype(np.float32)
+  dt = torch.float16 if f16 else torch.bfloat16
+  w = _dev_mx(lm, packed, scale)
+  out = lm.mxfp4_fused_gateup_situ(to_dev(x).to(dt), w, torch.from_numpy(gs).cuda(),
+                                   out_dtype=dt, row_index=torch.from_numpy(idx).cuda())
+  direct = lm.mxfp4_fused_gateup_situ(to_dev(rows).to(dt), w, torch.from_numpy(gs).cuda(),
+                                      out_dtype=dt)
+  assert torch.equal(out, direct)
+  ref = O.fused_gateup_situ(rows, O.LazyMXFP4Experts(packed, scale), gs, inter, 4.0, 25.0,
+                            dtype="bf16", out_dtype="fp32")
+  assert_bf16_close(ref, to_np(out), f"mxfp4 gather f16={f16}")

@@ -40,20 +40,24 @@ int lmoe_gemm_f32(const float* lhs, const float* rhs, const float* addend, float
 int lmoe_gemm_bf16(const void* lhs, const void* rhs, const void* addend, void* out, int64_t m,
                    int64_t k, int64_t n, int rhs_layout, int out_f32, int32_t* dev_status,
                    void* stream) {
-  if (addend != nullptr && out_f32) return LMOE_UNSUPPORTED;
-  const int epi = addend ? kEpiBf16Add : (out_f32 ? kEpiF32 : kEpiBf16);
+  // out_f32: 0 = bf16 out, 1 = f32 out, 2 = bf16-rounded values stored as f16
+  if (out_f32 < 0 || out_f32 > 2 || (addend != nullptr && out_f32 != 0)) return LMOE_UNSUPPORTED;
+  const int epi = addend ? kEpiBf16Add : (out_f32 == 1 ? kEpiF32 : kEpiBf16);
   return lmoe::grouped_gemm_bf16(lhs, rhs, nullptr, out, m, k, n, 1, rhs_layout, epi, addend, n,
-                                 0, 0.f, 0.f, 0, 0, dev_status, S(stream));
+                                 0, 0.f, 0.f, 0, 0, dev_status, S(stream), nullptr, 0,
+                                 out_f32 == 2 ? 1 : 0);
 }
 
 int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const int32_t* group_sizes,
                           void* out, int64_t m, int64_t k, int64_t intermediate,
                           int64_t num_groups, int rhs_layout, float beta, float linear_beta,
-                          int round_gate_up, int32_t* dev_status, void* stream) {
+                          int round_gate_up, const int32_t* lhs_row_index, int64_t lhs_src_rows,
+                          int32_t* dev_status, void* stream) {
   return lmoe::grouped_gemm_bf16(lhs, w_gateup, group_sizes, out, m, k, intermediate,
                                  group_sizes ? num_groups : 1, rhs_layout, kEpiSitu, nullptr, 0,
                                  intermediate, beta, linear_beta, round_gate_up,
-                                 group_sizes ? 1 : 0, dev_status, S(stream));
+                                 group_sizes ? 1 : 0, dev_status, S(stream), lhs_row_index,
+                                 lhs_src_rows);
 }
 
 int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed, const void* weight_scale,
@@ -69,12 +73,14 @@ int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed, const void
 int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed, const void* weight_scale,
                            const int32_t* group_sizes, void* out, int64_t m, int64_t k,
                            int64_t intermediate, int64_t num_groups, float beta, float linear_beta,
-                           int round_gate_up, int lhs_f16, int out_f16, int32_t* dev_status,
-                           void* stream) {
+                           int round_gate_up, int lhs_f16, int out_f16,
+                           const int32_t* lhs_row_index, int64_t lhs_src_rows,
+                           int32_t* dev_status, void* stream) {
   return lmoe::grouped_gemm_mxfp4(lhs, weight_packed, weight_scale, group_sizes, out, m, k,
                                   intermediate, group_sizes ? num_groups : 1, kEpiSitu,
                                   intermediate, beta, linear_beta, round_gate_up,
-                                  group_sizes ? 1 : 0, lhs_f16, out_f16, dev_status, S(stream));
+                                  group_sizes ? 1 : 0, lhs_f16, out_f16, dev_status, S(stream),
+                                  lhs_row_index, lhs_src_rows);
 }
 
 int lmoe_situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,

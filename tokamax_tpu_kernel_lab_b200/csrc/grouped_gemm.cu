@@ -80,6 +80,11 @@ struct GemmArgs {
   int round_gate_up;
   int zero_tail;
   int out_f16;  // EPI_BF16 / EPI_SITU: store the bf16-rounded value as f16
+  // Row gather of the A operand: logical row r of lhs is source row a_rows[r]
+  // of the tensor map (a_src_rows rows); -1 reads as zeros.  nullptr: A is
+  // read directly (row r of the map).
+  const int32_t* a_rows;
+  int a_src_rows;
 };
 
 // Shared-memory pipeline.  bf16 B: STAGES load stages of [A | B].  MXFP4 B:
@@ -330,22 +335,45 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // Direct A: lane 0 issues one 128-row box per stage.  Gathered A: every
+    // lane issues one tile::gather4 of 4 rows (lane i: tile rows 4i..4i+3),
+    // the row indices read once per tile.
+    const bool gather = args.a_rows != nullptr;
+    if (gather || lane == 0) {
       uint32_t stage = 0, phase = 0, issued = 0, last_parity = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const TileCoord tc = decode_tile(tile_start, row_off, G, args.n_tiles, t);
+        int32_t src[4] = {0, 0, 0, 0};
+        if (gather) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int row = tc.row0 + 4 * lane + j;
+            const int s = row < args.M ? __ldg(args.a_rows + row) : -1;
+            src[j] = (s < 0 || s >= args.a_src_rows) ? args.a_src_rows : s;  // past the end: zeros
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.status)) {
+          bool w = true;
+          if (lane == 0) w = mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.status);
+          if (gather) w = __shfl_sync(0xffffffffu, w ? 1 : 0, 0) != 0;
+          if (!w) {
             ok = false;
             break;
           }
           const uint32_t fb = smem_u32(full + stage);
-          mbar_arrive_expect_tx(fb, C::kABytes + (kMx ? C::kPackedBytes : C::kBBytes));
+          if (lane == 0) mbar_arrive_expect_tx(fb, C::kABytes + (kMx ? C::kPackedBytes : C::kBBytes));
           const uint32_t a_dst = smem_u32(stages + stage * C::kStageBytes);
           const uint32_t b_dst = a_dst + C::kABytes;  // bf16 B, or the packed codes (MXFP4)
           const uint32_t p_dst = b_dst;
-          tma_load_2d(a_dst, &tmA, fb, kb * kBK, tc.row0);
+          if (gather) {
+            __syncwarp();  // the expected byte count is registered before any copy lands
+            tma_gather4_2d(a_dst + lane * 4 * 128, &tmA, fb, kb * kBK, src[0], src[1], src[2],
+                           src[3]);
+          } else {
+            tma_load_2d(a_dst, &tmA, fb, kb * kBK, tc.row0);
+          }
+          if (lane == 0)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int nbase = b_half_base<BN, EPI>(args, tc.n_tile, h);
@@ -368,7 +396,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           }
         }
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         // abort: let every copy already issued land before the CTA retires
         for (int s = 0; s < STAGES; ++s)
           if (issued & (1u << s)) mbar_drain(smem_u32(full + s), (last_parity >> s) & 1u);
@@ -725,27 +753,41 @@ int max_tiles_of(const GemmArgs& a) {
   return static_cast<int>(std::min<int64_t>(t, 1 << 30));
 }
 
+// A operand map: a 128-row box over lhs (M, K), or, for a row gather, a
+// one-row box over the source rows (the tile::gather4 form).
+bool encode_a(CUtensorMap* ta, const void* lhs, int64_t M, int64_t K, const int32_t* a_rows,
+              int64_t a_src_rows) {
+  if (a_rows != nullptr)
+    return encode_tmap_bf16_2d(ta, lhs, static_cast<uint64_t>(K),
+                               static_cast<uint64_t>(a_src_rows), static_cast<uint64_t>(K) * 2,
+                               kBK, 1);
+  return encode_tmap_bf16_2d(ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                             static_cast<uint64_t>(K) * 2, kBK, kBM);
+}
+
 }  // namespace
 
 // rhs_layout: 0 = (G, K, N) ("gkn", N contiguous, the reference's layout);
 //             1 = (G, N, K) ("gnk", K contiguous, torch nn.Linear layout)
+// a_rows (optional, device): logical lhs row r = source row a_rows[r] of lhs,
+// which then has a_src_rows rows (-1 = zeros).
 int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
                       int64_t M, int64_t K, int64_t N_out, int64_t G, int rhs_layout, int epi,
                       const void* addend, int64_t ld_add, int64_t up_offset, float beta,
                       float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const int32_t* a_rows, int64_t a_src_rows,
+                      int out_f16) {
   if (rhs_layout != 0 && rhs_layout != 1) return kBadShape;
   int rc = common_checks(lhs, out, M, K, N_out, G, epi, addend, ld_add, up_offset);
   if (rc != kOk) return rc;
   if (reinterpret_cast<uintptr_t>(rhs) & 15) return kUnsupported;
+  if (a_rows != nullptr && (a_src_rows <= 0 || a_src_rows >= (1ll << 31))) return kBadShape;
   if (M == 0) return kOk;
   const bool b_mn = rhs_layout == 0;
   // width of the weight's N axis (the fused [gate|up] weight is 2I wide)
   const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
   CUtensorMap ta, tb;
-  if (!encode_tmap_bf16_2d(&ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
-                           static_cast<uint64_t>(K) * 2, kBK, kBM))
-    return kLaunchFailed;
+  if (!encode_a(&ta, lhs, M, K, a_rows, a_src_rows)) return kLaunchFailed;
   if (b_mn) {
     // dims {N, K, G}, box {64, 64, 1}
     if (!encode_tmap_bf16_3d(&tb, rhs, n_weight, K, G, n_weight * 2, n_weight * K * 2, 64, kBK))
@@ -755,8 +797,11 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
     if (!encode_tmap_bf16_3d(&tb, rhs, K, n_weight, G, K * 2, n_weight * K * 2, kBK, 128))
       return kLaunchFailed;
   }
-  const GemmArgs a = make_args(group_sizes, out, addend, ld_add, M, K, N_out, G, epi, up_offset,
-                               n_weight, beta, linear_beta, round_gate_up, zero_tail, status);
+  GemmArgs a = make_args(group_sizes, out, addend, ld_add, M, K, N_out, G, epi, up_offset,
+                         n_weight, beta, linear_beta, round_gate_up, zero_tail, status);
+  a.a_rows = a_rows;
+  a.a_src_rows = static_cast<int>(a_src_rows);
+  a.out_f16 = (epi == EPI_BF16 || epi == EPI_SITU) ? out_f16 : 0;
   return launch_epi(epi, b_mn ? B_NMAJOR : B_KMAJOR, ta, tb, a, max_tiles_of(a), stream);
 }
 
@@ -768,7 +813,8 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
                        const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N_out,
                        int64_t G, int epi, int64_t up_offset, float beta, float linear_beta,
                        int round_gate_up, int zero_tail, int lhs_f16, int out_f16,
-                       int32_t* status, cudaStream_t stream) {
+                       int32_t* status, cudaStream_t stream, const int32_t* a_rows,
+                       int64_t a_src_rows) {
   int rc = common_checks(lhs, out, M, K, N_out, G, epi, nullptr, 0, up_offset);
   if (rc != kOk) return rc;
   if (epi == EPI_BF16_ADD || (out_f16 && epi == EPI_F32)) return kUnsupported;
@@ -776,12 +822,11 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
   if (reinterpret_cast<uintptr_t>(packed) & 15 || scales == nullptr ||
       (reinterpret_cast<uintptr_t>(scales) & 1))
     return kUnsupported;
+  if (a_rows != nullptr && (a_src_rows <= 0 || a_src_rows >= (1ll << 31))) return kBadShape;
   if (M == 0) return kOk;
   const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
   CUtensorMap ta, tb;
-  if (!encode_tmap_bf16_2d(&ta, lhs, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
-                           static_cast<uint64_t>(K) * 2, kBK, kBM))
-    return kLaunchFailed;
+  if (!encode_a(&ta, lhs, M, K, a_rows, a_src_rows)) return kLaunchFailed;
   // dims {K/2 bytes, N, G}, box {32 bytes = 64 codes, 128 rows, 1}
   if (!encode_tmap_u8_3d(&tb, packed, K / 2, n_weight, G, K / 2, n_weight * (K / 2), kBK / 2, 128))
     return kLaunchFailed;
@@ -789,6 +834,8 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
                          beta, linear_beta, round_gate_up, zero_tail, status);
   a.scales = static_cast<const uint8_t*>(scales);
   a.out_f16 = out_f16;
+  a.a_rows = a_rows;
+  a.a_src_rows = static_cast<int>(a_src_rows);
   return launch_epi(epi, lhs_f16 ? B_MXFP4F16 : B_MXFP4, ta, tb, a, max_tiles_of(a), stream);
 }
 

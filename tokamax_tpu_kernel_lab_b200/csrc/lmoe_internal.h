@@ -26,13 +26,15 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
                       int64_t M, int64_t K, int64_t N_out, int64_t G, int rhs_layout, int epi,
                       const void* addend, int64_t ld_add, int64_t up_offset, float beta,
                       float linear_beta, int round_gate_up, int zero_tail, int32_t* status,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const int32_t* a_rows = nullptr,
+                      int64_t a_src_rows = 0, int out_f16 = 0);
 
 int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
                        const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N_out,
                        int64_t G, int epi, int64_t up_offset, float beta, float linear_beta,
                        int round_gate_up, int zero_tail, int lhs_f16, int out_f16,
-                       int32_t* status, cudaStream_t stream);
+                       int32_t* status, cudaStream_t stream, const int32_t* a_rows = nullptr,
+                       int64_t a_src_rows = 0);
 
 inline int current_device() {
   int d = 0;

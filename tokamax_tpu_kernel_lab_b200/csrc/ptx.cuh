@@ -130,6 +130,20 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// Four rows (r0..r3) of a 2D tensor map whose box is one row high, written
+// consecutively at dst (4 x box-row bytes), with the map's swizzle applied.
+// A row coordinate at or past the tensor's extent reads as zeros.
+__device__ __forceinline__ void tma_gather4_2d(uint32_t dst, const void* tmap, uint32_t bar,
+                                               int32_t c0, int32_t r0, int32_t r1, int32_t r2,
+                                               int32_t r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(r0), "r"(r1), "r"(r2),
+      "r"(r3)
+      : "memory");
+}
+
 // generic-proxy smem writes -> visible to the async proxy (UMMA operand reads)
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

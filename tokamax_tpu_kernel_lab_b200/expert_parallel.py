@@ -35,7 +35,7 @@ import torch
 import torch.distributed as dist
 
 from . import ops
-from .latent_moe import LatentMoEConfig, PreparedWeights, _dense
+from .latent_moe import LatentMoEConfig, PreparedWeights, _dense, mxfp4_f16_path
 
 
 class GpuBackend:
@@ -51,7 +51,8 @@ class GpuBackend:
                            routed_scaling_factor=c.routed_scaling_factor)
 
   def down(self, h):
-    return _dense(h, self.pw.down)
+    # f16 latent rows when the MXFP4 f16-operand kernels consume them
+    return _dense(h, self.pw.down, out_dtype=torch.float16 if mxfp4_f16_path(self.pw) else None)
 
   def dispatch(self, idx, w):
     d = ops.dispatch(idx, w, self.cfg.num_experts, want_order=False)
@@ -61,11 +62,8 @@ class GpuBackend:
     return ops.gather_rows(x, index)
 
   def gather_send(self, x, index):
-    """Rows to send: f16 when the MXFP4 f16-operand kernel will consume them."""
-    pw = self.pw
-    f16 = (pw.expert_gu_mx is not None and pw.expert_gu_mx.f16_operand_ok and
-           pw.expert_down_mx.f16_operand_ok)
-    return ops.gather_rows(x, index, to_f16=f16)
+    """Rows to send, in destination-rank-major expert order."""
+    return ops.gather_rows(x, index)
 
   def reorder(self, recv_counts, world, n_local, rows):
     dev = recv_counts.device
@@ -77,9 +75,11 @@ class GpuBackend:
                  sm.data_ptr(), gs.data_ptr(), ops._stream())
     return em[:rows], sm[:rows], gs
 
-  def experts(self, xe, gs_local):
+  def experts_indexed(self, src, index, gs_local):
+    """Expert FFN of rows src[index[p]] in expert-major order."""
     c, pw = self.cfg, self.pw
     b, lb = c.activation_situ_beta, c.activation_situ_linear_beta
+    xe = ops.gather_rows(src, index)
     if pw.expert_gu_mx is not None:
       act = ops.mxfp4_fused_gateup_situ(xe, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb,
                                         out_dtype=xe.dtype)
@@ -131,8 +131,7 @@ def ep_forward(h: torch.Tensor, backend, cfg: LatentMoEConfig, group=None,
                          group=group)
   em_src, sm_src, gs_local = backend.reorder(recv_counts.view(world, n_local), world, n_local,
                                              n_recv)
-  xe = backend.gather(recv, em_src)
-  ye = backend.experts(xe, gs_local)
+  ye = backend.experts_indexed(recv, em_src, gs_local)
   back_send = backend.gather(ye, sm_src)
   back = torch.empty(send.shape[0], L, dtype=ye.dtype, device=ye.device)
   dist.all_to_all_single(back, back_send, output_split_sizes=send_rows,

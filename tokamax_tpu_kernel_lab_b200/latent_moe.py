@@ -231,7 +231,7 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
                                      routed_scaling_factor=c.routed_scaling_factor,
                                      activation=router_activation)
-  x = _dense(h, pw.down)
+  x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw) else None)
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
   beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
   if pw.expert_gu_mx is not None:
@@ -261,28 +261,39 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                  latent_projection=x, sorted_token_indices=d.order, group_sizes=d.group_sizes,
                  situ_output=act, expert_down_output=down, routed_output_after_combine=routed,
                  normalized_output=normed, up_projection_output=upo, final_output=final,
-                 slot_pos=d.slot_pos)
+                 slot_pos=d.slot_pos, token_idx=d.token_idx)
     return final, inter
   return final
 
 
+def mxfp4_f16_path(pw: PreparedWeights) -> bool:
+  """True when the MXFP4 experts can run the f16-operand kernels (every scale
+  byte in their exact range); the latent activations then travel as f16
+  (the same bf16-rounded values)."""
+  return (pw.expert_gu_mx is not None and pw.expert_gu_mx.f16_operand_ok and
+          pw.expert_down_mx.f16_operand_ok)
+
+
 def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMoEConfig):
-  """Routed-expert FFN on MXFP4 weights: gather, fused gate/up + SiTU-GLU,
-  down.  When every scale byte allows it, the gathered rows and the
-  activation travel as f16 (the same bf16 values, exactly) and the GEMMs use
-  the f16-operand kernel; otherwise the bf16 operand kernel.
+  """Routed-expert FFN on MXFP4 weights: row gather into expert-sorted order,
+  fused gate/up + SiTU-GLU, down GEMM.  x is f16 on the f16-operand path (see
+  mxfp4_f16_path), bf16 otherwise.  (The gather can also run inside the
+  gate/up kernel's operand load, `row_index=`; at these sizes the one-row TMA
+  gathers feed the tensor cores ~2.5x slower than a separate gather kernel
+  plus contiguous tile loads, so the forward gathers first.)
   Returns (activation, down output bf16)."""
-  f16 = pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok
-  rows = ops.gather_rows(x, token_idx, to_f16=f16)
+  rows = ops.gather_rows(x, token_idx)
   act = ops.mxfp4_fused_gateup_situ(rows, pw.expert_gu_mx, group_sizes,
                                     beta=c.activation_situ_beta,
                                     linear_beta=c.activation_situ_linear_beta, round_gate_up=True,
-                                    out_dtype=torch.float16 if f16 else torch.bfloat16)
+                                    out_dtype=x.dtype)
   return act, ops.mxfp4_ragged_dot(act, pw.expert_down_mx, group_sizes)
 
 
-def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None):
-  """a @ W^T for W given (N, K); bf16 on the tensor cores, f32 on the CUDA cores."""
+def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None,
+           out_dtype: torch.dtype | None = None):
+  """a @ W^T for W given (N, K); bf16 on the tensor cores (out_dtype float16:
+  the bf16-rounded result stored as f16), f32 on the CUDA cores."""
   if a.dtype == torch.float32:
     from . import _native
     m, k = a.shape
@@ -292,7 +303,7 @@ def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = No
                  None if addend is None else addend.contiguous().data_ptr(), out.data_ptr(), m, k,
                  n, 1, ops.device_status(a.device).data_ptr(), ops._stream())
     return out
-  return ops.gemm(a, w_nk, addend=addend, rhs_layout="nk")
+  return ops.gemm(a, w_nk, addend=addend, rhs_layout="nk", out_dtype=out_dtype or torch.bfloat16)
 
 
 def latent_moe_forward_ragged_dot(hidden_states, weights, config, implementation=None):

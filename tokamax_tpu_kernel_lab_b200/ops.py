@@ -121,14 +121,17 @@ def gemm(lhs: torch.Tensor, rhs: torch.Tensor, *, addend: torch.Tensor | None = 
          rhs_layout: str = "nk", out_dtype: torch.dtype = torch.bfloat16,
          out: torch.Tensor | None = None) -> torch.Tensor:
   """Dense bf16 GEMM (one group of the tensor-core kernel):
-  out = bf16(bf16(lhs @ W) + addend) with W given as (N, K) ("nk") or (K, N) ("kn")."""
+  out = bf16(bf16(lhs @ W) + addend) with W given as (N, K) ("nk") or (K, N) ("kn").
+  out_dtype float32 keeps the f32 accumulator; float16 stores the bf16-rounded
+  result as f16."""
   _need_cuda(lhs, rhs, addend)
   layout = {"kn": 0, "nk": 1}[rhs_layout]
   m, k = lhs.shape
   n = rhs.shape[1] if layout == 0 else rhs.shape[0]
   res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
   _native.call("lmoe_gemm_bf16", _ptr(lhs), _ptr(rhs), _ptr(addend), _ptr(res), m, k, n, layout,
-               int(out_dtype == torch.float32), _ptr(device_status(lhs.device)), _stream())
+               code, _ptr(device_status(lhs.device)), _stream())
   return res
 
 
@@ -146,24 +149,30 @@ def prefuse_gateup_weights(expert_gate: torch.Tensor, expert_up: torch.Tensor,
 
 def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: torch.Tensor | None,
                       *, beta: float = 4.0, linear_beta: float = 25.0, round_gate_up: bool = True,
-                      rhs_layout: str = "gkn", out: torch.Tensor | None = None) -> torch.Tensor:
+                      rhs_layout: str = "gkn", out: torch.Tensor | None = None,
+                      row_index: torch.Tensor | None = None) -> torch.Tensor:
   """SiTU-GLU(lhs @ gate_g, lhs @ up_g) from ONE grouped matmul against the
   fused [gate | up] weight.  `group_sizes=None` means one dense group
-  (the shared expert).  Returns (M, I) bf16."""
-  _need_cuda(lhs, w_gateup, group_sizes)
+  (the shared expert).  With `row_index` (int32, one entry per logical row)
+  the dispatch gather happens inside the kernel's operand load: logical row r
+  is lhs[row_index[r]] (-1 = zeros).  Returns (M, I) bf16."""
+  _need_cuda(lhs, w_gateup, group_sizes, row_index)
   layout = {"gkn": 0, "gnk": 1}[rhs_layout]
   w = w_gateup if w_gateup.dim() == 3 else w_gateup.unsqueeze(0)
-  m, k = lhs.shape
+  src_rows, k = lhs.shape
+  m = src_rows if row_index is None else row_index.shape[0]
   two_i = w.shape[2] if layout == 0 else w.shape[1]
   inter = two_i // 2
   g = w.shape[0]
   if group_sizes is not None and group_sizes.shape != (g,):
     raise ValueError("group_sizes must have one entry per weight group")
   gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
+  ri = None if row_index is None else row_index.to(torch.int32).contiguous()
   res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
   _native.call("lmoe_gateup_situ_bf16", _ptr(lhs.contiguous()), _ptr(w.contiguous()), _ptr(gs),
                _ptr(res), m, k, inter, g, layout, float(beta), float(linear_beta),
-               int(round_gate_up), _ptr(device_status(lhs.device)), _stream())
+               int(round_gate_up), _ptr(ri), src_rows, _ptr(device_status(lhs.device)),
+               _stream())
   return res
 
 
@@ -222,23 +231,29 @@ def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
                             group_sizes: torch.Tensor | None, *, beta: float = 4.0,
                             linear_beta: float = 25.0, round_gate_up: bool = True,
                             out_dtype: torch.dtype = torch.bfloat16,
-                            out: torch.Tensor | None = None) -> torch.Tensor:
+                            out: torch.Tensor | None = None,
+                            row_index: torch.Tensor | None = None) -> torch.Tensor:
   """SiTU-GLU of one grouped matmul against MXFP4 [gate rows | up rows].
   lhs bf16, or f16 carrying bf16 values; out_dtype=torch.float16 stores the
-  bf16-rounded activation as f16 (the lhs of an f16 down-projection)."""
-  _need_cuda(lhs, w_gateup.packed, w_gateup.scale, group_sizes)
+  bf16-rounded activation as f16 (the lhs of an f16 down-projection).
+  `row_index` fuses the dispatch gather into the operand load (see
+  fused_gateup_situ)."""
+  _need_cuda(lhs, w_gateup.packed, w_gateup.scale, group_sizes, row_index)
   g, two_i, k = w_gateup.shape
   inter = two_i // 2
-  m = lhs.shape[0]
+  src_rows = lhs.shape[0]
+  m = src_rows if row_index is None else row_index.shape[0]
   lhs_f16 = lhs.dtype == torch.float16
   if lhs_f16 and not w_gateup.f16_operand_ok:
     raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
   gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
+  ri = None if row_index is None else row_index.to(torch.int32).contiguous()
   res = out if out is not None else torch.empty(m, inter, dtype=out_dtype, device=lhs.device)
   _native.call("lmoe_mxfp4_gateup_situ", _ptr(lhs.contiguous()), _ptr(w_gateup.packed),
                _ptr(w_gateup.scale), _ptr(gs), _ptr(res), m, k, inter, g, float(beta),
                float(linear_beta), int(round_gate_up), int(lhs_f16),
-               int(res.dtype == torch.float16), _ptr(device_status(lhs.device)), _stream())
+               int(res.dtype == torch.float16), _ptr(ri), src_rows,
+               _ptr(device_status(lhs.device)), _stream())
   return res
 
 
