@@ -60,6 +60,8 @@ def parse_args():
   p.add_argument("--seed", type=int, default=4)
   p.add_argument("--cpu-sample-tokens", type=int, default=16)
   p.add_argument("--no-cpu-baseline", action="store_true")
+  p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                 help="expert-parallel exchange (N>1): NVLink peer-memory puts or NCCL all-to-all")
   return p.parse_args()
 
 
@@ -72,6 +74,8 @@ def config_dict(args, world):
       "top_k": 16, "num_shared_experts": 2, "expert_format": "mxfp4 (e2m1 + E8M0/32)",
       "activations": "bf16", "router_bias_std": 0.5,
       "parallelism": f"ep{world}" if world > 1 else "single GPU",
+      "exchange": ("nvlink peer-memory puts" if args.exchange == "peer" else
+                   "nccl all_to_all_single") if world > 1 else None,
       "l2": "working set (3.2 GB weights) > 126 MB L2; no flush between steps",
   }
 
@@ -254,7 +258,8 @@ def main():
 
   import tokamax_tpu_kernel_lab_b200 as lm
   from tokamax_tpu_kernel_lab_b200 import _native, ops
-  from tokamax_tpu_kernel_lab_b200.expert_parallel import GpuBackend, ep_forward
+  from tokamax_tpu_kernel_lab_b200.expert_parallel import (GpuBackend, PeerExchange, ep_forward,
+                                                           ep_forward_peer)
 
   torch.cuda.set_device(local_rank)
   dev = torch.device("cuda", local_rank)
@@ -272,8 +277,11 @@ def main():
   gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + rank)
   h = torch.randn(t_local, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
   backend = GpuBackend(pw, cfg)
+  xchg = PeerExchange(cfg, t_local) if world > 1 and args.exchange == "peer" else None
 
   def forward(x):
+    if xchg is not None:
+      return ep_forward_peer(x, backend, cfg, xchg)
     if world > 1:
       return ep_forward(x, backend, cfg)
     return lm.latent_moe_forward(x, pw, cfg)
@@ -379,6 +387,9 @@ def main():
 
   if world > 1:
     torch.cuda.synchronize()
+    ops.check_device_status()
+    if xchg is not None:
+      xchg.close()
     dist.barrier()
     dist.destroy_process_group()
   if rank != 0:

@@ -8,7 +8,9 @@
  *     cudaStream_t passed as void*; NULL = the legacy default stream);
  *   - is stream-ordered and asynchronous, allocates nothing and never
  *     synchronises the host (group sizes live in device memory and are read
- *     only on the device);
+ *     only on the device) -- except the exchange-buffer setup calls
+ *     lmoe_ep_buffer_alloc / _open / _close / _free, which exist to allocate
+ *     and map memory and are synchronous;
  *   - returns LMOE_OK or a host-detected error code;
  *   - optionally records a device-detected error (group sizes that exceed the
  *     row count, a bounded wait that timed out) in `dev_status`, a device
@@ -48,15 +50,17 @@ enum { LMOE_ROUTER_SIGMOID = 0, LMOE_ROUTER_SOFTMAX = 1 };
 LMOE_API int lmoe_version(void);
 
 /* Grouped matmul, bf16 in, f32 accumulate (tcgen05), bf16 or f32 out.
- *   out[r] = lhs[r] @ rhs[g]  for r in group g's contiguous row range; rows at or
- *   past sum(group_sizes) are written as zero.
+ *   out[r] = lhs[r] @ rhs[g]  for r in group g's contiguous row range; with
+ *   zero_tail = 1 rows at or past sum(group_sizes) are written as zero (the
+ *   ragged_dot contract); 0 leaves them untouched (an exchange buffer sized by
+ *   capacity, whose tail nobody reads).
  * lhs (m, k); rhs (g, k, n) [LMOE_RHS_GKN] or (g, n, k) [LMOE_RHS_GNK];
  * group_sizes (g,) int32 device; out (m, n).  k, n multiples of 8.
  * Replaces tokamax.ragged_dot(lhs, rhs, group_sizes, implementation=...)
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:358-369, 604-607). */
 LMOE_API int lmoe_ragged_dot_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
                          int64_t m, int64_t k, int64_t n, int64_t num_groups, int rhs_layout,
-                         int out_f32, int32_t* dev_status, void* stream);
+                         int out_f32, int zero_tail, int32_t* dev_status, void* stream);
 
 /* Same semantics in IEEE float32 on the CUDA cores (f32 compute dtype).
  * Replaces ragged_dot with f32 operands (the reference's f32 configs,
@@ -91,6 +95,7 @@ LMOE_API int lmoe_gemm_bf16(const void* lhs, const void* rhs, const void* addend
  * into the operand load -- logical row r is row lhs_row_index[r] of lhs, which
  * then has lhs_src_rows rows (index -1 reads as zeros), so the sorted copy of
  * the tokens is never materialised.  NULL: lhs is read directly (m rows).
+ * zero_tail as in lmoe_ragged_dot_bf16 (ignored when group_sizes is NULL).
  * Replaces PallasMosaicTpuV2RaggedDot()(..., fuse_gateup_activation="situ:b:lb")
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:610-723) and the
  * dense own kernel (05_ragged_dot_on_tpu/own_gateup_situ_pallas_kernel.py:79-199). */
@@ -98,7 +103,8 @@ LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const 
                           void* out, int64_t m, int64_t k, int64_t intermediate,
                           int64_t num_groups, int rhs_layout, float beta, float linear_beta,
                           int round_gate_up, const int32_t* lhs_row_index,
-                          int64_t lhs_src_rows, int32_t* dev_status, void* stream);
+                          int64_t lhs_src_rows, int zero_tail, int32_t* dev_status,
+                          void* stream);
 
 /* Grouped matmul against MXFP4 weights: e2m1 codes (g, n, k/2) uint8, low nibble
  * = even k, and one E8M0 scale byte per 32-element k block (g, n, k/32) -- the
@@ -111,12 +117,14 @@ LMOE_API int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const 
  * lmoe_gather_rows with convert = 1); the codes are then expanded with the
  * hardware e2m1 -> f16 conversion and the MMA runs on f16 operands, which needs
  * every scale byte in [104, 140] (weights of magnitude 2^-23 .. 2^13 x 6).
+ * zero_tail as in lmoe_ragged_dot_bf16.
  * Replaces the MXFP4 dequant matmul
  * (05_ragged_dot_on_tpu/mxfp4_online_dequant_matmul_pallas.py:120-157). */
 LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
                                    const void* weight_scale, const int32_t* group_sizes, void* out,
                                    int64_t m, int64_t k, int64_t n, int64_t num_groups,
-                                   int lhs_f16, int out_f32, int32_t* dev_status, void* stream);
+                                   int lhs_f16, int out_f32, int zero_tail, int32_t* dev_status,
+                                   void* stream);
 
 /* Fused gate/up + SiTU-GLU against MXFP4 weights: the packed rows are
  * [gate (intermediate rows) | up (intermediate rows)] per group, i.e.
@@ -124,14 +132,15 @@ LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
  * checkpoint's w1 and w3 stacked).  group_sizes NULL = one dense group.
  * lhs_f16 as above; out_f16 = 1 stores the bf16-rounded activation as f16
  * (the lhs of a following lhs_f16 down-projection); lhs_row_index /
- * lhs_src_rows fuse the dispatch gather as in lmoe_gateup_situ_bf16. */
+ * lhs_src_rows fuse the dispatch gather and zero_tail behaves as in
+ * lmoe_gateup_situ_bf16. */
 LMOE_API int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed,
                                     const void* weight_scale, const int32_t* group_sizes,
                                     void* out, int64_t m, int64_t k, int64_t intermediate,
                                     int64_t num_groups, float beta, float linear_beta,
                                     int round_gate_up, int lhs_f16, int out_f16,
                                     const int32_t* lhs_row_index, int64_t lhs_src_rows,
-                                    int32_t* dev_status, void* stream);
+                                    int zero_tail, int32_t* dev_status, void* stream);
 
 /* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).
  * gate/up rows have pitch ld_in elements; bf16 = 1 for bf16 I/O, 0 for f32.
@@ -227,6 +236,62 @@ LMOE_API int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_po
 LMOE_API int lmoe_ep_reorder(const int32_t* recv_counts, int64_t world, int64_t num_local_experts,
                              int64_t rows_cap, int32_t* em_src, int32_t* sm_src,
                              int32_t* group_sizes, void* stream);
+
+/* Expert-parallel exchange over NVLink peer memory (one process per GPU).
+ * peers_dev is a device array of `world` pointers to every rank's symmetric
+ * buffer of lmoe_ep_buffer_bytes(...) bytes (same layout on every rank; index
+ * `rank` = this rank's own buffer); every call of one exchange passes the same
+ * epoch on every rank, one larger than the previous exchange's.  Rank r owns
+ * global experts [r*E/world, (r+1)*E/world).  Sequence per forward:
+ *   lmoe_ep_exchange_counts  publish this rank's per-expert row counts
+ *                            (group_sizes, E int32, from lmoe_dispatch over all E
+ *                            experts) to every peer, wait for all, write
+ *                            local_group_sizes (E/world int32)
+ *   lmoe_ep_dispatch_put     copy row x[token_idx[p]] of every dispatched row p
+ *                            straight into its owner's receive region, expert-major,
+ *                            then wait until every source's rows have landed here
+ *   (grouped GEMMs on the receive region, group sizes local_group_sizes)
+ *   lmoe_ep_return_put       copy each output row back into its source's return
+ *                            region at the row's original dispatch position, then
+ *                            wait for this rank's rows to come back
+ * Offsets are computed on the device from the exchanged counts: no host
+ * synchronisation.  Waits are bounded (LMOE_WAIT_TIMEOUT in dev_status).
+ * Region byte offsets within the buffer: lmoe_ep_region_offset (0 receive,
+ * 1 return, 2 counts).  No counterpart in the reference (its expert shards are
+ * simulated in one process, 05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:1531-1674). */
+LMOE_API int64_t lmoe_ep_buffer_bytes(int64_t world, int64_t num_experts,
+                                      int64_t recv_capacity_rows, int64_t back_capacity_rows,
+                                      int64_t row_bytes);
+/* The exchange buffer and its peer mappings, over CUDA IPC on the current
+ * device (plain point-to-point peer mappings): lmoe_ep_buffer_alloc
+ * allocates and zeroes `bytes`, returning the pointer and an IPC handle of
+ * LMOE_EP_IPC_HANDLE_BYTES bytes to send to every peer; lmoe_ep_buffer_open
+ * maps a peer's handle; close / free undo them (after every rank is done with
+ * the exchange). */
+#define LMOE_EP_IPC_HANDLE_BYTES 64
+LMOE_API int lmoe_ep_buffer_alloc(int64_t bytes, void** buffer, void* ipc_handle);
+LMOE_API int lmoe_ep_buffer_open(const void* ipc_handle, void** peer_buffer);
+LMOE_API int lmoe_ep_buffer_close(void* peer_buffer);
+LMOE_API int lmoe_ep_buffer_free(void* buffer);
+LMOE_API int64_t lmoe_ep_region_offset(int64_t world, int64_t num_experts,
+                                       int64_t recv_capacity_rows, int64_t back_capacity_rows,
+                                       int64_t row_bytes, int region);
+LMOE_API int lmoe_ep_exchange_counts(void* const* peers_dev, int64_t rank, int64_t world,
+                                     int64_t num_experts, int64_t recv_capacity_rows,
+                                     int64_t back_capacity_rows, int64_t row_bytes,
+                                     uint32_t epoch, const int32_t* group_sizes,
+                                     int32_t* local_group_sizes, int32_t* dev_status,
+                                     void* stream);
+LMOE_API int lmoe_ep_dispatch_put(void* const* peers_dev, int64_t rank, int64_t world,
+                                  int64_t num_experts, int64_t recv_capacity_rows,
+                                  int64_t back_capacity_rows, int64_t row_bytes, uint32_t epoch,
+                                  const void* x, int64_t x_rows, const int32_t* token_idx,
+                                  int64_t num_routed_rows, int32_t* dev_status, void* stream);
+LMOE_API int lmoe_ep_return_put(void* const* peers_dev, int64_t rank, int64_t world,
+                                int64_t num_experts, int64_t recv_capacity_rows,
+                                int64_t back_capacity_rows, int64_t row_bytes, uint32_t epoch,
+                                const void* y, int64_t num_rows, int32_t* dev_status,
+                                void* stream);
 
 /* Scatter-add combine of one expert shard:
  *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0

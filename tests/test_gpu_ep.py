@@ -1,5 +1,7 @@
-"""Expert parallelism on real GPUs (NCCL all-to-all): the concatenated
-per-rank outputs must equal the single-GPU forward of all tokens bit for bit.
+"""Expert parallelism on real GPUs, with the exchange over NCCL all-to-all
+and over NVLink peer memory (device-side puts): the concatenated per-rank
+outputs must equal the single-GPU forward of all tokens bit for bit.  The
+peer form runs several forwards through one exchange buffer (epoch reuse).
 Needs at least 2 GPUs; skipped otherwise."""
 
 import datetime
@@ -22,11 +24,12 @@ def _cfg(lm):
   return lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, mode="nccl"):
   import torch.distributed as dist
 
   import tokamax_tpu_kernel_lab_b200 as lm
-  from tokamax_tpu_kernel_lab_b200.expert_parallel import EPStats, GpuBackend, ep_forward
+  from tokamax_tpu_kernel_lab_b200.expert_parallel import (EPStats, GpuBackend, PeerExchange,
+                                                           ep_forward, ep_forward_peer)
 
   os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
   torch.cuda.set_device(rank)
@@ -41,6 +44,24 @@ def _worker(rank, world, port, results):
     gen = torch.Generator(device=dev).manual_seed(21)
     h = torch.randn(512, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
     t = h.shape[0] // world
+    if mode == "peer":
+      hs = [h] + [torch.randn(512, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
+                  for _ in range(2)]
+      backend = GpuBackend(pw, cfg)
+      xchg = PeerExchange(cfg, t)
+      try:
+        outs = [ep_forward_peer(x[rank * t:(rank + 1) * t].contiguous(), backend, cfg, xchg)
+                for x in hs]
+        torch.cuda.synchronize()
+        lm.check_device_status()
+      finally:
+        xchg.close()
+      results[rank] = [o.cpu() for o in outs]
+      if rank == 0:
+        full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
+        results["ref"] = [lm.latent_moe_forward(x, full, cfg).cpu() for x in hs]
+      dist.barrier()
+      return
     stats = EPStats([], [])
     out = ep_forward(h[rank * t:(rank + 1) * t].contiguous(), GpuBackend(pw, cfg), cfg,
                      stats=stats)
@@ -67,3 +88,17 @@ def test_ep_forward_bit_exact_vs_single_gpu(world):
   got = torch.cat([results[r][0] for r in range(world)])
   assert torch.equal(got, results["ref"])
   assert sum(sum(results[r][1]) for r in range(world)) == 512 * 8
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_forward_peer_bit_exact_vs_single_gpu(world):
+  if torch.cuda.device_count() < world:
+    pytest.skip(f"needs {world} GPUs")
+  import torch.multiprocessing as mp
+  mgr = mp.get_context("spawn").Manager()
+  results = mgr.dict()
+  mp.spawn(_worker, args=(world, _free_port(), results, "peer"), nprocs=world, join=True)
+  for i, ref in enumerate(results["ref"]):
+    got = torch.cat([results[r][i] for r in range(world)])
+    assert torch.equal(got, ref), f"forward {i}"

@@ -29,16 +29,17 @@ _sz = ctypes.c_size_t
 # name -> (restype, argtypes); mirrors include/lmoe.h one to one
 SIGNATURES = {
     "lmoe_version": (_i32, []),
-    "lmoe_ragged_dot_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p, _p]),
+    "lmoe_ragged_dot_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _p,
+                                    _p]),
     "lmoe_ragged_dot_f32": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p, _p]),
     "lmoe_gemm_f32": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p, _p]),
     "lmoe_gemm_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _i32, _p, _p]),
     "lmoe_gateup_situ_bf16": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _f32,
-                                     _i32, _p, _i64, _p, _p]),
-    "lmoe_mxfp4_ragged_dot": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _p,
-                                     _p]),
+                                     _i32, _p, _i64, _i32, _p, _p]),
+    "lmoe_mxfp4_ragged_dot": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
+                                     _p, _p]),
     "lmoe_mxfp4_gateup_situ": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _f32,
-                                      _i32, _i32, _i32, _p, _i64, _p, _p]),
+                                      _i32, _i32, _i32, _p, _i64, _i32, _p, _p]),
     "lmoe_situ_and_mul": (_i32, [_p, _p, _i64, _p, _i64, _i64, _f32, _f32, _i32, _p]),
     "lmoe_router_topk": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
     "lmoe_dispatch_workspace_size": (_sz, [_i64, _i64]),
@@ -50,10 +51,24 @@ SIGNATURES = {
     "lmoe_ep_reorder": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
     "lmoe_dispatch_static_scratch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p,
                                             _p, _p, _p, _p, _p, _p]),
+    "lmoe_ep_buffer_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "lmoe_ep_region_offset": (_i64, [_i64, _i64, _i64, _i64, _i64, _i32]),
+    "lmoe_ep_buffer_alloc": (_i32, [_i64, _p, _p]),
+    "lmoe_ep_buffer_open": (_i32, [_p, _p]),
+    "lmoe_ep_buffer_close": (_i32, [_p]),
+    "lmoe_ep_buffer_free": (_i32, [_p]),
+    "lmoe_ep_exchange_counts": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32,
+                                       _p, _p, _p, _p]),
+    "lmoe_ep_dispatch_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32, _p,
+                                    _i64, _p, _i64, _p, _p]),
+    "lmoe_ep_return_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32, _p,
+                                  _i64, _p, _p]),
 }
 
 # kernels launched by one call of each entry point (for the bench's launch count)
-KERNELS_PER_CALL = {"lmoe_dispatch": 3}
+KERNELS_PER_CALL = {"lmoe_dispatch": 3, "lmoe_ep_dispatch_put": 2, "lmoe_ep_return_put": 2,
+                    "lmoe_ep_buffer_alloc": 0, "lmoe_ep_buffer_open": 0,
+                    "lmoe_ep_buffer_close": 0, "lmoe_ep_buffer_free": 0}
 launch_count = 0
 
 

@@ -16,11 +16,11 @@ int lmoe_version(void) { return 100; }
 
 int lmoe_ragged_dot_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
                          int64_t m, int64_t k, int64_t n, int64_t num_groups, int rhs_layout,
-                         int out_f32, int32_t* dev_status, void* stream) {
+                         int out_f32, int zero_tail, int32_t* dev_status, void* stream) {
   if (group_sizes == nullptr) return LMOE_BAD_SHAPE;
   return lmoe::grouped_gemm_bf16(lhs, rhs, group_sizes, out, m, k, n, num_groups, rhs_layout,
-                                 out_f32 ? kEpiF32 : kEpiBf16, nullptr, 0, 0, 0.f, 0.f, 0, 1,
-                                 dev_status, S(stream));
+                                 out_f32 ? kEpiF32 : kEpiBf16, nullptr, 0, 0, 0.f, 0.f, 0,
+                                 zero_tail ? 1 : 0, dev_status, S(stream));
 }
 
 int lmoe_ragged_dot_f32(const float* lhs, const float* rhs, const int32_t* group_sizes, float* out,
@@ -52,35 +52,35 @@ int lmoe_gateup_situ_bf16(const void* lhs, const void* w_gateup, const int32_t* 
                           void* out, int64_t m, int64_t k, int64_t intermediate,
                           int64_t num_groups, int rhs_layout, float beta, float linear_beta,
                           int round_gate_up, const int32_t* lhs_row_index, int64_t lhs_src_rows,
-                          int32_t* dev_status, void* stream) {
+                          int zero_tail, int32_t* dev_status, void* stream) {
   return lmoe::grouped_gemm_bf16(lhs, w_gateup, group_sizes, out, m, k, intermediate,
                                  group_sizes ? num_groups : 1, rhs_layout, kEpiSitu, nullptr, 0,
                                  intermediate, beta, linear_beta, round_gate_up,
-                                 group_sizes ? 1 : 0, dev_status, S(stream), lhs_row_index,
-                                 lhs_src_rows);
+                                 (group_sizes && zero_tail) ? 1 : 0, dev_status, S(stream),
+                                 lhs_row_index, lhs_src_rows);
 }
 
 int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed, const void* weight_scale,
                           const int32_t* group_sizes, void* out, int64_t m, int64_t k, int64_t n,
-                          int64_t num_groups, int lhs_f16, int out_f32, int32_t* dev_status,
-                          void* stream) {
+                          int64_t num_groups, int lhs_f16, int out_f32, int zero_tail,
+                          int32_t* dev_status, void* stream) {
   if (group_sizes == nullptr) return LMOE_BAD_SHAPE;
   return lmoe::grouped_gemm_mxfp4(lhs, weight_packed, weight_scale, group_sizes, out, m, k, n,
-                                  num_groups, out_f32 ? kEpiF32 : kEpiBf16, 0, 0.f, 0.f, 0, 1,
-                                  lhs_f16, 0, dev_status, S(stream));
+                                  num_groups, out_f32 ? kEpiF32 : kEpiBf16, 0, 0.f, 0.f, 0,
+                                  zero_tail ? 1 : 0, lhs_f16, 0, dev_status, S(stream));
 }
 
 int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed, const void* weight_scale,
                            const int32_t* group_sizes, void* out, int64_t m, int64_t k,
                            int64_t intermediate, int64_t num_groups, float beta, float linear_beta,
                            int round_gate_up, int lhs_f16, int out_f16,
-                           const int32_t* lhs_row_index, int64_t lhs_src_rows,
+                           const int32_t* lhs_row_index, int64_t lhs_src_rows, int zero_tail,
                            int32_t* dev_status, void* stream) {
   return lmoe::grouped_gemm_mxfp4(lhs, weight_packed, weight_scale, group_sizes, out, m, k,
                                   intermediate, group_sizes ? num_groups : 1, kEpiSitu,
                                   intermediate, beta, linear_beta, round_gate_up,
-                                  group_sizes ? 1 : 0, lhs_f16, out_f16, dev_status, S(stream),
-                                  lhs_row_index, lhs_src_rows);
+                                  (group_sizes && zero_tail) ? 1 : 0, lhs_f16, out_f16,
+                                  dev_status, S(stream), lhs_row_index, lhs_src_rows);
 }
 
 int lmoe_situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,

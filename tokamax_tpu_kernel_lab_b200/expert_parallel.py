@@ -21,6 +21,13 @@ Every row meets the same weights and the same K-reduction as on one GPU and
 the combine order is the slot order, so the n-rank output equals the 1-rank
 output bit for bit (dropless dispatch).
 
+`ep_forward` runs the exchange on NCCL (all_to_all_single, one host read of
+the counts per forward); `ep_forward_peer` runs it as device kernels that
+store rows straight into the peer GPUs' buffers over NVLink (CUDA IPC
+mappings), with the counts exchanged in peer memory too: no host
+synchronisation inside the forward, and rows land expert-major in the
+receiver's buffer, so the expert GEMMs read them in place.
+
 The orchestration is written against a small kernel interface
 (`Backend`) so the exchange logic can be exercised on CPU `gloo` ranks with
 the oracle standing in for the kernels; production uses `GpuBackend`.
@@ -28,13 +35,14 @@ the oracle standing in for the kernels; production uses `GpuBackend`.
 
 from __future__ import annotations
 
+import ctypes
 import dataclasses
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _native, ops
 from .latent_moe import LatentMoEConfig, PreparedWeights, _dense, mxfp4_f16_path
 
 
@@ -88,6 +96,20 @@ class GpuBackend:
                                 rhs_layout="gnk")
     return ops.ragged_dot(act, pw.expert_down, gs_local, rhs_layout="gnk")
 
+  def experts_received(self, recv, gs_local):
+    """Expert FFN of rows already in expert-major order (the peer exchange's
+    receive buffer, sized by capacity: rows past sum(gs_local) are neither
+    read nor written)."""
+    c, pw = self.cfg, self.pw
+    b, lb = c.activation_situ_beta, c.activation_situ_linear_beta
+    if pw.expert_gu_mx is not None:
+      act = ops.mxfp4_fused_gateup_situ(recv, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb,
+                                        out_dtype=recv.dtype, zero_tail=False)
+      return ops.mxfp4_ragged_dot(act, pw.expert_down_mx, gs_local, zero_tail=False)
+    act = ops.fused_gateup_situ(recv, pw.expert_gu, gs_local, beta=b, linear_beta=lb,
+                                rhs_layout="gnk", zero_tail=False)
+    return ops.ragged_dot(act, pw.expert_down, gs_local, rhs_layout="gnk", zero_tail=False)
+
   def combine(self, back, slot_pos, w):
     return ops.combine_rmsnorm(back, slot_pos, w, self.pw.norm_scale, self.cfg.rms_norm_eps)
 
@@ -136,6 +158,130 @@ def ep_forward(h: torch.Tensor, backend, cfg: LatentMoEConfig, group=None,
   back = torch.empty(send.shape[0], L, dtype=ye.dtype, device=ye.device)
   dist.all_to_all_single(back, back_send, output_split_sizes=send_rows,
                          input_split_sizes=recv_rows, group=group)
+  normed = backend.combine(back, slot_pos, w)
+  return backend.tail(normed, h)
+
+
+class _RawDevice:
+  """A device byte range as a torch tensor (zero-copy, not owned)."""
+
+  def __init__(self, ptr: int, rows: int, row_bytes: int):
+    self.__cuda_array_interface__ = {"shape": (rows, row_bytes), "typestr": "|u1",
+                                     "data": (ptr, False), "version": 3, "strides": None}
+
+
+class PeerExchange:
+  """Buffers and peer mappings of the peer-memory expert exchange.
+
+  Every rank allocates one buffer (flags, counts, offset tables, a receive
+  region of `world * tokens_per_rank * top_k` rows -- the worst case, every
+  routed row of every rank landing here -- and a return region of
+  `tokens_per_rank * top_k` rows), sends its CUDA IPC handle to every peer
+  and maps theirs.  Collective: every rank of `group` constructs it, and
+  every rank calls close()."""
+
+  def __init__(self, cfg: LatentMoEConfig, tokens_per_rank: int, group=None):
+    self.group = group
+    self.world = dist.get_world_size(group)
+    self.rank = dist.get_rank(group)
+    if cfg.num_experts % self.world:
+      raise ValueError(f"num_experts {cfg.num_experts} is not divisible by world {self.world}")
+    self.E = cfg.num_experts
+    self.n_local = self.E // self.world
+    self.row_bytes = cfg.latent_size * 2
+    self.back_cap = tokens_per_rank * cfg.top_k
+    self.recv_cap = self.back_cap * self.world
+    lib = _native.load()
+    geo = (self.world, self.E, self.recv_cap, self.back_cap, self.row_bytes)
+    self.nbytes = int(lib.lmoe_ep_buffer_bytes(*geo))
+    if self.nbytes <= 0:
+      raise ValueError("invalid exchange geometry")
+    own = ctypes.c_void_p()
+    handle = (ctypes.c_uint8 * 64)()
+    _native.call("lmoe_ep_buffer_alloc", self.nbytes, ctypes.byref(own), handle)
+    self._own = own.value
+    handles = [None] * self.world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    ptrs, self._opened = [], []
+    for r, hb in enumerate(handles):
+      if r == self.rank:
+        ptrs.append(self._own)
+        continue
+      peer = ctypes.c_void_p()
+      _native.call("lmoe_ep_buffer_open", (ctypes.c_uint8 * 64).from_buffer_copy(hb),
+                   ctypes.byref(peer))
+      ptrs.append(peer.value)
+      self._opened.append(peer.value)
+    self.peers_dev = torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+    self.local_gs = torch.zeros(self.n_local, dtype=torch.int32, device="cuda")
+    self._recv = torch.as_tensor(
+        _RawDevice(self._own + int(lib.lmoe_ep_region_offset(*geo, 0)), self.recv_cap,
+                   self.row_bytes), device="cuda")
+    self._back = torch.as_tensor(
+        _RawDevice(self._own + int(lib.lmoe_ep_region_offset(*geo, 1)), self.back_cap,
+                   self.row_bytes), device="cuda")
+    self.epoch = 0
+    dist.barrier(group)  # every buffer is zeroed and mapped before the first signal
+
+  def _geo(self):
+    return (self.peers_dev.data_ptr(), self.rank, self.world, self.E, self.recv_cap,
+            self.back_cap, self.row_bytes)
+
+  def recv_rows(self, dtype: torch.dtype) -> torch.Tensor:
+    return self._recv.view(dtype)
+
+  def back_rows(self, rows: int, dtype: torch.dtype) -> torch.Tensor:
+    return self._back[:rows].view(dtype)
+
+  def exchange(self, x: torch.Tensor, token_idx: torch.Tensor, group_sizes: torch.Tensor,
+               experts) -> torch.Tensor:
+    """Send row x[token_idx[p]] of every dispatched row p to the owner of its
+    expert, run `experts(recv, local_group_sizes)` on the rows this rank
+    received, send each result back; returns the returned rows in this rank's
+    dispatch order (token_idx.shape[0] rows)."""
+    if x.shape[1] * x.element_size() != self.row_bytes:
+      raise ValueError("row width does not match the exchange buffer")
+    rows = token_idx.shape[0]
+    if rows > self.back_cap or group_sizes.shape[0] != self.E:
+      raise ValueError("dispatch does not fit the exchange buffer")
+    self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+    status = ops._ptr(ops.device_status(x.device))
+    stream = ops._stream()
+    geo = self._geo()
+    _native.call("lmoe_ep_exchange_counts", *geo, self.epoch, group_sizes.data_ptr(),
+                 self.local_gs.data_ptr(), status, stream)
+    _native.call("lmoe_ep_dispatch_put", *geo, self.epoch, x.data_ptr(), x.shape[0],
+                 token_idx.data_ptr(), rows, status, stream)
+    y = experts(self.recv_rows(x.dtype), self.local_gs)
+    if y.shape[1] * y.element_size() != self.row_bytes or not y.is_contiguous():
+      raise ValueError("expert output rows do not match the exchange buffer")
+    _native.call("lmoe_ep_return_put", *geo, self.epoch, y.data_ptr(), y.shape[0], status,
+                 stream)
+    return self.back_rows(rows, y.dtype)
+
+  def close(self):
+    """Collective: unmap the peers' buffers and free this rank's, once every
+    rank has finished with the exchange."""
+    if self._own is None:
+      return
+    torch.cuda.synchronize()
+    dist.barrier(self.group)
+    for p in self._opened:
+      _native.call("lmoe_ep_buffer_close", p)
+    self._opened = []
+    self._recv = self._back = None
+    _native.call("lmoe_ep_buffer_free", self._own)
+    self._own = None
+
+
+def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
+                    xchg: PeerExchange) -> torch.Tensor:
+  """Expert-parallel forward of this rank's tokens `h` (T_local, d) with the
+  exchange over NVLink peer memory (no host synchronisation)."""
+  idx, w = backend.route(h)
+  x = backend.down(h)
+  token_idx, slot_pos, group_sizes = backend.dispatch(idx, w)
+  back = xchg.exchange(x, token_idx, group_sizes, backend.experts_received)
   normed = backend.combine(back, slot_pos, w)
   return backend.tail(normed, h)
 

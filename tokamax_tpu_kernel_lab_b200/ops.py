@@ -76,10 +76,12 @@ def _check_impl(implementation):
 def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, *,
                implementation: str | None = None, precision=None,
                preferred_element_type: torch.dtype | None = None, rhs_layout: str = "gkn",
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, zero_tail: bool = True) -> torch.Tensor:
   """out[r] = lhs[r] @ rhs[g] for the rows r of group g; rows past
-  sum(group_sizes) are zero.  lhs (M, K); rhs (G, K, N) ("gkn", the reference's
-  layout) or (G, N, K) ("gnk"); group_sizes (G,) int32 on the device.
+  sum(group_sizes) are zero (zero_tail=False leaves them unwritten, for a
+  buffer sized by capacity).  lhs (M, K); rhs (G, K, N) ("gkn", the
+  reference's layout) or (G, N, K) ("gnk"); group_sizes (G,) int32 on the
+  device.
 
   bf16 operands run on the tensor cores (f32 accumulate, bf16 or f32 out);
   f32 operands run the f32 CUDA-core kernel."""
@@ -113,7 +115,8 @@ def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, 
     raise NotImplementedError(f"preferred_element_type={out_dtype}")
   res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
   _native.call("lmoe_ragged_dot_bf16", _ptr(lhs), _ptr(rhs), _ptr(gs), _ptr(res), m, k, n, g,
-               layout, int(out_dtype == torch.float32), _ptr(status), _stream())
+               layout, int(out_dtype == torch.float32), int(zero_tail), _ptr(status),
+               _stream())
   return res
 
 
@@ -150,7 +153,8 @@ def prefuse_gateup_weights(expert_gate: torch.Tensor, expert_up: torch.Tensor,
 def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: torch.Tensor | None,
                       *, beta: float = 4.0, linear_beta: float = 25.0, round_gate_up: bool = True,
                       rhs_layout: str = "gkn", out: torch.Tensor | None = None,
-                      row_index: torch.Tensor | None = None) -> torch.Tensor:
+                      row_index: torch.Tensor | None = None,
+                      zero_tail: bool = True) -> torch.Tensor:
   """SiTU-GLU(lhs @ gate_g, lhs @ up_g) from ONE grouped matmul against the
   fused [gate | up] weight.  `group_sizes=None` means one dense group
   (the shared expert).  With `row_index` (int32, one entry per logical row)
@@ -171,8 +175,8 @@ def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: to
   res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
   _native.call("lmoe_gateup_situ_bf16", _ptr(lhs.contiguous()), _ptr(w.contiguous()), _ptr(gs),
                _ptr(res), m, k, inter, g, layout, float(beta), float(linear_beta),
-               int(round_gate_up), _ptr(ri), src_rows, _ptr(device_status(lhs.device)),
-               _stream())
+               int(round_gate_up), _ptr(ri), src_rows, int(zero_tail),
+               _ptr(device_status(lhs.device)), _stream())
   return res
 
 
@@ -205,7 +209,7 @@ class MXFP4Weights:
 
 def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tensor, *,
                      preferred_element_type: torch.dtype | None = None,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, zero_tail: bool = True) -> torch.Tensor:
   """lhs (M, K) @ dequant(w[g])^T per group -> (M, N); the weights stay
   packed in HBM and are expanded tile by tile in shared memory.  lhs is bf16,
   or f16 carrying bf16 values (the f16-operand kernel; needs
@@ -222,8 +226,8 @@ def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tens
   res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
   _native.call("lmoe_mxfp4_ragged_dot", _ptr(lhs.contiguous()), _ptr(w.packed), _ptr(w.scale),
                _ptr(group_sizes.to(torch.int32).contiguous()), _ptr(res), m, k, n, g,
-               int(lhs_f16), int(out_dtype == torch.float32), _ptr(device_status(lhs.device)),
-               _stream())
+               int(lhs_f16), int(out_dtype == torch.float32), int(zero_tail),
+               _ptr(device_status(lhs.device)), _stream())
   return res
 
 
@@ -232,7 +236,8 @@ def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
                             linear_beta: float = 25.0, round_gate_up: bool = True,
                             out_dtype: torch.dtype = torch.bfloat16,
                             out: torch.Tensor | None = None,
-                            row_index: torch.Tensor | None = None) -> torch.Tensor:
+                            row_index: torch.Tensor | None = None,
+                            zero_tail: bool = True) -> torch.Tensor:
   """SiTU-GLU of one grouped matmul against MXFP4 [gate rows | up rows].
   lhs bf16, or f16 carrying bf16 values; out_dtype=torch.float16 stores the
   bf16-rounded activation as f16 (the lhs of an f16 down-projection).
@@ -252,7 +257,7 @@ def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
   _native.call("lmoe_mxfp4_gateup_situ", _ptr(lhs.contiguous()), _ptr(w_gateup.packed),
                _ptr(w_gateup.scale), _ptr(gs), _ptr(res), m, k, inter, g, float(beta),
                float(linear_beta), int(round_gate_up), int(lhs_f16),
-               int(res.dtype == torch.float16), _ptr(ri), src_rows,
+               int(res.dtype == torch.float16), _ptr(ri), src_rows, int(zero_tail),
                _ptr(device_status(lhs.device)), _stream())
   return res
 
