@@ -250,13 +250,16 @@ __device__ __forceinline__ float tanh_fast(float x) {
 
 // SiTU-GLU of one (gate, up) pair: beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb),
 // with inv_beta = 1/beta and inv_lbeta = 1/lb precomputed.  tanh on the MUFU
-// unit, sigmoid as 1 / (1 + 2^(-g*log2 e)) with the approximate exp2 and
-// reciprocal; every output is rounded to bf16 afterwards, far coarser than
-// these approximations.  Used by both the fused GEMM epilogue and the
-// standalone SiTU kernel, so the two produce identical bits.
+// unit, sigmoid as 1 / (1 + 2^(-g*log2 e)) with the MUFU exp2 and reciprocal
+// (ex2.approx / rcp.approx, relative error near 2^-22; the limits g -> +-inf
+// give 1 and 0).  Every output is rounded to bf16 afterwards, far coarser
+// than these approximations.  Used by both the fused GEMM epilogues and the
+// standalone SiTU kernel, so they produce identical bits.
 __device__ __forceinline__ float situ_fast(float g, float u, float beta, float inv_beta,
                                            float lbeta, float inv_lbeta) {
-  const float sig = __frcp_rn(1.0f + exp2f(-1.4426950408889634f * g));
+  float e, sig;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-1.4426950408889634f * g));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(sig) : "f"(1.0f + e));
   const float sg = (beta * tanh_fast(g * inv_beta)) * sig;
   const float bu = lbeta * tanh_fast(u * inv_lbeta);
   return sg * bu;
