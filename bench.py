@@ -60,6 +60,8 @@ def parse_args():
   p.add_argument("--seed", type=int, default=4)
   p.add_argument("--cpu-sample-tokens", type=int, default=16)
   p.add_argument("--no-cpu-baseline", action="store_true")
+  p.add_argument("--no-graph", action="store_true",
+                 help="time eager launches instead of a captured CUDA graph (one GPU)")
   p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                  help="expert-parallel exchange (N>1): NVLink peer-memory puts or NCCL all-to-all")
   return p.parse_args()
@@ -77,6 +79,7 @@ def config_dict(args, world):
       "exchange": ("nvlink peer-memory puts" if args.exchange == "peer" else
                    "nccl all_to_all_single") if world > 1 else None,
       "l2": "working set (3.2 GB weights) > 126 MB L2; no flush between steps",
+      "launch": ("cuda graph replay" if world == 1 and not args.no_graph else "eager"),
   }
 
 
@@ -303,6 +306,28 @@ def main():
   torch.cuda.synchronize()
   ops.check_device_status()
 
+  # One GPU: the forward is captured once as a CUDA graph and replayed, so the
+  # timed steps do not depend on host launch speed (every kernel still runs
+  # every step).  Expert parallelism runs eagerly (the exchange epochs and the
+  # NCCL form's count read live on the host).
+  graph = None
+  launches_per_step = None
+  if world == 1 and not args.no_graph:
+    graph = torch.cuda.CUDAGraph()
+    launches_cap = _native.launch_count
+    with torch.cuda.graph(graph):
+      out_graph = forward(h)
+    launches_per_step = _native.launch_count - launches_cap
+    graph.replay()
+    torch.cuda.synchronize()
+    ops.check_device_status()
+
+  def step():
+    if graph is not None:
+      graph.replay()
+      return out_graph
+    return forward(h)
+
   # ---------------------------------------------------------------- device-timed steps
   barrier()
   torch.cuda.synchronize()
@@ -311,11 +336,13 @@ def main():
   with ClockSampler(local_rank) as clk:
     ev0.record(stream)
     for _ in range(args.steps):
-      out = forward(h)
+      out = step()
     ev1.record(stream)
     torch.cuda.synchronize()
   barrier()
-  launches = (_native.launch_count - launches0) // max(args.steps, 1)
+  ops.check_device_status()
+  launches = (launches_per_step if graph is not None else
+              (_native.launch_count - launches0) // max(args.steps, 1))
   ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps)
   value = args.tokens / (ms / 1e3)
   clocks = clk.summary()

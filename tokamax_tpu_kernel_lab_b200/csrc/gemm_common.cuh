@@ -15,6 +15,9 @@ namespace lmoe {
 
 constexpr int kBK = 64;
 constexpr int kMaxGroups = 2048;
+// the weights-major MXFP4 kernel keeps its schedule in shared memory for up
+// to this many groups; more groups take the token-major kernel
+constexpr int kSwapMaxGroups = 1536;
 
 enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_BF16_ADD = 2, EPI_SITU = 3 };
 // B_MXFP4F16: the same packed MXFP4 weights, but the activations arrive as f16

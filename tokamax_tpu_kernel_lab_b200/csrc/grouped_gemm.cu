@@ -635,7 +635,7 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
   if (a_rows != nullptr && (a_src_rows <= 0 || a_src_rows >= (1ll << 31))) return kBadShape;
   if (M == 0) return kOk;
   const int64_t n_weight = (epi == EPI_SITU) ? 2 * up_offset : N_out;
-  if (a_rows == nullptr) {
+  if (a_rows == nullptr && (group_sizes == nullptr || G <= kSwapMaxGroups)) {
     // direct operand: the weights-major kernel (expands each weight tile once
     // per 256 tokens instead of per 128)
     GemmArgs a = make_args(group_sizes, out, nullptr, 0, M, K, N_out, G, epi, up_offset, n_weight,

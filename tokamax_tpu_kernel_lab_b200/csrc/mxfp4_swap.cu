@@ -12,8 +12,8 @@
 //
 // Three rings, so that expanding the weights never waits on the token loads:
 //   token ring   (4 x 32 KB)  256 token rows x 64 K, 128B swizzle  -> UMMA B
-//   packed ring  (6 x 4 KB)   e2m1 codes of the tile's 128 weight rows
-//   A ring       (3 x 16 KB)  expanded weights, K-major 128B swizzle -> UMMA A
+//   packed ring  (4 x 4 KB)   e2m1 codes of the tile's 128 weight rows
+//   A ring       (4 x 16 KB)  expanded weights, K-major 128B swizzle -> UMMA A
 // The packed ring has its own producer and runs ahead of the token ring, so a
 // weight tile is expanded well before the MMA that needs it.
 //
@@ -23,8 +23,8 @@
 //   warps 2-5   epilogue.  TMEM lane = weight row, column = token: each warp
 //               reads its 32 lanes, transposes through a small shared-memory
 //               tile and stores token-major rows.
-//   warps 6-13  dequant: 2 threads per weight row, 32 codes each per K step,
-//               written into the swizzled K-major A tile.
+//   warps 6-13  dequant: two groups of 4 warps on alternate K steps, one
+//               thread per weight row, into the swizzled K-major A tile.
 //   warp 14     packed-code producer (TMA).
 // EPI_SITU: the A tile interleaves gate and up rows (row 2i = gate feature i,
 // row 2i+1 = up feature i), so each (gate, up) pair sits in adjacent lanes of
@@ -44,20 +44,22 @@ namespace {
 constexpr int kTokTile = 256;  // UMMA N: token rows per tile
 constexpr int kWRows = 128;    // UMMA M: weight rows per tile
 constexpr int kTStages = 4;    // token ring
-constexpr int kPStages = 6;    // packed-code ring
-constexpr int kDStages = 3;    // expanded-weight (A) ring
-constexpr int kDeqWarps = 8;           // 2 threads per weight row
+constexpr int kPStages = 4;    // packed-code ring
+constexpr int kDStages = 4;    // expanded-weight (A) ring
+constexpr int kSwMaxGroups = kSwapMaxGroups;  // schedule arrays in shared memory
+constexpr int kDeqWarps = 8;           // two groups of 4, alternate K steps
 constexpr int kPkWarp = 6 + kDeqWarps;  // packed-code producer
 constexpr int kSwThreads = 32 * (kPkWarp + 1);
+static_assert(kPStages % 2 == 0 && kDStages % 2 == 0, "each ring slot belongs to one dequant group");
 
 struct SwCfg {
   static constexpr int kTokBytes = kTokTile * kBK * 2;     // 32 KB
   static constexpr int kPackedBytes = kWRows * (kBK / 2);  // 4 KB
   static constexpr int kABytes = kWRows * kBK * 2;         // 16 KB
-  static constexpr int kWarpStage = 2048;                  // epilogue transpose tile per warp
+  static constexpr int kWarpStage = 1024;                  // epilogue transpose tile per warp
   static constexpr int kOutStageBytes = 4 * kWarpStage;
   static constexpr int kTmemCols = 2 * kTokTile;
-  static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4;
+  static constexpr int kSchedBytes = 2 * (kSwMaxGroups + 1) * 4;
   static constexpr int kNumBars = 2 * kTStages + 2 * kPStages + 2 * kDStages + 5;
   static constexpr size_t kSmem = 1024 + size_t(kTStages) * kTokBytes +
                                   size_t(kPStages) * kPackedBytes + size_t(kDStages) * kABytes +
@@ -123,8 +125,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   uint8_t* astages = pstages + kPStages * C::kPackedBytes;
   uint8_t* ostage = astages + kDStages * C::kABytes;
   int32_t* row_off = reinterpret_cast<int32_t*>(ostage + C::kOutStageBytes);
-  int32_t* tile_start = row_off + (kMaxGroups + 1);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_start + (kMaxGroups + 1));
+  int32_t* tile_start = row_off + (kSwMaxGroups + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(tile_start + (kSwMaxGroups + 1));
   uint64_t* tok_full = bars;
   uint64_t* tok_empty = tok_full + kTStages;
   uint64_t* pk_full = tok_empty + kTStages;
@@ -153,10 +155,10 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     }
     for (int s = 0; s < kPStages; ++s) {
       mbar_init(smem_u32(pk_full + s), 1);
-      mbar_init(smem_u32(pk_empty + s), kDeqWarps);  // one arrival per dequant warp
+      mbar_init(smem_u32(pk_empty + s), kDeqWarps / 2);  // the step's dequant group
     }
     for (int s = 0; s < kDStages; ++s) {
-      mbar_init(smem_u32(a_ready + s), kDeqWarps);  // one arrival per dequant warp
+      mbar_init(smem_u32(a_ready + s), kDeqWarps / 2);  // the step's dequant group
       mbar_init(smem_u32(a_empty + s), 1);  // UMMA commit
     }
     for (int b = 0; b < 2; ++b) {
@@ -288,11 +290,10 @@ __global__ void __launch_bounds__(kSwThreads, 1)
         if (EPI == EPI_SITU) {
           // lanes 2i / 2i+1 hold gate / up of feature i; the even lane
           // finishes tokens 0-15 of the chunk, the odd lane tokens 16-31.
-          // Staged [token][16 features] (32-byte rows; rows 16-31 shifted by
-          // 32 bytes so the two lane halves write different banks).
-          static_assert(C::kWarpStage >= 1088, "SiTU staging");
+          // Staged [token][16 features] (32-byte rows).
+          static_assert(C::kWarpStage >= 1024, "SiTU staging");
           const int odd = lane & 1;
-          uint16_t* s16 = reinterpret_cast<uint16_t*>(stg + odd * 32);
+          uint16_t* s16 = reinterpret_cast<uint16_t*>(stg);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const uint32_t send = odd ? v[j] : v[16 + j];
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           const int tok = tok0 + lane;
           const int f0 = tc.n_tile * (kWRows / 2) + q * 16;
           if (tok < tc.row_end) {
-            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32 + (lane >> 4) * 32);
+            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
             uint16_t* orow =
                 reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
             if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = src[0];
@@ -320,12 +321,12 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           __syncwarp();
         } else {
           // lane = output feature, v[j] = token j.  Stage [token][feature]
-          // rows of 32 features (64 B, or 128 B for f32; f32 goes in two
-          // passes of 16 tokens), 16-byte chunks swizzled by the staged row.
+          // rows of 32 features (64 B, or 128 B for f32) in passes of
+          // kWarpStage bytes, 16-byte chunks swizzled by the staged row.
           constexpr int kRowBytes = 32 * esize;
           constexpr int kChunks = kRowBytes / 16;
           constexpr int kRows = C::kWarpStage / kRowBytes;  // token rows per pass
-          static_assert(kRows == 16 || kRows == 32, "staging rows");
+          static_assert(kRows >= 8 && 32 % kRows == 0, "staging rows");
           const int byte = lane * esize;
           const int f0 = tc.n_tile * kWRows + q * 32;
 #pragma unroll
@@ -388,75 +389,89 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     }
   } else if (warp < 6 + kDeqWarps) {
     // ------------------------------------------------------------ MXFP4 dequant
-    // thread d: A row r = d / 2, K half kh = d % 2 (32 codes = 16 packed bytes,
-    // one E8M0 block) -> 4 16-byte chunks of the 128-byte swizzled row
-    // (chunk c of row r lands in slot c ^ (r & 7)).  The codes are read (and
-    // their packed slot released) before waiting for a free A slot.
-    const int d = threadIdx.x - 192;
-    const int r = d >> 1;
-    const int kh = d & 1;
+    // The CTA's K steps form one sequence (its tiles in schedule order, num_kb
+    // steps each).  Two groups of 4 warps take alternate steps; within a
+    // group, thread i expands A row i: 64 codes (32 packed bytes, two E8M0
+    // blocks) -> the 8 16-byte chunks of its 128-byte swizzled row (chunk c
+    // lands in slot c ^ (r & 7)).  Each group has two MMA steps' time per
+    // step and fences once per step.  The packed and A slots of a step belong
+    // to its group alone (both ring sizes are even), and the group uses them
+    // in order, so the parity waits see their phases in order.
+    // The codes are read (and their packed slot released) before waiting for
+    // a free A slot; the scale bytes of the group's next step are fetched one
+    // step ahead.
+    const int grp = (warp - 6) / 4;
+    const int r = ((warp - 6) % 4) * 32 + lane;
     const int kgroups = args.K / 32;
-    RingPos ps, ds;
-    bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const TileCoord tc = decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, t);
-      const int w_row = weight_row<EPI>(args, tc.n_tile, r);
-      const bool row_in = EPI == EPI_SITU
-                              ? (tc.n_tile * (kWRows / 2) + (r >> 1)) < args.up_offset
-                              : w_row < args.n_weight;
-      const uint8_t* srow =
-          args.scales + (static_cast<int64_t>(tc.g) * args.n_weight + w_row) * kgroups + kh;
-      // the row's scale byte for each K step, fetched kPrefetch steps ahead
-      constexpr int kPrefetch = 4;
-      uint32_t sq[kPrefetch];
+    const int my_tiles = blockIdx.x < static_cast<unsigned>(total)
+                             ? (total - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x
+                             : 0;
+    const int n_steps = my_tiles * num_kb;
+    // scale row of A row r for the tile of the last looked-up step (decoded
+    // once per tile); nullptr when the row lies past the weight
+    int cached_tile = -1;
+    const uint16_t* srow = nullptr;
+    auto load_scale = [&](int st) -> uint32_t {  // two scale bytes of row r for step st
+      const int ti = st / num_kb;
+      if (ti != cached_tile) {
+        cached_tile = ti;
+        const TileCoord tc =
+            decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, blockIdx.x + ti * gridDim.x);
+        const int w_row = weight_row<EPI>(args, tc.n_tile, r);
+        const bool row_in = EPI == EPI_SITU
+                                ? (tc.n_tile * (kWRows / 2) + (r >> 1)) < args.up_offset
+                                : w_row < args.n_weight;
+        srow = row_in ? reinterpret_cast<const uint16_t*>(
+                            args.scales +
+                            (static_cast<int64_t>(tc.g) * args.n_weight + w_row) * kgroups)
+                      : nullptr;
+      }
+      return srow != nullptr ? __ldg(srow + (st - ti * num_kb)) : 0x7F7Fu;
+    };
+    // expand step st (scale bytes sc, loaded two of the group's steps earlier)
+    auto expand = [&](int st, uint32_t sc) -> bool {
+      const uint32_t pslot = st % kPStages, pph = (st / kPStages) & 1;
+      if (!mbar_wait(smem_u32(pk_full + pslot), pph, abort_flag, args.status)) return false;
+      const uint4* src = reinterpret_cast<const uint4*>(pstages + pslot * C::kPackedBytes +
+                                                        packed_row<EPI>(r) * (kBK / 2));
+      const uint4 p0 = src[0], p1 = src[1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(pk_empty + pslot));
+      const uint32_t aslot = st % kDStages, aph = (st / kDStages) & 1;
+      if (!mbar_wait(smem_u32(a_empty + aslot), aph ^ 1u, abort_flag, args.status)) return false;
+      const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      uint8_t* arow = astages + aslot * C::kABytes + r * 128;
+      if (kF16) {
+        const uint32_t b0 = e8m0_to_f16_bits(sc & 0xFFu), b1 = e8m0_to_f16_bits(sc >> 8);
+        const uint32_t s0 = b0 | (b0 << 16), s1 = b1 | (b1 << 16);
 #pragma unroll
-      for (int j = 0; j < kPrefetch; ++j)
-        sq[j] = (row_in && j < num_kb) ? __ldg(srow + 2 * j) : 127u;
-      for (int kb0 = 0; kb0 < num_kb && ok; kb0 += kPrefetch)
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
+              dequant_e2m1x8_f16(words[c], c < 4 ? s0 : s1);
+      } else {
+        const uint32_t b0 = e8m0_to_bf16_bits(sc & 0xFFu), b1 = e8m0_to_bf16_bits(sc >> 8);
+        const uint32_t s0 = b0 | (b0 << 16), s1 = b1 | (b1 << 16);
 #pragma unroll
-        for (int j = 0; j < kPrefetch; ++j) {
-          const int kb = kb0 + j;
-          if (kb >= num_kb) break;
-          const uint32_t s = sq[j];
-          if (kb + kPrefetch < num_kb) sq[j] = row_in ? __ldg(srow + 2 * (kb + kPrefetch)) : 127u;
-          if (!mbar_wait(smem_u32(pk_full + ps.stage), ps.phase, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          const uint4 pk = *reinterpret_cast<const uint4*>(
-              pstages + ps.stage * C::kPackedBytes + packed_row<EPI>(r) * (kBK / 2) + kh * 16);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(pk_empty + ps.stage));
-          ps.next<kPStages>();
-          if (!mbar_wait(smem_u32(a_empty + ds.stage), ds.phase ^ 1u, abort_flag, args.status)) {
-            ok = false;
-            break;
-          }
-          const uint32_t words[4] = {pk.x, pk.y, pk.z, pk.w};
-          uint8_t* arow = astages + ds.stage * C::kABytes + r * 128;
-          if (kF16) {
-            const uint32_t b = e8m0_to_f16_bits(s);
-            const uint32_t sc = b | (b << 16);
-#pragma unroll
-            for (int j2 = 0; j2 < 4; ++j2) {
-              const uint4 o = dequant_e2m1x8_f16(words[j2], sc);
-              *reinterpret_cast<uint4*>(arow + (((kh * 4 + j2) ^ (r & 7)) << 4)) = o;
-            }
-          } else {
-            const uint32_t b = e8m0_to_bf16_bits(s);
-            const uint32_t sc = b | (b << 16);
-#pragma unroll
-            for (int j2 = 0; j2 < 4; ++j2) {
-              const uint4 o =
-                  dequant_e2m1x8(words[j2], *reinterpret_cast<const __nv_bfloat162*>(&sc));
-              *reinterpret_cast<uint4*>(arow + (((kh * 4 + j2) ^ (r & 7)) << 4)) = o;
-            }
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(a_ready + ds.stage));
-          ds.next<kDStages>();
+        for (int c = 0; c < 8; ++c) {
+          const uint32_t sv = c < 4 ? s0 : s1;
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
+              dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sv));
         }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(a_ready + aslot));
+      return true;
+    };
+    // the group's steps are st0, st0 + 2, ...; scale bytes two steps ahead,
+    // alternating between two registers (no copy that would wait on a load)
+    uint32_t sa = grp < n_steps ? load_scale(grp) : 0x7F7Fu;
+    uint32_t sb = grp + 2 < n_steps ? load_scale(grp + 2) : 0x7F7Fu;
+    for (int st = grp; st < n_steps; st += 4) {
+      if (!expand(st, sa)) break;
+      if (st + 4 < n_steps) sa = load_scale(st + 4);
+      if (st + 2 >= n_steps || !expand(st + 2, sb)) break;
+      if (st + 6 < n_steps) sb = load_scale(st + 6);
     }
   }
 
