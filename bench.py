@@ -44,10 +44,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "LatentMoE layer tokens/s"
 UNIT = "tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram bytes (read + write) per launch of the dominant kernel from the ncu
-# capture summarised in profiles/mxfp4_gateup_situ_config5.md, scaled to one
-# full-size launch; None until that capture exists
-DOMINANT_TRAFFIC_BYTES = None
+# dram bytes (read + write) per launch of the dominant kernel: the ncu capture
+# summarised in profiles/mxfp4_swap_gemm_t8192.md measured 746.5 MB read +
+# 246.5 MB written at 8192 tokens (131072 routed rows); scaled by the routed
+# rows to the 16384-token launch (the weight bytes, about a fifth of it, do
+# not grow with the rows, so this overstates by at most ~12%)
+DOMINANT_TRAFFIC_BYTES = int((746.5e6 + 246.5e6) * 2)
 
 
 def parse_args():
