@@ -142,6 +142,24 @@ LMOE_API int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed,
                                     const int32_t* lhs_row_index, int64_t lhs_src_rows,
                                     int zero_tail, int32_t* dev_status, void* stream);
 
+/* Grouped matmul against e4m3 (float8_e4m3fn) weights with block scales:
+ *   out[r] = lhs[r] @ bf16(f32(rhs_q[g]) * rhs_scale[g][k / block_size])
+ * rhs_q (g, k, n) e4m3 -- the reference's (G, K, N) layout; rhs_scale
+ * (g, k / block_size, 1, n) f32 (one scale per column per K block; block_size
+ * a multiple of 32 dividing k, or k itself).  lhs bf16 (m, k); bf16 or f32
+ * out; the e4m3 tile is expanded to bf16 in shared memory (the dequantised
+ * weight, bit for bit) and multiplied on the tensor cores with f32
+ * accumulation.  k a multiple of 64, n a multiple of 16.  zero_tail as in
+ * lmoe_ragged_dot_bf16.
+ * Replaces PallasMosaicTpuV2RaggedDot()(lhs, rhs, group_sizes=..., rhs_scale=...,
+ * maybe_quantize_lhs=False) (05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:2804-2811,
+ * 2914-2921); its check compares against ragged_dot with the dequantised
+ * bf16 weight (same file, 2815-2827, 2923-2934). */
+LMOE_API int lmoe_fp8_ragged_dot(const void* lhs, const void* rhs_q, const float* rhs_scale,
+                                 const int32_t* group_sizes, void* out, int64_t m, int64_t k,
+                                 int64_t n, int64_t num_groups, int64_t block_size, int out_f32,
+                                 int zero_tail, int32_t* dev_status, void* stream);
+
 /* Elementwise SiTU-GLU: out = dtype(beta*tanh(g/beta)*sigmoid(g) * lb*tanh(u/lb)).
  * gate/up rows have pitch ld_in elements; bf16 = 1 for bf16 I/O, 0 for f32.
  * Replaces _situ_and_mul (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:296-310). */

@@ -523,6 +523,48 @@ def mxfp4_ragged_dot(lhs, weight_packed, weight_scale, group_sizes, dtype="bf16"
 
 
 # ----------------------------------------------------------------------------
+# fp8 (e4m3) block-quantised weights  (KRD:2714-2953)
+# ----------------------------------------------------------------------------
+
+FP8_E4M3_MAX = 448.0  # jnp.finfo(float8_e4m3fn).max
+
+
+def e4m3_round(x: np.ndarray) -> np.ndarray:
+  """float32 -> float8_e4m3fn (round to nearest even, as jnp's astype) -> float32."""
+  return np.asarray(x, np.float32).astype(ml_dtypes.float8_e4m3fn).astype(np.float32)
+
+
+def quantize_fp8_blockwise(rhs: np.ndarray, block_size: int):
+  """The reference's weight quantisation for the rhs_scale API (KRD:2883-2898;
+  block_size = K gives the whole-row form of KRD:2775-2786): per (group,
+  K block, column) scale = absmax / 448 in f32, codes = e4m3(clip(w / scale)).
+  rhs (G, K, N) -> (codes as float32 values (G, K, N), scale (G, K/block, N))."""
+  rhs = np.asarray(rhs, np.float32)
+  g, k, n = rhs.shape
+  nb = k // block_size
+  blocks = rhs.reshape(g, nb, block_size, n)
+  scale = (np.abs(blocks).max(axis=2) / np.float32(FP8_E4M3_MAX)).astype(np.float32)
+  with np.errstate(divide="ignore", invalid="ignore"):
+    q = np.clip(blocks / scale[:, :, None, :], -FP8_E4M3_MAX, FP8_E4M3_MAX)
+  q = e4m3_round(np.nan_to_num(q, nan=0.0))
+  return q.reshape(g, k, n), scale
+
+
+def dequantize_fp8_blockwise(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
+  """bf16(f32(q) * scale) per K block: the dequantised weight the reference
+  compares the quantised op against (KRD:2815, 2923-2924)."""
+  g, k, n = q.shape
+  nb = scale.shape[1]
+  w = q.reshape(g, nb, k // nb, n).astype(np.float32) * scale.reshape(g, nb, 1, n)
+  return bf16_round(w.reshape(g, k, n))
+
+
+def fp8_ragged_dot(lhs, q, scale, group_sizes, dtype="bf16"):
+  """ragged_dot(lhs, dequantize_fp8_blockwise(q, scale)) (KRD:2816-2821, 2925-2931)."""
+  return ragged_dot(lhs, dequantize_fp8_blockwise(q, scale), group_sizes, dtype=dtype)
+
+
+# ----------------------------------------------------------------------------
 # comparison metrics  (05_ragged_dot_on_tpu/hw_session_common.py:193-225)
 # ----------------------------------------------------------------------------
 

@@ -59,3 +59,31 @@ def test_mxfp4_ragged_dot_matches_dense_loop():
   assert np.allclose(out[:5], lhs[:5] @ w0.T, atol=1e-5)
   assert np.allclose(out[5:12], lhs[5:12] @ w2.T, atol=1e-5)
   assert np.all(out[12:] == 0)
+
+
+def test_fp8_blockwise_quantisation_round_trip():
+  """The restated rhs_scale quantisation (KRD:2883-2898): codes are e4m3
+  values within +-448, every block's absmax maps to 448, and the dequantised
+  weight is within e4m3's relative step (2^-3 of the block absmax) of the
+  input."""
+  rng = np.random.default_rng(11)
+  w = (rng.standard_normal((3, 256, 96)) * 0.02).astype(np.float32)
+  for block in (32, 256):
+    q, scale = O.quantize_fp8_blockwise(w, block)
+    assert q.shape == w.shape and scale.shape == (3, 256 // block, 96)
+    assert np.array_equal(O.e4m3_round(q), q)
+    assert float(np.abs(q).max()) == 448.0
+    d = O.dequantize_fp8_blockwise(q, scale)
+    blocks = np.abs(w.reshape(3, 256 // block, block, 96)).max(axis=2)
+    bound = np.repeat(blocks, block, axis=1).reshape(w.shape) * (2.0 ** -3) + 1e-8
+    assert np.all(np.abs(d - w) <= bound)
+
+
+def test_fp8_ragged_dot_is_ragged_dot_on_the_dequantised_weight():
+  rng = np.random.default_rng(12)
+  w = (rng.standard_normal((2, 64, 32)) * 0.02).astype(np.float32)
+  q, scale = O.quantize_fp8_blockwise(w, 32)
+  lhs = O.bf16_round(rng.standard_normal((10, 64)).astype(np.float32))
+  gs = np.array([7, 3], np.int32)
+  ref = O.ragged_dot(lhs, O.dequantize_fp8_blockwise(q, scale), gs, dtype="fp32")
+  assert np.array_equal(O.fp8_ragged_dot(lhs, q, scale, gs, dtype="fp32"), ref)

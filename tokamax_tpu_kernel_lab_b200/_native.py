@@ -40,6 +40,8 @@ SIGNATURES = {
                                      _p, _p]),
     "lmoe_mxfp4_gateup_situ": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _f32,
                                       _i32, _i32, _i32, _p, _i64, _i32, _p, _p]),
+    "lmoe_fp8_ragged_dot": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i32,
+                                   _p, _p]),
     "lmoe_situ_and_mul": (_i32, [_p, _p, _i64, _p, _i64, _i64, _f32, _f32, _i32, _p]),
     "lmoe_router_topk": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
     "lmoe_dispatch_workspace_size": (_sz, [_i64, _i64]),

@@ -83,6 +83,14 @@ int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed, const voi
                                   dev_status, S(stream), lhs_row_index, lhs_src_rows);
 }
 
+int lmoe_fp8_ragged_dot(const void* lhs, const void* rhs_q, const float* rhs_scale,
+                        const int32_t* group_sizes, void* out, int64_t m, int64_t k, int64_t n,
+                        int64_t num_groups, int64_t block_size, int out_f32, int zero_tail,
+                        int32_t* dev_status, void* stream) {
+  return lmoe::grouped_gemm_fp8(lhs, rhs_q, rhs_scale, group_sizes, out, m, k, n, num_groups,
+                                block_size, out_f32, zero_tail, dev_status, S(stream));
+}
+
 int lmoe_situ_and_mul(const void* gate, const void* up, int64_t ld_in, void* out, int64_t rows,
                       int64_t intermediate, float beta, float linear_beta, int bf16, void* stream) {
   return lmoe::situ_and_mul(gate, up, ld_in, out, rows, intermediate, beta, linear_beta, bf16,

@@ -25,9 +25,14 @@ enum EpiKind { EPI_BF16 = 0, EPI_F32 = 1, EPI_BF16_ADD = 2, EPI_SITU = 3 };
 // codes are expanded with the hardware e2m1x2 -> f16x2 conversion; the UMMA
 // runs kind::f16 with f16 operands.  The f16 scale 2^(s-127) and every scaled
 // code stay exact for scale bytes in [104, 140] (the caller checks the range).
-enum BFmt { B_KMAJOR = 0, B_NMAJOR = 1, B_MXFP4 = 2, B_MXFP4F16 = 3 };
+// B_FP8: e4m3 weights in the reference's (G, K, N) layout with one f32 scale
+// per (group, K block, column), expanded to bf16 (the dequantised weight
+// bf16(q * scale)) into the MN-major UMMA operand.
+enum BFmt { B_KMAJOR = 0, B_NMAJOR = 1, B_MXFP4 = 2, B_MXFP4F16 = 3, B_FP8 = 4 };
 
 __host__ __device__ constexpr bool is_mx(int bf) { return bf == B_MXFP4 || bf == B_MXFP4F16; }
+// formats whose B operand is expanded in shared memory by dequant warps
+__host__ __device__ constexpr bool is_expand(int bf) { return is_mx(bf) || bf == B_FP8; }
 
 struct GemmArgs {
   const int32_t* group_sizes;  // nullptr: a single group of M rows
@@ -50,6 +55,8 @@ struct GemmArgs {
   // read directly (row r of the map).
   const int32_t* a_rows;
   int a_src_rows;
+  // B_FP8: f32 scales (G, n_blocks, N) at `scales`, one per block_size rows of K
+  int block_size, n_blocks;
 };
 
 // Shared-memory pipeline.  bf16 B: STAGES load stages of [A | B].  MXFP4 B:

@@ -55,12 +55,12 @@ constexpr int kBM = 128;
 
 template <int BN, int STAGES, int BF, int EPI>
 struct GemmCfg {
-  static constexpr int kThreads = is_mx(BF) ? 448 : 192;
+  static constexpr int kThreads = is_expand(BF) ? 448 : 192;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kPackedBytes = is_mx(BF) ? BN * (kBK / 2) : 0;
-  static constexpr int kStageBytes = kABytes + (is_mx(BF) ? kPackedBytes : kBBytes);
-  static constexpr int kDStages = is_mx(BF) ? 2 : 0;
+  static constexpr int kPackedBytes = is_mx(BF) ? BN * (kBK / 2) : (BF == B_FP8 ? BN * kBK : 0);
+  static constexpr int kStageBytes = kABytes + (is_expand(BF) ? kPackedBytes : kBBytes);
+  static constexpr int kDStages = is_expand(BF) ? 2 : 0;
   static constexpr int kDAlloc = kDStages > 0 ? kDStages : 1;  // barrier slots
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kSchedBytes = 2 * (kMaxGroups + 1) * 4 + 2 * kThreads * 4;
@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using C = GemmCfg<BN, STAGES, BF, EPI>;
-  constexpr bool kMx = is_mx(BF);
+  constexpr bool kMx = is_expand(BF);  // B expanded by the dequant warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -194,6 +194,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                             kb * kBK, tc.g);
             } else if (BF == B_KMAJOR) {
               tma_load_3d(b_dst + h * (BN / 2) * 128, &tmB, fb, kb * kBK, nbase, tc.g);
+            } else if (BF == B_FP8) {
+              // one box: BN columns (bytes) x 64 K rows of the (G, K, N) e4m3 weight
+              if (h == 0) tma_load_3d(p_dst, &tmB, fb, tc.n_tile * BN, kb * kBK, tc.g);
             } else {
               tma_load_3d(p_dst + h * (BN / 2) * (kBK / 2), &tmB, fb, kb * (kBK / 2), nbase, tc.g);
             }
@@ -215,8 +218,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = (BF == B_MXFP4F16) ? idesc_f16_f32(kBM, BN, false)
-                                                    : idesc_bf16_f32(kBM, BN, BF == B_NMAJOR);
+      constexpr uint32_t idesc = (BF == B_MXFP4F16)
+                                     ? idesc_f16_f32(kBM, BN, false)
+                                     : idesc_bf16_f32(kBM, BN, BF == B_NMAJOR || BF == B_FP8);
       uint32_t stage = 0, phase = 0, dstage = 0, dphase = 0;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
@@ -239,7 +243,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = (BF == B_NMAJOR)
+            const uint64_t bdesc = (BF == B_NMAJOR || BF == B_FP8)
                                        ? smem_desc_sw128(b_addr + k * 2048, kBK * 128, 1024)
                                        : smem_desc_sw128(b_addr + k * 32, 16, 1024);
             umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
@@ -384,6 +388,86 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
             make_uint4(0, 0, 0, 0);
       }
     }
+  } else if (BF == B_FP8) {
+    // ------------------------------------------------------------ fp8 expansion
+    // The TMA stage holds the (64 K x BN) e4m3 tile, row k = BN bytes.  Thread d
+    // expands columns n = 8 (d % 32) .. +7 of rows k = d / 32 + 8 i (i < 8):
+    // bf16(f32(q) * scale[block(k)][n]) -- the reference's dequantised weight
+    // -- written into the MN-major 128B-swizzled operand: 64-column chunks of
+    // 64 rows x 128 B, the 16-byte group j of row k at slot j ^ (k & 7).
+    const int d = threadIdx.x - 192;
+    const int nc = d & 31;
+    const int k0 = d >> 5;
+    const int chunk = nc >> 3, sub = nc & 7;
+    const float* scales = reinterpret_cast<const float*>(args.scales);
+    uint32_t stage = 0, phase = 0, dstage = 0, dphase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      const TileCoord tc = decode_tile<kBM>(tile_start, row_off, G, args.n_tiles, t);
+      const int n0 = tc.n_tile * BN + nc * 8;
+      const bool col_in = n0 < args.N;
+      const float* sg = scales + static_cast<int64_t>(tc.g) * args.n_blocks * args.N + n0;
+      for (int kb = 0; kb < num_kb && ok; ++kb) {
+        // scales of the (at most two) K blocks this step's rows fall in
+        const int b_lo = (kb * kBK) / args.block_size;
+        const int b_hi = (kb * kBK + kBK - 1) / args.block_size;
+        float4 s_lo[2], s_hi[2];
+        if (col_in) {
+          s_lo[0] = __ldg(reinterpret_cast<const float4*>(sg + static_cast<int64_t>(b_lo) * args.N));
+          s_lo[1] = __ldg(reinterpret_cast<const float4*>(sg + static_cast<int64_t>(b_lo) * args.N) + 1);
+          s_hi[0] = __ldg(reinterpret_cast<const float4*>(sg + static_cast<int64_t>(b_hi) * args.N));
+          s_hi[1] = __ldg(reinterpret_cast<const float4*>(sg + static_cast<int64_t>(b_hi) * args.N) + 1);
+        } else {
+          s_lo[0] = s_lo[1] = s_hi[0] = s_hi[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status) ||
+            !mbar_wait(smem_u32(bempty + dstage), dphase ^ 1u, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = stages + stage * C::kStageBytes + C::kABytes + nc * 8;
+        uint8_t* dst = dstages + dstage * C::kBBytes + chunk * (kBK * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int k = k0 + 8 * i;
+          const bool hi = (kb * kBK + k) / args.block_size != b_lo;
+          const float sc[8] = {hi ? s_hi[0].x : s_lo[0].x, hi ? s_hi[0].y : s_lo[0].y,
+                               hi ? s_hi[0].z : s_lo[0].z, hi ? s_hi[0].w : s_lo[0].w,
+                               hi ? s_hi[1].x : s_lo[1].x, hi ? s_hi[1].y : s_lo[1].y,
+                               hi ? s_hi[1].z : s_lo[1].z, hi ? s_hi[1].w : s_lo[1].w};
+          const uint2 q = *reinterpret_cast<const uint2*>(src + k * BN);
+          uint32_t h2[4];
+          asm("{\n\t.reg .b16 l0, h0, l1, h1;\n\t"
+              "mov.b32 {l0, h0}, %4;\n\t"
+              "mov.b32 {l1, h1}, %5;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %0, l0;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %1, h0;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %2, l1;\n\t"
+              "cvt.rn.f16x2.e4m3x2 %3, h1;\n\t}"
+              : "=r"(h2[0]), "=r"(h2[1]), "=r"(h2[2]), "=r"(h2[3])
+              : "r"(q.x), "r"(q.y));
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2[e]));
+            o[e] = pack_bf16x2(f.x * sc[2 * e], f.y * sc[2 * e + 1]);
+          }
+          *reinterpret_cast<uint4*>(dst + k * 128 + ((sub ^ (k & 7)) << 4)) =
+              make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(bready + dstage));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+        if (++dstage == C::kDAlloc) {
+          dstage = 0;
+          dphase ^= 1u;
+        }
+      }
+    }
   } else if (kMx) {
     // ------------------------------------------------------------ MXFP4 dequant
     // thread i of the 256 dequant threads expands row i of the B tile: 64 K
@@ -494,6 +578,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
 
 constexpr int kStagesBf16 = 4;
 constexpr int kStagesMx = 5;
+constexpr int kStagesFp8 = 4;
 
 template <int EPI>
 int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
@@ -502,6 +587,11 @@ int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const 
     case B_NMAJOR: return launch_gemm<256, kStagesBf16, B_NMAJOR, EPI>(ta, tb, a, max_tiles, s);
     case B_KMAJOR: return launch_gemm<256, kStagesBf16, B_KMAJOR, EPI>(ta, tb, a, max_tiles, s);
     case B_MXFP4F16: return launch_gemm<256, kStagesMx, B_MXFP4F16, EPI>(ta, tb, a, max_tiles, s);
+    case B_FP8:
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32)
+        return launch_gemm<256, kStagesFp8, B_FP8, EPI>(ta, tb, a, max_tiles, s);
+      else
+        return kUnsupported;
     default: return launch_gemm<256, kStagesMx, B_MXFP4, EPI>(ta, tb, a, max_tiles, s);
   }
 }
@@ -656,6 +746,35 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
   a.a_rows = a_rows;
   a.a_src_rows = static_cast<int>(a_src_rows);
   return launch_epi(epi, lhs_f16 ? B_MXFP4F16 : B_MXFP4, ta, tb, a, max_tiles_of(a), stream);
+}
+
+
+// e4m3 weights (G, K, N) -- the reference's layout -- with f32 scales
+// (G, K / block_size, N): out = lhs @ bf16(f32(q) * scale) per group.
+int grouped_gemm_fp8(const void* lhs, const void* rhs_q, const float* rhs_scale,
+                     const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N,
+                     int64_t G, int64_t block_size, int out_f32, int zero_tail, int32_t* status,
+                     cudaStream_t stream) {
+  const int epi = out_f32 ? EPI_F32 : EPI_BF16;
+  int rc = common_checks(lhs, out, M, K, N, G, epi, nullptr, 0, 0);
+  if (rc != kOk) return rc;
+  if (group_sizes == nullptr || rhs_q == nullptr || rhs_scale == nullptr) return kBadShape;
+  if (K % kBK != 0 || block_size <= 0 || block_size % 32 != 0 || K % block_size != 0)
+    return kUnsupported;
+  if ((reinterpret_cast<uintptr_t>(rhs_q) | reinterpret_cast<uintptr_t>(rhs_scale)) & 15)
+    return kUnsupported;
+  if (N % 16 != 0) return kUnsupported;  // 16-byte TMA rows of the (K, N) e4m3 weight
+  if (M == 0) return kOk;
+  CUtensorMap ta, tb;
+  if (!encode_a(&ta, lhs, M, K, nullptr, 0)) return kLaunchFailed;
+  // dims {N bytes, K, G}, box {256 columns, 64 K rows}
+  if (!encode_tmap_u8_3d(&tb, rhs_q, N, K, G, N, N * K, 256, kBK)) return kLaunchFailed;
+  GemmArgs a = make_args(group_sizes, out, nullptr, 0, M, K, N, G, epi, 0, N, 0.f, 0.f, 0,
+                         zero_tail, status);
+  a.scales = reinterpret_cast<const uint8_t*>(rhs_scale);
+  a.block_size = static_cast<int>(block_size);
+  a.n_blocks = static_cast<int>(K / block_size);
+  return launch_epi(epi, B_FP8, ta, tb, a, max_tiles_of(a), stream);
 }
 
 }  // namespace lmoe

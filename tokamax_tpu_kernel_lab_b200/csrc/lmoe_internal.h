@@ -36,6 +36,11 @@ int grouped_gemm_mxfp4(const void* lhs, const void* packed, const void* scales,
                        int32_t* status, cudaStream_t stream, const int32_t* a_rows = nullptr,
                        int64_t a_src_rows = 0);
 
+int grouped_gemm_fp8(const void* lhs, const void* rhs_q, const float* rhs_scale,
+                     const int32_t* group_sizes, void* out, int64_t M, int64_t K, int64_t N,
+                     int64_t G, int64_t block_size, int out_f32, int zero_tail, int32_t* status,
+                     cudaStream_t stream);
+
 inline int current_device() {
   int d = 0;
   cudaGetDevice(&d);

@@ -13,6 +13,8 @@ Reference interfaces mirrored (paths relative to the reference project):
   router_gate                 kimi_k3_latent_moe_reference.py:347-356 / 601-631
   filter_and_pad_to_shard_jittable   kimi_k3_latent_moe_reference.py:754-877
   combine_shard_contribution  kimi_k3_latent_moe_reference.py:1113-1141
+  fp8_ragged_dot / RaggedDotOp  PallasMosaicTpuV2RaggedDot()(..., rhs_scale=...)
+                              kimi_k3_latent_moe_ragged_dot.py:2714-2953
 """
 
 from __future__ import annotations
@@ -260,6 +262,62 @@ def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
                int(res.dtype == torch.float16), _ptr(ri), src_rows, int(zero_tail),
                _ptr(device_status(lhs.device)), _stream())
   return res
+
+
+def fp8_ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor,
+                   rhs_scale: torch.Tensor, *, preferred_element_type: torch.dtype | None = None,
+                   out: torch.Tensor | None = None, zero_tail: bool = True) -> torch.Tensor:
+  """lhs (M, K) bf16 @ bf16(f32(rhs[g]) * rhs_scale[g]) per group, with rhs
+  (G, K, N) float8_e4m3fn and rhs_scale (G, K / block, 1, N) (or (G, K / block,
+  N)) float32 -- the quantised-weight form of PallasMosaicTpuV2RaggedDot
+  (kimi_k3_latent_moe_ragged_dot.py:2804-2811).  The e4m3 tiles are expanded
+  to the dequantised bf16 weight inside the kernel."""
+  _need_cuda(lhs, rhs, group_sizes, rhs_scale)
+  if lhs.dtype != torch.bfloat16:
+    raise NotImplementedError(f"lhs dtype {lhs.dtype}: bf16 only")
+  if rhs.dtype not in (torch.float8_e4m3fn, torch.uint8):
+    raise NotImplementedError(f"rhs dtype {rhs.dtype}: float8_e4m3fn only")
+  g, k, n = rhs.shape
+  m = lhs.shape[0]
+  if lhs.shape[1] != k or group_sizes.shape != (g,):
+    raise ValueError("shape mismatch")
+  scale = rhs_scale.reshape(g, -1, n) if rhs_scale.dim() == 4 else rhs_scale
+  if scale.dim() != 3 or scale.shape[0] != g or scale.shape[2] != n or k % scale.shape[1]:
+    raise ValueError(f"rhs_scale shape {tuple(rhs_scale.shape)} does not match rhs {tuple(rhs.shape)}")
+  if scale.dtype != torch.float32:
+    raise NotImplementedError("rhs_scale must be float32")
+  block = k // scale.shape[1]
+  out_dtype = preferred_element_type or torch.bfloat16
+  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  _native.call("lmoe_fp8_ragged_dot", _ptr(lhs.contiguous()), _ptr(rhs.contiguous()),
+               _ptr(scale.contiguous()), _ptr(group_sizes.to(torch.int32).contiguous()),
+               _ptr(res), m, k, n, g, block, int(res.dtype == torch.float32), int(zero_tail),
+               _ptr(device_status(lhs.device)), _stream())
+  return res
+
+
+class RaggedDotOp:
+  """Instance-call form of the grouped matmul, mirroring
+  `PallasMosaicTpuV2RaggedDot()(lhs, rhs, *, group_sizes, rhs_scale=None,
+  fuse_gateup_activation=None, maybe_quantize_lhs=False)`
+  (kimi_k3_latent_moe_ragged_dot.py:257-263, 713-723, 2804-2811): the keyword
+  arguments the public ragged_dot does not take."""
+
+  def __call__(self, lhs: torch.Tensor, rhs: torch.Tensor, *, group_sizes: torch.Tensor,
+               rhs_scale: torch.Tensor | None = None, fuse_gateup_activation: str | None = None,
+               maybe_quantize_lhs: bool = False, preferred_element_type=None) -> torch.Tensor:
+    if maybe_quantize_lhs:
+      raise NotImplementedError("maybe_quantize_lhs=True: activations stay bf16 on this path")
+    if rhs_scale is not None:
+      if fuse_gateup_activation is not None:
+        raise NotImplementedError("fused activation with quantised weights")
+      return fp8_ragged_dot(lhs, rhs, group_sizes, rhs_scale,
+                            preferred_element_type=preferred_element_type)
+    if fuse_gateup_activation is not None:
+      beta, linear_beta = parse_fused_activation(fuse_gateup_activation)
+      return fused_gateup_situ(lhs, rhs, group_sizes, beta=beta, linear_beta=linear_beta,
+                               round_gate_up=False)
+    return ragged_dot(lhs, rhs, group_sizes, preferred_element_type=preferred_element_type)
 
 
 def parse_fused_activation(spec: str) -> tuple[float, float]:
