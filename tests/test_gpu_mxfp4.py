@@ -178,3 +178,22 @@ def test_mxfp4_gateup_with_row_gather(lm, f16):
   ref = O.fused_gateup_situ(rows, O.LazyMXFP4Experts(packed, scale), gs, inter, 4.0, 25.0,
                             dtype="bf16", out_dtype="fp32")
   assert_bf16_close(ref, to_np(out), f"mxfp4 gather f16={f16}")
+
+
+def test_checkpoint_layer_runs_identically(lm, tmp_path):
+  """A layer exported in the checkpoint's key layout (safetensors) and loaded
+  back gives the same forward bits as the in-memory weights."""
+  from safetensors.torch import save_file
+  from tokamax_tpu_kernel_lab_b200 import checkpoint as ck
+  cfg = lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+  pw = lm.init_prepared_mxfp4(cfg, seed=8, bias_std=0.5)
+  path = tmp_path / "layer7.safetensors"
+  save_file(ck.layer_state_dict(pw, 7, cfg), str(path))
+  loaded = ck.load_latent_moe_layer(path, 7, cfg, device="cuda")
+  gen = torch.Generator(device="cuda").manual_seed(8)
+  h = torch.randn(256, 1024, generator=gen, device="cuda").to(torch.bfloat16)
+  a = lm.latent_moe_forward(h, pw, cfg)
+  b = lm.latent_moe_forward(h, loaded, cfg)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  assert torch.equal(a, b)
