@@ -63,7 +63,7 @@ def parse_args():
   p.add_argument("--cpu-sample-tokens", type=int, default=16)
   p.add_argument("--no-cpu-baseline", action="store_true")
   p.add_argument("--no-graph", action="store_true",
-                 help="time eager launches instead of a captured CUDA graph (one GPU)")
+                 help="time eager launches instead of a captured CUDA graph")
   p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                  help="expert-parallel exchange (N>1): NVLink peer-memory puts or NCCL all-to-all")
   return p.parse_args()
@@ -81,7 +81,8 @@ def config_dict(args, world):
       "exchange": ("nvlink peer-memory puts" if args.exchange == "peer" else
                    "nccl all_to_all_single") if world > 1 else None,
       "l2": "working set (3.2 GB weights) > 126 MB L2; no flush between steps",
-      "launch": ("cuda graph replay" if world == 1 and not args.no_graph else "eager"),
+      "launch": ("cuda graph replay" if (world == 1 or args.exchange == "peer") and not args.no_graph
+                 else "eager"),
   }
 
 
@@ -308,13 +309,13 @@ def main():
   torch.cuda.synchronize()
   ops.check_device_status()
 
-  # One GPU: the forward is captured once as a CUDA graph and replayed, so the
-  # timed steps do not depend on host launch speed (every kernel still runs
-  # every step).  Expert parallelism runs eagerly (the exchange epochs and the
-  # NCCL form's count read live on the host).
+  # The forward is captured once as a CUDA graph and replayed, so the timed
+  # steps do not depend on host launch speed (every kernel still runs every
+  # step).  The peer-memory exchange is capturable (its epoch lives on the
+  # device); the NCCL form reads its counts on the host and runs eagerly.
   graph = None
   launches_per_step = None
-  if world == 1 and not args.no_graph:
+  if (world == 1 or xchg is not None) and not args.no_graph:
     graph = torch.cuda.CUDAGraph()
     launches_cap = _native.launch_count
     with torch.cuda.graph(graph):

@@ -258,8 +258,9 @@ LMOE_API int lmoe_ep_reorder(const int32_t* recv_counts, int64_t world, int64_t 
 /* Expert-parallel exchange over NVLink peer memory (one process per GPU).
  * peers_dev is a device array of `world` pointers to every rank's symmetric
  * buffer of lmoe_ep_buffer_bytes(...) bytes (same layout on every rank; index
- * `rank` = this rank's own buffer); every call of one exchange passes the same
- * epoch on every rank, one larger than the previous exchange's.  Rank r owns
+ * `rank` = this rank's own buffer).  Each counts exchange advances an epoch
+ * word kept in the buffer itself (every rank runs the same exchanges, so the
+ * epochs agree; the calls are capturable in a CUDA graph).  Rank r owns
  * global experts [r*E/world, (r+1)*E/world).  Sequence per forward:
  *   lmoe_ep_exchange_counts  publish this rank's per-expert row counts
  *                            (group_sizes, E int32, from lmoe_dispatch over all E
@@ -297,17 +298,17 @@ LMOE_API int64_t lmoe_ep_region_offset(int64_t world, int64_t num_experts,
 LMOE_API int lmoe_ep_exchange_counts(void* const* peers_dev, int64_t rank, int64_t world,
                                      int64_t num_experts, int64_t recv_capacity_rows,
                                      int64_t back_capacity_rows, int64_t row_bytes,
-                                     uint32_t epoch, const int32_t* group_sizes,
+                                     const int32_t* group_sizes,
                                      int32_t* local_group_sizes, int32_t* dev_status,
                                      void* stream);
 LMOE_API int lmoe_ep_dispatch_put(void* const* peers_dev, int64_t rank, int64_t world,
                                   int64_t num_experts, int64_t recv_capacity_rows,
-                                  int64_t back_capacity_rows, int64_t row_bytes, uint32_t epoch,
+                                  int64_t back_capacity_rows, int64_t row_bytes,
                                   const void* x, int64_t x_rows, const int32_t* token_idx,
                                   int64_t num_routed_rows, int32_t* dev_status, void* stream);
 LMOE_API int lmoe_ep_return_put(void* const* peers_dev, int64_t rank, int64_t world,
                                 int64_t num_experts, int64_t recv_capacity_rows,
-                                int64_t back_capacity_rows, int64_t row_bytes, uint32_t epoch,
+                                int64_t back_capacity_rows, int64_t row_bytes,
                                 const void* y, int64_t num_rows, int32_t* dev_status,
                                 void* stream);
 

@@ -52,11 +52,27 @@ def _worker(rank, world, port, results, mode="nccl"):
       try:
         outs = [ep_forward_peer(x[rank * t:(rank + 1) * t].contiguous(), backend, cfg, xchg)
                 for x in hs]
+        # the same exchange captured as a CUDA graph, replayed on new inputs
+        static_h = hs[0][rank * t:(rank + 1) * t].clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+          ep_forward_peer(static_h, backend, cfg, xchg)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+          g_out = ep_forward_peer(static_h, backend, cfg, xchg)
+        replays = []
+        for x in hs[:2]:
+          static_h.copy_(x[rank * t:(rank + 1) * t])
+          graph.replay()
+          replays.append(g_out.clone())
         torch.cuda.synchronize()
         lm.check_device_status()
+        del graph
       finally:
         xchg.close()
-      results[rank] = [o.cpu() for o in outs]
+      results[rank] = [o.cpu() for o in outs] + [o.cpu() for o in replays]
       if rank == 0:
         full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
         results["ref"] = [lm.latent_moe_forward(x, full, cfg).cpu() for x in hs]
@@ -99,6 +115,7 @@ def test_ep_forward_peer_bit_exact_vs_single_gpu(world):
   mgr = mp.get_context("spawn").Manager()
   results = mgr.dict()
   mp.spawn(_worker, args=(world, _free_port(), results, "peer"), nprocs=world, join=True)
-  for i, ref in enumerate(results["ref"]):
+  refs = list(results["ref"]) + list(results["ref"])[:2]  # eager x3, then graph replays x2
+  for i, ref in enumerate(refs):
     got = torch.cat([results[r][i] for r in range(world)])
     assert torch.equal(got, ref), f"forward {i}"

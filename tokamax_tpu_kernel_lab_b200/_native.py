@@ -59,12 +59,10 @@ SIGNATURES = {
     "lmoe_ep_buffer_open": (_i32, [_p, _p]),
     "lmoe_ep_buffer_close": (_i32, [_p]),
     "lmoe_ep_buffer_free": (_i32, [_p]),
-    "lmoe_ep_exchange_counts": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32,
-                                       _p, _p, _p, _p]),
-    "lmoe_ep_dispatch_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32, _p,
-                                    _i64, _p, _i64, _p, _p]),
-    "lmoe_ep_return_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, ctypes.c_uint32, _p,
-                                  _i64, _p, _p]),
+    "lmoe_ep_exchange_counts": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "lmoe_ep_dispatch_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p,
+                                    _p]),
+    "lmoe_ep_return_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
 }
 
 # kernels launched by one call of each entry point (for the bench's launch count)

@@ -7,7 +7,8 @@
 //
 // Symmetric buffer layout (same byte offsets on every rank), see ep_layout():
 //   flags   [3][world] u32   epoch of the last (counts, rows, returns) signal from each source
-//   done    [2] u32          grid-completion counters of the two put kernels
+//   done    [3] u32          grid-completion counters of the two put kernels; the
+//                            exchange epoch (bumped by each counts exchange)
 //   counts  [world][E] i32   counts[s][g] = rows source s routes to global expert g
 //   tables  (local use)      base[E], cum[E+1], exp_off[E+1], src_pos[E] (see below)
 //   recv    [recv_cap][row_bytes]   rows this rank's experts receive, expert-major:
@@ -60,13 +61,20 @@ struct EpArgs {
   uint8_t* const* peers;  // device array [world] of symmetric-buffer bases (peers[rank] = own)
   int rank, world, E, n_local;
   int64_t recv_cap, back_cap, row_bytes;
-  uint32_t epoch;
+  uint32_t epoch;  // set on the device from the epoch word
   int32_t* status;
 };
 
 struct EpTablePtrs {
   int32_t *base, *cum, *exp_off, *src_pos;
 };
+
+// this rank's exchange epoch: one more per counts exchange, the same count on
+// every rank (each rank runs the same exchanges), so no host counter is needed
+// and a captured CUDA graph replays correctly
+__device__ __forceinline__ uint32_t* ep_epoch_word(const EpArgs& a, const EpLayout& l) {
+  return reinterpret_cast<uint32_t*>(a.peers[a.rank] + l.done) + 2;
+}
 
 __device__ __forceinline__ EpTablePtrs ep_tables(const EpArgs& a, const EpLayout& l) {
   int32_t* t = reinterpret_cast<int32_t*>(a.peers[a.rank] + l.tables);
@@ -111,6 +119,14 @@ __device__ bool wait_all_sources(const uint32_t* flags, int world, uint32_t epoc
 __global__ void __launch_bounds__(256) ep_counts_kernel(EpArgs a, const int32_t* __restrict__ gs,
                                                         int32_t* __restrict__ local_gs) {
   const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  __shared__ uint32_t epoch;
+  if (threadIdx.x == 0) {
+    uint32_t* w = ep_epoch_word(a, l);
+    epoch = *w + 1u;
+    *w = epoch;
+  }
+  __syncthreads();
+  a.epoch = epoch;
   for (int d = 0; d < a.world; ++d) {
     int32_t* dst = reinterpret_cast<int32_t*>(a.peers[d] + l.counts) + a.rank * a.E;
     for (int g = threadIdx.x; g < a.E; g += blockDim.x) dst[g] = gs[g];
@@ -202,6 +218,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_put_kernel(EpArgs a, const ui
                                                               const int32_t* __restrict__ token_idx,
                                                               int64_t S) {
   const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  a.epoch = *ep_epoch_word(a, l);  // set by this exchange's counts kernel
   const EpTablePtrs t = ep_tables(a, l);
   __shared__ int32_t base[kEpMaxExperts];
   __shared__ int32_t cum[kEpMaxExperts + 1];
@@ -254,6 +271,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_put_kernel(EpArgs a, const ui
 // for this epoch.
 __global__ void ep_wait_kernel(EpArgs a, int which) {
   const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  a.epoch = *ep_epoch_word(a, l);  // set by this exchange's counts kernel
   if (threadIdx.x == 0 && blockIdx.x == 0)
     wait_all_sources(reinterpret_cast<const uint32_t*>(a.peers[a.rank] + l.flags) + which * a.world,
                      a.world, a.epoch, a.status);
@@ -265,6 +283,7 @@ __global__ void ep_wait_kernel(EpArgs a, int which) {
 __global__ void __launch_bounds__(256) ep_return_put_kernel(EpArgs a, const uint8_t* __restrict__ y,
                                                             int64_t R) {
   const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  a.epoch = *ep_epoch_word(a, l);  // set by this exchange's counts kernel
   const EpTablePtrs t = ep_tables(a, l);
   __shared__ int32_t exp_off[kEpMaxExperts + 1];
   __shared__ int32_t src_pos[kEpMaxExperts];
@@ -332,7 +351,7 @@ int grid_for(int64_t rows) {
 }
 
 EpArgs make_ep(void* const* peers, int64_t rank, int64_t world, int64_t E, int64_t recv_cap,
-               int64_t back_cap, int64_t row_bytes, uint32_t epoch, int32_t* status) {
+               int64_t back_cap, int64_t row_bytes, int32_t* status) {
   EpArgs a;
   a.peers = reinterpret_cast<uint8_t* const*>(peers);
   a.rank = static_cast<int>(rank);
@@ -342,7 +361,7 @@ EpArgs make_ep(void* const* peers, int64_t rank, int64_t world, int64_t E, int64
   a.recv_cap = recv_cap;
   a.back_cap = back_cap;
   a.row_bytes = row_bytes;
-  a.epoch = epoch;
+  a.epoch = 0;
   a.status = status;
   return a;
 }
@@ -417,11 +436,11 @@ int64_t lmoe_ep_region_offset(int64_t world, int64_t num_experts, int64_t recv_c
 
 int lmoe_ep_exchange_counts(void* const* peers_dev, int64_t rank, int64_t world,
                             int64_t num_experts, int64_t recv_capacity_rows,
-                            int64_t back_capacity_rows, int64_t row_bytes, uint32_t epoch,
+                            int64_t back_capacity_rows, int64_t row_bytes,
                             const int32_t* group_sizes, int32_t* local_group_sizes,
                             int32_t* dev_status, void* stream) {
   const auto a = lmoe::make_ep(peers_dev, rank, world, num_experts, recv_capacity_rows,
-                               back_capacity_rows, row_bytes, epoch, dev_status);
+                               back_capacity_rows, row_bytes, dev_status);
   int rc = lmoe::check_ep(a);
   if (rc != lmoe::kOk) return rc;
   lmoe::ep_counts_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, group_sizes,
@@ -431,10 +450,10 @@ int lmoe_ep_exchange_counts(void* const* peers_dev, int64_t rank, int64_t world,
 
 int lmoe_ep_dispatch_put(void* const* peers_dev, int64_t rank, int64_t world, int64_t num_experts,
                          int64_t recv_capacity_rows, int64_t back_capacity_rows, int64_t row_bytes,
-                         uint32_t epoch, const void* x, int64_t x_rows, const int32_t* token_idx,
+                         const void* x, int64_t x_rows, const int32_t* token_idx,
                          int64_t num_routed_rows, int32_t* dev_status, void* stream) {
   const auto a = lmoe::make_ep(peers_dev, rank, world, num_experts, recv_capacity_rows,
-                               back_capacity_rows, row_bytes, epoch, dev_status);
+                               back_capacity_rows, row_bytes, dev_status);
   int rc = lmoe::check_ep(a);
   if (rc != lmoe::kOk) return rc;
   if (reinterpret_cast<uintptr_t>(x) & 15) return LMOE_UNSUPPORTED;
@@ -448,10 +467,10 @@ int lmoe_ep_dispatch_put(void* const* peers_dev, int64_t rank, int64_t world, in
 
 int lmoe_ep_return_put(void* const* peers_dev, int64_t rank, int64_t world, int64_t num_experts,
                        int64_t recv_capacity_rows, int64_t back_capacity_rows, int64_t row_bytes,
-                       uint32_t epoch, const void* y, int64_t num_rows, int32_t* dev_status,
+                       const void* y, int64_t num_rows, int32_t* dev_status,
                        void* stream) {
   const auto a = lmoe::make_ep(peers_dev, rank, world, num_experts, recv_capacity_rows,
-                               back_capacity_rows, row_bytes, epoch, dev_status);
+                               back_capacity_rows, row_bytes, dev_status);
   int rc = lmoe::check_ep(a);
   if (rc != lmoe::kOk) return rc;
   if (reinterpret_cast<uintptr_t>(y) & 15) return LMOE_UNSUPPORTED;

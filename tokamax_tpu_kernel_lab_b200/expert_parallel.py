@@ -220,7 +220,6 @@ class PeerExchange:
     self._back = torch.as_tensor(
         _RawDevice(self._own + int(lib.lmoe_ep_region_offset(*geo, 1)), self.back_cap,
                    self.row_bytes), device="cuda")
-    self.epoch = 0
     dist.barrier(group)  # every buffer is zeroed and mapped before the first signal
 
   def _geo(self):
@@ -238,24 +237,25 @@ class PeerExchange:
     """Send row x[token_idx[p]] of every dispatched row p to the owner of its
     expert, run `experts(recv, local_group_sizes)` on the rows this rank
     received, send each result back; returns the returned rows in this rank's
-    dispatch order (token_idx.shape[0] rows)."""
+    dispatch order (token_idx.shape[0] rows).  No host synchronisation: the
+    exchange epoch lives in the device buffer, so a forward that calls this
+    can be captured as a CUDA graph."""
     if x.shape[1] * x.element_size() != self.row_bytes:
       raise ValueError("row width does not match the exchange buffer")
     rows = token_idx.shape[0]
     if rows > self.back_cap or group_sizes.shape[0] != self.E:
       raise ValueError("dispatch does not fit the exchange buffer")
-    self.epoch = (self.epoch + 1) & 0xFFFFFFFF
     status = ops._ptr(ops.device_status(x.device))
     stream = ops._stream()
     geo = self._geo()
-    _native.call("lmoe_ep_exchange_counts", *geo, self.epoch, group_sizes.data_ptr(),
+    _native.call("lmoe_ep_exchange_counts", *geo, group_sizes.data_ptr(),
                  self.local_gs.data_ptr(), status, stream)
-    _native.call("lmoe_ep_dispatch_put", *geo, self.epoch, x.data_ptr(), x.shape[0],
+    _native.call("lmoe_ep_dispatch_put", *geo, x.data_ptr(), x.shape[0],
                  token_idx.data_ptr(), rows, status, stream)
     y = experts(self.recv_rows(x.dtype), self.local_gs)
     if y.shape[1] * y.element_size() != self.row_bytes or not y.is_contiguous():
       raise ValueError("expert output rows do not match the exchange buffer")
-    _native.call("lmoe_ep_return_put", *geo, self.epoch, y.data_ptr(), y.shape[0], status,
+    _native.call("lmoe_ep_return_put", *geo, y.data_ptr(), y.shape[0], status,
                  stream)
     return self.back_rows(rows, y.dtype)
 
