@@ -113,9 +113,54 @@ __device__ bool wait_all_sources(const uint32_t* flags, int world, uint32_t epoc
 }
 
 // --------------------------------------------------------------------------- counts
+// Exclusive prefix sum of v[0..n) in shared memory by the whole block (256
+// threads, n <= 256 * kScanPer); returns the total.
+constexpr int kScanPer = kEpMaxExperts / 256;
+
+__device__ int block_exclusive_scan(int32_t* v, int n) {
+  __shared__ int32_t warp_tot[8];
+  __shared__ int32_t total;
+  const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+  const int b0 = t * kScanPer;
+  int local[kScanPer];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    local[i] = (b0 + i < n) ? v[b0 + i] : 0;
+    sum += local[i];
+  }
+  int inc = sum;  // inclusive scan of the per-thread sums
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) warp_tot[w] = inc;
+  __syncthreads();
+  if (t == 0) {
+    int run = 0;
+    for (int i = 0; i < 8; ++i) {
+      const int x = warp_tot[i];
+      warp_tot[i] = run;
+      run += x;
+    }
+    total = run;
+  }
+  __syncthreads();
+  int run = warp_tot[w] + inc - sum;
+#pragma unroll
+  for (int i = 0; i < kScanPer; ++i) {
+    if (b0 + i < n) v[b0 + i] = run;
+    run += local[i];
+  }
+  __syncthreads();
+  return total;
+}
+
 // One block: publish this rank's per-expert counts into every peer's matrix,
 // signal, wait for every source's counts, then build this rank's offset
-// tables and local group sizes (rows per local expert over all sources).
+// tables and local group sizes (rows per local expert over all sources), all
+// with block-parallel prefix sums over the experts.
 __global__ void __launch_bounds__(256) ep_counts_kernel(EpArgs a, const int32_t* __restrict__ gs,
                                                         int32_t* __restrict__ local_gs) {
   const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
@@ -143,69 +188,84 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpArgs a, const int32_t*
                           a.epoch, a.status);
   __syncthreads();
   const EpTablePtrs t = ep_tables(a, l);
-  const int El = a.n_local, W = a.world;
+  const int El = a.n_local, W = a.world, E = a.E, r = a.rank;
   if (!ok) {
     // timed out: empty tables, so the puts and the expert GEMMs do no work
     for (int e = threadIdx.x; e < El; e += blockDim.x) local_gs[e] = 0;
     if (threadIdx.x == 0) {
-      t.cum[a.E] = 0;
+      t.cum[E] = 0;
       t.exp_off[El * W] = 0;
     }
     return;
   }
   const int32_t* cnt = reinterpret_cast<const int32_t*>(a.peers[a.rank] + l.counts);
-  // sending side: base[g] for every destination d (one thread per d)
-  for (int d = threadIdx.x; d < W; d += blockDim.x) {
-    int run = 0;
-    for (int e = 0; e < El; ++e) {
-      const int g = d * El + e;
-      int before = 0, tot = 0;
-      for (int s = 0; s < W; ++s) {
-        const int c = cnt[s * a.E + g];
-        tot += c;
-        if (s < a.rank) before += c;
+  __shared__ int32_t tot[kEpMaxExperts];     // rows all sources send to expert g -> its scan
+  __shared__ int32_t mine[kEpMaxExperts];    // rows this rank sends to expert g -> its scan
+  __shared__ int32_t before[kEpMaxExperts];  // rows sources < r send to expert g
+  for (int g = threadIdx.x; g < E; g += blockDim.x) {
+    int s_all = 0, s_before = 0;
+    for (int s = 0; s < W; ++s) {
+      const int c = cnt[s * E + g];
+      s_all += c;
+      if (s < r) s_before += c;
+    }
+    tot[g] = s_all;
+    before[g] = s_before;
+    mine[g] = cnt[r * E + g];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < El; e += blockDim.x) local_gs[e] = tot[r * El + e];
+  const int recv_total_all = block_exclusive_scan(tot, E);  // tot -> exclusive scan
+  const int send_total = block_exclusive_scan(mine, E);     // mine -> cum of this rank
+  // sending side: row p of global expert g goes to rank d = g / El at
+  // base[g] + (p - cum[g]) of d's receive region
+  for (int g = threadIdx.x; g < E; g += blockDim.x) {
+    t.base[g] = tot[g] - tot[(g / El) * El] + before[g];
+    t.cum[g] = mine[g];
+  }
+  // receiving side: block (e, s) of this rank's region starts at exp_off[e*W+s]
+  const int g0 = r * El;
+  const int recv_total = (r + 1 < W ? tot[g0 + El] : recv_total_all) - tot[g0];
+  for (int i = threadIdx.x; i < El * W; i += blockDim.x) {
+    const int e = i / W, s = i % W;
+    int pre = 0;
+    for (int s2 = 0; s2 < s; ++s2) pre += cnt[s2 * E + g0 + e];
+    t.exp_off[i] = tot[g0 + e] - tot[g0] + pre;
+  }
+  // src_pos[e*W+s] = rows source s routes to experts below g0 + e (the
+  // dispatch-order position of its rows for this rank's expert e): warp s
+  // reduces row s below g0, then scans it across the El local experts
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int s = warp; s < W; s += blockDim.x / 32) {
+    const int32_t* row = cnt + s * E;
+    int pre = 0;
+    for (int g = lane; g < g0; g += 32) pre += row[g];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, o);
+    int run = pre;
+    for (int e0 = 0; e0 < El; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < El ? row[g0 + e] : 0;
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
       }
-      t.base[g] = run + before;
-      run += tot;
+      if (e < El) t.src_pos[e * W + s] = run + inc - c;
+      run += __shfl_sync(0xffffffffu, inc, 31);
     }
   }
-  // receiving side: src_pos for every source s (one thread per s)
-  for (int s = threadIdx.x; s < W; s += blockDim.x) {
-    int run = 0;
-    const int g0 = a.rank * El;
-    for (int g = 0; g < g0; ++g) run += cnt[s * a.E + g];
-    for (int e = 0; e < El; ++e) {
-      t.src_pos[e * W + s] = run;
-      run += cnt[s * a.E + g0 + e];
-    }
-  }
+  __shared__ int over;
   if (threadIdx.x == 0) {
-    int run = 0;
-    for (int g = 0; g < a.E; ++g) {
-      t.cum[g] = run;
-      run += cnt[a.rank * a.E + g];
-    }
-    t.cum[a.E] = run;
-    run = 0;
-    for (int e = 0; e < El; ++e) {
-      int tot = 0;
-      for (int s = 0; s < W; ++s) {
-        t.exp_off[e * W + s] = run;
-        const int c = cnt[s * a.E + a.rank * El + e];
-        run += c;
-        tot += c;
-      }
-      local_gs[e] = tot;
-    }
-    t.exp_off[El * W] = run;
-    if (run > a.recv_cap || t.cum[a.E] > a.back_cap) {
-      // over capacity: record it and run nothing downstream
-      record_status(a.status, kDeviceBounds);
-      for (int e = 0; e < El; ++e) local_gs[e] = 0;
-      t.cum[a.E] = 0;
-      t.exp_off[El * W] = 0;
-    }
+    over = recv_total > a.recv_cap || send_total > a.back_cap;
+    t.cum[E] = over ? 0 : send_total;
+    t.exp_off[El * W] = over ? 0 : recv_total;
+    if (over) record_status(a.status, kDeviceBounds);  // run nothing downstream
   }
+  __syncthreads();
+  if (over)
+    for (int e = threadIdx.x; e < El; e += blockDim.x) local_gs[e] = 0;
 }
 
 // --------------------------------------------------------------------------- dispatch put

@@ -120,6 +120,28 @@ class GpuBackend:
                                    linear_beta=c.activation_situ_linear_beta, rhs_layout="gnk")
     return _dense(shared, pw.shared_down, addend=upo)
 
+  def shared_expert_buffers(self, h):
+    """(activation, output) buffers of shared_expert for tokens h."""
+    si = self.pw.shared_gu.shape[0] // 2
+    return (torch.empty(h.shape[0], si, dtype=torch.bfloat16, device=h.device),
+            torch.empty(h.shape[0], self.pw.shared_down.shape[0], dtype=torch.bfloat16,
+                        device=h.device))
+
+  def shared_expert(self, h, out=None):
+    """The shared-expert MLP alone (it depends only on h): bf16(situ-glu(h) @ W_sd),
+    into `out` = shared_expert_buffers(h) when given."""
+    c, pw = self.cfg, self.pw
+    act, res = out if out is not None else (None, None)
+    shared = ops.fused_gateup_situ(h, pw.shared_gu, None, beta=c.activation_situ_beta,
+                                   linear_beta=c.activation_situ_linear_beta, rhs_layout="gnk",
+                                   out=act)
+    return ops.gemm(shared, pw.shared_down, rhs_layout="nk", out=res)
+
+  def tail_with_shared(self, normed, shared_out):
+    """bf16(bf16(normed @ W_up) + shared_out): the same bits as tail() (the
+    output sum of KR:435 is one bf16 add of two bf16 terms)."""
+    return _dense(normed, self.pw.up, addend=shared_out)
+
 
 @dataclasses.dataclass
 class EPStats:
@@ -233,13 +255,15 @@ class PeerExchange:
     return self._back[:rows].view(dtype)
 
   def exchange(self, x: torch.Tensor, token_idx: torch.Tensor, group_sizes: torch.Tensor,
-               experts) -> torch.Tensor:
+               experts, after_counts=None) -> torch.Tensor:
     """Send row x[token_idx[p]] of every dispatched row p to the owner of its
     expert, run `experts(recv, local_group_sizes)` on the rows this rank
     received, send each result back; returns the returned rows in this rank's
-    dispatch order (token_idx.shape[0] rows).  No host synchronisation: the
-    exchange epoch lives in the device buffer, so a forward that calls this
-    can be captured as a CUDA graph."""
+    dispatch order (token_idx.shape[0] rows).  `after_counts()` (optional) is
+    called once the counts exchange is enqueued, before the row puts -- the
+    place to fork work that should overlap the NVLink transfers.  No host
+    synchronisation: the exchange epoch lives in the device buffer, so a
+    forward that calls this can be captured as a CUDA graph."""
     if x.shape[1] * x.element_size() != self.row_bytes:
       raise ValueError("row width does not match the exchange buffer")
     rows = token_idx.shape[0]
@@ -250,6 +274,8 @@ class PeerExchange:
     geo = self._geo()
     _native.call("lmoe_ep_exchange_counts", *geo, group_sizes.data_ptr(),
                  self.local_gs.data_ptr(), status, stream)
+    if after_counts is not None:
+      after_counts()
     _native.call("lmoe_ep_dispatch_put", *geo, x.data_ptr(), x.shape[0],
                  token_idx.data_ptr(), rows, status, stream)
     y = experts(self.recv_rows(x.dtype), self.local_gs)
@@ -274,16 +300,41 @@ class PeerExchange:
     self._own = None
 
 
+_side_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(device: torch.device) -> torch.cuda.Stream:
+  idx = device.index if device.index is not None else torch.cuda.current_device()
+  if idx not in _side_streams:
+    _side_streams[idx] = torch.cuda.Stream(device=idx)
+  return _side_streams[idx]
+
+
 def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
                     xchg: PeerExchange) -> torch.Tensor:
   """Expert-parallel forward of this rank's tokens `h` (T_local, d) with the
-  exchange over NVLink peer memory (no host synchronisation)."""
+  exchange over NVLink peer memory (no host synchronisation).  The shared
+  expert depends only on h, so it runs on a side stream forked after the
+  counts exchange, filling the SMs while the row puts wait on NVLink; its
+  buffers are allocated on the main stream before the fork, and the streams
+  join before the output sum."""
+  main = torch.cuda.current_stream(h.device)
+  side = _side_stream(h.device)
   idx, w = backend.route(h)
   x = backend.down(h)
   token_idx, slot_pos, group_sizes = backend.dispatch(idx, w)
-  back = xchg.exchange(x, token_idx, group_sizes, backend.experts_received)
+  bufs = backend.shared_expert_buffers(h)
+
+  def fork_shared():
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+      backend.shared_expert(h, out=bufs)
+
+  back = xchg.exchange(x, token_idx, group_sizes, backend.experts_received,
+                       after_counts=fork_shared)
   normed = backend.combine(back, slot_pos, w)
-  return backend.tail(normed, h)
+  main.wait_stream(side)
+  return backend.tail_with_shared(normed, bufs[1])
 
 
 def shard_experts(pw_full: PreparedWeights, rank: int, world: int) -> PreparedWeights:
