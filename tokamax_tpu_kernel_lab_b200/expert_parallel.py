@@ -300,16 +300,6 @@ class PeerExchange:
     self._own = None
 
 
-_side_streams: dict[int, torch.cuda.Stream] = {}
-
-
-def _side_stream(device: torch.device) -> torch.cuda.Stream:
-  idx = device.index if device.index is not None else torch.cuda.current_device()
-  if idx not in _side_streams:
-    _side_streams[idx] = torch.cuda.Stream(device=idx)
-  return _side_streams[idx]
-
-
 def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
                     xchg: PeerExchange) -> torch.Tensor:
   """Expert-parallel forward of this rank's tokens `h` (T_local, d) with the
@@ -319,7 +309,7 @@ def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
   buffers are allocated on the main stream before the fork, and the streams
   join before the output sum."""
   main = torch.cuda.current_stream(h.device)
-  side = _side_stream(h.device)
+  side = ops.side_stream(h.device)
   idx, w = backend.route(h)
   x = backend.down(h)
   token_idx, slot_pos, group_sizes = backend.dispatch(idx, w)

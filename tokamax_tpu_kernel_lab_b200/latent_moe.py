@@ -227,13 +227,28 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   c = config
   t = h.shape[0]
   inter = {}
+  beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
+  # The shared expert depends only on h: on the bf16 path it runs on a side
+  # stream beside the routing, dispatch and gather kernels (which leave most of
+  # the tensor cores idle) and joins before the output sum, computed as
+  # bf16(bf16(normed @ W_up) + shared) -- the same bits as the other order.
+  overlap = pw.dtype == torch.bfloat16 and not return_intermediates
+  if overlap:
+    main = torch.cuda.current_stream(h.device)
+    side = ops.side_stream(h.device)
+    shared_act = torch.empty(t, pw.shared_gu.shape[0] // 2, dtype=h.dtype, device=h.device)
+    shared_out = torch.empty(t, pw.shared_down.shape[0], dtype=h.dtype, device=h.device)
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+      ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
+                            round_gate_up=True, rhs_layout="gnk", out=shared_act)
+      ops.gemm(shared_act, pw.shared_down, rhs_layout="nk", out=shared_out)
   logits = ops.router_logits(h, pw.router)
   topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
                                      routed_scaling_factor=c.routed_scaling_factor,
                                      activation=router_activation)
   x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw) else None)
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
-  beta, lbeta = c.activation_situ_beta, c.activation_situ_linear_beta
   if pw.expert_gu_mx is not None:
     act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c)
   elif pw.dtype == torch.bfloat16:
@@ -249,6 +264,9 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
     down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
   routed, normed = ops.combine_rmsnorm(down, d.slot_pos, topk_w, pw.norm_scale, c.rms_norm_eps,
                                        want_routed=True)
+  if overlap:
+    main.wait_stream(side)
+    return _dense(normed, pw.up, addend=shared_out)
   upo = _dense(normed, pw.up)
   if pw.dtype == torch.bfloat16:
     shared_act = ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
