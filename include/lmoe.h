@@ -126,6 +126,20 @@ LMOE_API int lmoe_mxfp4_ragged_dot(const void* lhs, const void* weight_packed,
                                    int lhs_f16, int out_f32, int zero_tail, int32_t* dev_status,
                                    void* stream);
 
+/* lmoe_mxfp4_ragged_dot with bf16 output rows stored at arbitrary addresses:
+ * output row r (r < sum(group_sizes)) goes to the byte address row_dest[r]
+ * (uint64 device array of m entries, each 16-byte aligned; a peer GPU's
+ * mapped buffer included), rows past sum(group_sizes) are not written.  The
+ * expert-parallel down projection uses it to write each result straight into
+ * the exchange buffer of the rank the row came from.  Replaces the down
+ * ragged_dot of KRD:367-369 followed by the scatter back of KR:413, in one
+ * kernel. */
+LMOE_API int lmoe_mxfp4_ragged_dot_scatter(const void* lhs, const void* weight_packed,
+                                           const void* weight_scale, const int32_t* group_sizes,
+                                           const uint64_t* row_dest, int64_t m, int64_t k,
+                                           int64_t n, int64_t num_groups, int lhs_f16,
+                                           int32_t* dev_status, void* stream);
+
 /* Fused gate/up + SiTU-GLU against MXFP4 weights: the packed rows are
  * [gate (intermediate rows) | up (intermediate rows)] per group, i.e.
  * (g, 2*intermediate, k/2) codes and (g, 2*intermediate, k/32) scales (the
@@ -311,6 +325,25 @@ LMOE_API int lmoe_ep_return_put(void* const* peers_dev, int64_t rank, int64_t wo
                                 int64_t back_capacity_rows, int64_t row_bytes,
                                 const void* y, int64_t num_rows, int32_t* dev_status,
                                 void* stream);
+
+/* The fused return (an alternative to lmoe_ep_return_put): after
+ * lmoe_ep_dispatch_put, lmoe_ep_return_destinations writes, for each of the
+ * first num_rows received (expert-major) rows, the byte address in its source
+ * rank's return region where that row's result belongs (uint64 device array);
+ * the down-projection GEMM then stores its output rows there directly
+ * (lmoe_mxfp4_ragged_dot_scatter), over NVLink, while it runs; and
+ * lmoe_ep_return_signal tells every source this rank's rows are in place and
+ * waits (bounded) until every rank's rows for this rank have arrived.  No
+ * counterpart in the reference (see above). */
+LMOE_API int lmoe_ep_return_destinations(void* const* peers_dev, int64_t rank, int64_t world,
+                                         int64_t num_experts, int64_t recv_capacity_rows,
+                                         int64_t back_capacity_rows, int64_t row_bytes,
+                                         uint64_t* row_dest, int64_t num_rows,
+                                         int32_t* dev_status, void* stream);
+LMOE_API int lmoe_ep_return_signal(void* const* peers_dev, int64_t rank, int64_t world,
+                                   int64_t num_experts, int64_t recv_capacity_rows,
+                                   int64_t back_capacity_rows, int64_t row_bytes,
+                                   int32_t* dev_status, void* stream);
 
 /* Scatter-add combine of one expert shard:
  *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0

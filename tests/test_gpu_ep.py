@@ -57,11 +57,11 @@ def _worker(rank, world, port, results, mode="nccl"):
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-          ep_forward_peer(static_h, backend, cfg, xchg)
+          ep_forward_peer(static_h, backend, cfg, xchg, fused_return=True)
         torch.cuda.current_stream().wait_stream(side)
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-          g_out = ep_forward_peer(static_h, backend, cfg, xchg)
+        with torch.cuda.graph(graph):  # the fused-return form, captured
+          g_out = ep_forward_peer(static_h, backend, cfg, xchg, fused_return=True)
         replays = []
         for x in hs[:2]:
           static_h.copy_(x[rank * t:(rank + 1) * t])

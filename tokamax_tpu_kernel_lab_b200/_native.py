@@ -40,6 +40,11 @@ SIGNATURES = {
                                      _p, _p]),
     "lmoe_mxfp4_gateup_situ": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32, _f32,
                                       _i32, _i32, _i32, _p, _i64, _i32, _p, _p]),
+    "lmoe_mxfp4_ragged_dot_scatter": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _p,
+                                             _p]),
+    "lmoe_ep_return_destinations": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p,
+                                           _p]),
+    "lmoe_ep_return_signal": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _p]),
     "lmoe_fp8_ragged_dot": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _i32,
                                    _p, _p]),
     "lmoe_situ_and_mul": (_i32, [_p, _p, _i64, _p, _i64, _i64, _f32, _f32, _i32, _p]),

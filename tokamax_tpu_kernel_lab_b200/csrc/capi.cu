@@ -83,6 +83,15 @@ int lmoe_mxfp4_gateup_situ(const void* lhs, const void* weight_packed, const voi
                                   dev_status, S(stream), lhs_row_index, lhs_src_rows);
 }
 
+int lmoe_mxfp4_ragged_dot_scatter(const void* lhs, const void* weight_packed,
+                                  const void* weight_scale, const int32_t* group_sizes,
+                                  const uint64_t* row_dest, int64_t m, int64_t k, int64_t n,
+                                  int64_t num_groups, int lhs_f16, int32_t* dev_status,
+                                  void* stream) {
+  return lmoe::grouped_gemm_mxfp4_scatter(lhs, weight_packed, weight_scale, group_sizes, row_dest,
+                                          m, k, n, num_groups, lhs_f16, dev_status, S(stream));
+}
+
 int lmoe_fp8_ragged_dot(const void* lhs, const void* rhs_q, const float* rhs_scale,
                         const int32_t* group_sizes, void* out, int64_t m, int64_t k, int64_t n,
                         int64_t num_groups, int64_t block_size, int out_f32, int zero_tail,

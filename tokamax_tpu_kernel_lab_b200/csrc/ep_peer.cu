@@ -389,6 +389,57 @@ __global__ void __launch_bounds__(256) ep_return_put_kernel(EpArgs a, const uint
   }
 }
 
+// --------------------------------------------------------------------------- fused return
+// Destination of every received row: expert-major row q (block (e, s),
+// j-th) belongs at position src_pos[e*world+s] + j of source s's return
+// region.  A GEMM given these addresses stores its output rows straight into
+// the sources' buffers over NVLink, so the return needs no copy kernel.
+__global__ void __launch_bounds__(256) ep_row_dest_kernel(EpArgs a, uint64_t* __restrict__ dest,
+                                                          int64_t R) {
+  const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  const EpTablePtrs t = ep_tables(a, l);
+  __shared__ int32_t exp_off[kEpMaxExperts + 1];
+  __shared__ int32_t src_pos[kEpMaxExperts];
+  const int nb = a.n_local * a.world;
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+    exp_off[i] = t.exp_off[i];
+    src_pos[i] = t.src_pos[i];
+  }
+  if (threadIdx.x == 0) exp_off[nb] = t.exp_off[nb];
+  __syncthreads();
+  const int64_t R_eff = R < exp_off[nb] ? R : exp_off[nb];
+  for (int64_t q = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < R_eff;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    int lo = 0, hi = nb - 1;  // last block with exp_off <= q
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (exp_off[mid] <= q) lo = mid; else hi = mid - 1;
+    }
+    const int64_t pos = src_pos[lo] + (q - exp_off[lo]);
+    if (pos >= a.back_cap) {
+      record_status(a.status, kDeviceBounds);
+      dest[q] = reinterpret_cast<uint64_t>(a.peers[a.rank] + l.back);  // a harmless own row
+      continue;
+    }
+    dest[q] = reinterpret_cast<uint64_t>(a.peers[lo % a.world] + l.back + pos * a.row_bytes);
+  }
+}
+
+// One thread: after the kernel that stored this rank's returned rows into the
+// sources' buffers, signal every source, then wait (bounded) until every
+// rank's rows for this rank have landed.
+__global__ void ep_return_signal_kernel(EpArgs a) {
+  const EpLayout l = ep_layout(a.world, a.E, a.recv_cap, a.back_cap, a.row_bytes);
+  a.epoch = *ep_epoch_word(a, l);
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  __threadfence_system();
+  for (int d = 0; d < a.world; ++d)
+    st_release_sys(reinterpret_cast<uint32_t*>(a.peers[d] + l.flags) + 2 * a.world + a.rank,
+                   a.epoch);
+  wait_all_sources(reinterpret_cast<const uint32_t*>(a.peers[a.rank] + l.flags) + 2 * a.world,
+                   a.world, a.epoch, a.status);
+}
+
 // --------------------------------------------------------------------------- host
 
 namespace {
@@ -539,6 +590,34 @@ int lmoe_ep_return_put(void* const* peers_dev, int64_t rank, int64_t world, int6
       a, static_cast<const uint8_t*>(y), num_rows);
   if (cudaGetLastError() != cudaSuccess) return LMOE_LAUNCH_FAILED;
   lmoe::ep_wait_kernel<<<1, 32, 0, s>>>(a, 2);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+int lmoe_ep_return_destinations(void* const* peers_dev, int64_t rank, int64_t world,
+                                int64_t num_experts, int64_t recv_capacity_rows,
+                                int64_t back_capacity_rows, int64_t row_bytes, uint64_t* row_dest,
+                                int64_t num_rows, int32_t* dev_status, void* stream) {
+  const auto a = lmoe::make_ep(peers_dev, rank, world, num_experts, recv_capacity_rows,
+                               back_capacity_rows, row_bytes, dev_status);
+  int rc = lmoe::check_ep(a);
+  if (rc != lmoe::kOk) return rc;
+  if (row_dest == nullptr || num_rows < 0) return LMOE_BAD_SHAPE;
+  const int64_t want = (num_rows + 255) / 256;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 1024)));
+  lmoe::ep_row_dest_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(a, row_dest,
+                                                                                  num_rows);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+int lmoe_ep_return_signal(void* const* peers_dev, int64_t rank, int64_t world,
+                          int64_t num_experts, int64_t recv_capacity_rows,
+                          int64_t back_capacity_rows, int64_t row_bytes, int32_t* dev_status,
+                          void* stream) {
+  const auto a = lmoe::make_ep(peers_dev, rank, world, num_experts, recv_capacity_rows,
+                               back_capacity_rows, row_bytes, dev_status);
+  int rc = lmoe::check_ep(a);
+  if (rc != lmoe::kOk) return rc;
+  lmoe::ep_return_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
 }
 

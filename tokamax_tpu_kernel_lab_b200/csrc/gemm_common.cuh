@@ -57,6 +57,10 @@ struct GemmArgs {
   int a_src_rows;
   // B_FP8: f32 scales (G, n_blocks, N) at `scales`, one per block_size rows of K
   int block_size, n_blocks;
+  // weights-major MXFP4 kernel, plain epilogue: when set, output row r is
+  // stored at the byte address row_dest[r] (any address the GPU can write, a
+  // peer GPU's buffer included) instead of out + r * ldo
+  const uint64_t* row_dest;
 };
 
 // Shared-memory pipeline.  bf16 B: STAGES load stages of [A | B].  MXFP4 B:

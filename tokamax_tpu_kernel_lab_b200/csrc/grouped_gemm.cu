@@ -777,4 +777,29 @@ int grouped_gemm_fp8(const void* lhs, const void* rhs_q, const float* rhs_scale,
   return launch_epi(epi, B_FP8, ta, tb, a, max_tiles_of(a), stream);
 }
 
+
+// MXFP4 grouped matmul whose output row r goes to the byte address
+// row_dest[r] (16-byte aligned; any GPU-writable address, a peer GPU's buffer
+// included) -- the down projection writing straight into the exchange buffers
+// of the ranks the rows came from.  bf16 out, rows past sum(group_sizes) are
+// not written.
+int grouped_gemm_mxfp4_scatter(const void* lhs, const void* packed, const void* scales,
+                               const int32_t* group_sizes, const uint64_t* row_dest, int64_t M,
+                               int64_t K, int64_t N, int64_t G, int lhs_f16, int32_t* status,
+                               cudaStream_t stream) {
+  if (group_sizes == nullptr || row_dest == nullptr || scales == nullptr) return kBadShape;
+  if (M < 0 || K <= 0 || N <= 0 || G <= 0 || G > kSwapMaxGroups) return kBadShape;
+  if (M >= (1ll << 31) || K >= (1ll << 31) || N >= (1ll << 31)) return kBadShape;
+  if (K % 64 != 0 || N % 8 != 0) return kUnsupported;
+  if ((reinterpret_cast<uintptr_t>(lhs) | reinterpret_cast<uintptr_t>(packed)) & 15 ||
+      (reinterpret_cast<uintptr_t>(scales) & 1))
+    return kUnsupported;
+  if (M == 0) return kOk;
+  GemmArgs a = make_args(group_sizes, nullptr, nullptr, 0, M, K, N, G, EPI_BF16, 0, N, 0.f, 0.f, 0,
+                         0, status);
+  a.scales = static_cast<const uint8_t*>(scales);
+  a.row_dest = row_dest;
+  return mxfp4_swap_gemm(lhs, packed, a, EPI_BF16, lhs_f16, stream);
+}
+
 }  // namespace lmoe

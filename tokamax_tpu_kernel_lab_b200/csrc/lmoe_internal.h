@@ -41,6 +41,11 @@ int grouped_gemm_fp8(const void* lhs, const void* rhs_q, const float* rhs_scale,
                      int64_t G, int64_t block_size, int out_f32, int zero_tail, int32_t* status,
                      cudaStream_t stream);
 
+int grouped_gemm_mxfp4_scatter(const void* lhs, const void* packed, const void* scales,
+                               const int32_t* group_sizes, const uint64_t* row_dest, int64_t M,
+                               int64_t K, int64_t N, int64_t G, int lhs_f16, int32_t* status,
+                               cudaStream_t stream);
+
 inline int current_device() {
   int d = 0;
   cudaGetDevice(&d);

@@ -353,8 +353,11 @@ __global__ void __launch_bounds__(kSwThreads, 1)
             __syncwarp();
             const int tok = tok0 + p0 + lane;
             if (lane < kRows && tok < tc.row_end) {
-              uint8_t* orow = reinterpret_cast<uint8_t*>(args.out) +
-                              (static_cast<int64_t>(tok) * args.ldo + f0) * esize;
+              uint8_t* orow =
+                  args.row_dest != nullptr
+                      ? reinterpret_cast<uint8_t*>(args.row_dest[tok]) + static_cast<int64_t>(f0) * esize
+                      : reinterpret_cast<uint8_t*>(args.out) +
+                            (static_cast<int64_t>(tok) * args.ldo + f0) * esize;
 #pragma unroll
               for (int cc = 0; cc < kChunks; ++cc) {
                 if (f0 + (cc + 1) * (16 / esize) <= args.N)
@@ -371,6 +374,9 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // rows scattered to other GPUs: make them visible system-wide before the
+    // kernel ends (the next kernel on the stream signals their arrival)
+    if (args.row_dest != nullptr) __threadfence_system();
     // rows at or past sum(group_sizes) are zero (ragged_dot semantics)
     if (args.zero_tail) {
       const int64_t row_bytes = static_cast<int64_t>(args.N) * esize;

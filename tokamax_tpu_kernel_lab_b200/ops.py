@@ -245,6 +245,24 @@ def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tens
   return res
 
 
+def mxfp4_ragged_dot_scatter(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tensor,
+                             row_dest: torch.Tensor) -> None:
+  """mxfp4_ragged_dot with each bf16 output row r stored at the byte address
+  row_dest[r] (int64 device tensor; 16-byte aligned addresses, a peer GPU's
+  mapped buffer included).  Rows past sum(group_sizes) are not written."""
+  _need_cuda(lhs, w.packed, w.scale, group_sizes, row_dest)
+  g, n, k = w.shape
+  m = lhs.shape[0]
+  if lhs.shape[1] != k or row_dest.shape[0] < m or row_dest.dtype != torch.int64:
+    raise ValueError("shape mismatch")
+  lhs_f16 = lhs.dtype == torch.float16
+  if lhs_f16 and not w.f16_operand_ok:
+    raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
+  _native.call("lmoe_mxfp4_ragged_dot_scatter", _ptr(lhs.contiguous()), _ptr(w.packed),
+               _ptr(w.scale), _ptr(group_sizes.to(torch.int32).contiguous()), _ptr(row_dest), m, k,
+               n, g, int(lhs_f16), _ptr(device_status(lhs.device)), _stream())
+
+
 def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
                             group_sizes: torch.Tensor | None, *, beta: float = 4.0,
                             linear_beta: float = 25.0, round_gate_up: bool = True,
