@@ -197,3 +197,28 @@ def test_checkpoint_layer_runs_identically(lm, tmp_path):
   torch.cuda.synchronize()
   lm.check_device_status()
   assert torch.equal(a, b)
+
+
+def test_mxfp4_ragged_dot_scatter_matches_gathered_output(lm):
+  """Output rows stored at per-row addresses (here a permutation of a local
+  buffer) equal the ordinary MXFP4 ragged_dot rows moved by that permutation."""
+  rng = np.random.default_rng(21)
+  g, n, k, m = 5, 512, 1024, 1500
+  packed, scale = _mx(rng, g, n, k)
+  gs = rng.multinomial(m - 100, np.full(g, 1.0 / g)).astype(np.int32)  # 100 tail rows unused
+  w = _dev_mx(lm, packed, scale)
+  lhs = to_dev(O.bf16_round(rng.standard_normal((m, k)).astype(np.float32))).to(torch.float16)
+  gsd = torch.from_numpy(gs).cuda()
+  ref = lm.mxfp4_ragged_dot(lhs, w, gsd)
+  perm = torch.from_numpy(rng.permutation(m)).cuda()
+  out = torch.full((m, n), 7.0, dtype=torch.bfloat16, device="cuda")
+  row_dest = (out.data_ptr() + perm.to(torch.int64) * n * 2).contiguous()
+  from tokamax_tpu_kernel_lab_b200 import ops
+  ops.mxfp4_ragged_dot_scatter(lhs, w, gsd, row_dest)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  used = int(gs.sum())
+  assert torch.equal(out[perm[:used]], ref[:used])
+  untouched = torch.ones(m, dtype=torch.bool, device="cuda")
+  untouched[perm[:used]] = False
+  assert bool((out[untouched] == 7.0).all())
