@@ -222,3 +222,35 @@ def test_mxfp4_ragged_dot_scatter_matches_gathered_output(lm):
   untouched = torch.ones(m, dtype=torch.bool, device="cuda")
   untouched[perm[:used]] = False
   assert bool((out[untouched] == 7.0).all())
+
+
+def test_mxfp4_kernels_repeat_bit_exactly_at_full_size(lm):
+  """Configuration-5 shapes (262144 routed rows over 896 experts, skewed
+  group sizes, f16 operands): repeated gate/up + SiTU and down calls give
+  identical bits, with every output element written.  Many thousands of
+  tiles per call cycle each CTA's packed-code, expanded-weight and token rings
+  through many laps, so a slot reused before its reader finished shows up
+  here as a few changed rows."""
+  from tokamax_tpu_kernel_lab_b200.latent_moe import random_mxfp4
+  rng = np.random.default_rng(31)
+  g, latent, inter, m = 896, 2048, 1024, 262144
+  gs = rng.multinomial(m, rng.dirichlet(np.full(g, 0.5))).astype(np.int32)
+  gsd = torch.from_numpy(gs).cuda()
+  gu = random_mxfp4(g, 2 * inter, latent, seed=31)
+  dn = random_mxfp4(g, latent, inter, seed=32)
+  assert gu.f16_operand_ok and dn.f16_operand_ok
+  gen = torch.Generator(device="cuda").manual_seed(31)
+  rows = torch.randn(m, latent, generator=gen, device="cuda").to(torch.bfloat16).to(torch.float16)
+  kw = dict(round_gate_up=True, out_dtype=torch.float16)
+  act0 = lm.mxfp4_fused_gateup_situ(rows, gu, gsd, **kw)
+  down0 = lm.mxfp4_ragged_dot(act0, dn, gsd)
+  for _ in range(4):
+    act = torch.full_like(act0, float("nan"))
+    lm.mxfp4_fused_gateup_situ(rows, gu, gsd, out=act, **kw)
+    down = torch.full_like(down0, float("nan"))
+    lm.mxfp4_ragged_dot(act0, dn, gsd, out=down)
+    torch.cuda.synchronize()
+    lm.check_device_status()
+    assert torch.equal(act.view(torch.int16), act0.view(torch.int16))
+    assert torch.equal(down.view(torch.int16), down0.view(torch.int16))
+  assert not bool(torch.isnan(act0).any()) and not bool(torch.isnan(down0).any())

@@ -320,10 +320,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = tc.n_tile * BN + c * 32;
+          // the residual's 32 columns are fetched before the accumulator is
+          // read, so the global load overlaps the TMEM load
+          uint4 addv[4];
+          if (EPI == EPI_BF16_ADD) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              addv[j] = (valid && col0 + j * 8 < args.N)
+                            ? *reinterpret_cast<const uint4*>(args.addend + r * args.ld_add + col0 + j * 8)
+                            : make_uint4(0, 0, 0, 0);
+          }
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_ld_wait();
-          const int col0 = tc.n_tile * BN + c * 32;
           if (valid && col0 < args.N) {
             if (EPI == EPI_F32) {
               float* orow = reinterpret_cast<float*>(args.out) + r * args.ldo + col0;
@@ -335,14 +345,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
             } else {
               __nv_bfloat16* orow =
                   reinterpret_cast<__nv_bfloat16*>(args.out) + r * args.ldo + col0;
-              const __nv_bfloat16* arow =
-                  (EPI == EPI_BF16_ADD) ? args.addend + r * args.ld_add + col0 : nullptr;
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 if (col0 + j * 8 < args.N) {
                   uint32_t pk[4];
                   if (EPI == EPI_BF16_ADD) {
-                    const uint4 av = *reinterpret_cast<const uint4*>(arow + j * 8);
+                    const uint4 av = addv[j];
                     const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {

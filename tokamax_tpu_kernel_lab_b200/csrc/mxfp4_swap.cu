@@ -403,9 +403,12 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     // step and fences once per step.  The packed and A slots of a step belong
     // to its group alone (both ring sizes are even), and the group uses them
     // in order, so the parity waits see their phases in order.
-    // The codes are read (and their packed slot released) before waiting for
-    // a free A slot; the scale bytes of the group's next step are fetched one
-    // step ahead.
+    // The codes are expanded into registers (and their packed slot released)
+    // before waiting for a free A slot; the scale bytes of the group's next
+    // step are fetched one step ahead.  The packed slot is refilled by TMA
+    // (async proxy) after generic-proxy reads, so each thread consumes its
+    // loaded codes and issues fence.proxy.async before the release: without
+    // it a refill could land before a read and corrupt that row's K step.
     const int grp = (warp - 6) / 4;
     const int r = ((warp - 6) % 4) * 32 + lane;
     const int kgroups = args.K / 32;
@@ -441,29 +444,30 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       const uint4* src = reinterpret_cast<const uint4*>(pstages + pslot * C::kPackedBytes +
                                                         packed_row<EPI>(r) * (kBK / 2));
       const uint4 p0 = src[0], p1 = src[1];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(pk_empty + pslot));
-      const uint32_t aslot = st % kDStages, aph = (st / kDStages) & 1;
-      if (!mbar_wait(smem_u32(a_empty + aslot), aph ^ 1u, abort_flag, args.status)) return false;
       const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      uint8_t* arow = astages + aslot * C::kABytes + r * 128;
+      uint4 dq[8];
       if (kF16) {
         const uint32_t b0 = e8m0_to_f16_bits(sc & 0xFFu), b1 = e8m0_to_f16_bits(sc >> 8);
         const uint32_t s0 = b0 | (b0 << 16), s1 = b1 | (b1 << 16);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
-              dequant_e2m1x8_f16(words[c], c < 4 ? s0 : s1);
+        for (int c = 0; c < 8; ++c) dq[c] = dequant_e2m1x8_f16(words[c], c < 4 ? s0 : s1);
       } else {
         const uint32_t b0 = e8m0_to_bf16_bits(sc & 0xFFu), b1 = e8m0_to_bf16_bits(sc >> 8);
         const uint32_t s0 = b0 | (b0 << 16), s1 = b1 | (b1 << 16);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint32_t sv = c < 4 ? s0 : s1;
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) =
-              dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sv));
+          dq[c] = dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sv));
         }
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(pk_empty + pslot));
+      const uint32_t aslot = st % kDStages, aph = (st / kDStages) & 1;
+      if (!mbar_wait(smem_u32(a_empty + aslot), aph ^ 1u, abort_flag, args.status)) return false;
+      uint8_t* arow = astages + aslot * C::kABytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dq[c];
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(a_ready + aslot));

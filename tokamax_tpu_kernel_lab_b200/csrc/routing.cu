@@ -340,12 +340,24 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   auto cv = [](uint4 v) { return CONVERT ? bf16x8_to_f16x8(v) : v; };
+  // the next row's source index is fetched while this row is copied, and each
+  // lane keeps eight 16-byte loads in flight, so neither load latency is paid
+  // once per row
+  int t_next = warp < rows ? token_idx[warp] : -1;
   for (int64_t p = warp; p < rows; p += nwarps) {
-    const int t = token_idx[p];
+    const int t = t_next;
+    t_next = p + nwarps < rows ? token_idx[p + nwarps] : -1;
     uint4* dst = out + p * vec_per_row;
     if (t >= 0 && t < x_rows) {
       const uint4* src = x + static_cast<int64_t>(t) * vec_per_row;
       int v = lane;
+      for (; v + 224 < vec_per_row; v += 256) {
+        uint4 a[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = __ldg(src + v + 32 * i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[v + 32 * i] = cv(a[i]);
+      }
       for (; v + 96 < vec_per_row; v += 128) {
         const uint4 a = __ldg(src + v), b = __ldg(src + v + 32), c = __ldg(src + v + 64),
                     d = __ldg(src + v + 96);
