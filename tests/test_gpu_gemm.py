@@ -194,3 +194,55 @@ def test_fused_gateup_with_row_gather(lm, layout):
                                 rhs_layout=layout)
   assert torch.equal(out, direct)  # same rows, same bits
   assert_bf16_close(ref, to_np(out), f"gather {layout}")
+
+
+def test_token_major_kernels_repeat_bit_exactly(lm):
+  """Large grouped calls of the token-major kernel -- bf16 ragged_dot, fused
+  gate/up with the in-kernel row gather, its MXFP4 form (more groups than the
+  weights-major kernel's schedule holds) and the fp8 form -- give identical
+  bits on every call, with every output element written (NaN-prefilled)."""
+  from tokamax_tpu_kernel_lab_b200.latent_moe import random_mxfp4
+  rng = np.random.default_rng(41)
+  gen = torch.Generator(device="cuda").manual_seed(41)
+  m, k, inter, g = 65536, 2048, 1024, 128
+
+  def groups(rows, n, alpha):
+    return torch.from_numpy(rng.multinomial(rows, rng.dirichlet(np.full(n, alpha)))
+                            .astype(np.int32)).cuda()
+
+  def repeats(shape, dtype, run, reps=3):
+    first = None
+    for _ in range(reps):
+      o = torch.full(shape, float("nan"), dtype=dtype, device="cuda")
+      run(o)
+      torch.cuda.synchronize()
+      lm.check_device_status()
+      assert not bool(torch.isnan(o).any())
+      if first is None:
+        first = o
+      else:
+        assert torch.equal(o.view(torch.int16), first.view(torch.int16))
+
+  x = torch.randn(m, k, generator=gen, device="cuda").to(torch.bfloat16)
+  gs = groups(m, g, 0.5)
+  w_gu = (torch.randn(g, 2 * inter, k, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+  row_index = torch.randint(-1, m, (m,), generator=gen, device="cuda").to(torch.int32)
+  repeats((m, inter), torch.bfloat16,
+          lambda o: lm.fused_gateup_situ(x, w_gu, gs, rhs_layout="gnk", out=o,
+                                         row_index=row_index))
+  w_dn = (torch.randn(g, k, inter, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+  act = torch.randn(m, inter, generator=gen, device="cuda").to(torch.bfloat16)
+  repeats((m, k), torch.bfloat16, lambda o: lm.ragged_dot(act, w_dn, gs, rhs_layout="gnk", out=o))
+  del w_gu, w_dn
+  g_many = 2000
+  gs_many = groups(m, g_many, 2.0)
+  gu_mx = random_mxfp4(g_many, 2 * inter, k, seed=41)
+  repeats((m, inter), torch.float16,
+          lambda o: lm.mxfp4_fused_gateup_situ(x.to(torch.float16), gu_mx, gs_many, out=o,
+                                               out_dtype=torch.float16))
+  del gu_mx
+  q = (torch.randn(32, k, k, generator=gen, device="cuda") * 4).to(torch.float8_e4m3fn)
+  scale = torch.rand(32, k // 128, k, generator=gen, device="cuda") * 0.01
+  gs_fp8 = groups(m // 2, 32, 0.5)
+  repeats((m // 2, k), torch.bfloat16,
+          lambda o: lm.fp8_ragged_dot(x[:m // 2], q, gs_fp8, scale, out=o))

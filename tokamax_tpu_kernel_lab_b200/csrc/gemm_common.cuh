@@ -227,4 +227,9 @@ __device__ __forceinline__ uint32_t pack_f16x2_of_bf16(float lo, float hi) {
 int mxfp4_swap_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, int lhs_f16,
                     cudaStream_t stream);
 
+// The same on CTA pairs (mxfp4_pair.cu): one MMA over two SMs, 256 weight
+// rows x 256 tokens per pair tile, each SM staging half of the tokens.
+int mxfp4_pair_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, int lhs_f16,
+                    cudaStream_t stream);
+
 }  // namespace lmoe

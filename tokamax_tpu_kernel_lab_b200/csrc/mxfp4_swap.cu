@@ -31,6 +31,7 @@
 // one warp and meets through one shuffle.
 #include <cuda.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_common.cuh"
@@ -532,6 +533,11 @@ int launch_swap_epi(int epi, const CUtensorMap& tok, const CUtensorMap& w, const
 // parameters (validated by the caller); its n_tiles is set here.
 int mxfp4_swap_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, int lhs_f16,
                     cudaStream_t stream) {
+  static const bool pair = [] {
+    const char* e = std::getenv("LMOE_MXFP4_PAIR");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (pair) return mxfp4_pair_gemm(lhs, packed, a, epi, lhs_f16, stream);
   CUtensorMap tok, w;
   // tokens: dims {K, M}, box {64, 256}, 128-byte swizzle (K-major UMMA B)
   if (!encode_tmap_bf16_2d(&tok, lhs, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M),
