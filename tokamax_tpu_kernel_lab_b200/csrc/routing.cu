@@ -33,75 +33,113 @@ __global__ void __launch_bounds__(256) router_topk_kernel(
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
   const float* row = logits + static_cast<int64_t>(warp) * E;
-  float sc[PER], key[PER];
+  // key[j] first holds the logit of expert lane + 32j, then its selection key
+  float key[PER];
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    sc[j] = (e < E) ? row[e] : -FLT_MAX;
+    key[j] = (e < E) ? row[e] : -FLT_MAX;
   }
-  if (activation == 0) {
-#pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = 1.0f / (1.0f + expf(-sc[j]));
-  } else {
-    float m = -FLT_MAX;
+  // softmax normaliser: the max, then the sum of exp(x - max) in lane order
+  // and a butterfly; kept so that a winner's score is recomputed from its
+  // logit with the same operations instead of holding every score
+  float m = -FLT_MAX, ssum = 0.f;
+  if (activation != 0) {
 #pragma unroll
     for (int j = 0; j < PER; ++j)
-      if (lane + 32 * j < E) m = fmaxf(m, sc[j]);
+      if (lane + 32 * j < E) m = fmaxf(m, key[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
 #pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      sc[j] = (lane + 32 * j < E) ? expf(sc[j] - m) : 0.f;
-      s += sc[j];
-    }
+    for (int j = 0; j < PER; ++j) ssum += (lane + 32 * j < E) ? expf(key[j] - m) : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-#pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = sc[j] / s;
+    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
   }
+  auto score = [&](float x) -> float {
+    return activation == 0 ? 1.0f / (1.0f + expf(-x)) : expf(x - m) / ssum;
+  };
+  // Selection order: key descending, expert id ascending on equal keys -- a
+  // total order, so the winners leave in exactly one sequence.  Each lane
+  // keeps its two best remaining (key, id, score) entries; a round is one
+  // warp-wide argmax over the lanes' bests, after which the winning lane
+  // promotes its second.  Only a lane that has used up both rescans its
+  // entries, for the two best strictly after the last one it gave up (every
+  // better entry of the lane is already taken).
+  auto before = [](float av, int ae, float bv, int be) { return av > bv || (av == bv && ae < be); };
+  float v1 = -FLT_MAX, v2 = -FLT_MAX, s1 = 0.f, s2 = 0.f;
+  int e1 = INT_MAX, e2 = INT_MAX;
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    key[j] = (e < E) ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
+    if (e < E) {
+      const float sj = score(key[j]);
+      const float kj = sj + (bias ? bias[e] : 0.f);
+      key[j] = kj;
+      if (before(kj, e, v1, e1)) {
+        v2 = v1; e2 = e1; s2 = s1;
+        v1 = kj; e1 = e; s1 = sj;
+      } else if (before(kj, e, v2, e2)) {
+        v2 = kj; e2 = e; s2 = sj;
+      }
+    } else {
+      key[j] = -FLT_MAX;
+    }
   }
+  auto refill = [&](float tv, int te) {  // two best entries strictly after (tv, te)
+    v1 = v2 = -FLT_MAX;
+    e1 = e2 = INT_MAX;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && before(tv, te, key[j], e)) {
+        if (before(key[j], e, v1, e1)) {
+          v2 = v1; e2 = e1;
+          v1 = key[j]; e1 = e;
+        } else if (before(key[j], e, v2, e2)) {
+          v2 = key[j]; e2 = e;
+        }
+      }
+    }
+    // their scores, recomputed from the logits
+    s1 = e1 < E ? score(row[e1]) : 0.f;
+    s2 = e2 < E ? score(row[e2]) : 0.f;
+  };
+  bool have2 = true;  // (v2, e2) is this lane's next entry after (v1, e1)
   float wsum = 0.f;
   float my_w = 0.f;
   int my_idx = 0;
   for (int s = 0; s < k; ++s) {
-    float bv = -FLT_MAX;
-    int bi = INT_MAX;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && (key[j] > bv || (key[j] == bv && e < bi))) {
-        bv = key[j];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    // owner lane takes the winner out and broadcasts its un-biased score
-    float wv = 0.f;
-#pragma unroll
-    for (int j = 0; j < PER; ++j) {
-      if (lane + 32 * j == bi) {
-        wv = sc[j];
-        key[j] = -FLT_MAX;
-      }
-    }
-    wv = __shfl_sync(0xffffffffu, wv, bi & 31);
-    wsum += wv;
+    // warp argmax in two hardware reductions: the largest key (as an
+    // order-preserving unsigned), then the lowest expert id holding it; the
+    // winner's lane is its id mod 32 (lane l holds experts l + 32j)
+    const uint32_t fb = __float_as_uint(v1);
+    const uint32_t ku = fb ^ ((fb & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, ku);
+    const int bi = static_cast<int>(
+        __reduce_min_sync(0xffffffffu, ku == kmax ? static_cast<uint32_t>(e1) : 0xFFFFFFFFu));
+    const bool won = bi == e1;  // exactly one lane
+    const float bv = v1;        // the winner's key (used by the winner only)
+    const float bw = __shfl_sync(0xffffffffu, s1, bi & 31);
+    wsum += bw;
     if (lane == s) {
-      my_w = wv;
+      my_w = bw;
       my_idx = bi;
+    }
+    if (won) {
+      if (have2) {
+        v1 = v2; e1 = e2; s1 = s2;
+        have2 = false;
+      } else {
+        v1 = -FLT_MAX;
+        e1 = INT_MAX;  // exhausted until the rescan below
+      }
+    }
+    // the winner had no second left: it rescans after the entry it just gave up
+    if (__any_sync(0xffffffffu, won && e1 == INT_MAX) && s + 1 < k) {
+      if (won && e1 == INT_MAX) {
+        refill(bv, bi);
+        have2 = true;
+      }
     }
   }
   if (lane < k) {
