@@ -47,6 +47,30 @@ def test_router_topk_bit_exact_given_logits(lm, t, e, k):
   assert np.allclose(w.cpu().numpy()[ok], ref_w[ok], rtol=1e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("k", [16, 32])
+def test_router_topk_one_lane_holds_every_winner(lm, k):
+  """All winners among experts e = 3 (mod 32): the kernel's lane 3 (which
+  holds those experts) wins every round and rescans its entries after every
+  second win; the selection and its slot order still equal the oracle's."""
+  rng = np.random.default_rng(k)
+  t, e = 300, 1024
+  logits = rng.standard_normal((t, e), dtype=np.float32) * np.float32(0.5)
+  bias = np.zeros(e, np.float32)
+  bias[3::32] = np.float32(4.0) + rng.random(e // 32, dtype=np.float32)
+  _, _, sfc, ref_idx, ref_w = O.router_from_logits(logits, bias, k)
+  idx, w = lm.router_topk(torch.from_numpy(logits).cuda(), torch.from_numpy(bias).cuda(), k)
+  got = idx.cpu().numpy()
+  assert np.all(got % 32 == 3)
+  mismatch = np.any(got != ref_idx, axis=1)
+  if mismatch.any():
+    srt = -np.sort(-sfc, axis=1)
+    gap = srt[:, k - 1] - srt[:, k]
+    assert np.all(gap[mismatch] < 1e-6), f"{mismatch.sum()} rows differ beyond near-ties"
+  assert mismatch.sum() <= 1
+  ok = ~mismatch
+  assert np.allclose(w.cpu().numpy()[ok], ref_w[ok], rtol=1e-6, atol=1e-7)
+
+
 def test_router_ties_go_to_lower_index(lm):
   logits = np.zeros((3, 16), np.float32)
   logits[0, [3, 7, 9]] = 1.0
