@@ -26,6 +26,15 @@ with nvidia-smi during the timed region.
 `--impl reference` times the reference's algorithm on the host CPU instead
 (the reference is JAX/TPU code; JAX is not installed, so its numpy
 restatement runs, with all host threads), same metric and config.
+
+On one GPU the line also carries `configs`: the standalone kernels of the
+other benchmark configurations (2: bf16 ragged_dot; 3: bf16 fused gate/up +
+SiTU-GLU and down grouped GEMMs over 65536 routed rows; 4: the MXFP4 grouped
+matmul) with their time, TFLOP/s and fraction of the roofline that binds
+them, and configuration 5 at 128, 1024 and 4096 tokens (`--no-extras` skips
+them).  `--phases` instead prints one line of per-phase device times of
+eager forwards (CUDA events between the phases, every rank, max over steps
+of the median), the phase table of the expert-parallel exchange.
 """
 
 from __future__ import annotations
@@ -46,11 +55,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "LatentMoE layer tokens/s"
 UNIT = "tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram bytes (read + write) per launch of the dominant kernel: the ncu capture
-# summarised in profiles/mxfp4_swap_gemm_t8192.md measured 746.5 MB read +
-# 246.5 MB written at 8192 tokens (131072 routed rows); scaled by the routed
-# rows to the 16384-token launch (the weight bytes, about a fifth of it, do
-# not grow with the rows, so this overstates by at most ~12%)
+# dram bytes (read + write) per launch of the dominant kernel: an ncu capture
+# (`--metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:mxfp4_swap_kernel`)
+# at 8192 tokens (131072 routed rows) measured 746.5 MB read + 246.5 MB
+# written; scaled by the routed rows to the 16384-token launch (the weight
+# bytes, about a fifth of it, do not grow with the rows, so this overstates
+# by at most ~12%)
 DOMINANT_TRAFFIC_BYTES = int((746.5e6 + 246.5e6) * 2)
 
 
@@ -68,6 +78,10 @@ def parse_args():
                  help="time eager launches instead of a captured CUDA graph")
   p.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                  help="expert-parallel exchange (N>1): NVLink peer-memory puts or NCCL all-to-all")
+  p.add_argument("--no-extras", action="store_true",
+                 help="skip the standalone-kernel and token-sweep measurements (N=1)")
+  p.add_argument("--phases", action="store_true",
+                 help="print per-phase device times of eager forwards instead of the bench line")
   return p.parse_args()
 
 
@@ -141,13 +155,14 @@ def cpu_weights(seed: int, cfg, touched):
   return w
 
 
-def cpu_forward_timer(seed: int, sample_tokens: int):
-  """Returns (callable running one oracle forward of the sample, description)."""
+def cpu_forward_timer(seed: int, sample_tokens: int, w=None):
+  """Returns (callable running one oracle forward of the sample, description,
+  the host weights -- pass them back in to reuse their dequantised experts)."""
   from oracle import lmoe_oracle as O
   import numpy as np
 
   cfg = O.LatentMoEConfig(7168, 2048, 1024, 896, 16, 2)
-  w = cpu_weights(seed, cfg, None)
+  w = cpu_weights(seed, cfg, None) if w is None else w
   h = O.bf16_round(np.random.default_rng(seed + 1).standard_normal((sample_tokens, 7168),
                                                                    dtype=np.float32))
 
@@ -157,25 +172,111 @@ def cpu_forward_timer(seed: int, sample_tokens: int):
   run()  # materialise (dequantise) the touched experts outside the timing
   return run, (f"{sample_tokens} tokens of configuration 5 through the numpy restatement of "
                "latent_moe_forward (bf16 emulated, MXFP4 experts dequantised once before "
-               "timing, as the reference dequantises its checkpoint)")
+               "timing, as the reference dequantises its checkpoint)"), w
 
 
-def cpu_baseline(seed: int, sample_tokens: int, reps: int = 3) -> dict:
-  run, desc = cpu_forward_timer(seed, sample_tokens)
+def _median_s(run, reps: int) -> float:
   times = []
   for _ in range(reps):
     t0 = time.perf_counter()
     run()
     times.append(time.perf_counter() - t0)
-  t = statistics.median(times)
-  return {"value": sample_tokens / t, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-          "sample": desc + f"; median of {reps}"}
+  return statistics.median(times)
+
+
+def cpu_threads() -> dict:
+  """The host threads the CPU runs could use: cores, affinity, thread env,
+  and the BLAS pools numpy actually runs (threadpoolctl)."""
+  info = {"cpu_count": os.cpu_count(),
+          "affinity_cores": len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
+          else None,
+          "env": {k: os.environ.get(k) for k in ("OMP_NUM_THREADS", "MKL_NUM_THREADS",
+                                                 "OPENBLAS_NUM_THREADS")}}
+  try:
+    from threadpoolctl import threadpool_info
+    info["blas"] = [{"api": d.get("internal_api"), "threads": d.get("num_threads")}
+                    for d in threadpool_info()]
+  except Exception:  # pragma: no cover - threadpoolctl missing
+    info["blas"] = None
+  return info
+
+
+def cpu_coverage(seed: int, reps: int, w5) -> dict:
+  """The numpy restatement on the other benchmark configurations, each a
+  bounded sample, median of `reps` runs after one warm-up."""
+  from oracle import lmoe_oracle as O
+  import numpy as np
+
+  out = {}
+  # configuration 1: the reduced fp32 layer, all 128 tokens
+  c1 = O.LatentMoEConfig(512, 256, 512, 64, 8, 1)
+  w1 = O.init_weights_np(c1, 0, dtype="fp32")
+  h1 = np.random.default_rng(0).standard_normal((128, 512), dtype=np.float32)
+  run1 = lambda: O.latent_moe_forward(h1, w1, c1, dtype="fp32")
+  run1()
+  t = _median_s(run1, reps)
+  out["config1"] = {"tokens_per_s": 128 / t, "ms": t * 1e3, "sample": "all 128 tokens, fp32"}
+  # configuration 2: ragged_dot 8192 x 2048 @ (128, 2048, 1536), Zipf(1.1) groups
+  rng = np.random.default_rng(1)
+  m, k, n, g = 8192, 2048, 1536, 128
+  gs = zipf_group_sizes(rng, m, g)
+  lhs = O.bf16_round(rng.standard_normal((m, k), dtype=np.float32) / np.float32(np.sqrt(k)))
+  rhs = O.bf16_round(rng.standard_normal((g, k, n), dtype=np.float32) / np.float32(np.sqrt(k)))
+  run2 = lambda: O.ragged_dot(lhs, rhs, gs, dtype="bf16")
+  run2()
+  t = _median_s(run2, reps)
+  out["config2"] = {"tflops": 2.0 * m * k * n / t / 1e12, "ms": t * 1e3,
+                    "sample": "the full configuration (f32 matmuls of bf16 values)"}
+  del lhs, rhs
+  # configuration 4: MXFP4 dequant-then-matmul, 8 of the 128 experts with
+  # their rows (uniform group sizes over 16384 rows), dequantised once
+  k4, n4, g4 = 4096, 2048, 8
+  gs4 = rng.multinomial(16384, np.full(128, 1 / 128))[:g4].astype(np.int32)
+  packed = rng.integers(0, 256, (g4, n4, k4 // 2), dtype=np.uint8)
+  scale = rng.integers(121, 130, (g4, n4, k4 // 32), dtype=np.uint8)
+  lazy = O.LazyMXFP4Experts(packed, scale)
+  x4 = O.bf16_round(rng.standard_normal((int(gs4.sum()), k4), dtype=np.float32))
+  run4 = lambda: O.ragged_dot(x4, lazy, gs4, dtype="bf16")
+  run4()
+  t = _median_s(run4, reps)
+  rows4 = int(gs4.sum())
+  out["config4"] = {"tflops": 2.0 * rows4 * k4 * n4 / t / 1e12, "ms": t * 1e3,
+                    "sample": f"{g4} of 128 experts, their {rows4} rows (weights dequantised "
+                              "once before timing)"}
+  # configuration 5 at 128 and 1024 tokens (n = 1 semantics)
+  for t5 in (128, 1024):
+    run5, _, _ = cpu_forward_timer(seed, t5, w5)
+    t = _median_s(run5, reps)
+    out[f"config5_t{t5}"] = {"tokens_per_s": t5 / t, "ms": t * 1e3,
+                             "sample": f"{t5} tokens, n = 1 semantics"}
+  return out
+
+
+def zipf_group_sizes(rng, m: int, g: int, s: float = 1.1, n_zero: int = 8):
+  """Zipf(s) multinomial over a seeded permutation of the groups with n_zero
+  groups forced empty (benchmark configuration 2)."""
+  import numpy as np
+  p = (np.arange(g) + 1.0) ** (-s)
+  p = p[rng.permutation(g)]
+  p[rng.choice(g, size=min(n_zero, g - 1), replace=False)] = 0
+  p /= p.sum()
+  return rng.multinomial(m, p).astype(np.int32)
+
+
+def cpu_baseline(seed: int, sample_tokens: int, reps: int = 5, coverage: bool = True) -> dict:
+  run, desc, w = cpu_forward_timer(seed, sample_tokens)
+  t = _median_s(run, reps)
+  res = {"value": sample_tokens / t, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+         "sample": desc + f"; median of {reps} after one warm-up", "threads": cpu_threads()}
+  if coverage:
+    res["coverage"] = cpu_coverage(seed, reps, w)
+  return res
 
 
 def run_reference(args, world, rank):
   if rank != 0:
     return
-  run, desc = cpu_forward_timer(args.seed, args.cpu_sample_tokens)
+  run, desc, _ = cpu_forward_timer(args.seed, args.cpu_sample_tokens)
   for _ in range(args.warmup):
     run()
   t0 = time.perf_counter()
@@ -190,7 +291,8 @@ def run_reference(args, world, rank):
       "data": "synthetic", "config": config_dict(args, world),
       "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
                        "sample": desc + " (JAX is not installed: the reference's own JAX path "
-                                        "cannot run; its numpy restatement runs instead)"},
+                                        "cannot run; its numpy restatement runs instead)",
+                       "threads": cpu_threads()},
       "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
   }
   print(json.dumps(line), flush=True)
@@ -252,6 +354,174 @@ class ClockSampler:
             "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def time_launches(fn, iters: int, warmup: int = 2) -> float:
+  """Mean device time (ms) of fn() over `iters` launches, CUDA events on the
+  current stream around each launch."""
+  import torch
+  stream = torch.cuda.current_stream()
+  for _ in range(warmup):
+    fn()
+  torch.cuda.synchronize()
+  ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        for _ in range(iters)]
+  for a, b in ev:
+    a.record(stream)
+    fn()
+    b.record(stream)
+  torch.cuda.synchronize()
+  return statistics.mean(a.elapsed_time(b) for a, b in ev)
+
+
+def roofline_entry(ms: float, flops: float, bytes_: float, peaks: dict, peak_src: str) -> dict:
+  """Achieved TFLOP/s and GB/s of the algorithmic work, and the fraction of
+  the binding roofline (the larger of the tensor-time and HBM-time floors)."""
+  t_tc = flops / (peaks["bf16_tflops"] * 1e12)
+  t_hbm = bytes_ / (peaks["hbm_gbs"] * 1e9)
+  bound = "tensor" if t_tc >= t_hbm else "hbm"
+  return {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "gbs": bytes_ / (ms / 1e3) / 1e9,
+          "bound": bound, "frac": max(t_tc, t_hbm) / (ms / 1e3),
+          "flops": flops, "bytes": bytes_,
+          "peak": f"{peak_src}: {peaks['bf16_tflops']} TFLOP/s bf16, {peaks['hbm_gbs']} GB/s"}
+
+
+def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
+  """Standalone kernels of benchmark configurations 2, 3 and 4 at full size."""
+  import numpy as np
+  import torch
+
+  iters = max(3, min(args.steps, 10))
+  out = {}
+  gen = torch.Generator(device=dev).manual_seed(args.seed)
+
+  # configuration 2: ragged_dot, lhs (8192, 2048), rhs (128, 2048, 1536) in the
+  # reference's (G, K, N) layout, Zipf(1.1) group sizes with empty groups
+  m, k, n, g = 8192, 2048, 1536, 128
+  gs = zipf_group_sizes(np.random.default_rng(1), m, g)
+  lhs = (torch.randn(m, k, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
+  rhs = (torch.randn(g, k, n, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
+  gsd = torch.from_numpy(gs).to(dev)
+  res = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+  ms = time_launches(lambda: ops.ragged_dot(lhs, rhs, gsd, out=res), iters)
+  nz = int((gs > 0).sum())
+  out["config2_ragged_dot_bf16"] = roofline_entry(
+      ms, 2.0 * m * k * n, m * k * 2 + nz * k * n * 2 + m * n * 2, peaks, peak_src)
+  out["config2_ragged_dot_bf16"]["nonempty_groups"] = nz
+  del lhs, rhs, res
+
+  # configuration 3: 4096 tokens x top-16 over 896 experts (router bias
+  # N(0, 0.5^2)), latent 2048, intermediate 1024, bf16 weights
+  E, L, I, T, K = 896, 2048, 1024, 4096, 16
+  x = torch.randn(T, L, generator=gen, device=dev).to(torch.bfloat16)
+  wr = (torch.randn(E, L, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+  bias = torch.randn(E, generator=gen, device=dev) * 0.5
+  idx, wts = ops.router_gate(x, wr, bias, K)
+  d = ops.dispatch(idx, wts, E)
+  rows = ops.gather_rows(x, d.token_idx)
+  w_gu = torch.empty(E, 2 * I, L, dtype=torch.bfloat16, device=dev)
+  w_dn = torch.empty(E, L, I, dtype=torch.bfloat16, device=dev)
+  for e0 in range(0, E, 64):
+    w_gu[e0:e0 + 64] = (torch.randn(64, 2 * I, L, generator=gen, device=dev) * 0.02).to(
+        torch.bfloat16)
+    w_dn[e0:e0 + 64] = (torch.randn(64, L, I, generator=gen, device=dev) * 0.02).to(
+        torch.bfloat16)
+  M = T * K
+  act = torch.empty(M, I, dtype=torch.bfloat16, device=dev)
+  dn = torch.empty(M, L, dtype=torch.bfloat16, device=dev)
+  ms_gu = time_launches(lambda: ops.fused_gateup_situ(rows, w_gu, d.group_sizes, rhs_layout="gnk",
+                                                      out=act), iters)
+  ms_dn = time_launches(lambda: ops.ragged_dot(act, w_dn, d.group_sizes, rhs_layout="gnk",
+                                               out=dn), iters)
+  nz = int((d.group_sizes > 0).sum())
+  out["config3_gateup_situ_bf16"] = roofline_entry(
+      ms_gu, 2.0 * M * L * 2 * I, M * L * 2 + nz * 2 * I * L * 2 + M * I * 2, peaks, peak_src)
+  out["config3_down_bf16"] = roofline_entry(
+      ms_dn, 2.0 * M * I * L, M * I * 2 + nz * L * I * 2 + M * L * 2, peaks, peak_src)
+  out["config3_gateup_situ_bf16"]["nonempty_groups"] = nz
+  del x, w_gu, w_dn, act, dn, rows
+
+  # configuration 4: MXFP4 (128 experts, K 4096, N 2048; codes uniform over
+  # all 16, scale exponents uniform in [-6, 2]), bf16 x (16384, 4096),
+  # uniform-random group sizes
+  g4, k4, n4, m4 = 128, 4096, 2048, 16384
+  w4 = lm.random_mxfp4(g4, n4, k4, seed=3, device=dev, scale_exp=(-6, 2))
+  x4 = torch.randn(m4, k4, generator=gen, device=dev).to(torch.bfloat16)
+  gs4 = torch.from_numpy(np.random.default_rng(3).multinomial(m4, np.full(g4, 1 / g4)).astype(
+      np.int32)).to(dev)
+  o4 = torch.empty(m4, n4, dtype=torch.bfloat16, device=dev)
+  ms4 = time_launches(lambda: ops.mxfp4_ragged_dot(x4, w4, gs4, out=o4), iters)
+  byt = m4 * k4 * 2 + g4 * n4 * (k4 // 2 + k4 // 32) + m4 * n4 * 2
+  out["config4_mxfp4_bf16_operands"] = roofline_entry(ms4, 2.0 * m4 * k4 * n4, byt, peaks,
+                                                      peak_src)
+  x4h = x4.to(torch.float16)
+  ms4h = time_launches(lambda: ops.mxfp4_ragged_dot(x4h, w4, gs4, out=o4), iters)
+  out["config4_mxfp4_f16_operands"] = roofline_entry(ms4h, 2.0 * m4 * k4 * n4, byt, peaks,
+                                                     peak_src)
+  del w4, x4, x4h, o4
+  torch.cuda.synchronize()
+  torch.cuda.empty_cache()
+  return out
+
+
+def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
+  """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay)."""
+  import torch
+  out = {}
+  for t in tokens:
+    gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + t)
+    h = torch.randn(t, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
+    for _ in range(2):
+      lm.latent_moe_forward(h, pw, cfg)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+      lm.latent_moe_forward(h, pw, cfg)
+    ms = time_launches(graph.replay, max(5, args.steps))
+    out[f"T{t}"] = {"ms": ms, "tokens_per_s": t / (ms / 1e3)}
+    del graph
+  return out
+
+
+def run_phases(args, lm, ops, forward_marked, world, rank, dev, stats=None):
+  """Per-phase device times of eager forwards: CUDA events recorded on the
+  main stream after each phase is enqueued; per rank the median over steps."""
+  import torch
+  import torch.distributed as dist
+  stream = torch.cuda.current_stream()
+  for _ in range(args.warmup):
+    forward_marked(None)
+  torch.cuda.synchronize()
+  per_step = []
+  for _ in range(args.steps):
+    names, evs = [], []
+    e0 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+
+    def mark(name):
+      e = torch.cuda.Event(enable_timing=True)
+      e.record(torch.cuda.current_stream())
+      names.append(name)
+      evs.append(e)
+
+    forward_marked(mark)
+    torch.cuda.synchronize()
+    prev, d = e0, {}
+    for nm, e in zip(names, evs):
+      d[nm] = d.get(nm, 0.0) + prev.elapsed_time(e)
+      prev = e
+    d["total"] = e0.elapsed_time(evs[-1])
+    per_step.append(d)
+  ops.check_device_status()
+  med = {k: statistics.median(s[k] for s in per_step) for k in per_step[0]}
+  if stats is not None:
+    med.update(stats())
+  table = [None] * world
+  if world > 1:
+    dist.all_gather_object(table, med)
+  else:
+    table = [med]
+  return table
+
+
 def main():
   args = parse_args()
   world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -287,12 +557,27 @@ def main():
   backend = GpuBackend(pw, cfg)
   xchg = PeerExchange(cfg, t_local) if world > 1 and args.exchange == "peer" else None
 
-  def forward(x):
+  def forward(x, mark=None):
     if xchg is not None:
-      return ep_forward_peer(x, backend, cfg, xchg)
+      return ep_forward_peer(x, backend, cfg, xchg, mark=mark)
     if world > 1:
       return ep_forward(x, backend, cfg)
-    return lm.latent_moe_forward(x, pw, cfg)
+    return lm.latent_moe_forward(x, pw, cfg, mark=mark)
+
+  if args.phases:
+    stats = (lambda: {"rows_received": int(xchg.local_gs.sum().item())}) if xchg else None
+    table = run_phases(args, lm, ops, lambda mark: forward(h, mark), world, rank, dev, stats)
+    if xchg is not None:
+      xchg.close()
+    if world > 1:
+      dist.barrier()
+      dist.destroy_process_group()
+    if rank == 0:
+      print(json.dumps({"phases_ms": table, "n_gpus": world, "steps": args.steps,
+                        "warmup": args.warmup, "config": config_dict(args, world),
+                        "launch": "eager, CUDA events between phases on the main stream; "
+                                  "median over steps per rank"}), flush=True)
+    return
 
   def barrier():
     if world > 1:
@@ -434,6 +719,13 @@ def main():
               "weight_bytes_per_launch": int(pw.expert_gu_mx.packed.numel() +
                                              pw.expert_gu_mx.scale.numel())}
 
+  # ---------------------------------------------------------------- other configurations
+  configs = sweep = None
+  if world == 1 and not args.no_extras:
+    del xs, act, gs
+    configs = gpu_config_extras(args, lm, ops, dev, peaks, peak_src)
+    sweep = gpu_token_sweep(args, lm, pw, cfg, dev)
+
   # ---------------------------------------------------------------- CPU baseline
   cpu = None
   if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -456,6 +748,9 @@ def main():
       "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
       "tflops": (2.0 * args.tokens * layer_macs(cfg)) / (ms / 1e3) / 1e12,
   }
+  if configs is not None:
+    line["configs"] = configs
+    line["token_sweep"] = sweep
   print(json.dumps(line), flush=True)
 
 

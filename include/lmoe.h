@@ -40,7 +40,9 @@ enum {
   LMOE_LAUNCH_FAILED = 3,  /* CUDA launch or tensor-map encode failed */
   LMOE_DEVICE_BOUNDS = 4,  /* (dev_status) group sizes invalid on the device */
   LMOE_WAIT_TIMEOUT = 5,   /* (dev_status) a bounded device wait gave up */
-  LMOE_SCRATCH_TOO_SMALL = 6 /* request exceeds the library's built-in scratch */
+  LMOE_SCRATCH_TOO_SMALL = 6, /* request exceeds the library's built-in scratch */
+  LMOE_F16_RANGE = 7       /* (dev_status) a value written as an f16 operand was
+                              outside f16's finite range (|x| > 65504) */
 };
 
 enum { LMOE_RHS_GKN = 0, LMOE_RHS_GNK = 1 };
@@ -241,11 +243,14 @@ LMOE_API int lmoe_dispatch_static_scratch(const int32_t* topk_idx, const float* 
 
 /* Row gather: out[p] = token_idx[p] >= 0 ? x[token_idx[p]] : 0, rows of row_bytes
  * (a multiple of 16).  convert = 1 reads bf16 rows and writes them as f16
- * (exact in f16's normal range), the lhs_f16 form of the MXFP4 kernels.
+ * (exact in f16's normal range), the lhs_f16 form of the MXFP4 kernels; a
+ * value above 65504 in magnitude becomes inf there and records LMOE_F16_RANGE
+ * in dev_status (may be NULL).
  * Replaces `x[sorted_token_idx]` / `where(valid, x[idx], 0)`
  * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:372-374, 867-868). */
 LMOE_API int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out,
-                              int64_t rows, int64_t row_bytes, int convert, void* stream);
+                              int64_t rows, int64_t row_bytes, int convert, int32_t* dev_status,
+                              void* stream);
 
 /* Weighted combine + RMSNorm:
  *   routed[t] = dtype(sum_s expert_out[slot_pos[t*k+s]] * topk_w[t,s])   (f32, slot order)
@@ -295,6 +300,16 @@ LMOE_API int lmoe_ep_reorder(const int32_t* recv_counts, int64_t world, int64_t 
 LMOE_API int64_t lmoe_ep_buffer_bytes(int64_t world, int64_t num_experts,
                                       int64_t recv_capacity_rows, int64_t back_capacity_rows,
                                       int64_t row_bytes);
+/* Limit, in nanoseconds, of every device-side wait on another rank's signal
+ * (counts, rows, returns) in the exchange calls enqueued (or captured into a
+ * CUDA graph) after this call; 0 restores the default of 2 s.  Accepted range
+ * 1 us .. 60 s (LMOE_BAD_SHAPE otherwise).  A wait that runs out records
+ * LMOE_WAIT_TIMEOUT in dev_status, empties the offset tables (so the puts and
+ * the expert GEMMs that follow do no work) and returns; the CUDA context stays
+ * usable.  Process-wide setting.  lmoe_peer_wait_timeout_ns reads it back.
+ * No counterpart in the reference (it has no cross-device waits). */
+LMOE_API int lmoe_set_peer_wait_timeout_ns(uint64_t ns);
+LMOE_API uint64_t lmoe_peer_wait_timeout_ns(void);
 /* The exchange buffer and its peer mappings, over CUDA IPC on the current
  * device (plain point-to-point peer mappings): lmoe_ep_buffer_alloc
  * allocates and zeroes `bytes`, returning the pointer and an IPC handle of

@@ -47,3 +47,21 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
   monkeypatch.setattr(_native, "_lib", None)
   with pytest.raises(_native.NativeLibraryMissing):
     _native.load()
+
+
+def test_peer_wait_limit_is_a_runtime_setting():
+  """The limit of the exchange's waits on other ranks is set per process
+  (no GPU work: the value is read when an exchange call is enqueued)."""
+  from tokamax_tpu_kernel_lab_b200 import _native
+  lib = _native.load()
+  default = int(lib.lmoe_peer_wait_timeout_ns())
+  assert default == 2_000_000_000
+  try:
+    assert lib.lmoe_set_peer_wait_timeout_ns(5_000_000) == _native.LMOE_OK
+    assert int(lib.lmoe_peer_wait_timeout_ns()) == 5_000_000
+    assert lib.lmoe_set_peer_wait_timeout_ns(10) == _native.LMOE_BAD_SHAPE  # below 1 us
+    assert lib.lmoe_set_peer_wait_timeout_ns(61 * 10**9) == _native.LMOE_BAD_SHAPE
+    assert int(lib.lmoe_peer_wait_timeout_ns()) == 5_000_000
+  finally:
+    assert lib.lmoe_set_peer_wait_timeout_ns(0) == _native.LMOE_OK
+  assert int(lib.lmoe_peer_wait_timeout_ns()) == default

@@ -19,6 +19,8 @@ LMOE_UNSUPPORTED = 2
 LMOE_LAUNCH_FAILED = 3
 LMOE_DEVICE_BOUNDS = 4
 LMOE_WAIT_TIMEOUT = 5
+LMOE_SCRATCH_TOO_SMALL = 6
+LMOE_F16_RANGE = 7
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -52,13 +54,15 @@ SIGNATURES = {
     "lmoe_dispatch_workspace_size": (_sz, [_i64, _i64]),
     "lmoe_dispatch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p,
                              _p, _p, _sz, _p]),
-    "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i32, _p]),
+    "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i32, _p, _p]),
     "lmoe_combine_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p, _p, _p]),
     "lmoe_combine_scatter_add": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]),
     "lmoe_ep_reorder": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
     "lmoe_dispatch_static_scratch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p,
                                             _p, _p, _p, _p, _p, _p]),
     "lmoe_ep_buffer_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
+    "lmoe_set_peer_wait_timeout_ns": (_i32, [ctypes.c_uint64]),
+    "lmoe_peer_wait_timeout_ns": (ctypes.c_uint64, []),
     "lmoe_ep_region_offset": (_i64, [_i64, _i64, _i64, _i64, _i64, _i32]),
     "lmoe_ep_buffer_alloc": (_i32, [_i64, _p, _p]),
     "lmoe_ep_buffer_open": (_i32, [_p, _p]),
@@ -73,7 +77,8 @@ SIGNATURES = {
 # kernels launched by one call of each entry point (for the bench's launch count)
 KERNELS_PER_CALL = {"lmoe_dispatch": 3, "lmoe_ep_dispatch_put": 2, "lmoe_ep_return_put": 2,
                     "lmoe_ep_buffer_alloc": 0, "lmoe_ep_buffer_open": 0,
-                    "lmoe_ep_buffer_close": 0, "lmoe_ep_buffer_free": 0}
+                    "lmoe_ep_buffer_close": 0, "lmoe_ep_buffer_free": 0,
+                    "lmoe_set_peer_wait_timeout_ns": 0}
 launch_count = 0
 
 

@@ -132,8 +132,10 @@ int lmoe_dispatch(const int32_t* topk_idx, const float* topk_w, int64_t num_toke
 }
 
 int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out,
-                     int64_t rows, int64_t row_bytes, int convert, void* stream) {
-  return lmoe::gather_rows(x, x_rows, token_idx, out, rows, row_bytes, convert, S(stream));
+                     int64_t rows, int64_t row_bytes, int convert, int32_t* dev_status,
+                     void* stream) {
+  return lmoe::gather_rows(x, x_rows, token_idx, out, rows, row_bytes, convert, dev_status,
+                           S(stream));
 }
 
 int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,

@@ -23,9 +23,11 @@
 //   cum[g]        = cum_r(g)
 //   exp_off[e*world+s] = exp_off_r(e, s)                 (this rank receiving)
 //   src_pos[e*world+s] = cum_s(r*El + e)
-// Every wait is bounded (LMOE_WAIT_TIMEOUT_NS); a timeout records
+// Every wait on another rank is bounded: by LMOE_WAIT_TIMEOUT_NS unless
+// lmoe_set_peer_wait_timeout_ns chose another limit; a timeout records
 // LMOE_WAIT_TIMEOUT in the status word and the kernel returns.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <cstdint>
 
@@ -63,6 +65,7 @@ struct EpArgs {
   int64_t recv_cap, back_cap, row_bytes;
   uint32_t epoch;  // set on the device from the epoch word
   int32_t* status;
+  uint64_t timeout_ns;  // limit of every wait on another rank's signal
 };
 
 struct EpTablePtrs {
@@ -98,11 +101,11 @@ __device__ __forceinline__ bool epoch_reached(uint32_t seen, uint32_t want) {
 
 // Bounded wait until flags[s] reached epoch for every source s (one thread).
 __device__ bool wait_all_sources(const uint32_t* flags, int world, uint32_t epoch,
-                                 int32_t* status) {
+                                 int32_t* status, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (int s = 0; s < world; ++s) {
     while (!epoch_reached(ld_acquire_sys(flags + s), epoch)) {
-      if (globaltimer_ns() - t0 > LMOE_WAIT_TIMEOUT_NS) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
         record_status(status, kWaitTimeout);
         return false;
       }
@@ -185,7 +188,7 @@ __global__ void __launch_bounds__(256) ep_counts_kernel(EpArgs a, const int32_t*
   __shared__ int ok;
   if (threadIdx.x == 0)
     ok = wait_all_sources(reinterpret_cast<const uint32_t*>(a.peers[a.rank] + l.flags), a.world,
-                          a.epoch, a.status);
+                          a.epoch, a.status, a.timeout_ns);
   __syncthreads();
   const EpTablePtrs t = ep_tables(a, l);
   const int El = a.n_local, W = a.world, E = a.E, r = a.rank;
@@ -334,7 +337,7 @@ __global__ void ep_wait_kernel(EpArgs a, int which) {
   a.epoch = *ep_epoch_word(a, l);  // set by this exchange's counts kernel
   if (threadIdx.x == 0 && blockIdx.x == 0)
     wait_all_sources(reinterpret_cast<const uint32_t*>(a.peers[a.rank] + l.flags) + which * a.world,
-                     a.world, a.epoch, a.status);
+                     a.world, a.epoch, a.status, a.timeout_ns);
 }
 
 // --------------------------------------------------------------------------- return put
@@ -437,12 +440,15 @@ __global__ void ep_return_signal_kernel(EpArgs a) {
     st_release_sys(reinterpret_cast<uint32_t*>(a.peers[d] + l.flags) + 2 * a.world + a.rank,
                    a.epoch);
   wait_all_sources(reinterpret_cast<const uint32_t*>(a.peers[a.rank] + l.flags) + 2 * a.world,
-                   a.world, a.epoch, a.status);
+                   a.world, a.epoch, a.status, a.timeout_ns);
 }
 
 // --------------------------------------------------------------------------- host
 
 namespace {
+
+// limit of the waits on other ranks, for every exchange enqueued after it is set
+std::atomic<uint64_t> g_peer_wait_timeout_ns{LMOE_WAIT_TIMEOUT_NS};
 
 int check_ep(const EpArgs& a) {
   if (a.world < 1 || a.world > kEpMaxWorld || a.rank < 0 || a.rank >= a.world) return kBadShape;
@@ -474,6 +480,7 @@ EpArgs make_ep(void* const* peers, int64_t rank, int64_t world, int64_t E, int64
   a.row_bytes = row_bytes;
   a.epoch = 0;
   a.status = status;
+  a.timeout_ns = g_peer_wait_timeout_ns.load(std::memory_order_relaxed);
   return a;
 }
 
@@ -482,6 +489,17 @@ EpArgs make_ep(void* const* peers, int64_t rank, int64_t world, int64_t E, int64
 
 // --------------------------------------------------------------------------- C ABI
 extern "C" {
+
+int lmoe_set_peer_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) ns = LMOE_WAIT_TIMEOUT_NS;
+  if (ns < 1000ull || ns > 60000000000ull) return LMOE_BAD_SHAPE;
+  lmoe::g_peer_wait_timeout_ns.store(ns, std::memory_order_relaxed);
+  return LMOE_OK;
+}
+
+uint64_t lmoe_peer_wait_timeout_ns(void) {
+  return lmoe::g_peer_wait_timeout_ns.load(std::memory_order_relaxed);
+}
 
 int64_t lmoe_ep_buffer_bytes(int64_t world, int64_t num_experts, int64_t recv_capacity_rows,
                              int64_t back_capacity_rows, int64_t row_bytes) {

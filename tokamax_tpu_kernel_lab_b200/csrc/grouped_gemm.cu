@@ -41,6 +41,8 @@
 //                 when round_gate_up, the convention of
 //                 kimi_k3_latent_moe_reference.py:296-310 / own_gateup_situ_pallas_kernel.py:116-125)
 #include <cuda.h>
+
+#include <cfloat>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -276,6 +278,9 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint32_t acc = 0, acc_phase = 0;
+    // f16 range guard: the largest magnitude this thread stored as an f16
+    // operand, and the smallest nonzero peak of its 32-value runs
+    float f16_peak = 0.f, f16_low = FLT_MAX;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileCoord tc = decode_tile<kBM>(tile_start, row_off, G, args.n_tiles, t);
       if (!mbar_wait(smem_u32(tfull + acc), acc_phase, abort_flag, args.status)) break;
@@ -345,6 +350,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
             } else {
               __nv_bfloat16* orow =
                   reinterpret_cast<__nv_bfloat16*>(args.out) + r * args.ldo + col0;
+              const float peak0 = f16_peak;
+              if (EPI == EPI_BF16 && args.out_f16) f16_peak = 0.f;  // this run's peak
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 if (col0 + j * 8 < args.N) {
@@ -364,11 +371,20 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                     for (int e = 0; e < 4; ++e) {
                       const float x0 = __uint_as_float(v[j * 8 + e * 2]);
                       const float x1 = __uint_as_float(v[j * 8 + e * 2 + 1]);
-                      pk[e] = args.out_f16 ? pack_f16x2_of_bf16(x0, x1) : pack_bf16x2(x0, x1);
+                      if (args.out_f16) {
+                        f16_peak = fmaxf(f16_peak, fmaxf(fabsf(x0), fabsf(x1)));
+                        pk[e] = pack_f16x2_of_bf16(x0, x1);
+                      } else {
+                        pk[e] = pack_bf16x2(x0, x1);
+                      }
                     }
                   }
                   *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 }
+              }
+              if (EPI == EPI_BF16 && args.out_f16) {
+                if (f16_peak > 0.f) f16_low = fminf(f16_low, f16_peak);
+                f16_peak = fmaxf(f16_peak, peak0);
               }
             }
           }
@@ -379,6 +395,12 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // f16 range guard: a bf16 result above 65504 became inf in its f16 slot,
+    // or a whole run of results was too small for f16 to carry accurately
+    if (EPI == EPI_BF16 &&
+        __any_sync(0xffffffffu, bf16_round_f(f16_peak) > kF16Max || f16_low < kF16RunMin) &&
+        lane == 0)
+      record_status(args.status, kF16Range);
     // rows at or past sum(group_sizes) are zero (ragged_dot semantics)
     if (args.zero_tail) {
       const int esize = (EPI == EPI_F32) ? 4 : 2;

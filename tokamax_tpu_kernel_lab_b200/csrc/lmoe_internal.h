@@ -75,7 +75,7 @@ int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64
                   int64_t start, int64_t num_keys, int64_t m_out, int pad_bucket, DispatchOut o,
                   void* workspace, size_t ws_bytes, cudaStream_t stream);
 int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
-                int64_t row_bytes, int convert, cudaStream_t stream);
+                int64_t row_bytes, int convert, int32_t* status, cudaStream_t stream);
 int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
                     const void* norm_scale, int64_t T, int64_t k, int64_t L, float eps, int bf16,
                     void* routed_out, void* normed_out, cudaStream_t stream);

@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     uint8_t* stg = ostage + q * C::kWarpStage;
     constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
     uint32_t acc = 0, acc_phase = 0;
+    float f16_peak = 0.f;  // largest magnitude stored as f16 by the plain epilogue
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileCoord tc = decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, t);
       if (!mbar_wait(smem_u32(acc_full + acc), acc_phase, abort_flag, args.status)) break;
@@ -340,10 +341,12 @@ __global__ void __launch_bounds__(kSwThreads, 1)
                                              (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4)) = v[p0 + jj];
             } else if (args.out_f16) {
 #pragma unroll
-              for (int jj = 0; jj < kRows; ++jj)
+              for (int jj = 0; jj < kRows; ++jj) {
+                f16_peak = fmaxf(f16_peak, fabsf(__uint_as_float(v[p0 + jj])));
                 *reinterpret_cast<uint16_t*>(dst0 + jj * kRowBytes +
                                              (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4)) =
                     out16(__uint_as_float(v[p0 + jj]), 1);
+              }
             } else {
 #pragma unroll
               for (int jj = 0; jj < kRows; ++jj)
@@ -375,6 +378,9 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // f16 range guard (the SiTU activations are bounded by beta * linear_beta)
+    if (EPI == EPI_BF16 && __any_sync(0xffffffffu, bf16_round_f(f16_peak) > kF16Max) && lane == 0)
+      record_status(args.status, kF16Range);
     // rows scattered to other GPUs: make them visible system-wide before the
     // kernel ends (the next kernel on the stream signals their arrival)
     if (args.row_dest != nullptr) __threadfence_system();

@@ -28,7 +28,18 @@ enum : int32_t {
   kLaunchFailed = 3,
   kDeviceBounds = 4,
   kWaitTimeout = 5,
+  kScratchTooSmall = 6,
+  kF16Range = 7,  // a value stored as an f16 operand was outside f16's finite range
 };
+
+// The f16 range guard.  A bf16-rounded value stored as f16 is exact for
+// magnitudes up to 65504 (the largest finite f16; the next bf16 up, 65536,
+// becomes inf) and down to 2^-17; below that the f16 subnormals keep it to
+// within 2^-25.  That error is far below bf16's own rounding unless a whole
+// run of values is tiny, so a 32-value run (32 consecutive elements of a row)
+// whose largest magnitude is nonzero but under 2^-14 is flagged too.
+constexpr float kF16Max = 65504.0f;
+constexpr float kF16RunMin = 6.103515625e-05f;  // 2^-14, the smallest normal f16
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -373,15 +373,36 @@ __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
 
 // Kernel 4: row gather, one warp per output row, 16-byte vectors.
 //   out[p, :] = token_idx[p] >= 0 ? x[token_idx[p], :] : 0      (CONVERT: bf16 -> f16)
+// Largest bf16 magnitude among 8 packed bf16 (NaN compares false and is ignored).
+__device__ __forceinline__ float bf16x8_peak(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  return m;
+}
+
 template <bool CONVERT>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restrict__ x,
                                                           const int32_t* __restrict__ token_idx,
                                                           uint4* __restrict__ out, int64_t rows,
-                                                          int vec_per_row, int64_t x_rows) {
+                                                          int vec_per_row, int64_t x_rows,
+                                                          int32_t* status) {
   const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
-  auto cv = [](uint4 v) { return CONVERT ? bf16x8_to_f16x8(v) : v; };
+  // f16 range guard of the converting form: the largest magnitude of the
+  // row being converted (per lane), checked once per row
+  float peak = 0.f;
+  bool out_of_range = false;
+  auto cv = [&peak](uint4 v) {
+    if (!CONVERT) return v;
+    peak = fmaxf(peak, bf16x8_peak(v));
+    return bf16x8_to_f16x8(v);
+  };
   // the next row's source index is fetched while this row is copied, and each
   // lane keeps eight 16-byte loads in flight, so neither load latency is paid
   // once per row
@@ -409,10 +430,19 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
         dst[v + 96] = cv(d);
       }
       for (; v < vec_per_row; v += 32) dst[v] = cv(__ldg(src + v));
+      if (CONVERT) {
+        // the whole row above f16's range, or all of it too small for f16
+        // to carry accurately (see kF16RunMin)
+        // peaks are non-negative, so their bit patterns order like the values
+        const float rp = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(peak)));
+        out_of_range |= rp > kF16Max || (rp > 0.f && rp < kF16RunMin);
+        peak = 0.f;
+      }
     } else {
       for (int v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
     }
   }
+  if (CONVERT && out_of_range && lane == 0) record_status(status, kF16Range);
 }
 
 size_t dispatch_workspace_bytes(int64_t n_ext, int64_t num_keys) {
@@ -466,7 +496,7 @@ int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64
 }
 
 int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
-                int64_t row_bytes, int convert, cudaStream_t stream) {
+                int64_t row_bytes, int convert, int32_t* status, cudaStream_t stream) {
   if (rows < 0 || row_bytes <= 0 || row_bytes % 16 != 0) return kBadShape;
   if (convert != 0 && convert != 1) return kBadShape;
   if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return kUnsupported;
@@ -477,11 +507,11 @@ int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* o
   if (convert)
     gather_rows_kernel<true><<<blocks, threads, 0, stream>>>(
         static_cast<const uint4*>(x), token_idx, static_cast<uint4*>(out), rows,
-        static_cast<int>(row_bytes / 16), x_rows);
+        static_cast<int>(row_bytes / 16), x_rows, status);
   else
     gather_rows_kernel<false><<<blocks, threads, 0, stream>>>(
         static_cast<const uint4*>(x), token_idx, static_cast<uint4*>(out), rows,
-        static_cast<int>(row_bytes / 16), x_rows);
+        static_cast<int>(row_bytes / 16), x_rows, status);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

@@ -268,7 +268,7 @@ class PeerExchange:
     return self._back[:rows].view(dtype)
 
   def exchange(self, x: torch.Tensor, token_idx: torch.Tensor, group_sizes: torch.Tensor,
-               experts, after_counts=None, experts_scatter=None) -> torch.Tensor:
+               experts, after_counts=None, experts_scatter=None, mark=None) -> torch.Tensor:
     """Send row x[token_idx[p]] of every dispatched row p to the owner of its
     expert, run `experts(recv, local_group_sizes)` on the rows this rank
     received, send each result back; returns the returned rows in this rank's
@@ -280,7 +280,14 @@ class PeerExchange:
     address there), so the return overlaps the down projection instead of
     following it as a copy.  No host
     synchronisation: the exchange epoch lives in the device buffer, so a
-    forward that calls this can be captured as a CUDA graph."""
+    forward that calls this can be captured as a CUDA graph.  `mark(name)`
+    (optional) is called on the host after each phase is enqueued ("counts",
+    "dispatch put", "experts", "return"), e.g. to record timing events.
+
+    Device-side errors (a bounded wait that ran out, a row past the buffer)
+    are recorded in this rank's device status word only; the other ranks see
+    empty or stale rows, not an error.  Call ops.check_device_status() on every
+    rank at step boundaries (bench.py does after each timed region)."""
     if x.shape[1] * x.element_size() != self.row_bytes:
       raise ValueError("row width does not match the exchange buffer")
     rows = token_idx.shape[0]
@@ -289,23 +296,30 @@ class PeerExchange:
     status = ops._ptr(ops.device_status(x.device))
     stream = ops._stream()
     geo = self._geo()
+    mark = mark or (lambda name: None)
     _native.call("lmoe_ep_exchange_counts", *geo, group_sizes.data_ptr(),
                  self.local_gs.data_ptr(), status, stream)
+    mark("counts")
     if after_counts is not None:
       after_counts()
     _native.call("lmoe_ep_dispatch_put", *geo, x.data_ptr(), x.shape[0],
                  token_idx.data_ptr(), rows, status, stream)
+    mark("dispatch put")
     if experts_scatter is not None:
       _native.call("lmoe_ep_return_destinations", *geo, self.row_dest.data_ptr(), self.recv_cap,
                    status, stream)
       experts_scatter(self.recv_rows(x.dtype), self.local_gs, self.row_dest)
+      mark("experts")
       _native.call("lmoe_ep_return_signal", *geo, status, stream)
+      mark("return")
       return self.back_rows(rows, torch.bfloat16)
     y = experts(self.recv_rows(x.dtype), self.local_gs)
+    mark("experts")
     if y.shape[1] * y.element_size() != self.row_bytes or not y.is_contiguous():
       raise ValueError("expert output rows do not match the exchange buffer")
     _native.call("lmoe_ep_return_put", *geo, y.data_ptr(), y.shape[0], status,
                  stream)
+    mark("return")
     return self.back_rows(rows, y.dtype)
 
   def close(self):
@@ -324,7 +338,7 @@ class PeerExchange:
 
 
 def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
-                    xchg: PeerExchange, fused_return: bool = False) -> torch.Tensor:
+                    xchg: PeerExchange, fused_return: bool = False, mark=None) -> torch.Tensor:
   """Expert-parallel forward of this rank's tokens `h` (T_local, d) with the
   exchange over NVLink peer memory (no host synchronisation).  The shared
   expert depends only on h, so it runs on a side stream forked after the
@@ -337,12 +351,22 @@ def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
   (lmoe_mxfp4_ragged_dot_scatter) instead of a separate return copy.  Same
   bits; slower on B200 at configuration 5 (n = 2: 4.69 vs 3.83 ms per step),
   because the epilogue's scattered peer stores hold up the GEMM's
-  accumulator hand-off longer than the separate copy takes."""
+  accumulator hand-off longer than the separate copy takes.
+
+  `mark(name)` (optional) is called on the host after each phase of the main
+  stream is enqueued (route, down-projection, dispatch, the exchange's
+  phases, combine, tail), e.g. to record CUDA events for a phase timeline.
+  Device-side errors land in this rank's status word only: check it on every
+  rank at step boundaries (ops.check_device_status)."""
+  mark = mark or (lambda name: None)
   main = torch.cuda.current_stream(h.device)
   side = ops.side_stream(h.device)
   idx, w = backend.route(h)
+  mark("route")
   x = backend.down(h)
+  mark("down-projection")
   token_idx, slot_pos, group_sizes = backend.dispatch(idx, w)
+  mark("dispatch sort")
   bufs = backend.shared_expert_buffers(h)
 
   def fork_shared():
@@ -353,10 +377,14 @@ def ep_forward_peer(h: torch.Tensor, backend, cfg: LatentMoEConfig,
   fused = fused_return and backend.pw.expert_gu_mx is not None
   back = xchg.exchange(x, token_idx, group_sizes, backend.experts_received,
                        after_counts=fork_shared,
-                       experts_scatter=backend.experts_received_scatter if fused else None)
+                       experts_scatter=backend.experts_received_scatter if fused else None,
+                       mark=mark)
   normed = backend.combine(back, slot_pos, w)
+  mark("combine")
   main.wait_stream(side)
-  return backend.tail_with_shared(normed, bufs[1])
+  out = backend.tail_with_shared(normed, bufs[1])
+  mark("tail")
+  return out
 
 
 def shard_experts(pw_full: PreparedWeights, rank: int, world: int) -> PreparedWeights:

@@ -219,9 +219,24 @@ def prepare_weights(w: LatentMoEWeights, dtype: torch.dtype | None = None) -> Pr
 
 def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoEConfig, *,
                        router_activation: str = "sigmoid",
-                       return_intermediates: bool = False):
+                       return_intermediates: bool = False, mxfp4_operand: str = "auto",
+                       mark=None):
   """The 8-step LatentMoE forward (kimi_k3_latent_moe_reference.py:330-435).
-  `weights` is a LatentMoEWeights (prepared on the fly) or PreparedWeights."""
+  `weights` is a LatentMoEWeights (prepared on the fly) or PreparedWeights.
+
+  mxfp4_operand (MXFP4 experts only): "auto" runs the f16-operand kernels
+  when every weight scale allows it (see mxfp4_f16_path): the latent rows
+  then travel as f16 carrying their bf16-rounded values.  That is exact for
+  magnitudes up to 65504 (bf16 values below 2^-17 lose low bits as f16
+  subnormals, an absolute error below 2^-25); a larger latent value would
+  become inf, so the kernel that writes the f16 rows records LMOE_F16_RANGE
+  in the device status word (check_device_status raises it).  "bf16" keeps
+  the latent rows in bf16 and runs the bf16-operand kernels: the same result
+  without the range limit, somewhat slower.
+
+  `mark(name)` (optional) is called on the host after each phase of the main
+  stream is enqueued, e.g. to record CUDA events for a phase timeline."""
+  mark = mark or (lambda name: None)
   pw = weights if isinstance(weights, PreparedWeights) else prepare_weights(weights)
   h = hidden_states.to(pw.dtype).contiguous()
   c = config
@@ -247,10 +262,13 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
                                      routed_scaling_factor=c.routed_scaling_factor,
                                      activation=router_activation)
-  x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw) else None)
+  mark("route")
+  x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else None)
+  mark("down-projection")
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
+  mark("dispatch sort")
   if pw.expert_gu_mx is not None:
-    act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c)
+    act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c, mark)
   elif pw.dtype == torch.bfloat16:
     sorted_tokens = ops.gather_rows(x, d.token_idx)
     act = ops.fused_gateup_situ(sorted_tokens, pw.expert_gu, d.group_sizes, beta=beta,
@@ -262,11 +280,16 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
     up = ops.ragged_dot(sorted_tokens, pw.expert_up, d.group_sizes, rhs_layout="gnk")
     act = ops.situ_and_mul(gate, up, beta, lbeta)
     down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
+  if pw.expert_gu_mx is None:
+    mark("experts")
   routed, normed = ops.combine_rmsnorm(down, d.slot_pos, topk_w, pw.norm_scale, c.rms_norm_eps,
                                        want_routed=True)
+  mark("combine")
   if overlap:
     main.wait_stream(side)
-    return _dense(normed, pw.up, addend=shared_out)
+    out = _dense(normed, pw.up, addend=shared_out)
+    mark("tail")
+    return out
   upo = _dense(normed, pw.up)
   if pw.dtype == torch.bfloat16:
     shared_act = ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
@@ -284,15 +307,18 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   return final
 
 
-def mxfp4_f16_path(pw: PreparedWeights) -> bool:
-  """True when the MXFP4 experts can run the f16-operand kernels (every scale
-  byte in their exact range); the latent activations then travel as f16
-  (the same bf16-rounded values)."""
-  return (pw.expert_gu_mx is not None and pw.expert_gu_mx.f16_operand_ok and
-          pw.expert_down_mx.f16_operand_ok)
+def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "auto") -> bool:
+  """True when the MXFP4 experts run the f16-operand kernels: mxfp4_operand
+  is "auto" and every scale byte lies in their exact range.  The latent
+  activations then travel as f16 (the same bf16-rounded values)."""
+  if mxfp4_operand not in ("auto", "bf16"):
+    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto' or 'bf16'")
+  return (mxfp4_operand == "auto" and pw.expert_gu_mx is not None and
+          pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok)
 
 
-def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMoEConfig):
+def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMoEConfig,
+                     mark=None):
   """Routed-expert FFN on MXFP4 weights: row gather into expert-sorted order,
   fused gate/up + SiTU-GLU, down GEMM.  x is f16 on the f16-operand path (see
   mxfp4_f16_path), bf16 otherwise.  (The gather can also run inside the
@@ -300,12 +326,17 @@ def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMo
   gathers feed the tensor cores ~2.5x slower than a separate gather kernel
   plus contiguous tile loads, so the forward gathers first.)
   Returns (activation, down output bf16)."""
+  mark = mark or (lambda name: None)
   rows = ops.gather_rows(x, token_idx)
+  mark("gather")
   act = ops.mxfp4_fused_gateup_situ(rows, pw.expert_gu_mx, group_sizes,
                                     beta=c.activation_situ_beta,
                                     linear_beta=c.activation_situ_linear_beta, round_gate_up=True,
                                     out_dtype=x.dtype)
-  return act, ops.mxfp4_ragged_dot(act, pw.expert_down_mx, group_sizes)
+  mark("expert gate/up")
+  down = ops.mxfp4_ragged_dot(act, pw.expert_down_mx, group_sizes)
+  mark("expert down")
+  return act, down
 
 
 def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None,

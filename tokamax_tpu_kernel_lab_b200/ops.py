@@ -467,7 +467,8 @@ def dispatch(topk_idx: torch.Tensor, topk_weight: torch.Tensor | None, num_local
 def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | None = None,
                 to_f16: bool = False):
   """out[p] = x[token_idx[p]] (zero where token_idx < 0); to_f16 converts bf16
-  rows to f16 on the way (exact in f16's normal range)."""
+  rows to f16 on the way (exact in f16's normal range; a magnitude above 65504
+  becomes inf and records LMOE_F16_RANGE in the device status word)."""
   _need_cuda(x, token_idx)
   x = x.contiguous()
   rows = token_idx.shape[0]
@@ -476,7 +477,8 @@ def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | No
   dt = torch.float16 if to_f16 else x.dtype
   res = out if out is not None else torch.empty(rows, x.shape[1], dtype=dt, device=x.device)
   _native.call("lmoe_gather_rows", _ptr(x), x.shape[0], _ptr(token_idx.to(torch.int32)),
-               _ptr(res), rows, x.shape[1] * x.element_size(), int(to_f16), _stream())
+               _ptr(res), rows, x.shape[1] * x.element_size(), int(to_f16),
+               _ptr(device_status(x.device)), _stream())
   return res
 
 
