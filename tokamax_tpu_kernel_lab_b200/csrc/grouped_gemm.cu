@@ -297,6 +297,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           tmem_ld_wait();
           const int col0 = tc.n_tile * (BN / 2) + c * 32;
           if (valid && col0 < args.N) {
+            float run_peak = 0.f;  // this run of 32 activations (f16 range guard)
             __nv_bfloat16* orow = reinterpret_cast<__nv_bfloat16*>(args.out) + r * args.ldo + col0;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -315,11 +316,13 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                     }
                     o[h] = situ_fast(g, u, args.beta, args.inv_beta, args.linear_beta, args.inv_linear_beta);
                   }
+                  if (args.out_f16) run_peak = fmaxf(run_peak, fmaxf(fabsf(o[0]), fabsf(o[1])));
                   pk[e] = args.out_f16 ? pack_f16x2_of_bf16(o[0], o[1]) : pack_bf16x2(o[0], o[1]);
                 }
                 *reinterpret_cast<uint4*>(orow + j * 8) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
               }
             }
+            if (run_peak > 0.f) f16_low = fminf(f16_low, bf16_round_f(run_peak));
           }
         }
       } else {
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
     }
     // f16 range guard: a bf16 result above 65504 became inf in its f16 slot,
     // or a whole run of results was too small for f16 to carry accurately
-    if (EPI == EPI_BF16 &&
+    if ((EPI == EPI_BF16 || EPI == EPI_SITU) &&
         __any_sync(0xffffffffu, bf16_round_f(f16_peak) > kF16Max || f16_low < kF16RunMin) &&
         lane == 0)
       record_status(args.status, kF16Range);

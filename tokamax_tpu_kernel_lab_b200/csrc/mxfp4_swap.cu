@@ -19,7 +19,11 @@
 //
 //   warp 0      token producer (TMA).
 //   warp 1      TMEM owner and UMMA issuer: M=128, N=256, K=16, f32 in TMEM,
-//               two accumulators (2 x 256 columns).
+//               two accumulators (2 x 256 columns).  A tile with fewer token
+//               rows (the last one of a group) runs its MMAs with N = its row
+//               count rounded up to 16, and its token boxes cover only those
+//               rows, so a group of 40 rows costs 48 columns of tensor time,
+//               not 256.
 //   warps 2-5   epilogue.  TMEM lane = weight row, column = token: each warp
 //               reads its 32 lanes, transposes through a small shared-memory
 //               tile and stores token-major rows.
@@ -31,6 +35,7 @@
 // one warp and meets through one shuffle.
 #include <cuda.h>
 
+#include <cfloat>
 #include <cstdlib>
 #include <mutex>
 
@@ -55,6 +60,11 @@ static_assert(kPStages % 2 == 0 && kDStages % 2 == 0, "each ring slot belongs to
 
 struct SwCfg {
   static constexpr int kTokBytes = kTokTile * kBK * 2;     // 32 KB
+  // token rows are copied in boxes of 64 (8 KB, a multiple of the 1 KB
+  // 128-byte-swizzle atom, so stacked boxes form the same layout as one
+  // 256-row box); a partial tile copies only the boxes it needs
+  static constexpr int kTokBoxRows = 64;
+  static constexpr int kTokBoxBytes = kTokBoxRows * kBK * 2;
   static constexpr int kPackedBytes = kWRows * (kBK / 2);  // 4 KB
   static constexpr int kABytes = kWRows * kBK * 2;         // 16 KB
   static constexpr int kWarpStage = 1024;                  // epilogue transpose tile per warp
@@ -195,6 +205,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
         const TileCoord tc = decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, t);
         const int wb0 = weight_row<EPI>(args, tc.n_tile, 0);
         const int wb1 = EPI == EPI_SITU ? weight_row<EPI>(args, tc.n_tile, 1) : wb0 + 64;
+        // token boxes this tile needs (a tile holds at least one row)
+        const int n_box = (min(kTokTile, tc.row_end - tc.row0) + C::kTokBoxRows - 1) / C::kTokBoxRows;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(emptyb + stage), phase ^ 1u, abort_flag, args.status)) {
             ok = false;
@@ -202,8 +214,11 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           }
           const uint32_t fb = smem_u32(fullb + stage);
           if (tok) {
-            mbar_arrive_expect_tx(fb, C::kTokBytes);
-            tma_load_2d(smem_u32(tstages + stage * C::kTokBytes), &tmTok, fb, kb * kBK, tc.row0);
+            mbar_arrive_expect_tx(fb, n_box * C::kTokBoxBytes);
+            const uint32_t t_dst = smem_u32(tstages + stage * C::kTokBytes);
+            for (int i = 0; i < n_box; ++i)
+              tma_load_2d(t_dst + i * C::kTokBoxBytes, &tmTok, fb, kb * kBK,
+                          tc.row0 + i * C::kTokBoxRows);
           } else {
             mbar_arrive_expect_tx(fb, C::kPackedBytes);
             const uint32_t p_dst = smem_u32(pstages + stage * C::kPackedBytes);
@@ -227,12 +242,15 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc =
-          kF16 ? idesc_f16_f32(kWRows, kTokTile, false) : idesc_bf16_f32(kWRows, kTokTile, false);
       RingPos ts, ds;
       uint32_t acc = 0, acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        // UMMA N: the tile's token rows rounded up to 16 (N % 16 == 0 for M = 128)
+        const TileCoord tc = decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, t);
+        const uint32_t n_mma = (min(kTokTile, tc.row_end - tc.row0) + 15) & ~15;
+        const uint32_t idesc =
+            kF16 ? idesc_f16_f32(kWRows, n_mma, false) : idesc_bf16_f32(kWRows, n_mma, false);
         if (!mbar_wait(smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.status)) {
           ok = false;
           break;
@@ -277,6 +295,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
     uint32_t acc = 0, acc_phase = 0;
     float f16_peak = 0.f;  // largest magnitude stored as f16 by the plain epilogue
+    float f16_low = FLT_MAX;  // smallest nonzero peak of a stored f16 SiTU run
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       const TileCoord tc = decode_tile<kTokTile>(tile_start, row_off, G, args.n_tiles, t);
       if (!mbar_wait(smem_u32(acc_full + acc), acc_phase, abort_flag, args.status)) break;
@@ -317,8 +336,14 @@ __global__ void __launch_bounds__(kSwThreads, 1)
             const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
             uint16_t* orow =
                 reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
-            if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = src[0];
-            if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = src[1];
+            const uint4 s0 = src[0], s1 = src[1];
+            if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = s0;
+            if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = s1;
+            if (args.out_f16) {
+              // f16 range guard: this token's 16 activations all tiny
+              const float run = fmaxf(f16x8_peak(s0), f16x8_peak(s1));
+              if (run > 0.f) f16_low = fminf(f16_low, run);
+            }
           }
           __syncwarp();
         } else {
@@ -378,8 +403,12 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // f16 range guard (the SiTU activations are bounded by beta * linear_beta)
-    if (EPI == EPI_BF16 && __any_sync(0xffffffffu, bf16_round_f(f16_peak) > kF16Max) && lane == 0)
+    // f16 range guard: above 65504 (the SiTU activations are bounded by
+    // beta * linear_beta, so only the plain epilogue can overflow), or a run
+    // of SiTU activations too small for f16 to carry accurately
+    if (__any_sync(0xffffffffu, (EPI == EPI_BF16 && bf16_round_f(f16_peak) > kF16Max) ||
+                                    (EPI == EPI_SITU && f16_low < kF16RunMin)) &&
+        lane == 0)
       record_status(args.status, kF16Range);
     // rows scattered to other GPUs: make them visible system-wide before the
     // kernel ends (the next kernel on the stream signals their arrival)
@@ -545,9 +574,9 @@ int mxfp4_swap_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, in
   }();
   if (pair) return mxfp4_pair_gemm(lhs, packed, a, epi, lhs_f16, stream);
   CUtensorMap tok, w;
-  // tokens: dims {K, M}, box {64, 256}, 128-byte swizzle (K-major UMMA B)
+  // tokens: dims {K, M}, box {64, 64}, 128-byte swizzle (K-major UMMA B)
   if (!encode_tmap_bf16_2d(&tok, lhs, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M),
-                           static_cast<uint64_t>(a.K) * 2, kBK, kTokTile))
+                           static_cast<uint64_t>(a.K) * 2, kBK, SwCfg::kTokBoxRows))
     return kLaunchFailed;
   // packed codes: dims {K/2 bytes, n_weight, G}, box {32 bytes, 64 rows}
   const int64_t kh = a.K / 2;

@@ -41,6 +41,18 @@ enum : int32_t {
 constexpr float kF16Max = 65504.0f;
 constexpr float kF16RunMin = 6.103515625e-05f;  // 2^-14, the smallest normal f16
 
+// Largest magnitude of 8 packed f16 (NaN ignored).
+__device__ __forceinline__ float f16x8_peak(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+    m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+  }
+  return m;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
