@@ -462,6 +462,70 @@ def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
   return out
 
 
+def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
+  """The opt-in block-scaled path (MXFP8 activations x MXFP4 weights on
+  kind::mxf8f6f4): the configuration-5 layer forward with
+  mxfp4_operand="mxfp8", its two routed GEMMs and the quantising gather
+  standalone, and configuration 4 on it.  Its MMA runs at twice the bf16
+  rate, so its roofline peak here is twice the measured bf16 burst."""
+  import numpy as np
+  import torch
+
+  iters = max(3, min(args.steps, 10))
+  fp8_peak = dict(peaks, bf16_tflops=2 * peaks["bf16_tflops"])
+  src = f"{peak_src} (fp8 = 2 x bf16 burst)"
+  out = {}
+  for _ in range(2):
+    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp8")
+  torch.cuda.synchronize()
+  graph = torch.cuda.CUDAGraph()
+  with torch.cuda.graph(graph):
+    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp8")
+  ms = time_launches(graph.replay, max(5, args.steps))
+  out["layer"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
+  del graph
+  _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True, mxfp4_operand="mxfp8")
+  gs, tix = inter["group_sizes"], inter["token_idx"]
+  x = inter["latent_projection"]
+  gu, dn = lm.latent_moe.blockscaled_experts(pw)
+  rows = ops.quantize_mxfp8_rows(x, gs, tix)
+  act = ops.mxfp8_mxfp4_gateup_situ(rows, gu)
+  act_q = ops.quantize_mxfp8_rows(act, gs, padded_input=True)
+  down = ops.mxfp8_mxfp4_ragged_dot(act_q, dn)
+  M = tix.shape[0]
+  L, I = cfg.latent_size, cfg.intermediate_size
+  nz = int((gs > 0).sum())
+  ms_q = time_launches(lambda: ops.quantize_mxfp8_rows(x, gs, tix, out=rows), iters)
+  ms_gu = time_launches(lambda: ops.mxfp8_mxfp4_gateup_situ(rows, gu, out=act), iters)
+  ms_dn = time_launches(lambda: ops.mxfp8_mxfp4_ragged_dot(act_q, dn, out=down), iters)
+  out["gather_quantize"] = {"ms": ms_q, "gbs": (M * L * 2 + M * L * (1 + 1 / 32)) / (ms_q / 1e3) / 1e9}
+  out["gateup_situ"] = roofline_entry(ms_gu, 2.0 * M * L * 2 * I,
+                                      M * L * (1 + 1 / 32) + nz * 2 * I * L * 0.53 + M * I * 2,
+                                      fp8_peak, src)
+  out["down"] = roofline_entry(ms_dn, 2.0 * M * I * L,
+                               M * I * (1 + 1 / 32) + nz * L * I * 0.53 + M * L * 2, fp8_peak, src)
+  # configuration 4 (bf16 x quantised to MXFP8 first; the quantisation is
+  # timed with the GEMM)
+  g4, k4, n4, m4 = 128, 4096, 2048, 16384
+  gen = torch.Generator(device=dev).manual_seed(args.seed + 4)
+  w4 = ops.prepare_mxfp4_blockscaled(lm.random_mxfp4(g4, n4, k4, seed=3, device=dev,
+                                                     scale_exp=(-6, 2)))
+  x4 = torch.randn(m4, k4, generator=gen, device=dev).to(torch.bfloat16)
+  gs4 = torch.from_numpy(np.random.default_rng(3).multinomial(m4, np.full(g4, 1 / g4)).astype(
+      np.int32)).to(dev)
+  a4 = ops.quantize_mxfp8_rows(x4, gs4)
+  o4 = ops.mxfp8_mxfp4_ragged_dot(a4, w4)
+  ms4 = time_launches(lambda: (ops.quantize_mxfp8_rows(x4, gs4, out=a4),
+                               ops.mxfp8_mxfp4_ragged_dot(a4, w4, out=o4)), iters)
+  out["config4"] = roofline_entry(ms4, 2.0 * m4 * k4 * n4,
+                                  m4 * k4 * 2 + g4 * n4 * (k4 // 2 + k4 // 32) + m4 * n4 * 2,
+                                  fp8_peak, src)
+  del w4, x4, a4, o4
+  torch.cuda.synchronize()
+  torch.cuda.empty_cache()
+  return out
+
+
 def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
   """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay)."""
   import torch
@@ -720,11 +784,12 @@ def main():
                                              pw.expert_gu_mx.scale.numel())}
 
   # ---------------------------------------------------------------- other configurations
-  configs = sweep = None
+  configs = sweep = mx8 = None
   if world == 1 and not args.no_extras:
     del xs, act, gs
     configs = gpu_config_extras(args, lm, ops, dev, peaks, peak_src)
     sweep = gpu_token_sweep(args, lm, pw, cfg, dev)
+    mx8 = gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src)
 
   # ---------------------------------------------------------------- CPU baseline
   cpu = None
@@ -751,6 +816,7 @@ def main():
   if configs is not None:
     line["configs"] = configs
     line["token_sweep"] = sweep
+    line["mxfp8_fast_path"] = mx8
   print(json.dumps(line), flush=True)
 
 

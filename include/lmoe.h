@@ -360,6 +360,60 @@ LMOE_API int lmoe_ep_return_signal(void* const* peers_dev, int64_t rank, int64_t
                                    int64_t back_capacity_rows, int64_t row_bytes,
                                    int32_t* dev_status, void* stream);
 
+/* Block-scaled fast path: MXFP8 activations x MXFP4 weights on
+ * tcgen05.mma kind::mxf8f6f4.block_scale (opt-in; the activations are
+ * rounded to e4m3 with one E8M0 scale per 32 K values, so results differ
+ * from the exact MXFP4 path by that rounding, ~3% normwise on N(0,1) rows).
+ * Activation rows live in a padded layout: every group's rows start at a
+ * multiple of 128 (lmoe_mxfp8_padded_rows gives the capacity for num_rows
+ * rows in num_groups groups); scale factors live in 512-byte atoms of 128
+ * rows x 4 K blocks (byte r0*16 + r1*4 + kb for row r0 + 32*r1), the layout
+ * the tensor core's scale copies read.
+ * The reference's operator has the hook for quantising the activations
+ * (`maybe_quantize_lhs`, 05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:257-263)
+ * but never uses it; its MXFP4 weights are dequantised first
+ * (05_ragged_dot_on_tpu/mxfp4_dequant.py:29-67). */
+LMOE_API int64_t lmoe_mxfp8_padded_rows(int64_t num_rows, int64_t num_groups);
+/* One-time weight preparation: MXFP4 codes (g, n, k/2) + E8M0 scales (g, n,
+ * k/32) -> scale atoms (g, n/128, k/128, 512) and, with interleave_gateup = 1
+ * (a fused [gate | up] weight of n = 2I rows), the codes with gate/up rows
+ * interleaved (row 2i = gate i, 2i+1 = up i; out_packed, same size);
+ * interleave_gateup = 0 leaves the codes as they are (out_packed unused). */
+LMOE_API int lmoe_mxfp4_repack_blockscaled(const void* weight_packed, const void* weight_scale,
+                                           int64_t g, int64_t n, int64_t k, int interleave_gateup,
+                                           void* out_packed, void* out_sf, void* stream);
+/* Quantise rows to MXFP8: row p of the output is x[token_idx[p]] (token_idx
+ * NULL: x[p]; an index < 0 gives a zero row), stored at its padded position
+ * (group_sizes NULL: position p) as e4m3 (out_q, m_pad_capacity x k bytes)
+ * with its scales in atoms (out_sf, m_pad_capacity/128 x k/128 x 512).  x is
+ * bf16 (x_f16 = 0) or f16.  k a multiple of 128. */
+LMOE_API int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16,
+                                      const int32_t* token_idx, const int32_t* group_sizes,
+                                      int64_t num_groups, int64_t rows, int64_t k, void* out_q,
+                                      void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                      void* stream);
+/* positions (n int32, sorted-order rows; < 0 passes through as -1) -> their
+ * padded positions (the slot positions the combine reads the padded expert
+ * outputs with). */
+LMOE_API int lmoe_mxfp8_pad_positions(const int32_t* positions, int64_t n,
+                                      const int32_t* group_sizes, int64_t num_groups, int32_t* out,
+                                      void* stream);
+/* Grouped GEMM of padded MXFP8 rows against prepared MXFP4 weights:
+ *   epi 0: out[r] = act[r] @ W[g]^T, out_dtype 0 bf16 / 1 f32 / 2 f16 (bf16 values)
+ *   epi 3: SiTU-GLU over interleaved gate/up rows (n_out = intermediate size),
+ *          out_dtype 0 bf16 / 2 f16; beta, linear_beta, round_gate_up as in
+ *          lmoe_gateup_situ_bf16
+ * Output rows are the padded rows (out has m_pad rows); only each group's
+ * first group_sizes[g] rows are written.  g <= 1024.  Replaces the quantised
+ * form of PallasMosaicTpuV2RaggedDot (kimi_k3_latent_moe_ragged_dot.py:2714-2953)
+ * for MXFP4 weights with MXFP8 activations. */
+LMOE_API int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf,
+                                           const void* w_packed, const void* w_sf,
+                                           const int32_t* group_sizes, void* out, int64_t m_pad,
+                                           int64_t k, int64_t n_out, int64_t g, int epi,
+                                           float beta, float linear_beta, int round_gate_up,
+                                           int out_dtype, int32_t* dev_status, void* stream);
+
 /* Scatter-add combine of one expert shard:
  *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0
  * Replaces _combine_shard_contribution

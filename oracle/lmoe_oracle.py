@@ -301,9 +301,12 @@ def combine_full(outs: np.ndarray, order: np.ndarray, topk_weight: np.ndarray, d
 
 def latent_moe_forward(hidden_states: np.ndarray, w: Weights, cfg: LatentMoEConfig,
                        dtype: str = "fp32", router_activation: str = "sigmoid",
-                       return_intermediates: bool = False):
+                       return_intermediates: bool = False, quantize_activations: bool = False):
   """Restates `latent_moe_forward` (KR:330-435) with the 18 staged
-  intermediates of the golden bundles (06_.../generate_pytorch_golden.py)."""
+  intermediates of the golden bundles (06_.../generate_pytorch_golden.py).
+  quantize_activations=True models the block-scaled fast path: the expert
+  FFN's two activation operands (the dispatched latent rows and the SiTU
+  output) are rounded to MXFP8 (quantize_mxfp8) before their matmuls."""
   inter = {}
   h = to_dtype(hidden_states, dtype)
   logits, scores, sfc, topk_idx, topk_weight = router_gate(
@@ -317,10 +320,11 @@ def latent_moe_forward(hidden_states: np.ndarray, w: Weights, cfg: LatentMoEConf
   inter["sorted_token_indices"] = order
   inter["group_sizes"] = group_sizes
   sorted_tokens = x[sorted_token_idx]
-  gate = ragged_dot(sorted_tokens, w.expert_gate, group_sizes, dtype)
-  up = ragged_dot(sorted_tokens, w.expert_up, group_sizes, dtype)
+  mx = (lambda a: dequantize_mxfp8(*quantize_mxfp8(a))) if quantize_activations else (lambda a: a)
+  gate = ragged_dot(mx(sorted_tokens), w.expert_gate, group_sizes, dtype)
+  up = ragged_dot(mx(sorted_tokens), w.expert_up, group_sizes, dtype)
   situ = situ_and_mul(gate, up, cfg.activation_situ_beta, cfg.activation_situ_linear_beta, dtype)
-  down = ragged_dot(situ, w.expert_down, group_sizes, dtype)
+  down = ragged_dot(mx(situ), w.expert_down, group_sizes, dtype)
   inter.update(expert_gate_output=gate, expert_up_output=up, situ_output=situ,
                expert_down_output=down)
   routed, unsorted = combine_full(down, order, topk_weight, dtype)
@@ -562,6 +566,58 @@ def dequantize_fp8_blockwise(q: np.ndarray, scale: np.ndarray) -> np.ndarray:
 def fp8_ragged_dot(lhs, q, scale, group_sizes, dtype="bf16"):
   """ragged_dot(lhs, dequantize_fp8_blockwise(q, scale)) (KRD:2816-2821, 2925-2931)."""
   return ragged_dot(lhs, dequantize_fp8_blockwise(q, scale), group_sizes, dtype=dtype)
+
+
+# ----------------------------------------------------------------------------
+# MXFP8 activations x MXFP4 weights: the block-scaled fast path
+# ----------------------------------------------------------------------------
+# The reference's operator has a hook for quantising the activations inside
+# the grouped matmul (`maybe_quantize_lhs`, KRD:257-263, 2749-2757) but never
+# exercises it; its MXFP4 weights are always dequantised first (MXD:29-67).
+# The fast path quantises each activation row to MXFP8 (OCP microscaling:
+# one E8M0 power-of-two scale per 32 consecutive K values, e4m3 elements)
+# and multiplies it with the MXFP4 weights on the block-scaled tensor core.
+# Scale rule: the smallest power of two 2^e with amax <= 448 * 2^e (so no
+# element saturates), elements rounded to nearest even in e4m3.
+
+
+def mxfp8_scale_exponent(amax: np.ndarray) -> np.ndarray:
+  """Per-block exponent e (int32) with amax <= 448 * 2^e, the smallest such:
+  with amax = f * 2^E (f in [1, 2)), e = E - 8, or E - 7 when f > 1.75.
+  amax == 0 gives -127 (E8M0 byte 0).  Clamped to [-127, 127]."""
+  a = np.asarray(amax, np.float32)
+  bits = a.view(np.uint32)
+  E = ((bits >> 23) & 0xFF).astype(np.int32) - 127
+  mant = (bits & 0x7FFFFF).astype(np.int64)
+  e = E - 8 + (mant > 0x600000).astype(np.int32)
+  e = np.where(a == 0, -127, e)
+  return np.clip(e, -127, 127).astype(np.int32)
+
+
+def quantize_mxfp8(x: np.ndarray, block: int = 32):
+  """(rows, K) float32 -> (e4m3 values as float32 (rows, K), E8M0 bytes
+  (rows, K / block) uint8); x ~= values * 2^(byte - 127) blockwise."""
+  x = np.asarray(x, np.float32)
+  r, k = x.shape
+  xb = x.reshape(r, k // block, block)
+  e = mxfp8_scale_exponent(np.abs(xb).max(axis=2))
+  q = e4m3_round(xb * np.ldexp(np.float32(1.0), -e)[:, :, None].astype(np.float32))
+  return q.reshape(r, k), (e + 127).astype(np.uint8)
+
+
+def dequantize_mxfp8(q: np.ndarray, sf: np.ndarray, block: int = 32) -> np.ndarray:
+  r, k = q.shape
+  scale = np.ldexp(np.float32(1.0), sf.astype(np.int32) - 127).astype(np.float32)
+  return (q.reshape(r, k // block, block) * scale[:, :, None]).reshape(r, k).astype(np.float32)
+
+
+def mxfp8_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_sizes):
+  """f32 result of the block-scaled grouped matmul: the dequantised MXFP8
+  rows times the dequantised MXFP4 weights (every product is exact in f32;
+  only the summation order can differ).  weight (G, N, K/2) codes + (G, N,
+  K/32) scales in the checkpoint's (out, in) layout."""
+  lhs = dequantize_mxfp8(lhs_q, lhs_sf)
+  return ragged_dot(lhs, LazyMXFP4Experts(weight_packed, weight_scale), group_sizes, dtype="fp32")
 
 
 # ----------------------------------------------------------------------------

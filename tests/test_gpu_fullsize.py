@@ -20,7 +20,7 @@ import pytest
 import torch
 
 from oracle import lmoe_oracle as O
-from tests.gpu_util import assert_bf16_close, routing_agreement, to_np
+from tests.gpu_util import assert_bf16_allclose, assert_bf16_close, routing_agreement, to_np
 
 pytestmark = pytest.mark.gpu
 
@@ -91,8 +91,22 @@ def test_config5_full_layer_sampled_tokens_match_oracle(lm):
   ref, rinter = O.latent_moe_forward(hs, w, ocfg, dtype="bf16", return_intermediates=True)
   got_idx = inter["topk_indices"].cpu().numpy()[sample]
   same = routing_agreement(got_idx, rinter["router_scores_for_choice"], rinter["topk_indices"])
-  got = to_np(final)[sample]
-  assert_bf16_close(ref[same], got[same], "config 5 sampled tokens")
+  sel = lambda name: to_np(inter[name])[sample][same]
+  # every stage: per element |d| <= 2e-2 + 1e-2 |ref| (the RMS-normalised
+  # values and the dense branches reach 4-8, where one bf16 spacing is 1/32)
+  # and 1e-2 normwise
+  for name in ("routed_output_after_combine", "normalized_output"):
+    assert_bf16_allclose(rinter[name][same], sel(name), f"config 5 {name}")
+  upo, shr = rinter["up_projection_output"][same], rinter["shared_expert_output"][same]
+  assert_bf16_allclose(upo, sel("up_projection_output"), "config 5 up-projection")
+  assert_bf16_allclose(shr, sel("shared_expert_output"), "config 5 shared expert")
+  # the output is bf16(upo + shared): where the two cancel, their own one-ulp
+  # differences remain, so the per-element bound scales with |upo| + |shared|
+  got = to_np(final)[sample][same]
+  ref_f = ref[same]
+  bound = 2e-2 + 1e-2 * (np.abs(upo) + np.abs(shr))
+  assert np.all(np.abs(got - ref_f) <= bound), float((np.abs(got - ref_f) - bound).max())
+  assert float(np.abs(got - ref_f).max() / np.abs(ref_f).max()) <= 1e-2
 
 
 def test_config3_bf16_fused_gateup_and_down_full_size(lm):

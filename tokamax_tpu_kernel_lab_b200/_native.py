@@ -58,6 +58,13 @@ SIGNATURES = {
     "lmoe_combine_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p, _p, _p]),
     "lmoe_combine_scatter_add": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]),
     "lmoe_ep_reorder": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
+    "lmoe_mxfp8_padded_rows": (_i64, [_i64, _i64]),
+    "lmoe_mxfp4_repack_blockscaled": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _p, _p, _p]),
+    "lmoe_mxfp8_quantize_rows": (_i32, [_p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p, _p, _i64,
+                                        _p, _p]),
+    "lmoe_mxfp8_pad_positions": (_i32, [_p, _i64, _p, _i64, _p, _p]),
+    "lmoe_mxfp8_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32,
+                                             _f32, _f32, _i32, _i32, _p, _p]),
     "lmoe_dispatch_static_scratch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p,
                                             _p, _p, _p, _p, _p, _p]),
     "lmoe_ep_buffer_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),
@@ -78,7 +85,8 @@ SIGNATURES = {
 KERNELS_PER_CALL = {"lmoe_dispatch": 3, "lmoe_ep_dispatch_put": 2, "lmoe_ep_return_put": 2,
                     "lmoe_ep_buffer_alloc": 0, "lmoe_ep_buffer_open": 0,
                     "lmoe_ep_buffer_close": 0, "lmoe_ep_buffer_free": 0,
-                    "lmoe_set_peer_wait_timeout_ns": 0}
+                    "lmoe_set_peer_wait_timeout_ns": 0,
+                    "lmoe_mxfp4_repack_blockscaled": 2}
 launch_count = 0
 
 

@@ -17,6 +17,14 @@ bool encode_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uin
 bool encode_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                          uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
                          uint32_t box1);
+// 2D uint8 tensor map (e4m3 rows) with 128-byte swizzle; box {box_inner bytes, box_outer rows}.
+bool encode_tmap_u8_2d_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                             uint64_t outer_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+// 3D tensor map over packed 4-bit codes (groups, rows, k codes; k/2 bytes per
+// row) that the TMA unpacks into the block-scaled MMA's shared-memory form
+// (16 codes per 16 bytes), 128-byte swizzle, box {128 codes, 128 rows, 1}.
+bool encode_tmap_fp4_unpacked_3d(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows,
+                                 uint64_t groups);
 // Tensor map for raw bytes (uint8), no swizzle, 3D.
 bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                        uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,

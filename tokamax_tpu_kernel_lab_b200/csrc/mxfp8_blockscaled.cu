@@ -1,0 +1,842 @@
+// Block-scaled fast path: MXFP8 activations x MXFP4 weights on the
+// block-scaled tensor core (tcgen05.mma kind::mxf8f6f4.block_scale).
+//
+// The exact MXFP4 kernels (mxfp4_swap.cu) expand every weight tile to f16 or
+// bf16 in shared memory and multiply on kind::f16.  This path instead feeds
+// the e2m1 codes to the tensor core as they are -- the TMA unpacks each group
+// of 16 codes into the 16-byte-per-16-element shared-memory form the MMA
+// reads -- with their E8M0 block scales in tensor memory, and quantises the
+// activations to MXFP8 (e4m3 elements, one E8M0 scale per 32 K values; the
+// scale rule is the smallest power of two that fits the block's absolute
+// maximum under 448, so no element saturates).  No expansion work at all,
+// and each MMA instruction covers K = 32 instead of 16.  The price is the
+// activation rounding: this is an opt-in path with a measured error, not a
+// replacement for the exact one.  The reference's operator carries the hook
+// for this (`maybe_quantize_lhs`,
+// 05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:257-263) but never
+// exercises it.
+//
+// Layouts (all prepared once, or produced by the kernels here):
+//   weights     codes (G, N, K/2) u8, the checkpoint's (out, in) layout; for a
+//               fused gate/up weight the rows are interleaved (row 2i = gate
+//               feature i, 2i+1 = up feature i) so a (gate, up) pair lands in
+//               adjacent accumulator lanes
+//   weight SF   (G, N/128, K/128) atoms of 512 bytes: the scales of 128 rows
+//               x 4 K blocks, byte r0*16 + r1*4 + kb for row r0 + 32*r1,
+//               the layout tcgen05.cp 32x128b.warpx4 copies to tensor memory
+//               (row r's scales for the MMA's 4 K blocks land in TMEM column
+//               r/32 of every lane quarter, byte kb)
+//   activations e4m3 rows (M_pad, K); every expert's rows start at a multiple
+//               of 128 (rows past an expert's count up to that boundary are
+//               padding nobody reads), so a 128-row tile owns whole atoms
+//   act SF      (M_pad/128, K/128) atoms, the same byte layout per 128 rows
+//
+// GEMM tile: 128 weight rows (UMMA M) x 192 token rows (UMMA N, or the tile's
+// row count rounded up to 16), K step 128 = 4 MMAs of K 32.  Two 192-column
+// accumulators (at columns 0 and 256) leave room for the scale columns, and
+// every tile of a group starts 64-row aligned inside its 128-aligned group, so
+// the tokens' scales for the tile are whole atoms starting 0 or 2 columns in
+// (64 rows = 2 columns).  Per ring stage: weights 16 KB (8 KB moved), tokens
+// up to 192 rows (24 KB), one weight-scale atom and up to two token-scale
+// atoms.
+//   warp 0     producer: TMA (weights, tokens) and bulk copies (scale atoms)
+//   warp 1     TMEM owner and MMA issuer; copies each stage's scale atoms into
+//              tensor memory (tcgen05.cp) ahead of its MMAs
+//   warps 2-5  epilogue (tensor-memory lane = weight row, column = token)
+#include <cuda.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/lmoe.h"
+#include "gemm_common.cuh"
+#include "lmoe_internal.h"
+#include "ptx.cuh"
+
+namespace lmoe {
+
+namespace {
+
+constexpr int kMxBK = 128;     // K elements per stage (4 MMAs of K 32)
+constexpr int kMxRows = 128;   // weight rows per tile (UMMA M)
+constexpr int kMxTok = 192;    // token rows per tile (UMMA N at most)
+constexpr int kMxStages = 4;
+constexpr int kMxAlign = 128;  // row alignment of every expert's activation rows
+constexpr int kMxMaxGroups = 1024;
+constexpr int kMxThreads = 32 * 6;
+
+struct MxCfg {
+  static constexpr int kABytes = kMxRows * kMxBK;        // 16 KB in shared memory
+  static constexpr int kATx = kMxRows * kMxBK / 2;       // 8 KB moved (4-bit codes)
+  static constexpr int kBoxRows = 64;
+  static constexpr int kBoxBytes = kBoxRows * kMxBK;     // 8 KB
+  static constexpr int kBBytes = 3 * kBoxBytes;          // up to 192 token rows of e4m3
+  static constexpr int kSfBytes = 512;
+  static constexpr int kSfbAtoms = 2;                    // 192 rows from a 0- or 64-row offset
+  // 41.5 KB of operands, padded so every stage starts 1024-byte aligned
+  static constexpr int kStageBytes =
+      (kABytes + kBBytes + (1 + kSfbAtoms) * kSfBytes + 1023) / 1024 * 1024;
+  static constexpr int kWarpStage = 1024;
+  static constexpr int kOutStageBytes = 4 * kWarpStage;
+  static constexpr int kSchedBytes = 3 * (kMxMaxGroups + 1) * 4;
+  static constexpr int kNumBars = 2 * kMxStages + 5;
+  static constexpr size_t kSmem = 1024 + size_t(kMxStages) * kStageBytes + kOutStageBytes +
+                                  kSchedBytes + 16 + 8 * kNumBars + 16;
+  static constexpr int kTmemCols = 512;  // accumulators at columns 0 and 256 (192 wide)
+  static constexpr int kAccStride = 256;
+  static constexpr int kSfaCol = kMxTok;          // scales in the gap after accumulator 0
+  static constexpr int kSfbCol = kMxTok + 4;
+  static_assert(kSfbCol + 4 * kSfbAtoms <= kAccStride, "scale columns in the gap");
+  static_assert(kStageBytes % 1024 == 0, "1024-byte aligned stages");
+  static_assert(kOutStageBytes >= 2 * kMxThreads * 4, "scan scratch");
+  static_assert(kSmem <= 232448, "shared memory");
+};
+
+// ------------------------------------------------------------------ PTX
+// D (+)= A x B with per-32-K E8M0 scales of A rows and B columns read from
+// tensor memory; A = e2m1 weights, B = e4m3 tokens (formats in idesc).
+__device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
+          "r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+      : "memory");
+}
+
+// 32 rows x 16 bytes of shared memory -> tensor-memory lanes 0-31 of every
+// lane quarter, 4 columns
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// contiguous global -> shared copy counted on an mbarrier (16-byte aligned)
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Shared-memory descriptor of a scale atom for tcgen05.cp: no swizzle,
+// 8-row core matrices of 16-byte rows 128 bytes apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>(16 >> 4) << 16;
+  d |= static_cast<uint64_t>(128 >> 4) << 32;
+  d |= 1ull << 46;
+  return d;
+}
+
+// Instruction descriptor, kind::mxf8f6f4 with block scales: A e2m1 (5), B
+// e4m3 (0), both K-major, E8M0 scales (bit 23), M, N; the scale byte of each
+// operand's TMEM word (the K block of this MMA) goes in bits 29-30 (A) and
+// 4-5 (B).
+__host__ __device__ constexpr uint32_t idesc_mx(uint32_t m, uint32_t n) {
+  return (5u << 7) | (0u << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
+}
+
+struct MxArgs {
+  const int32_t* group_sizes;
+  int32_t* status;
+  void* out;
+  const uint8_t* w_sf;    // (G, n_weight/128, K/128, 512)
+  const uint8_t* act_sf;  // (M_pad/128, K/128, 512)
+  int64_t ldo;
+  int M_pad, N, K, G;
+  int n_tiles;
+  int n_weight;
+  float beta, linear_beta, inv_beta, inv_linear_beta;
+  int round_gate_up;
+  int out_f16;
+};
+
+struct MxTile {
+  int g, n_tile, row0, rows;
+};
+
+// Schedule: padded row starts (multiples of 128), true row counts, tile starts.
+__device__ int mx_schedule(const MxArgs& a, int32_t* row_off, int32_t* row_cnt,
+                           int32_t* tile_start, int32_t* scan_rows, int32_t* scan_tiles) {
+  const int G = a.G;
+  const int nthr = blockDim.x;
+  const int per = (G + nthr - 1) / nthr;
+  const int g0 = min(G, static_cast<int>(threadIdx.x) * per);
+  const int g1 = min(G, g0 + per);
+  long long rows = 0, tiles = 0;
+  int bad = 0;
+  for (int g = g0; g < g1; ++g) {
+    const int s = __ldg(a.group_sizes + g);
+    if (s < 0) bad = 1;
+    const int ss = max(s, 0);
+    rows += (ss + kMxAlign - 1) / kMxAlign * kMxAlign;
+    tiles += static_cast<long long>((ss + kMxTok - 1) / kMxTok) * a.n_tiles;
+  }
+  scan_rows[threadIdx.x] = bad ? -1 : static_cast<int32_t>(min(rows, (long long)INT32_MAX));
+  scan_tiles[threadIdx.x] = static_cast<int32_t>(min(tiles, (long long)INT32_MAX));
+  __syncthreads();
+  __shared__ int s_total;
+  if (threadIdx.x == 0) {
+    long long r = 0, t = 0;
+    int invalid = 0;
+    for (int i = 0; i < nthr; ++i) {
+      const int rr = scan_rows[i];
+      const int tt = scan_tiles[i];
+      if (rr < 0) invalid = 1;
+      scan_rows[i] = static_cast<int32_t>(r);
+      scan_tiles[i] = static_cast<int32_t>(t);
+      r += max(rr, 0);
+      t += tt;
+    }
+    if (invalid || r > a.M_pad || t > INT32_MAX) {
+      record_status(a.status, kDeviceBounds);
+      s_total = -1;
+    } else {
+      s_total = static_cast<int>(t);
+      row_off[G] = static_cast<int32_t>(r);
+      tile_start[G] = static_cast<int32_t>(t);
+    }
+  }
+  __syncthreads();
+  if (s_total >= 0) {
+    int r = scan_rows[threadIdx.x];
+    int t = scan_tiles[threadIdx.x];
+    for (int g = g0; g < g1; ++g) {
+      const int s = __ldg(a.group_sizes + g);
+      row_off[g] = r;
+      row_cnt[g] = s;
+      tile_start[g] = t;
+      r += (s + kMxAlign - 1) / kMxAlign * kMxAlign;
+      t += ((s + kMxTok - 1) / kMxTok) * a.n_tiles;
+    }
+  }
+  __syncthreads();
+  return s_total;
+}
+
+__device__ __forceinline__ MxTile mx_tile(const int32_t* tile_start, const int32_t* row_off,
+                                          const int32_t* row_cnt, int G, int n_tiles, int t) {
+  MxTile c;
+  c.g = find_group(tile_start, G, t);
+  const int local = t - tile_start[c.g];
+  const int m_tile = local / n_tiles;
+  c.n_tile = local - m_tile * n_tiles;
+  c.row0 = row_off[c.g] + m_tile * kMxTok;
+  c.rows = min(kMxTok, row_cnt[c.g] - m_tile * kMxTok);
+  return c;
+}
+
+__device__ __forceinline__ uint16_t mx_out16(float v, int out_f16) {
+  if (out_f16) {
+    const __half h = __float2half_rn(bf16_round_f(v));
+    return *reinterpret_cast<const uint16_t*>(&h);
+  }
+  const __nv_bfloat16 b = __float2bfloat16_rn(v);
+  return *reinterpret_cast<const uint16_t*>(&b);
+}
+
+template <int kChunks>
+__device__ __forceinline__ int mx_swz(int row) {
+  return kChunks == 4 ? ((row >> 1) & 3) : (row & 7);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kMxThreads, 1)
+    mx_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
+                   const MxArgs args) {
+  using C = MxCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* ostage = stages + kMxStages * C::kStageBytes;
+  int32_t* row_off = reinterpret_cast<int32_t*>(ostage + C::kOutStageBytes);
+  int32_t* row_cnt = row_off + (kMxMaxGroups + 1);
+  int32_t* tile_start = row_cnt + (kMxMaxGroups + 1);
+  // mbarriers need 8-byte alignment (three schedule arrays of 1025 ints end at 4 mod 8)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(tile_start + (kMxMaxGroups + 1)) + 15) & ~uintptr_t(15));
+  uint64_t* full = bars;
+  uint64_t* empty = full + kMxStages;
+  uint64_t* acc_full = empty + kMxStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = args.G;
+  if (threadIdx.x == 0) *abort_flag = 0;
+  int32_t* scan = reinterpret_cast<int32_t*>(ostage);
+  const int total = mx_schedule(args, row_off, row_cnt, tile_start, scan, scan + kMxThreads);
+  if (total < 0) return;  // uniform across the CTA; nothing allocated yet
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < kMxStages; ++s) {
+      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(empty + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(acc_full + b), 1);
+      mbar_init(smem_u32(acc_empty + b), 128);
+    }
+    mbar_init(smem_u32(drain), 1);
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmT);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = args.K / kMxBK;
+  const int64_t w_sf_per_g = static_cast<int64_t>(args.n_weight / kMxRows) * num_kb * C::kSfBytes;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0, last_parity = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+        const int n_box = (tc.rows + C::kBoxRows - 1) / C::kBoxRows;
+        const uint8_t* wsf = args.w_sf + tc.g * w_sf_per_g +
+                             static_cast<int64_t>(tc.n_tile) * num_kb * C::kSfBytes;
+        // token-scale atoms from the one holding row0 through the tile's last row
+        const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
+        const uint8_t* asf = args.act_sf + static_cast<int64_t>(tc.row0 / kMxAlign) * num_kb * C::kSfBytes;
+        const int64_t atom_stride = static_cast<int64_t>(num_kb) * C::kSfBytes;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(full + stage);
+          const uint32_t base = smem_u32(stages + stage * C::kStageBytes);
+          mbar_arrive_expect_tx(fb, C::kATx + n_box * C::kBoxBytes + (1 + n_atoms) * C::kSfBytes);
+          tma_load_3d(base, &tmW, fb, kb * kMxBK, tc.n_tile * kMxRows, tc.g);
+          for (int i = 0; i < n_box; ++i)
+            tma_load_2d(base + C::kABytes + i * C::kBoxBytes, &tmT, fb, kb * kMxBK,
+                        tc.row0 + i * C::kBoxRows);
+          bulk_load(base + C::kABytes + C::kBBytes, wsf + kb * C::kSfBytes, C::kSfBytes, fb);
+          for (int i = 0; i < n_atoms; ++i)
+            bulk_load(base + C::kABytes + C::kBBytes + (1 + i) * C::kSfBytes,
+                      asf + i * atom_stride + kb * C::kSfBytes, C::kSfBytes, fb);
+          issued |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kMxStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (uint32_t s = 0; s < kMxStages; ++s)
+          if (issued & (1u << s)) mbar_drain(smem_u32(full + s), (last_parity >> s) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t sfa_t = tmem_base + C::kSfaCol;
+      const uint32_t sfb_t = tmem_base + C::kSfbCol;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+        const uint32_t n_mma = (tc.rows + 15) & ~15;
+        const uint32_t idesc = idesc_mx(kMxRows, n_mma);
+        const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
+        // token n's scales sit in column (row0 % 128 + n) / 32 of the copied
+        // atoms; row0 % 128 is 0 or 64 (tiles of 192 from 128-aligned group starts)
+        const uint32_t sfb_mma = sfb_t + static_cast<uint32_t>((tc.row0 % kMxAlign) / 32);
+        if (!mbar_wait(smem_u32(acc_empty + acc), acc_phase ^ 1u, abort_flag, args.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * C::kAccStride;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_u32(full + stage), phase, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(stages + stage * C::kStageBytes);
+          // this stage's scales into tensor memory; the tensor pipe runs them
+          // in order, after the previous stage's MMAs and before these
+          tmem_cp_sf(sfa_t, sf_desc(base + C::kABytes + C::kBBytes));
+          for (int i = 0; i < n_atoms; ++i)
+            tmem_cp_sf(sfb_t + 4 * i, sf_desc(base + C::kABytes + C::kBBytes + (1 + i) * C::kSfBytes));
+#pragma unroll
+          for (int k = 0; k < kMxBK / 32; ++k) {
+            const uint64_t adesc = smem_desc_sw128(base + k * 32, 16, 1024);
+            const uint64_t bdesc = smem_desc_sw128(base + C::kABytes + k * 32, 16, 1024);
+            const uint32_t kk = static_cast<uint32_t>(k);
+            umma_mx(d_tmem, adesc, bdesc, idesc | (kk << 29) | (kk << 4), sfa_t | (kk << 30),
+                    sfb_mma | (kk << 30), (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(smem_u32(empty + stage));
+          if (++stage == kMxStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(smem_u32(acc_full + acc));
+        acc ^= 1u;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        umma_commit(smem_u32(drain));
+        mbar_drain(smem_u32(drain), 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    uint8_t* stg = ostage + q * C::kWarpStage;
+    constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
+    uint32_t acc = 0, acc_phase = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+      if (!mbar_wait(smem_u32(acc_full + acc), acc_phase, abort_flag, args.status)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::kAccStride;
+#pragma unroll 1
+      for (int c = 0; c < kMxTok / 32; ++c) {
+        if (c * 32 >= tc.rows) break;  // warp-uniform
+        const int tok0 = tc.row0 + c * 32;
+        const int tok_end = tc.row0 + tc.rows;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, v);
+        tmem_ld_wait();
+        if (EPI == EPI_SITU) {
+          // lanes 2i / 2i+1 hold gate / up of feature i (interleaved weight rows)
+          const int odd = lane & 1;
+          uint16_t* s16 = reinterpret_cast<uint16_t*>(stg);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint32_t send = odd ? v[j] : v[16 + j];
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            float g = __uint_as_float(odd ? recv : v[j]);
+            float u = __uint_as_float(odd ? v[16 + j] : recv);
+            if (args.round_gate_up) {
+              g = bf16_round_f(g);
+              u = bf16_round_f(u);
+            }
+            const float o = situ_fast(g, u, args.beta, args.inv_beta, args.linear_beta,
+                                      args.inv_linear_beta);
+            s16[(odd * 16 + j) * 16 + (lane >> 1)] = mx_out16(o, args.out_f16);
+          }
+          __syncwarp();
+          const int tok = tok0 + lane;
+          const int f0 = tc.n_tile * (kMxRows / 2) + q * 16;
+          if (tok < tok_end) {
+            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
+            uint16_t* orow =
+                reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
+            if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = src[0];
+            if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = src[1];
+          }
+          __syncwarp();
+        } else {
+          constexpr int kRowBytes = 32 * esize;
+          constexpr int kChunks = kRowBytes / 16;
+          constexpr int kRows = C::kWarpStage / kRowBytes;
+          const int byte = lane * esize;
+          const int f0 = tc.n_tile * kMxRows + q * 32;
+#pragma unroll
+          for (int p0 = 0; p0 < 32; p0 += kRows) {
+            uint8_t* dst0 = stg + (byte & 15);
+#pragma unroll
+            for (int jj = 0; jj < kRows; ++jj) {
+              uint8_t* d = dst0 + jj * kRowBytes + (((byte >> 4) ^ mx_swz<kChunks>(jj)) << 4);
+              if (EPI == EPI_F32)
+                *reinterpret_cast<uint32_t*>(d) = v[p0 + jj];
+              else
+                *reinterpret_cast<uint16_t*>(d) = mx_out16(__uint_as_float(v[p0 + jj]), args.out_f16);
+            }
+            __syncwarp();
+            const int tok = tok0 + p0 + lane;
+            if (lane < kRows && tok < tok_end) {
+              uint8_t* orow = reinterpret_cast<uint8_t*>(args.out) +
+                              (static_cast<int64_t>(tok) * args.ldo + f0) * esize;
+#pragma unroll
+              for (int cc = 0; cc < kChunks; ++cc) {
+                if (f0 + (cc + 1) * (16 / esize) <= args.N)
+                  *reinterpret_cast<uint4*>(orow + cc * 16) = *reinterpret_cast<const uint4*>(
+                      stg + lane * kRowBytes + ((cc ^ mx_swz<kChunks>(lane)) * 16));
+              }
+            }
+            __syncwarp();
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(acc_empty + acc));
+      acc ^= 1u;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+template <int EPI>
+int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const MxArgs& a, int max_tiles,
+              cudaStream_t stream) {
+  auto kern = mx_gemm_kernel<EPI>;
+  const int dev = current_device();
+  static std::mutex mu;
+  static uint64_t configured = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(configured & (1ull << dev))) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(MxCfg::kSmem)) != cudaSuccess)
+        return kLaunchFailed;
+      configured |= 1ull << dev;
+    }
+  }
+  const int grid = max(1, min(num_sms(dev), max_tiles));
+  kern<<<grid, kMxThreads, MxCfg::kSmem, stream>>>(tw, tt, a);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+// ------------------------------------------------------------------ repack
+// Weight repack, once per weight set: rows optionally interleaved (gate/up),
+// scales gathered into 512-byte atoms, one warp per atom (lane r0 writes the
+// 16 bytes of atom row r0).
+__global__ void mx_repack_sf_kernel(const uint8_t* __restrict__ scales, int G, int N, int K,
+                                    int interleave, uint8_t* __restrict__ sf_out) {
+  const int kg_n = K / 128, rb_n = N / 128, kblocks = K / 32;
+  const int64_t atoms = static_cast<int64_t>(G) * rb_n * kg_n;
+  const int half = N / 2;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < atoms;
+       w += (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5) {
+    const int lane = threadIdx.x & 31;
+    const int kg = static_cast<int>(w % kg_n);
+    const int rb = static_cast<int>((w / kg_n) % rb_n);
+    const int g = static_cast<int>(w / (static_cast<int64_t>(kg_n) * rb_n));
+    uint32_t words[4];
+#pragma unroll
+    for (int r1 = 0; r1 < 4; ++r1) {
+      const int r = rb * 128 + lane + 32 * r1;  // row of the repacked matrix
+      const int src = interleave ? ((r & 1) ? half + (r >> 1) : (r >> 1)) : r;
+      const uint8_t* s = scales + (static_cast<int64_t>(g) * N + src) * kblocks + kg * 4;
+      words[r1] = static_cast<uint32_t>(s[0]) | (static_cast<uint32_t>(s[1]) << 8) |
+                  (static_cast<uint32_t>(s[2]) << 16) | (static_cast<uint32_t>(s[3]) << 24);
+    }
+    *reinterpret_cast<uint4*>(sf_out + w * 512 + lane * 16) =
+        make_uint4(words[0], words[1], words[2], words[3]);
+  }
+}
+
+__global__ void mx_repack_rows_kernel(const uint8_t* __restrict__ packed, int G, int N, int K,
+                                      uint8_t* __restrict__ out) {
+  // interleave gate/up rows: out row 2i = in row i, 2i+1 = in row N/2 + i
+  const int rb = K / 2 / 16;  // 16-byte chunks per row
+  const int64_t total = static_cast<int64_t>(G) * N * rb;
+  const int half = N / 2;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % rb);
+    const int64_t row = i / rb;
+    const int r = static_cast<int>(row % N);
+    const int64_t g = row / N;
+    const int src = (r & 1) ? half + (r >> 1) : (r >> 1);
+    reinterpret_cast<uint4*>(out)[i] =
+        reinterpret_cast<const uint4*>(packed)[(g * N + src) * rb + c];
+  }
+}
+
+// ------------------------------------------------------------------ quantise
+// Exponent e of a block with absolute maximum `amax`: the smallest with
+// amax <= 448 * 2^e (e4m3's largest finite is 448 = 1.75 * 2^8), E8M0 byte
+// e + 127, clamped to [0, 254]; 0 for an all-zero block.
+__device__ __forceinline__ int mx_scale_exp(float amax) {
+  if (!(amax > 0.f)) return -127;
+  const uint32_t b = __float_as_uint(amax);
+  const int E = static_cast<int>((b >> 23) & 0xFF) - 127;
+  int e = E - 8 + ((b & 0x7FFFFF) > 0x600000 ? 1 : 0);
+  return max(-127, min(127, e));
+}
+
+// 2^-e as a float for e in [-127, 127] (exact powers of two; 2^-127 is subnormal)
+__device__ __forceinline__ float mx_inv_scale(int e) {
+  const int x = -e;
+  return x >= -126 ? __uint_as_float(static_cast<uint32_t>(x + 127) << 23)
+                   : __uint_as_float(1u << (x + 149));
+}
+
+// Padded start of every group (multiples of 128) from the group sizes, in
+// shared memory: pad_off[g] = padded_start[g] - start[g]; start[g] also kept.
+__device__ void mx_group_offsets(const int32_t* gs, int G, int32_t* start, int32_t* pad_off) {
+  if (threadIdx.x == 0) {
+    int32_t s = 0, ps = 0;
+    for (int g = 0; g < G; ++g) {
+      start[g] = s;
+      pad_off[g] = ps - s;
+      const int n = max(gs[g], 0);
+      s += n;
+      ps += (n + kMxAlign - 1) / kMxAlign * kMxAlign;
+    }
+    start[G] = s;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ int mx_group_of(const int32_t* start, int G, int p) {
+  int lo = 0, hi = G - 1;  // last g with start[g] <= p
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (start[mid] <= p) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// One warp per row: gather (optional), quantise to MXFP8, store the row at its
+// padded position and its scales in the atom layout.
+template <bool F16>
+__global__ void __launch_bounds__(256) mx_quantize_kernel(
+    const uint16_t* __restrict__ x, int64_t x_rows, const int32_t* __restrict__ token_idx,
+    const int32_t* __restrict__ gs, int G, int64_t rows, int K, int64_t m_pad_cap,
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf, int32_t* status) {
+  extern __shared__ int32_t sh[];
+  int32_t* start = sh;
+  int32_t* pad_off = sh + G + 1;
+  if (gs != nullptr) mx_group_offsets(gs, G, start, pad_off);
+  const int lane = threadIdx.x & 31;
+  const int nblk = K / 32;
+  const int kg_n = K / 128;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < rows;
+       p += nwarps) {
+    int64_t dst = p;
+    if (gs != nullptr) {
+      if (p >= start[G]) continue;  // past sum(group_sizes): nothing to place
+      dst = p + pad_off[mx_group_of(start, G, static_cast<int>(p))];
+    }
+    if (dst >= m_pad_cap) {
+      if (lane == 0) record_status(status, kDeviceBounds);
+      continue;
+    }
+    const int64_t src_row = token_idx != nullptr ? token_idx[p] : p;
+    const bool zero = src_row < 0 || src_row >= x_rows;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (zero ? 0 : src_row) * K);
+    uint8_t* qrow = q + dst * K;
+    for (int b = lane; b < nblk; b += 32) {
+      float v[32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 w = zero ? make_uint4(0, 0, 0, 0) : __ldg(src + b * 4 + c);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f;
+          if (F16)
+            f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+          else
+            f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+          v[c * 8 + i * 2] = f.x;
+          v[c * 8 + i * 2 + 1] = f.y;
+        }
+      }
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      const int e = mx_scale_exp(amax);
+      const float inv = mx_inv_scale(e);
+      uint32_t packed[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        uint16_t lo, hi;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
+        packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+      uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
+      qd[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      qd[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      // atom (row block, K group), byte r0*16 + r1*4 + kb
+      const int64_t atom = (dst / 128) * kg_n + b / 4;
+      const int r = static_cast<int>(dst % 128);
+      sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
+    }
+  }
+}
+
+// positions[i] -> padded positions (the combine's slot positions)
+__global__ void mx_pad_positions_kernel(const int32_t* __restrict__ pos, int64_t n,
+                                        const int32_t* __restrict__ gs, int G,
+                                        int32_t* __restrict__ out) {
+  extern __shared__ int32_t sh[];
+  int32_t* start = sh;
+  int32_t* pad_off = sh + G + 1;
+  mx_group_offsets(gs, G, start, pad_off);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int p = pos[i];
+    out[i] = (p < 0 || p >= start[G]) ? -1 : p + pad_off[mx_group_of(start, G, p)];
+  }
+}
+
+}  // namespace
+
+}  // namespace lmoe
+
+// --------------------------------------------------------------------------- C ABI
+extern "C" {
+
+int64_t lmoe_mxfp8_padded_rows(int64_t num_rows, int64_t num_groups) {
+  if (num_rows < 0 || num_groups <= 0) return -1;
+  // every group rounded up to 128 rows
+  return (num_rows + 127 * (num_rows < num_groups ? num_rows : num_groups) + 127) / 128 * 128;
+}
+
+int lmoe_mxfp4_repack_blockscaled(const void* weight_packed, const void* weight_scale, int64_t g,
+                                  int64_t n, int64_t k, int interleave_gateup,
+                                  void* out_packed, void* out_sf, void* stream) {
+  using namespace lmoe;
+  if (g <= 0 || n <= 0 || k <= 0 || n % 128 || k % 128 || (interleave_gateup && n % 2))
+    return LMOE_BAD_SHAPE;
+  if (out_sf == nullptr || weight_scale == nullptr || (interleave_gateup && out_packed == nullptr))
+    return LMOE_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(out_sf) | reinterpret_cast<uintptr_t>(weight_packed) |
+       reinterpret_cast<uintptr_t>(out_packed)) & 15)
+    return LMOE_UNSUPPORTED;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t atoms = g * (n / 128) * (k / 128);
+  const int blocks = static_cast<int>(std::min<int64_t>((atoms * 32 + 255) / 256, 4096));
+  mx_repack_sf_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(weight_scale), (int)g,
+                                             (int)n, (int)k, interleave_gateup,
+                                             static_cast<uint8_t*>(out_sf));
+  if (cudaGetLastError() != cudaSuccess) return LMOE_LAUNCH_FAILED;
+  if (interleave_gateup) {
+    mx_repack_rows_kernel<<<4096, 256, 0, s>>>(static_cast<const uint8_t*>(weight_packed), (int)g,
+                                               (int)n, (int)k, static_cast<uint8_t*>(out_packed));
+    if (cudaGetLastError() != cudaSuccess) return LMOE_LAUNCH_FAILED;
+  }
+  return LMOE_OK;
+}
+
+int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16, const int32_t* token_idx,
+                             const int32_t* group_sizes, int64_t num_groups, int64_t rows,
+                             int64_t k, void* out_q, void* out_sf, int64_t m_pad_capacity,
+                             int32_t* dev_status, void* stream) {
+  using namespace lmoe;
+  if (rows < 0 || k <= 0 || k % 128 || m_pad_capacity < 0 || m_pad_capacity % 128) return LMOE_BAD_SHAPE;
+  if (group_sizes != nullptr && (num_groups <= 0 || num_groups > 4096)) return LMOE_BAD_SHAPE;
+  if (group_sizes == nullptr && rows > m_pad_capacity) return LMOE_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
+    return LMOE_UNSUPPORTED;
+  if (rows == 0) return LMOE_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t want = (rows * 32 + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
+  const size_t sh = group_sizes != nullptr ? static_cast<size_t>(2 * (num_groups + 1)) * 4 : 0;
+  if (x_f16)
+    mx_quantize_kernel<true><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
+        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
+        dev_status);
+  else
+    mx_quantize_kernel<false><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
+        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
+        dev_status);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+int lmoe_mxfp8_pad_positions(const int32_t* positions, int64_t n, const int32_t* group_sizes,
+                             int64_t num_groups, int32_t* out, void* stream) {
+  using namespace lmoe;
+  if (n < 0 || num_groups <= 0 || num_groups > 4096 || group_sizes == nullptr) return LMOE_BAD_SHAPE;
+  if (n == 0) return LMOE_OK;
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 1024));
+  mx_pad_positions_kernel<<<blocks, 256, static_cast<size_t>(2 * (num_groups + 1)) * 4,
+                            static_cast<cudaStream_t>(stream)>>>(positions, n, group_sizes,
+                                                                 (int)num_groups, out);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
+                                  const void* w_sf, const int32_t* group_sizes, void* out,
+                                  int64_t m_pad, int64_t k, int64_t n_out, int64_t g, int epi,
+                                  float beta, float linear_beta, int round_gate_up, int out_dtype,
+                                  int32_t* dev_status, void* stream) {
+  using namespace lmoe;
+  // epi: 0 plain (out_dtype 0 bf16, 1 f32, 2 f16), 3 SiTU-GLU over interleaved
+  // gate/up rows (n_out = intermediate; out_dtype 0 bf16, 2 f16)
+  if (g <= 0 || g > kMxMaxGroups || m_pad < 0 || m_pad % 128 || k <= 0 || k % 128 || n_out <= 0)
+    return LMOE_BAD_SHAPE;
+  if (epi != EPI_BF16 && epi != EPI_SITU) return LMOE_BAD_SHAPE;
+  if (out_dtype < 0 || out_dtype > 2 || (epi == EPI_SITU && out_dtype == 1)) return LMOE_BAD_SHAPE;
+  const int64_t n_weight = epi == EPI_SITU ? 2 * n_out : n_out;
+  if (n_weight % 128 || (epi == EPI_SITU ? n_out % 16 : n_out % 8)) return LMOE_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(w_packed) & 31) ||
+      ((reinterpret_cast<uintptr_t>(act_q) | reinterpret_cast<uintptr_t>(out) |
+        reinterpret_cast<uintptr_t>(act_sf) | reinterpret_cast<uintptr_t>(w_sf)) & 15))
+    return LMOE_UNSUPPORTED;
+  if (m_pad == 0) return LMOE_OK;
+  if (m_pad >= (1ll << 31) || k >= (1 << 20)) return LMOE_BAD_SHAPE;
+  MxArgs a{};
+  a.group_sizes = group_sizes;
+  a.status = dev_status;
+  a.out = out;
+  a.w_sf = static_cast<const uint8_t*>(w_sf);
+  a.act_sf = static_cast<const uint8_t*>(act_sf);
+  a.ldo = n_out;
+  a.M_pad = static_cast<int>(m_pad);
+  a.N = static_cast<int>(n_out);
+  a.K = static_cast<int>(k);
+  a.G = static_cast<int>(g);
+  a.n_weight = static_cast<int>(n_weight);
+  a.n_tiles = static_cast<int>(n_weight / kMxRows);
+  a.beta = beta;
+  a.linear_beta = linear_beta;
+  a.inv_beta = beta != 0.f ? 1.f / beta : 0.f;
+  a.inv_linear_beta = linear_beta != 0.f ? 1.f / linear_beta : 0.f;
+  a.round_gate_up = round_gate_up;
+  a.out_f16 = out_dtype == 2;
+  CUtensorMap tw, tt;
+  if (!encode_tmap_fp4_unpacked_3d(&tw, w_packed, static_cast<uint64_t>(k),
+                                   static_cast<uint64_t>(n_weight), static_cast<uint64_t>(g)))
+    return LMOE_LAUNCH_FAILED;
+  if (!encode_tmap_u8_2d_sw128(&tt, act_q, static_cast<uint64_t>(k), static_cast<uint64_t>(m_pad),
+                               static_cast<uint64_t>(k), kMxBK, MxCfg::kBoxRows))
+    return LMOE_LAUNCH_FAILED;
+  const int64_t tiles = (m_pad / kMxTok + g) * a.n_tiles;
+  const int max_tiles = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
+  auto s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (epi == EPI_SITU)
+    rc = launch_mx<EPI_SITU>(tw, tt, a, max_tiles, s);
+  else if (out_dtype == 1)
+    rc = launch_mx<EPI_F32>(tw, tt, a, max_tiles, s);
+  else
+    rc = launch_mx<EPI_BF16>(tw, tt, a, max_tiles, s);
+  return rc;
+}
+
+}  // extern "C"

@@ -533,3 +533,130 @@ def combine_shard_contribution(routed_out: torch.Tensor, shard_out: torch.Tensor
                _ptr(padded_combine_weight.float().contiguous()), _ptr(out), rows, L,
                out.shape[0], int(out.dtype == torch.bfloat16), _stream())
   return out
+
+
+# ----------------------------------------------------------------------------- MXFP8 x MXFP4
+# The block-scaled fast path (opt-in): activations rounded to MXFP8 (e4m3, one
+# E8M0 scale per 32 K values), MXFP4 weights fed to the block-scaled tensor
+# core as they are.  Rows live in a padded layout where every group starts at
+# a multiple of 128; scales live in 512-byte atoms of 128 rows x 4 K blocks.
+
+
+@dataclasses.dataclass
+class MXFP4BlockScaled:
+  """MXFP4 weights prepared for the block-scaled MMA: codes (G, N, K/2)
+  (gate/up rows interleaved when `gateup`), scale atoms (G, N/128, K/128, 512)."""
+
+  packed: torch.Tensor
+  sf: torch.Tensor
+  gateup: bool
+
+  @property
+  def shape(self):
+    g, n, kh = self.packed.shape
+    return g, n, kh * 2
+
+
+def prepare_mxfp4_blockscaled(w: MXFP4Weights, gateup: bool = False) -> MXFP4BlockScaled:
+  """One-time repack of MXFP4 weights (G, N, K/2) codes + (G, N, K/32) scales;
+  `gateup` marks a fused [gate | up] weight (N = 2I) whose rows are then
+  interleaved so each (gate, up) pair meets in adjacent accumulator lanes."""
+  _need_cuda(w.packed, w.scale)
+  g, n, k = w.shape
+  sf = torch.empty(g, n // 128, k // 128, 512, dtype=torch.uint8, device=w.packed.device)
+  packed = torch.empty_like(w.packed) if gateup else w.packed
+  _native.call("lmoe_mxfp4_repack_blockscaled", _ptr(w.packed.contiguous()),
+               _ptr(w.scale.contiguous()), g, n, k, int(gateup), _ptr(packed) if gateup else None,
+               _ptr(sf), _stream())
+  return MXFP4BlockScaled(packed, sf, gateup)
+
+
+@dataclasses.dataclass
+class MXFP8Rows:
+  """Activation rows quantised to MXFP8 in the padded layout: q (M_pad, K)
+  e4m3 bytes, sf (M_pad/128, K/128, 512) scale atoms, group_sizes (G,) the
+  true row counts (group g's rows start at the sum of the earlier groups'
+  counts rounded up to 128)."""
+
+  q: torch.Tensor
+  sf: torch.Tensor
+  group_sizes: torch.Tensor
+
+
+def mxfp8_padded_rows(num_rows: int, num_groups: int) -> int:
+  return int(_native.load().lmoe_mxfp8_padded_rows(num_rows, num_groups))
+
+
+def quantize_mxfp8_rows(x: torch.Tensor, group_sizes: torch.Tensor,
+                        token_idx: torch.Tensor | None = None, *, padded_input: bool = False,
+                        out: MXFP8Rows | None = None) -> MXFP8Rows:
+  """Rows x[token_idx[p]] (or x[p]) quantised to MXFP8 and placed in the
+  padded layout of `group_sizes` (the gather, the quantisation and the
+  padding in one kernel).  With padded_input=True, x is already in that
+  layout (the padded output of an earlier block-scaled GEMM) and every row
+  keeps its position.  x bf16 or f16 (K a multiple of 128)."""
+  _need_cuda(x, group_sizes, token_idx)
+  rows = token_idx.shape[0] if token_idx is not None else x.shape[0]
+  k = x.shape[1]
+  g = group_sizes.shape[0]
+  if out is None:
+    m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
+    out = MXFP8Rows(torch.empty(m_pad, k, dtype=torch.uint8, device=x.device),
+                    torch.empty(m_pad // 128, k // 128, 512, dtype=torch.uint8, device=x.device),
+                    group_sizes)
+  gs = group_sizes.to(torch.int32).contiguous()
+  out.group_sizes = gs
+  ti = None if token_idx is None else token_idx.to(torch.int32).contiguous()
+  _native.call("lmoe_mxfp8_quantize_rows", _ptr(x.contiguous()), x.shape[0],
+               int(x.dtype == torch.float16), _ptr(ti), None if padded_input else _ptr(gs), g,
+               rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)),
+               _stream())
+  return out
+
+
+def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> torch.Tensor:
+  """Sorted-order row positions -> their rows in the padded layout."""
+  _need_cuda(positions, group_sizes)
+  pos = positions.to(torch.int32).contiguous()
+  out = torch.empty_like(pos)
+  _native.call("lmoe_mxfp8_pad_positions", _ptr(pos), pos.numel(),
+               _ptr(group_sizes.to(torch.int32).contiguous()), group_sizes.shape[0], _ptr(out),
+               _stream())
+  return out
+
+
+def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows, w: MXFP4BlockScaled,
+                           out_dtype: torch.dtype = torch.bfloat16,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+  """Padded MXFP8 rows @ dequant(w[g])^T per group -> (M_pad, N); rows past
+  each group's count are not written."""
+  g, n, k = w.shape
+  if w.gateup:
+    raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
+  m_pad = a.q.shape[0]
+  res = out if out is not None else torch.empty(m_pad, n, dtype=out_dtype, device=a.q.device)
+  code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
+  _native.call("lmoe_mxfp8_mxfp4_grouped_gemm", _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
+               _ptr(a.group_sizes), _ptr(res), m_pad, k, n, g, 0, 0.0, 0.0, 0, code,
+               _ptr(device_status(a.q.device)), _stream())
+  return res
+
+
+def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows, w: MXFP4BlockScaled, *, beta: float = 4.0,
+                            linear_beta: float = 25.0, round_gate_up: bool = True,
+                            out_dtype: torch.dtype = torch.bfloat16,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+  """SiTU-GLU of the block-scaled grouped matmul against gate/up-interleaved
+  MXFP4 weights -> (M_pad, I) (padded rows)."""
+  g, two_i, k = w.shape
+  if not w.gateup:
+    raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
+  m_pad = a.q.shape[0]
+  res = out if out is not None else torch.empty(m_pad, two_i // 2, dtype=out_dtype,
+                                                device=a.q.device)
+  code = {torch.bfloat16: 0, torch.float16: 2}[res.dtype]
+  _native.call("lmoe_mxfp8_mxfp4_grouped_gemm", _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
+               _ptr(a.group_sizes), _ptr(res), m_pad, k, two_i // 2, g, 3, float(beta),
+               float(linear_beta), int(round_gate_up), code, _ptr(device_status(a.q.device)),
+               _stream())
+  return res
