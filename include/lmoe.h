@@ -385,7 +385,8 @@ LMOE_API int lmoe_mxfp4_repack_blockscaled(const void* weight_packed, const void
 /* Quantise rows to MXFP8: row p of the output is x[token_idx[p]] (token_idx
  * NULL: x[p]; an index < 0 gives a zero row), stored at its padded position
  * (group_sizes NULL: position p) as e4m3 (out_q, m_pad_capacity x k bytes)
- * with its scales in atoms (out_sf, m_pad_capacity/128 x k/128 x 512).  x is
+ * with its scales in atoms (out_sf, k/128 x m_pad_capacity/128 x 512: K-step
+ * major, so the atoms of consecutive row blocks are adjacent).  x is
  * bf16 (x_f16 = 0) or f16.  k a multiple of 128. */
 LMOE_API int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16,
                                       const int32_t* token_idx, const int32_t* group_sizes,

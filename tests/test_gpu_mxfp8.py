@@ -51,12 +51,13 @@ def padded_rows_of(gs):
   return np.concatenate([starts[g] + np.arange(int(n)) for g, n in enumerate(gs)]).astype(np.int64)
 
 
-def sf_bytes_at(sf: np.ndarray, rows: np.ndarray, k: int) -> np.ndarray:
-  """(len(rows), k/32) scale bytes read out of the atom layout."""
+def sf_bytes_at(sf: np.ndarray, rows: np.ndarray, k: int, m_pad: int) -> np.ndarray:
+  """(len(rows), k/32) scale bytes read out of the atom layout (atoms K-step
+  major: atom (kg, row block) at index kg * m_pad/128 + row block)."""
   flat = sf.reshape(-1)
   nb = k // 32
   b = np.arange(nb)
-  atom = (rows[:, None] // 128) * (k // 128) + b[None, :] // 4
+  atom = (b[None, :] // 4) * (m_pad // 128) + rows[:, None] // 128
   off = atom * 512 + (rows[:, None] % 32) * 16 + ((rows[:, None] // 32) % 4) * 4 + (b[None, :] % 4)
   return flat[off]
 
@@ -97,7 +98,7 @@ def test_quantize_rows_bit_exact_with_gather_and_padding(lm, x_dtype):
   prow = padded_rows_of(gs)
   got_q = e4m3_values(a.q)[prow]
   assert np.array_equal(got_q, qv)
-  assert np.array_equal(sf_bytes_at(a.sf.cpu().numpy(), prow, k), sf)
+  assert np.array_equal(sf_bytes_at(a.sf.cpu().numpy(), prow, k, a.q.shape[0]), sf)
 
 
 def test_pad_positions(lm):

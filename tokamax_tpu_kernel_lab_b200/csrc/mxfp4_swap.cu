@@ -60,9 +60,11 @@ static_assert(kPStages % 2 == 0 && kDStages % 2 == 0, "each ring slot belongs to
 
 struct SwCfg {
   static constexpr int kTokBytes = kTokTile * kBK * 2;     // 32 KB
-  // token rows are copied in boxes of 64 (8 KB, a multiple of the 1 KB
-  // 128-byte-swizzle atom, so stacked boxes form the same layout as one
-  // 256-row box); a partial tile copies only the boxes it needs
+  // A full tile's token rows are one 256-row box (32 KB); a partial tile
+  // copies boxes of 64 rows (8 KB, a multiple of the 1 KB 128-byte-swizzle
+  // atom, so stacked boxes form the same layout), only as many as it needs.
+  // One thread issues a copy every few hundred cycles at best, so a step's
+  // copies are kept few and large.
   static constexpr int kTokBoxRows = 64;
   static constexpr int kTokBoxBytes = kTokBoxRows * kBK * 2;
   static constexpr int kPackedBytes = kWRows * (kBK / 2);  // 4 KB
@@ -125,6 +127,7 @@ struct RingPos {
 template <int BF, int EPI>
 __global__ void __launch_bounds__(kSwThreads, 1)
     mxfp4_swap_kernel(const __grid_constant__ CUtensorMap tmTok,
+                      const __grid_constant__ CUtensorMap tmTok64,
                       const __grid_constant__ CUtensorMap tmW, const GemmArgs args) {
   using C = SwCfg;
   constexpr bool kF16 = BF == B_MXFP4F16;
@@ -179,6 +182,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     mbar_init(smem_u32(drain), 1);
     fence_mbarrier_init();
     tma_prefetch_desc(&tmTok);
+    tma_prefetch_desc(&tmTok64);
     tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
@@ -206,7 +210,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
         const int wb0 = weight_row<EPI>(args, tc.n_tile, 0);
         const int wb1 = EPI == EPI_SITU ? weight_row<EPI>(args, tc.n_tile, 1) : wb0 + 64;
         // token boxes this tile needs (a tile holds at least one row)
-        const int n_box = (min(kTokTile, tc.row_end - tc.row0) + C::kTokBoxRows - 1) / C::kTokBoxRows;
+        const int tile_rows = min(kTokTile, tc.row_end - tc.row0);
+        const int n_box = (tile_rows + C::kTokBoxRows - 1) / C::kTokBoxRows;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(emptyb + stage), phase ^ 1u, abort_flag, args.status)) {
             ok = false;
@@ -214,11 +219,16 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           }
           const uint32_t fb = smem_u32(fullb + stage);
           if (tok) {
-            mbar_arrive_expect_tx(fb, n_box * C::kTokBoxBytes);
             const uint32_t t_dst = smem_u32(tstages + stage * C::kTokBytes);
-            for (int i = 0; i < n_box; ++i)
-              tma_load_2d(t_dst + i * C::kTokBoxBytes, &tmTok, fb, kb * kBK,
-                          tc.row0 + i * C::kTokBoxRows);
+            if (tile_rows == kTokTile) {
+              mbar_arrive_expect_tx(fb, C::kTokBytes);
+              tma_load_2d(t_dst, &tmTok, fb, kb * kBK, tc.row0);
+            } else {
+              mbar_arrive_expect_tx(fb, n_box * C::kTokBoxBytes);
+              for (int i = 0; i < n_box; ++i)
+                tma_load_2d(t_dst + i * C::kTokBoxBytes, &tmTok64, fb, kb * kBK,
+                            tc.row0 + i * C::kTokBoxRows);
+            }
           } else {
             mbar_arrive_expect_tx(fb, C::kPackedBytes);
             const uint32_t p_dst = smem_u32(pstages + stage * C::kPackedBytes);
@@ -530,8 +540,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
 }
 
 template <int BF, int EPI>
-int launch_swap(const CUtensorMap& tok, const CUtensorMap& w, const GemmArgs& a, int max_tiles,
-                cudaStream_t stream) {
+int launch_swap(const CUtensorMap& tok, const CUtensorMap& tok64, const CUtensorMap& w,
+                const GemmArgs& a, int max_tiles, cudaStream_t stream) {
   auto kern = mxfp4_swap_kernel<BF, EPI>;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,17 +557,17 @@ int launch_swap(const CUtensorMap& tok, const CUtensorMap& w, const GemmArgs& a,
     }
   }
   const int grid = max(1, min(num_sms(dev), max_tiles));
-  kern<<<grid, kSwThreads, SwCfg::kSmem, stream>>>(tok, w, a);
+  kern<<<grid, kSwThreads, SwCfg::kSmem, stream>>>(tok, tok64, w, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
 template <int BF>
-int launch_swap_epi(int epi, const CUtensorMap& tok, const CUtensorMap& w, const GemmArgs& a,
-                    int max_tiles, cudaStream_t s) {
+int launch_swap_epi(int epi, const CUtensorMap& tok, const CUtensorMap& tok64,
+                    const CUtensorMap& w, const GemmArgs& a, int max_tiles, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return launch_swap<BF, EPI_BF16>(tok, w, a, max_tiles, s);
-    case EPI_F32: return launch_swap<BF, EPI_F32>(tok, w, a, max_tiles, s);
-    case EPI_SITU: return launch_swap<BF, EPI_SITU>(tok, w, a, max_tiles, s);
+    case EPI_BF16: return launch_swap<BF, EPI_BF16>(tok, tok64, w, a, max_tiles, s);
+    case EPI_F32: return launch_swap<BF, EPI_F32>(tok, tok64, w, a, max_tiles, s);
+    case EPI_SITU: return launch_swap<BF, EPI_SITU>(tok, tok64, w, a, max_tiles, s);
     default: return kUnsupported;
   }
 }
@@ -573,9 +583,12 @@ int mxfp4_swap_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, in
     return e != nullptr && e[0] == '1';
   }();
   if (pair) return mxfp4_pair_gemm(lhs, packed, a, epi, lhs_f16, stream);
-  CUtensorMap tok, w;
-  // tokens: dims {K, M}, box {64, 64}, 128-byte swizzle (K-major UMMA B)
+  CUtensorMap tok, tok64, w;
+  // tokens: dims {K, M}, boxes {64, 256} (full tiles) and {64, 64} (partial
+  // tiles), 128-byte swizzle (K-major UMMA B)
   if (!encode_tmap_bf16_2d(&tok, lhs, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M),
+                           static_cast<uint64_t>(a.K) * 2, kBK, kTokTile) ||
+      !encode_tmap_bf16_2d(&tok64, lhs, static_cast<uint64_t>(a.K), static_cast<uint64_t>(a.M),
                            static_cast<uint64_t>(a.K) * 2, kBK, SwCfg::kTokBoxRows))
     return kLaunchFailed;
   // packed codes: dims {K/2 bytes, n_weight, G}, box {32 bytes, 64 rows}
@@ -587,8 +600,8 @@ int mxfp4_swap_gemm(const void* lhs, const void* packed, GemmArgs a, int epi, in
   a.n_tiles = (a.N + feat - 1) / feat;
   const int64_t t = ((static_cast<int64_t>(a.M) + kTokTile - 1) / kTokTile + a.G) * a.n_tiles;
   const int max_tiles = static_cast<int>(t < (1 << 30) ? t : (1 << 30));
-  return lhs_f16 ? launch_swap_epi<B_MXFP4F16>(epi, tok, w, a, max_tiles, stream)
-                 : launch_swap_epi<B_MXFP4>(epi, tok, w, a, max_tiles, stream);
+  return lhs_f16 ? launch_swap_epi<B_MXFP4F16>(epi, tok, tok64, w, a, max_tiles, stream)
+                 : launch_swap_epi<B_MXFP4>(epi, tok, tok64, w, a, max_tiles, stream);
 }
 
 }  // namespace lmoe

@@ -29,7 +29,8 @@
 //   activations e4m3 rows (M_pad, K); every expert's rows start at a multiple
 //               of 128 (rows past an expert's count up to that boundary are
 //               padding nobody reads), so a 128-row tile owns whole atoms
-//   act SF      (M_pad/128, K/128) atoms, the same byte layout per 128 rows
+//   act SF      (K/128, M_pad/128) atoms, the same byte layout per 128 rows,
+//               K-step major so a tile's consecutive row blocks are one copy
 //
 // GEMM tile: 128 weight rows (UMMA M) x 192 token rows (UMMA N, or the tile's
 // row count rounded up to 16), K step 128 = 4 MMAs of K 32.  Two 192-column
@@ -39,7 +40,11 @@
 // (64 rows = 2 columns).  Per ring stage: weights 16 KB (8 KB moved), tokens
 // up to 192 rows (24 KB), one weight-scale atom and up to two token-scale
 // atoms.
-//   warp 0     producer: TMA (weights, tokens) and bulk copies (scale atoms)
+//   warp 0     weight producer: TMA (codes) and the weight-scale atom
+//   warp 6     token producer: TMA (e4m3 rows; one 192-row box for a full
+//              tile) and the token-scale atoms (one bulk copy)
+//              (one thread issues a copy only every few hundred cycles, so
+//              the copies of a step are split over two threads and kept few)
 //   warp 1     TMEM owner and MMA issuer; copies each stage's scale atoms into
 //              tensor memory (tcgen05.cp) ahead of its MMAs
 //   warps 2-5  epilogue (tensor-memory lane = weight row, column = token)
@@ -65,7 +70,8 @@ constexpr int kMxTok = 192;    // token rows per tile (UMMA N at most)
 constexpr int kMxStages = 4;
 constexpr int kMxAlign = 128;  // row alignment of every expert's activation rows
 constexpr int kMxMaxGroups = 1024;
-constexpr int kMxThreads = 32 * 6;
+constexpr int kMxThreads = 32 * 7;
+constexpr int kMxTokWarp = 6;
 
 struct MxCfg {
   static constexpr int kABytes = kMxRows * kMxBK;        // 16 KB in shared memory
@@ -252,7 +258,7 @@ __device__ __forceinline__ int mx_swz(int row) {
 template <int EPI>
 __global__ void __launch_bounds__(kMxThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
-                   const MxArgs args) {
+                   const __grid_constant__ CUtensorMap tmT64, const MxArgs args) {
   using C = MxCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -283,7 +289,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < kMxStages; ++s) {
-      mbar_init(smem_u32(full + s), 1);
+      mbar_init(smem_u32(full + s), 2);  // the weight and the token producer
       mbar_init(smem_u32(empty + s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -294,6 +300,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     fence_mbarrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmT);
+    tma_prefetch_desc(&tmT64);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::kTmemCols);
@@ -306,11 +313,13 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   const int num_kb = args.K / kMxBK;
   const int64_t w_sf_per_g = static_cast<int64_t>(args.n_weight / kMxRows) * num_kb * C::kSfBytes;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == kMxTokWarp) {
+    // ------------------------------------------------------------ producers
     if (lane == 0) {
+      const bool tok = warp == kMxTokWarp;
       uint32_t stage = 0, phase = 0, issued = 0, last_parity = 0;
       bool ok = true;
+      const int64_t row_blocks = args.M_pad / kMxAlign;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
         const int n_box = (tc.rows + C::kBoxRows - 1) / C::kBoxRows;
@@ -318,8 +327,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                              static_cast<int64_t>(tc.n_tile) * num_kb * C::kSfBytes;
         // token-scale atoms from the one holding row0 through the tile's last row
         const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
-        const uint8_t* asf = args.act_sf + static_cast<int64_t>(tc.row0 / kMxAlign) * num_kb * C::kSfBytes;
-        const int64_t atom_stride = static_cast<int64_t>(num_kb) * C::kSfBytes;
+        const int64_t rb0 = tc.row0 / kMxAlign;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(smem_u32(empty + stage), phase ^ 1u, abort_flag, args.status)) {
             ok = false;
@@ -327,15 +335,26 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           }
           const uint32_t fb = smem_u32(full + stage);
           const uint32_t base = smem_u32(stages + stage * C::kStageBytes);
-          mbar_arrive_expect_tx(fb, C::kATx + n_box * C::kBoxBytes + (1 + n_atoms) * C::kSfBytes);
-          tma_load_3d(base, &tmW, fb, kb * kMxBK, tc.n_tile * kMxRows, tc.g);
-          for (int i = 0; i < n_box; ++i)
-            tma_load_2d(base + C::kABytes + i * C::kBoxBytes, &tmT, fb, kb * kMxBK,
-                        tc.row0 + i * C::kBoxRows);
-          bulk_load(base + C::kABytes + C::kBBytes, wsf + kb * C::kSfBytes, C::kSfBytes, fb);
-          for (int i = 0; i < n_atoms; ++i)
-            bulk_load(base + C::kABytes + C::kBBytes + (1 + i) * C::kSfBytes,
-                      asf + i * atom_stride + kb * C::kSfBytes, C::kSfBytes, fb);
+          if (!tok) {
+            mbar_arrive_expect_tx(fb, C::kATx + C::kSfBytes);
+            tma_load_3d(base, &tmW, fb, kb * kMxBK, tc.n_tile * kMxRows, tc.g);
+            bulk_load(base + C::kABytes + C::kBBytes, wsf + kb * C::kSfBytes, C::kSfBytes, fb);
+          } else {
+            const uint32_t b_dst = base + C::kABytes;
+            if (tc.rows == kMxTok) {
+              mbar_arrive_expect_tx(fb, C::kBBytes + n_atoms * C::kSfBytes);
+              tma_load_2d(b_dst, &tmT, fb, kb * kMxBK, tc.row0);
+            } else {
+              mbar_arrive_expect_tx(fb, n_box * C::kBoxBytes + n_atoms * C::kSfBytes);
+              for (int i = 0; i < n_box; ++i)
+                tma_load_2d(b_dst + i * C::kBoxBytes, &tmT64, fb, kb * kMxBK,
+                            tc.row0 + i * C::kBoxRows);
+            }
+            // the tile's token-scale atoms of this K step are consecutive
+            bulk_load(base + C::kABytes + C::kBBytes + C::kSfBytes,
+                      args.act_sf + (static_cast<int64_t>(kb) * row_blocks + rb0) * C::kSfBytes,
+                      n_atoms * C::kSfBytes, fb);
+          }
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kMxStages) {
@@ -503,8 +522,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 }
 
 template <int EPI>
-int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const MxArgs& a, int max_tiles,
-              cudaStream_t stream) {
+int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const CUtensorMap& tt64,
+              const MxArgs& a, int max_tiles, cudaStream_t stream) {
   auto kern = mx_gemm_kernel<EPI>;
   const int dev = current_device();
   static std::mutex mu;
@@ -519,7 +538,7 @@ int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const MxArgs& a, int
     }
   }
   const int grid = max(1, min(num_sms(dev), max_tiles));
-  kern<<<grid, kMxThreads, MxCfg::kSmem, stream>>>(tw, tt, a);
+  kern<<<grid, kMxThreads, MxCfg::kSmem, stream>>>(tw, tt, tt64, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
@@ -628,7 +647,6 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
   if (gs != nullptr) mx_group_offsets(gs, G, start, pad_off);
   const int lane = threadIdx.x & 31;
   const int nblk = K / 32;
-  const int kg_n = K / 128;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < rows;
        p += nwarps) {
@@ -678,8 +696,8 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
       uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
       qd[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
       qd[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-      // atom (row block, K group), byte r0*16 + r1*4 + kb
-      const int64_t atom = (dst / 128) * kg_n + b / 4;
+      // atom (K group, row block), byte r0*16 + r1*4 + kb
+      const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
       const int r = static_cast<int>(dst % 128);
       sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
     }
@@ -819,23 +837,27 @@ int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const v
   a.inv_linear_beta = linear_beta != 0.f ? 1.f / linear_beta : 0.f;
   a.round_gate_up = round_gate_up;
   a.out_f16 = out_dtype == 2;
-  CUtensorMap tw, tt;
+  CUtensorMap tw, tt, tt64;
   if (!encode_tmap_fp4_unpacked_3d(&tw, w_packed, static_cast<uint64_t>(k),
                                    static_cast<uint64_t>(n_weight), static_cast<uint64_t>(g)))
     return LMOE_LAUNCH_FAILED;
+  // token rows: one box of a full tile, or boxes of 64 rows for a partial one
   if (!encode_tmap_u8_2d_sw128(&tt, act_q, static_cast<uint64_t>(k), static_cast<uint64_t>(m_pad),
-                               static_cast<uint64_t>(k), kMxBK, MxCfg::kBoxRows))
+                               static_cast<uint64_t>(k), kMxBK, kMxTok) ||
+      !encode_tmap_u8_2d_sw128(&tt64, act_q, static_cast<uint64_t>(k),
+                               static_cast<uint64_t>(m_pad), static_cast<uint64_t>(k), kMxBK,
+                               MxCfg::kBoxRows))
     return LMOE_LAUNCH_FAILED;
   const int64_t tiles = (m_pad / kMxTok + g) * a.n_tiles;
   const int max_tiles = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
   auto s = static_cast<cudaStream_t>(stream);
   int rc;
   if (epi == EPI_SITU)
-    rc = launch_mx<EPI_SITU>(tw, tt, a, max_tiles, s);
+    rc = launch_mx<EPI_SITU>(tw, tt, tt64, a, max_tiles, s);
   else if (out_dtype == 1)
-    rc = launch_mx<EPI_F32>(tw, tt, a, max_tiles, s);
+    rc = launch_mx<EPI_F32>(tw, tt, tt64, a, max_tiles, s);
   else
-    rc = launch_mx<EPI_BF16>(tw, tt, a, max_tiles, s);
+    rc = launch_mx<EPI_BF16>(tw, tt, tt64, a, max_tiles, s);
   return rc;
 }
 

@@ -574,7 +574,7 @@ def prepare_mxfp4_blockscaled(w: MXFP4Weights, gateup: bool = False) -> MXFP4Blo
 @dataclasses.dataclass
 class MXFP8Rows:
   """Activation rows quantised to MXFP8 in the padded layout: q (M_pad, K)
-  e4m3 bytes, sf (M_pad/128, K/128, 512) scale atoms, group_sizes (G,) the
+  e4m3 bytes, sf (K/128, M_pad/128, 512) scale atoms, group_sizes (G,) the
   true row counts (group g's rows start at the sum of the earlier groups'
   counts rounded up to 128)."""
 
@@ -602,7 +602,7 @@ def quantize_mxfp8_rows(x: torch.Tensor, group_sizes: torch.Tensor,
   if out is None:
     m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
     out = MXFP8Rows(torch.empty(m_pad, k, dtype=torch.uint8, device=x.device),
-                    torch.empty(m_pad // 128, k // 128, 512, dtype=torch.uint8, device=x.device),
+                    torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=x.device),
                     group_sizes)
   gs = group_sizes.to(torch.int32).contiguous()
   out.group_sizes = gs
