@@ -193,6 +193,27 @@ LMOE_API int lmoe_router_topk(const float* logits, const float* bias, int64_t nu
                      int64_t num_experts, int64_t top_k, int activation, int renormalize,
                      float routed_scaling_factor, int32_t* topk_idx, float* topk_w, void* stream);
 
+/* Workspace bytes lmoe_router_fused_bf16 needs (0 for unsupported shapes). */
+LMOE_API size_t lmoe_router_fused_workspace_size(int64_t num_tokens, int64_t num_experts,
+                                                 int64_t top_k);
+
+/* Router gate straight from the hidden states, sigmoid activation: the logits
+ * h @ W_router^T run on the tensor cores (bf16 products, f32 accumulation)
+ * and the selection of lmoe_router_topk (activation 0) runs in the GEMM's
+ * epilogue on the accumulator, so the f32 logits are never stored.  topk_idx
+ * and topk_w equal lmoe_gemm_bf16(out f32) followed by lmoe_router_topk bit
+ * for bit.  hidden (T, d) bf16, router_weight (E, d) bf16 (d contiguous, the
+ * nn.Linear layout), bias (E,) f32 or NULL; d % 8 == 0, E <= 1024,
+ * top_k <= 16, 16-byte aligned pointers.  workspace: device scratch of
+ * lmoe_router_fused_workspace_size bytes (LMOE_SCRATCH_TOO_SMALL otherwise).
+ * Replaces the gate of latent_moe_forward
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:347-356). */
+LMOE_API int lmoe_router_fused_bf16(const void* hidden, const void* router_weight, const float* bias,
+                           int64_t num_tokens, int64_t hidden_size, int64_t num_experts,
+                           int64_t top_k, int renormalize, float routed_scaling_factor,
+                           int32_t* topk_idx, float* topk_w, void* workspace,
+                           size_t workspace_bytes, int32_t* dev_status, void* stream);
+
 /* Workspace bytes lmoe_dispatch needs for max(num_tokens*top_k, m_out) entries. */
 LMOE_API size_t lmoe_dispatch_workspace_size(int64_t num_entries, int64_t num_local_experts);
 

@@ -52,6 +52,9 @@ SIGNATURES = {
     "lmoe_situ_and_mul": (_i32, [_p, _p, _i64, _p, _i64, _i64, _f32, _f32, _i32, _p]),
     "lmoe_router_topk": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _i32, _f32, _p, _p, _p]),
     "lmoe_dispatch_workspace_size": (_sz, [_i64, _i64]),
+    "lmoe_router_fused_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "lmoe_router_fused_bf16": (_i32, [_p, _p, _p, _i64, _i64, _i64, _i64, _i32, _f32, _p, _p, _p,
+                                      _sz, _p, _p]),
     "lmoe_dispatch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p,
                              _p, _p, _sz, _p]),
     "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i32, _p, _p]),
@@ -86,7 +89,7 @@ KERNELS_PER_CALL = {"lmoe_dispatch": 3, "lmoe_ep_dispatch_put": 2, "lmoe_ep_retu
                     "lmoe_ep_buffer_alloc": 0, "lmoe_ep_buffer_open": 0,
                     "lmoe_ep_buffer_close": 0, "lmoe_ep_buffer_free": 0,
                     "lmoe_set_peer_wait_timeout_ns": 0,
-                    "lmoe_mxfp4_repack_blockscaled": 2}
+                    "lmoe_mxfp4_repack_blockscaled": 2, "lmoe_router_fused_bf16": 2}
 launch_count = 0
 
 

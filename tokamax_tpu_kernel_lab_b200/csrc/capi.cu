@@ -113,6 +113,20 @@ int lmoe_router_topk(const float* logits, const float* bias, int64_t num_tokens,
                            routed_scaling_factor, topk_idx, topk_w, S(stream));
 }
 
+size_t lmoe_router_fused_workspace_size(int64_t num_tokens, int64_t num_experts, int64_t top_k) {
+  return lmoe::router_fused_workspace_size(num_tokens, num_experts, top_k);
+}
+
+int lmoe_router_fused_bf16(const void* hidden, const void* router_weight, const float* bias,
+                           int64_t num_tokens, int64_t hidden_size, int64_t num_experts,
+                           int64_t top_k, int renormalize, float routed_scaling_factor,
+                           int32_t* topk_idx, float* topk_w, void* workspace,
+                           size_t workspace_bytes, int32_t* dev_status, void* stream) {
+  return lmoe::router_fused_bf16(hidden, router_weight, bias, num_tokens, hidden_size, num_experts,
+                                 top_k, renormalize, routed_scaling_factor, topk_idx, topk_w,
+                                 workspace, workspace_bytes, dev_status, S(stream));
+}
+
 size_t lmoe_dispatch_workspace_size(int64_t num_entries, int64_t num_local_experts) {
   if (num_entries < 0 || num_local_experts <= 0) return 0;
   return lmoe::dispatch_workspace_bytes(num_entries, num_local_experts);

@@ -90,8 +90,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
   using C = GemmCfg<BN, STAGES, BF, EPI>;
   constexpr bool kMx = is_expand(BF);  // B expanded by the dequant warps
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* stages = smem;
   uint8_t* dstages = smem + STAGES * C::kStageBytes;  // expanded B ring (MXFP4)
   int32_t* row_off = reinterpret_cast<int32_t*>(dstages + C::kDStages * C::kBBytes);

@@ -68,6 +68,12 @@ int router_topk(const float* logits, const float* bias, int64_t T, int64_t E, in
                 int activation, int renormalize, float rsf, int32_t* topk_idx, float* topk_w,
                 cudaStream_t stream);
 
+size_t router_fused_workspace_size(int64_t T, int64_t E, int64_t k);
+int router_fused_bf16(const void* hidden, const void* router_w, const float* bias, int64_t T,
+                      int64_t K, int64_t E, int64_t k, int renormalize, float rsf,
+                      int32_t* topk_idx, float* topk_w, void* workspace, size_t workspace_bytes,
+                      int32_t* status, cudaStream_t stream);
+
 // Dispatch outputs (device pointers; optional ones may be null).
 struct DispatchOut {
   int32_t* order;              // [m_out] entry index at each sorted position

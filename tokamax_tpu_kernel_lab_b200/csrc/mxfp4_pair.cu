@@ -117,8 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = PairCfg;
   constexpr bool kF16 = BF == B_MXFP4F16;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* tstages = smem;
   uint8_t* pstages = tstages + kTStages * C::kTokBytes;
   uint8_t* astages = pstages + kPStages * C::kPackedBytes;

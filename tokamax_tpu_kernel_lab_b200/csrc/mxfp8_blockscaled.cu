@@ -261,16 +261,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                    const __grid_constant__ CUtensorMap tmT64, const MxArgs args) {
   using C = MxCfg;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
+  uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* stages = smem;
   uint8_t* ostage = stages + kMxStages * C::kStageBytes;
   int32_t* row_off = reinterpret_cast<int32_t*>(ostage + C::kOutStageBytes);
   int32_t* row_cnt = row_off + (kMxMaxGroups + 1);
   int32_t* tile_start = row_cnt + (kMxMaxGroups + 1);
   // mbarriers need 8-byte alignment (three schedule arrays of 1025 ints end at 4 mod 8)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(
-      (reinterpret_cast<uintptr_t>(tile_start + (kMxMaxGroups + 1)) + 15) & ~uintptr_t(15));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_align_up<16>(tile_start + (kMxMaxGroups + 1)));
   uint64_t* full = bars;
   uint64_t* empty = full + kMxStages;
   uint64_t* acc_full = empty + kMxStages;

@@ -57,6 +57,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// `p` (a pointer into shared memory) moved up to the next multiple of ALIGN
+// bytes.  The offset is added to the pointer itself rather than round-tripped
+// through an integer, so the compiler still knows the result (and everything
+// derived from it) is shared memory and emits shared loads and stores; a
+// pointer rebuilt from an integer is generic, and generic loads of shared
+// data run several times slower.
+template <int ALIGN, typename T>
+__device__ __forceinline__ uint8_t* smem_align_up(T* p) {
+  uint8_t* b = reinterpret_cast<uint8_t*>(p);
+  return b + ((ALIGN - (smem_u32(b) & (ALIGN - 1))) & (ALIGN - 1));
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

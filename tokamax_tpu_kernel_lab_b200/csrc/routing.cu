@@ -16,6 +16,7 @@
 
 #include "lmoe_internal.h"
 #include "ptx.cuh"
+#include "router_select.cuh"
 
 namespace lmoe {
 
@@ -60,7 +61,7 @@ __global__ void __launch_bounds__(256, 3) router_topk_kernel(
     for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
   }
   auto score = [&](float x) -> float {
-    return activation == 0 ? 1.0f / (1.0f + expf(-x)) : expf(x - m) / ssum;
+    return activation == 0 ? router_sigmoid(x) : expf(x - m) / ssum;
   };
   // Selection order: key descending, expert id ascending on equal keys -- a
   // total order, so the winners leave in exactly one sequence.  Each lane
@@ -69,7 +70,7 @@ __global__ void __launch_bounds__(256, 3) router_topk_kernel(
   // promotes its second.  Only a lane that has used up both rescans its
   // entries, for the two best strictly after the last one it gave up (every
   // better entry of the lane is already taken).
-  auto before = [](float av, int ae, float bv, int be) { return av > bv || (av == bv && ae < be); };
+  auto before = [](float av, int ae, float bv, int be) { return sel_before(av, ae, bv, be); };
   float v1 = -FLT_MAX, v2 = -FLT_MAX, s1 = 0.f, s2 = 0.f;
   int e1 = INT_MAX, e2 = INT_MAX;
 #pragma unroll

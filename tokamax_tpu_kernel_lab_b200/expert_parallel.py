@@ -54,8 +54,8 @@ class GpuBackend:
 
   def route(self, h):
     c = self.cfg
-    logits = ops.router_logits(h, self.pw.router)
-    return ops.router_topk(logits, self.pw.bias, c.top_k, renormalize=c.moe_renormalize,
+    return ops.router_gate(h, self.pw.router, self.pw.bias, c.top_k,
+                           renormalize=c.moe_renormalize,
                            routed_scaling_factor=c.routed_scaling_factor)
 
   def down(self, h):

@@ -15,9 +15,12 @@ the reference's one-time `prefuse_gateup_weights`, kimi_k3_latent_moe_ragged_dot
   shared_gu   (2*Is, d)       [gate | up] of the shared expert (one dense group)
   shared_down (d, Is)
 
-bf16 forward, in stream order (11 launches, no host synchronisation):
-  1 logits      tensor-core GEMM, f32 out          (exact bf16 products, f32 sums)
-  2 top-k       router_topk                         (sigmoid, bias for selection only)
+bf16 forward, in stream order (no host synchronisation):
+  1 logits      tensor-core GEMM with the top-k selection in its epilogue
+                (exact bf16 products, f32 sums; sigmoid, bias for selection
+                only; the f32 logits stay in tensor memory)
+  2 top-k       merge of the per-chunk candidates (router_topk on stored
+                logits when the intermediates are requested)
   3 x           tensor-core GEMM (down-projection)
   4-6 dispatch  stable counting sort by expert      (order, slot_pos, group_sizes)
   7 gather      sorted rows of x
@@ -266,10 +269,18 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
       ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
                             round_gate_up=True, rhs_layout="gnk", out=shared_act)
       ops.gemm(shared_act, pw.shared_down, rhs_layout="nk", out=shared_out)
-  logits = ops.router_logits(h, pw.router)
-  topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
-                                     routed_scaling_factor=c.routed_scaling_factor,
-                                     activation=router_activation)
+  if return_intermediates or not ops.router_fused_supported(h, pw.router, c.top_k,
+                                                             router_activation):
+    logits = ops.router_logits(h, pw.router)
+    topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
+                                       routed_scaling_factor=c.routed_scaling_factor,
+                                       activation=router_activation)
+  else:
+    # logits GEMM with the selection in its epilogue: the same bits, no f32
+    # logits in memory
+    topk_idx, topk_w = ops.router_gate_fused(h, pw.router, pw.bias, c.top_k,
+                                             renormalize=c.moe_renormalize,
+                                             routed_scaling_factor=c.routed_scaling_factor)
   mark("route")
   x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else None)
   mark("down-projection")

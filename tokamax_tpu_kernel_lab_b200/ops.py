@@ -402,9 +402,55 @@ def router_logits(hidden_states: torch.Tensor, router_weight_nk: torch.Tensor) -
   return gemm(hidden_states, router_weight_nk, rhs_layout="nk", out_dtype=torch.float32)
 
 
+def router_fused_supported(hidden_states: torch.Tensor, router_weight_nk: torch.Tensor,
+                           top_k: int, activation: str = "sigmoid") -> bool:
+  """True when router_gate can run the fused kernel: sigmoid activation, bf16
+  hidden states and router weight, E <= 1024, top_k <= 16, d % 8 == 0."""
+  e, d = router_weight_nk.shape
+  return (activation == "sigmoid" and hidden_states.dtype == torch.bfloat16
+          and router_weight_nk.dtype == torch.bfloat16 and 0 < top_k <= 16 and top_k <= e <= 1024
+          and d % 8 == 0 and hidden_states.shape[-1] == d)
+
+
+def router_fused_workspace_size(num_tokens: int, num_experts: int, top_k: int) -> int:
+  return int(_native.load().lmoe_router_fused_workspace_size(num_tokens, num_experts, top_k))
+
+
+def router_gate_fused(hidden_states: torch.Tensor, router_weight_nk: torch.Tensor,
+                      bias: torch.Tensor | None, top_k: int, *, renormalize: bool = True,
+                      routed_scaling_factor: float = 1.0,
+                      workspace: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+  """The gate of kimi_k3_latent_moe_reference.py:347-356 straight from bf16
+  hidden states (sigmoid): the logits GEMM runs on the tensor cores with the
+  top-k selection in its epilogue, so the f32 logits are never stored.
+  Returns the same bits as router_topk(router_logits(h, W), ...)."""
+  _need_cuda(hidden_states, router_weight_nk, bias)
+  h = hidden_states.contiguous()
+  w = router_weight_nk.contiguous()
+  t, d = h.shape
+  e = w.shape[0]
+  b = None if bias is None else bias.float().contiguous()
+  idx = torch.empty(t, top_k, dtype=torch.int32, device=h.device)
+  tw = torch.empty(t, top_k, dtype=torch.float32, device=h.device)
+  ws_bytes = router_fused_workspace_size(t, e, top_k)
+  if workspace is None or workspace.numel() < ws_bytes:
+    workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=h.device)
+  _native.call("lmoe_router_fused_bf16", _ptr(h), _ptr(w), _ptr(b), t, d, e, top_k,
+               int(renormalize), float(routed_scaling_factor), _ptr(idx), _ptr(tw),
+               _ptr(workspace), workspace.numel(), _ptr(device_status(h.device)), _stream())
+  return idx, tw
+
+
 def router_gate(hidden_states, router_weight_nk, bias, top_k, *, renormalize=True,
-                routed_scaling_factor=1.0, activation="sigmoid"):
-  """(topk_idx, topk_weight f32) on the original hidden states."""
+                routed_scaling_factor=1.0, activation="sigmoid", fused: bool | None = None):
+  """(topk_idx, topk_weight f32) on the original hidden states.  fused=None
+  takes the fused logits+selection kernel whenever router_fused_supported
+  allows it (the results are the same bits either way)."""
+  if fused is None:
+    fused = router_fused_supported(hidden_states, router_weight_nk, top_k, activation)
+  if fused:
+    return router_gate_fused(hidden_states, router_weight_nk, bias, top_k,
+                             renormalize=renormalize, routed_scaling_factor=routed_scaling_factor)
   logits = router_logits(hidden_states, router_weight_nk)
   return router_topk(logits, bias, top_k, renormalize=renormalize,
                      routed_scaling_factor=routed_scaling_factor, activation=activation)
