@@ -457,8 +457,8 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           ok = false;
           break;
         }
-        const uint8_t* src = stages + stage * C::kStageBytes + C::kABytes + nc * 8;
-        uint8_t* dst = dstages + dstage * C::kBBytes + chunk * (kBK * 128);
+        const uint32_t src = smem_u32(stages + stage * C::kStageBytes + C::kABytes + nc * 8);
+        const uint32_t dst = smem_u32(dstages + dstage * C::kBBytes + chunk * (kBK * 128));
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int k = k0 + 8 * i;
@@ -467,7 +467,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
                                hi ? s_hi[0].z : s_lo[0].z, hi ? s_hi[0].w : s_lo[0].w,
                                hi ? s_hi[1].x : s_lo[1].x, hi ? s_hi[1].y : s_lo[1].y,
                                hi ? s_hi[1].z : s_lo[1].z, hi ? s_hi[1].w : s_lo[1].w};
-          const uint2 q = *reinterpret_cast<const uint2*>(src + k * BN);
+          const uint2 q = lds_v2(src + k * BN);
           uint32_t h2[4];
           asm("{\n\t.reg .b16 l0, h0, l1, h1;\n\t"
               "mov.b32 {l0, h0}, %4;\n\t"
@@ -484,8 +484,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
             const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h2[e]));
             o[e] = pack_bf16x2(f.x * sc[2 * e], f.y * sc[2 * e + 1]);
           }
-          *reinterpret_cast<uint4*>(dst + k * 128 + ((sub ^ (k & 7)) << 4)) =
-              make_uint4(o[0], o[1], o[2], o[3]);
+          sts_v4(dst + k * 128 + ((sub ^ (k & 7)) << 4), make_uint4(o[0], o[1], o[2], o[3]));
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -534,18 +533,17 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           ok = false;
           break;
         }
-        const uint8_t* st = stages + stage * C::kStageBytes;
-        const uint4* prow = reinterpret_cast<const uint4*>(st + C::kABytes + r * (kBK / 2));
-        const uint4 p0 = prow[0], p1 = prow[1];
+        const uint32_t prow = smem_u32(stages + stage * C::kStageBytes + C::kABytes + r * (kBK / 2));
+        const uint4 p0 = lds_v4(prow), p1 = lds_v4(prow + 16);
         const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        uint8_t* brow = dstages + dstage * C::kBBytes + r * 128;
+        const uint32_t brow = smem_u32(dstages + dstage * C::kBBytes + r * 128);
         if (BF == B_MXFP4F16) {
           const uint32_t b0 = e8m0_to_f16_bits(s01 & 0xFFu), b1 = e8m0_to_f16_bits(s01 >> 8);
           const uint32_t sc0 = b0 | (b0 << 16), sc1 = b1 | (b1 << 16);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint4 v = dequant_e2m1x8_f16(words[c], c < 4 ? sc0 : sc1);
-            *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+            sts_v4(brow + ((c ^ (r & 7)) << 4), v);
           }
         } else {
           const uint32_t b0 = e8m0_to_bf16_bits(s01 & 0xFFu), b1 = e8m0_to_bf16_bits(s01 >> 8);
@@ -554,7 +552,7 @@ __global__ void __launch_bounds__(GemmCfg<BN, STAGES, BF, EPI>::kThreads, 1)
           for (int c = 0; c < 8; ++c) {
             const uint32_t sc = c < 4 ? sc0 : sc1;
             const uint4 v = dequant_e2m1x8(words[c], *reinterpret_cast<const __nv_bfloat162*>(&sc));
-            *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = v;
+            sts_v4(brow + ((c ^ (r & 7)) << 4), v);
           }
         }
         fence_proxy_async_smem();

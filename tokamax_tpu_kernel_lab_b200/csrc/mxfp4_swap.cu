@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(kSwThreads, 1)
   } else if (warp < 6) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    uint8_t* stg = ostage + q * C::kWarpStage;
+    const uint32_t stg = smem_u32(ostage + q * C::kWarpStage);
     constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
     uint32_t acc = 0, acc_phase = 0;
     float f16_peak = 0.f;  // largest magnitude stored as f16 by the plain epilogue
@@ -323,7 +323,6 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           // Staged [token][16 features] (32-byte rows).
           static_assert(C::kWarpStage >= 1024, "SiTU staging");
           const int odd = lane & 1;
-          uint16_t* s16 = reinterpret_cast<uint16_t*>(stg);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const uint32_t send = odd ? v[j] : v[16 + j];
@@ -336,16 +335,15 @@ __global__ void __launch_bounds__(kSwThreads, 1)
             }
             const float o = situ_fast(g, u, args.beta, args.inv_beta, args.linear_beta,
                                       args.inv_linear_beta);
-            s16[(odd * 16 + j) * 16 + (lane >> 1)] = out16(o, args.out_f16);
+            sts_u16(stg + 2u * ((odd * 16 + j) * 16 + (lane >> 1)), out16(o, args.out_f16));
           }
           __syncwarp();
           const int tok = tok0 + lane;
           const int f0 = tc.n_tile * (kWRows / 2) + q * 16;
           if (tok < tc.row_end) {
-            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
             uint16_t* orow =
                 reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
-            const uint4 s0 = src[0], s1 = src[1];
+            const uint4 s0 = lds_v4(stg + lane * 32), s1 = lds_v4(stg + lane * 32 + 16);
             if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = s0;
             if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = s1;
             if (args.out_f16) {
@@ -367,26 +365,23 @@ __global__ void __launch_bounds__(kSwThreads, 1)
           const int f0 = tc.n_tile * kWRows + q * 32;
 #pragma unroll
           for (int p0 = 0; p0 < 32; p0 += kRows) {
-            uint8_t* dst0 = stg + (byte & 15);
+            const uint32_t dst0 = stg + (byte & 15);
             if (EPI == EPI_F32) {
 #pragma unroll
               for (int jj = 0; jj < kRows; ++jj)
-                *reinterpret_cast<uint32_t*>(dst0 + jj * kRowBytes +
-                                             (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4)) = v[p0 + jj];
+                sts_u32(dst0 + jj * kRowBytes + (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4), v[p0 + jj]);
             } else if (args.out_f16) {
 #pragma unroll
               for (int jj = 0; jj < kRows; ++jj) {
                 f16_peak = fmaxf(f16_peak, fabsf(__uint_as_float(v[p0 + jj])));
-                *reinterpret_cast<uint16_t*>(dst0 + jj * kRowBytes +
-                                             (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4)) =
-                    out16(__uint_as_float(v[p0 + jj]), 1);
+                sts_u16(dst0 + jj * kRowBytes + (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4),
+                        out16(__uint_as_float(v[p0 + jj]), 1));
               }
             } else {
 #pragma unroll
               for (int jj = 0; jj < kRows; ++jj)
-                *reinterpret_cast<uint16_t*>(dst0 + jj * kRowBytes +
-                                             (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4)) =
-                    out16(__uint_as_float(v[p0 + jj]), 0);
+                sts_u16(dst0 + jj * kRowBytes + (((byte >> 4) ^ swz_key<kChunks>(jj)) << 4),
+                        out16(__uint_as_float(v[p0 + jj]), 0));
             }
             __syncwarp();
             const int tok = tok0 + p0 + lane;
@@ -399,8 +394,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
 #pragma unroll
               for (int cc = 0; cc < kChunks; ++cc) {
                 if (f0 + (cc + 1) * (16 / esize) <= args.N)
-                  *reinterpret_cast<uint4*>(orow + cc * 16) = *reinterpret_cast<const uint4*>(
-                      stg + lane * kRowBytes + ((cc ^ swz_key<kChunks>(lane)) * 16));
+                  *reinterpret_cast<uint4*>(orow + cc * 16) =
+                      lds_v4(stg + lane * kRowBytes + ((cc ^ swz_key<kChunks>(lane)) * 16));
               }
             }
             __syncwarp();
@@ -486,9 +481,8 @@ __global__ void __launch_bounds__(kSwThreads, 1)
     auto expand = [&](int st, uint32_t sc) -> bool {
       const uint32_t pslot = st % kPStages, pph = (st / kPStages) & 1;
       if (!mbar_wait(smem_u32(pk_full + pslot), pph, abort_flag, args.status)) return false;
-      const uint4* src = reinterpret_cast<const uint4*>(pstages + pslot * C::kPackedBytes +
-                                                        packed_row<EPI>(r) * (kBK / 2));
-      const uint4 p0 = src[0], p1 = src[1];
+      const uint32_t src = smem_u32(pstages + pslot * C::kPackedBytes + packed_row<EPI>(r) * (kBK / 2));
+      const uint4 p0 = lds_v4(src), p1 = lds_v4(src + 16);
       const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
       uint4 dq[8];
       if (kF16) {
@@ -510,9 +504,9 @@ __global__ void __launch_bounds__(kSwThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(pk_empty + pslot));
       const uint32_t aslot = st % kDStages, aph = (st / kDStages) & 1;
       if (!mbar_wait(smem_u32(a_empty + aslot), aph ^ 1u, abort_flag, args.status)) return false;
-      uint8_t* arow = astages + aslot * C::kABytes + r * 128;
+      const uint32_t arow = smem_u32(astages + aslot * C::kABytes + r * 128);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dq[c];
+      for (int c = 0; c < 8; ++c) sts_v4(arow + ((c ^ (r & 7)) << 4), dq[c]);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(a_ready + aslot));

@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    uint8_t* stg = ostage + q * C::kWarpStage;
+    const uint32_t stg = smem_u32(ostage + q * C::kWarpStage);
     constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
     uint32_t acc = 0, acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
@@ -445,7 +445,6 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         if (EPI == EPI_SITU) {
           // lanes 2i / 2i+1 hold gate / up of feature i (interleaved weight rows)
           const int odd = lane & 1;
-          uint16_t* s16 = reinterpret_cast<uint16_t*>(stg);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const uint32_t send = odd ? v[j] : v[16 + j];
@@ -458,17 +457,16 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             }
             const float o = situ_fast(g, u, args.beta, args.inv_beta, args.linear_beta,
                                       args.inv_linear_beta);
-            s16[(odd * 16 + j) * 16 + (lane >> 1)] = mx_out16(o, args.out_f16);
+            sts_u16(stg + 2u * ((odd * 16 + j) * 16 + (lane >> 1)), mx_out16(o, args.out_f16));
           }
           __syncwarp();
           const int tok = tok0 + lane;
           const int f0 = tc.n_tile * (kMxRows / 2) + q * 16;
           if (tok < tok_end) {
-            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
             uint16_t* orow =
                 reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
-            if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = src[0];
-            if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = src[1];
+            if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = lds_v4(stg + lane * 32);
+            if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = lds_v4(stg + lane * 32 + 16);
           }
           __syncwarp();
         } else {
@@ -479,14 +477,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const int f0 = tc.n_tile * kMxRows + q * 32;
 #pragma unroll
           for (int p0 = 0; p0 < 32; p0 += kRows) {
-            uint8_t* dst0 = stg + (byte & 15);
+            const uint32_t dst0 = stg + (byte & 15);
 #pragma unroll
             for (int jj = 0; jj < kRows; ++jj) {
-              uint8_t* d = dst0 + jj * kRowBytes + (((byte >> 4) ^ mx_swz<kChunks>(jj)) << 4);
+              const uint32_t d = dst0 + jj * kRowBytes + (((byte >> 4) ^ mx_swz<kChunks>(jj)) << 4);
               if (EPI == EPI_F32)
-                *reinterpret_cast<uint32_t*>(d) = v[p0 + jj];
+                sts_u32(d, v[p0 + jj]);
               else
-                *reinterpret_cast<uint16_t*>(d) = mx_out16(__uint_as_float(v[p0 + jj]), args.out_f16);
+                sts_u16(d, mx_out16(__uint_as_float(v[p0 + jj]), args.out_f16));
             }
             __syncwarp();
             const int tok = tok0 + p0 + lane;
@@ -496,8 +494,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
               for (int cc = 0; cc < kChunks; ++cc) {
                 if (f0 + (cc + 1) * (16 / esize) <= args.N)
-                  *reinterpret_cast<uint4*>(orow + cc * 16) = *reinterpret_cast<const uint4*>(
-                      stg + lane * kRowBytes + ((cc ^ mx_swz<kChunks>(lane)) * 16));
+                  *reinterpret_cast<uint4*>(orow + cc * 16) =
+                      lds_v4(stg + lane * kRowBytes + ((cc ^ mx_swz<kChunks>(lane)) * 16));
               }
             }
             __syncwarp();

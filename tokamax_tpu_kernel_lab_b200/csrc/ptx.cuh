@@ -58,15 +58,52 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // `p` (a pointer into shared memory) moved up to the next multiple of ALIGN
-// bytes.  The offset is added to the pointer itself rather than round-tripped
-// through an integer, so the compiler still knows the result (and everything
-// derived from it) is shared memory and emits shared loads and stores; a
-// pointer rebuilt from an integer is generic, and generic loads of shared
-// data run several times slower.
+// bytes.
 template <int ALIGN, typename T>
 __device__ __forceinline__ uint8_t* smem_align_up(T* p) {
   uint8_t* b = reinterpret_cast<uint8_t*>(p);
   return b + ((ALIGN - (smem_u32(b) & (ALIGN - 1))) & (ALIGN - 1));
+}
+
+// Explicit shared-state-space accesses by 32-bit shared address.  C++ loads
+// through pointers into the dynamic shared window were measured about 4x
+// slower than these in the router's selection loop (the compiler does not
+// always prove such a pointer is shared and falls back to generic accesses),
+// so hot loops use these.  Volatile: they stay in program order with each
+// other and with the other shared-memory asm of this file.
+__device__ __forceinline__ float lds_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void sts_u16(uint32_t addr, uint16_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
+__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
@@ -318,6 +355,25 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr)
       : "memory");
+}
+
+// The inverse of tmem_ld_32x32b_x32: thread i writes r[0..31] into lane
+// (base+i), 32 consecutive columns.  Complete once tmem_st_wait returns.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
 // UMMA shared-memory matrix descriptor, 128-byte swizzle.

@@ -25,13 +25,14 @@
 //              of tensor memory 32 columns at a time; the thread keeps the
 //              chunk's best LIST (key, expert, score) entries in registers,
 //              sorted in the selection order, and writes them to the
-//              candidate buffer (T, n_chunks, LIST).  Per block of 32
-//              columns it computes the scores and keys, marks the columns
-//              whose key beats its current LIST-th entry, parks the 32
-//              scores in its own shared-memory row and then inserts only the
-//              marked columns (the insertion is the costly part; the 32
-//              tokens of a warp have independent lists, so inserting column
-//              by column would run the insertion for almost every column)
+//              candidate buffer (T, n_chunks, LIST).  A first pass over
+//              the chunk computes every score and key (the scores replace
+//              the logits in tensor memory) and a lower bound tau of the
+//              LIST-th largest key; a second pass inserts only the columns
+//              whose key reaches tau (the insertion is the costly part; the
+//              32 tokens of a warp have independent lists, so inserting
+//              column by column would run the insertion for almost every
+//              column)
 // The merge kernel then runs the selection over each token's n_chunks x LIST
 // candidates (one warp per token).  A chunk's top LIST >= k holds every
 // expert of that chunk that is in the token's overall top-k, so the merge
@@ -220,37 +221,82 @@ __global__ void __launch_bounds__(kRtThreads, 1)
         ks[j] = 0.f;
       }
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kRtAccStride;
-      // this thread's row of parked scores: 16-byte group g of the row sits
-      // in slot g ^ (lane & 7), so a warp's vector stores spread over the banks
-      float* row = park + (q * 32 + lane) * 32;
+      const uint32_t bias_a = smem_u32(bias_s);
+      // Pass A: scores and keys of every column.  The scores go back into
+      // tensor memory over the logits; per group of columns (column mod LIST)
+      // the two largest keys are kept.  The LIST-th largest of those 2 x LIST
+      // keys is a lower bound tau of the token's LIST-th largest key in the
+      // chunk (they are keys of 2 x LIST distinct experts), and usually close
+      // to it: pass B only has to insert columns whose key reaches tau.
+      float m1[LIST], m2[LIST];
+#pragma unroll
+      for (int g = 0; g < LIST; ++g) m1[g] = m2[g] = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c * 32 < width; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = c * 32 + j;
+          const float sc = router_sigmoid(__uint_as_float(v[j]));
+          float key = sc + lds_f32(bias_a + 4u * static_cast<uint32_t>(min(e0 + col, args.E - 1)));
+          key = (col < width && key == key) ? key : -INFINITY;  // NaN keys never enter
+          const int g = j % LIST;
+          m2[g] = fmaxf(m2[g], fminf(m1[g], key));
+          m1[g] = fmaxf(m1[g], key);
+          v[j] = __float_as_uint(sc);
+        }
+        tmem_st_32x32b_x32(tbase + c * 32, v);
+      }
+      tmem_st_wait();
+      sort_desc<LIST>(m1);
+      sort_desc<LIST>(m2);
+      const float tau = lth_largest_of_two<LIST>(m1, m2);
+      // Pass B: the columns whose key reaches tau and beats the list's last
+      // entry are parked (their scores in this thread's shared-memory row,
+      // 16-byte group g of the row in slot g ^ (lane & 7) so a warp's vector
+      // stores spread over the banks) and inserted one by one, the next
+      // one's loads issued before the current insertion.
+      const uint32_t row = smem_u32(park + (q * 32 + lane) * 32);
       const int sw = lane & 7;
 #pragma unroll 1
       for (int c = 0; c * 32 < width; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + c * 32, v);
         tmem_ld_wait();
-        const float thr = kv[LIST - 1];
+        // experts arrive in increasing id order: a new key must beat the
+        // last entry strictly (on an equal key the lower id already held wins)
+        const float last = kv[LIST - 1];
         uint32_t marked = 0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int col = c * 32 + j;
-          const float s = router_sigmoid(__uint_as_float(v[j]));
-          const float key = s + bias_s[min(e0 + col, args.E - 1)];
-          v[j] = __float_as_uint(s);
-          // experts arrive in increasing id order: a new key must beat the
-          // last entry strictly (on an equal key the lower id already held wins)
-          marked |= (col < width && key > thr) ? (1u << j) : 0u;
+          const float key =
+              __uint_as_float(v[j]) + lds_f32(bias_a + 4u * static_cast<uint32_t>(min(e0 + col, args.E - 1)));
+          marked |= (col < width && key >= tau && key > last) ? (1u << j) : 0u;
         }
+        if (__any_sync(0xffffffffu, marked != 0u)) {
 #pragma unroll
-        for (int g = 0; g < 8; ++g)
-          *reinterpret_cast<uint4*>(row + ((g ^ sw) << 2)) =
-              make_uint4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+          for (int g = 0; g < 8; ++g)
+            sts_v4(row + ((g ^ sw) << 4), make_uint4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
+        }
+        int j = marked != 0u ? __ffs(marked) - 1 : 0;
+        float s_next = 0.f, b_next = 0.f;
+        if (marked != 0u) {
+          s_next = lds_f32(row + ((((j >> 2) ^ sw) << 4) | ((j & 3) << 2)));
+          b_next = lds_f32(bias_a + 4u * static_cast<uint32_t>(e0 + c * 32 + j));
+        }
         while (marked != 0u) {
-          const int j = __ffs(marked) - 1;
-          marked &= marked - 1u;
-          const float s = row[(((j >> 2) ^ sw) << 2) | (j & 3)];
           const int e = e0 + c * 32 + j;
-          const float key = s + bias_s[e];
+          const float s = s_next;
+          const float key = s + b_next;
+          marked &= marked - 1u;
+          if (marked != 0u) {
+            j = __ffs(marked) - 1;
+            s_next = lds_f32(row + ((((j >> 2) ^ sw) << 4) | ((j & 3) << 2)));
+            b_next = lds_f32(bias_a + 4u * static_cast<uint32_t>(e0 + c * 32 + j));
+          }
           if (key > kv[LIST - 1]) sel_insert_ascending<LIST>(kv, ke, ks, key, e, s);
         }
       }

@@ -14,12 +14,18 @@
 
 namespace lmoe {
 
-// sigmoid(x) = 1 / (1 + exp(-x)), each operation rounded on its own (the
-// explicit round-to-nearest intrinsics keep the compiler from fusing the add
-// into the exponential's last multiply, so every kernel gets the same bits;
-// the correctly rounded reciprocal is the correctly rounded 1 / y)
+// sigmoid(x) = 1 / (1 + exp(-x)): expf, a round-to-nearest add (the
+// intrinsic keeps the compiler from fusing it into the exponential's last
+// multiply) and the hardware reciprocal (rcp.approx, within 1 ulp; results
+// below 2^-126 flush to zero).  Every router kernel calls this one function,
+// so they all get the same bits; against the correctly rounded sigmoid the
+// score is within a few ulp (~4e-7 relative).  The IEEE reciprocal costs
+// several times more in the selection loop, where the sigmoid runs once per
+// (token, expert).
 __device__ __forceinline__ float router_sigmoid(float x) {
-  return __frcp_rn(__fadd_rn(1.0f, expf(-x)));
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, expf(-x))));
+  return r;
 }
 
 // true when (av, ae) comes before (bv, be) in the selection order
@@ -66,6 +72,39 @@ __device__ __forceinline__ void sel_insert_ascending(float (&kv)[L], int (&ke)[L
     ke[j] = stay[j] ? ke[j] : (here ? e : ke[p]);
     ks[j] = stay[j] ? ks[j] : (here ? s : ks[p]);
   }
+}
+
+// Sort L values descending in place (bitonic network; L a power of two).
+template <int L>
+__device__ __forceinline__ void sort_desc(float (&v)[L]) {
+#pragma unroll
+  for (int size = 2; size <= L; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < L; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          // descending runs where bit `size` of i is clear, ascending where set,
+          // so that each merge level sees a bitonic sequence
+          const bool desc = (i & size) == 0;
+          const float a = v[i], b = v[j];
+          v[i] = desc ? fmaxf(a, b) : fminf(a, b);
+          v[j] = desc ? fminf(a, b) : fmaxf(a, b);
+        }
+      }
+    }
+  }
+}
+
+// The L-th largest of the 2L values a[] u b[] (each sorted descending): the
+// element-wise max of a and reversed b is the top L of the union.
+template <int L>
+__device__ __forceinline__ float lth_largest_of_two(const float (&a)[L], const float (&b)[L]) {
+  float m = fmaxf(a[0], b[L - 1]);
+#pragma unroll
+  for (int i = 1; i < L; ++i) m = fminf(m, fmaxf(a[i], b[L - 1 - i]));
+  return m;
 }
 
 }  // namespace lmoe
