@@ -606,18 +606,52 @@ __device__ __forceinline__ float mx_inv_scale(int e) {
 
 // Padded start of every group (multiples of 128) from the group sizes, in
 // shared memory: pad_off[g] = padded_start[g] - start[g]; start[g] also kept.
+// start[g] = sum of the counts before group g, pad_off[g] = (the same sum of
+// the counts rounded up to kMxAlign) - start[g], start[G] = the total.  A
+// block-wide exclusive scan, blockDim.x (a multiple of 32, at most 1024)
+// groups at a time: warp scans by shuffles, then the warps' totals.
 __device__ void mx_group_offsets(const int32_t* gs, int G, int32_t* start, int32_t* pad_off) {
-  if (threadIdx.x == 0) {
-    int32_t s = 0, ps = 0;
-    for (int g = 0; g < G; ++g) {
-      start[g] = s;
-      pad_off[g] = ps - s;
-      const int n = max(gs[g], 0);
-      s += n;
-      ps += (n + kMxAlign - 1) / kMxAlign * kMxAlign;
+  __shared__ int32_t warp_tot[2][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  int32_t carry_s = 0, carry_p = 0;
+  for (int base = 0; base < G; base += blockDim.x) {
+    const int g = base + threadIdx.x;
+    const int32_t n = g < G ? max(gs[g], 0) : 0;
+    const int32_t np = (n + kMxAlign - 1) / kMxAlign * kMxAlign;
+    int32_t is = n, ip = np;  // inclusive scans within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t ts = __shfl_up_sync(0xffffffffu, is, o);
+      const int32_t tp = __shfl_up_sync(0xffffffffu, ip, o);
+      if (lane >= o) {
+        is += ts;
+        ip += tp;
+      }
     }
-    start[G] = s;
+    if (lane == 31) {
+      warp_tot[0][warp] = is;
+      warp_tot[1][warp] = ip;
+    }
+    __syncthreads();
+    int32_t before_s = 0, before_p = 0, all_s = 0, all_p = 0;
+    for (int w = 0; w < nwarps; ++w) {
+      if (w < warp) {
+        before_s += warp_tot[0][w];
+        before_p += warp_tot[1][w];
+      }
+      all_s += warp_tot[0][w];
+      all_p += warp_tot[1][w];
+    }
+    if (g < G) {
+      const int32_t s_excl = carry_s + before_s + is - n;
+      start[g] = s_excl;
+      pad_off[g] = carry_p + before_p + ip - np - s_excl;
+    }
+    carry_s += all_s;
+    carry_p += all_p;
+    __syncthreads();  // warp_tot is rewritten by the next chunk
   }
+  if (threadIdx.x == 0) start[G] = carry_s;
   __syncthreads();
 }
 
@@ -659,43 +693,59 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
     const bool zero = src_row < 0 || src_row >= x_rows;
     const uint4* src = reinterpret_cast<const uint4*>(x + (zero ? 0 : src_row) * K);
     uint8_t* qrow = q + dst * K;
-    for (int b = lane; b < nblk; b += 32) {
-      float v[32];
+    // the lane's blocks two at a time, the second block's loads issued with
+    // the first's (nblk is a multiple of 4)
+    for (int b0 = lane; b0 < nblk; b0 += 64) {
+      uint4 raw[2][4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 w = zero ? make_uint4(0, 0, 0, 0) : __ldg(src + b * 4 + c);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      for (int u = 0; u < 2; ++u)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f;
-          if (F16)
-            f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
-          else
-            f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
-          v[c * 8 + i * 2] = f.x;
-          v[c * 8 + i * 2 + 1] = f.y;
+        for (int c = 0; c < 4; ++c)
+          raw[u][c] = (zero || b0 + 32 * u >= nblk) ? make_uint4(0, 0, 0, 0)
+                                                     : __ldg(src + (b0 + 32 * u) * 4 + c);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int b = b0 + 32 * u;
+        if (b >= nblk) break;
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 w = raw[u][c];
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float2 f;
+            if (F16)
+              f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+            else
+              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+            v[c * 8 + i * 2] = f.x;
+            v[c * 8 + i * 2 + 1] = f.y;
+          }
         }
-      }
-      float amax = 0.f;
+        float amax = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-      const int e = mx_scale_exp(amax);
-      const float inv = mx_inv_scale(e);
-      uint32_t packed[8];
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        const int e = mx_scale_exp(amax);
+        const float inv = mx_inv_scale(e);
+        uint32_t packed[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint16_t lo, hi;
-        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
-        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
-        packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+        for (int i = 0; i < 8; ++i) {
+          uint16_t lo, hi;
+          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
+          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
+          packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+        }
+        // evict-first stores: the source rows are re-read k times across the
+        // whole output and must stay in L2
+        uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
+        __stcs(qd, make_uint4(packed[0], packed[1], packed[2], packed[3]));
+        __stcs(qd + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
+        // atom (K group, row block), byte r0*16 + r1*4 + kb
+        const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
+        const int r = static_cast<int>(dst % 128);
+        sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
       }
-      uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
-      qd[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      qd[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-      // atom (K group, row block), byte r0*16 + r1*4 + kb
-      const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
-      const int r = static_cast<int>(dst % 128);
-      sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
     }
   }
 }

@@ -406,7 +406,10 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
   };
   // the next row's source index is fetched while this row is copied, and each
   // lane keeps eight 16-byte loads in flight, so neither load latency is paid
-  // once per row
+  // once per row.  The gathered rows are stored evict-first: every source row
+  // is read k times spread over the whole output, and plain stores of the
+  // (much larger) output would push the source rows out of L2 and have them
+  // re-read from memory.
   int t_next = warp < rows ? token_idx[warp] : -1;
   for (int64_t p = warp; p < rows; p += nwarps) {
     const int t = t_next;
@@ -420,17 +423,17 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
 #pragma unroll
         for (int i = 0; i < 8; ++i) a[i] = __ldg(src + v + 32 * i);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[v + 32 * i] = cv(a[i]);
+        for (int i = 0; i < 8; ++i) __stcs(dst + v + 32 * i, cv(a[i]));
       }
       for (; v + 96 < vec_per_row; v += 128) {
         const uint4 a = __ldg(src + v), b = __ldg(src + v + 32), c = __ldg(src + v + 64),
                     d = __ldg(src + v + 96);
-        dst[v] = cv(a);
-        dst[v + 32] = cv(b);
-        dst[v + 64] = cv(c);
-        dst[v + 96] = cv(d);
+        __stcs(dst + v, cv(a));
+        __stcs(dst + v + 32, cv(b));
+        __stcs(dst + v + 64, cv(c));
+        __stcs(dst + v + 96, cv(d));
       }
-      for (; v < vec_per_row; v += 32) dst[v] = cv(__ldg(src + v));
+      for (; v < vec_per_row; v += 32) __stcs(dst + v, cv(__ldg(src + v)));
       if (CONVERT) {
         // the whole row above f16's range, or all of it too small for f16
         // to carry accurately (see kF16RunMin)
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
         peak = 0.f;
       }
     } else {
-      for (int v = lane; v < vec_per_row; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+      for (int v = lane; v < vec_per_row; v += 32) __stcs(dst + v, make_uint4(0, 0, 0, 0));
     }
   }
   if (CONVERT && out_of_range && lane == 0) record_status(status, kF16Range);
