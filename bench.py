@@ -391,11 +391,13 @@ def roofline_entry(ms: float, flops: float, bytes_: float, peaks: dict, peak_src
 def gpu_routing_kernels(args, lm, ops, dev, peaks, peak_src, tokens: int) -> dict:
   """The routing-phase kernels of configuration 5 at `tokens` tokens, each
   timed alone (back-to-back launches): the fused router gate beside the
-  two-step path it replaces, the dispatch sort, the row gather (bf16 -> f16,
-  as the layer runs it), the MXFP8 quantising gather and the weighted combine
-  + RMSNorm.  The gathers write far more than they read (each source row is
-  read k times from L2), so their bound is the write-only HBM bandwidth,
-  measured here as a torch fill of the same size beside a plain copy."""
+  two-step path it replaces, the dispatch sort, the row gather in token order
+  (each latent row read once and stored top_k times, as the layer runs it)
+  beside the sorted-order gather, the MXFP8 quantising gather in both orders
+  and the weighted combine + RMSNorm.  The gathers write k times what they
+  read; their bytes are the rows written (+ the rows read once), against the
+  measured copy bandwidth (a torch fill and copy of the same size are timed
+  beside them for reference)."""
   import torch
 
   iters = max(3, min(args.steps, 20))
@@ -427,20 +429,25 @@ def gpu_routing_kernels(args, lm, ops, dev, peaks, peak_src, tokens: int) -> dic
   src = torch.empty_like(buf)
   ms_copy = time_launches(lambda: buf.copy_(src), iters)
   del src
-  write_gbs = gb / (ms_fill / 1e3) / 1e9
-  out["hbm_measured_here"] = {"write_only_gbs": write_gbs,
-                              "copy_gbs": 2 * gb / (ms_copy / 1e3) / 1e9,
-                              "how": f"torch fill / copy_ of {gb / 1e9:.2f} GB"}
+  out["torch_reference_kernels"] = {"fill_gbs": gb / (ms_fill / 1e3) / 1e9,
+                                    "copy_gbs": 2 * gb / (ms_copy / 1e3) / 1e9,
+                                    "how": f"torch fill_ / copy_ of {gb / 1e9:.2f} GB"}
+  moved = gb + T * L * 2  # rows written + each source row read once
+  ms = time_launches(lambda: ops.scatter_rows(x, d_.slot_pos, K, out=buf, to_f16=True), iters)
+  out["gather_rows_f16_token_order"] = {"ms": ms, "gbs": moved / (ms / 1e3) / 1e9,
+                                        "frac_of_copy_peak": moved / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
   ms = time_launches(lambda: ops.gather_rows(x, d_.token_idx, out=buf, to_f16=True), iters)
-  out["gather_rows_f16"] = {"ms": ms, "gbs_written": gb / (ms / 1e3) / 1e9,
-                            "frac_of_write_only": (gb / (ms / 1e3) / 1e9) / write_gbs,
-                            "frac_of_copy_peak": (gb / (ms / 1e3) / 1e9) / peaks["hbm_gbs"]}
-  mx = ops.quantize_mxfp8_rows(x, d_.group_sizes, d_.token_idx)
+  out["gather_rows_f16_sorted_order"] = {"ms": ms, "gbs": moved / (ms / 1e3) / 1e9,
+                                         "frac_of_copy_peak": moved / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+  mx = ops.quantize_mxfp8_scatter(x, d_.group_sizes, d_.slot_pos, K)
+  qb = rows * L + rows * L // 32 + T * L * 2
+  ms = time_launches(lambda: ops.quantize_mxfp8_scatter(x, d_.group_sizes, d_.slot_pos, K, out=mx),
+                     iters)
+  out["gather_quantize_mxfp8_token_order"] = {"ms": ms, "gbs": qb / (ms / 1e3) / 1e9,
+                                              "frac_of_copy_peak": qb / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
   ms = time_launches(lambda: ops.quantize_mxfp8_rows(x, d_.group_sizes, d_.token_idx, out=mx),
                      iters)
-  qb = rows * L + rows * L // 32
-  out["gather_quantize_mxfp8"] = {"ms": ms, "gbs_written": qb / (ms / 1e3) / 1e9,
-                                  "frac_of_write_only": (qb / (ms / 1e3) / 1e9) / write_gbs}
+  out["gather_quantize_mxfp8_sorted_order"] = {"ms": ms, "gbs": qb / (ms / 1e3) / 1e9}
   del mx
   eo = buf.view(torch.bfloat16)
   ns = torch.ones(L, device=dev).to(torch.bfloat16)

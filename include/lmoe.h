@@ -273,6 +273,19 @@ LMOE_API int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* toke
                               int64_t rows, int64_t row_bytes, int convert, int32_t* dev_status,
                               void* stream);
 
+/* The gather in token order: out[slot_pos[t*k + s]] = x[t] for every token t
+ * and slot s with slot_pos >= 0 (rows of row_bytes; convert as in
+ * lmoe_gather_rows).  Each source row is read (and converted) once and
+ * stored k times; rows that no slot points at are left untouched, so for a
+ * dropless dispatch (every sorted position is some slot's) the output equals
+ * lmoe_gather_rows(x, token_idx) bit for bit.  A position >= out_rows is
+ * skipped and records LMOE_DEVICE_BOUNDS.  top_k <= 32.
+ * Replaces `x[sorted_token_idx]` of the dropless forward
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:372-374). */
+LMOE_API int lmoe_scatter_rows(const void* x, const int32_t* slot_pos, int64_t num_tokens,
+                               int64_t top_k, void* out, int64_t out_rows, int64_t row_bytes,
+                               int convert, int32_t* dev_status, void* stream);
+
 /* Weighted combine + RMSNorm:
  *   routed[t] = dtype(sum_s expert_out[slot_pos[t*k+s]] * topk_w[t,s])   (f32, slot order)
  *   normed[t] = dtype(dtype(routed[t] / sqrt(mean(routed[t]^2) + eps)) * norm_scale)
@@ -414,6 +427,17 @@ LMOE_API int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16,
                                       int64_t num_groups, int64_t rows, int64_t k, void* out_q,
                                       void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
                                       void* stream);
+/* The same in token order for a dropless dispatch: token t's row x[t] is
+ * quantised once and stored at the padded position of each of its sorted
+ * positions slot_pos[t*top_k + s] (the rows lmoe_mxfp8_quantize_rows writes
+ * with token_idx the dispatch's, bit for bit).  Padding rows are left
+ * untouched; a destination past m_pad_capacity is skipped and records
+ * LMOE_DEVICE_BOUNDS.  top_k <= 32, k a multiple of 128, group_sizes required. */
+LMOE_API int lmoe_mxfp8_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                         int64_t num_tokens, int64_t top_k, int64_t k,
+                                         const int32_t* group_sizes, int64_t num_groups,
+                                         void* out_q, void* out_sf, int64_t m_pad_capacity,
+                                         int32_t* dev_status, void* stream);
 /* positions (n int32, sorted-order rows; < 0 passes through as -1) -> their
  * padded positions (the slot positions the combine reads the padded expert
  * outputs with). */

@@ -264,3 +264,33 @@ def test_layer_mxfp8_mode_stages_and_error(lm):
   graph.replay()
   torch.cuda.synchronize()
   assert torch.equal(out, final)
+
+
+@pytest.mark.parametrize("t,k,e,dim,f16", [(300, 8, 64, 256, False), (1000, 16, 896, 2048, True),
+                                           (7, 3, 4, 128, False)])
+def test_quantize_scatter_equals_row_order(lm, t, k, e, dim, f16):
+  """The token-order quantising gather (each token's row quantised once and
+  stored at its k padded positions) writes the same codes and scale bytes as
+  the row-order kernel on every row of the groups."""
+  ops = _ops()
+  g = torch.Generator(device="cuda").manual_seed(t + k)
+  x = torch.randn(t, dim, generator=g, device="cuda").to(torch.float16 if f16 else torch.bfloat16)
+  idx = torch.stack([torch.randperm(e, generator=g, device="cuda")[:k] for _ in range(t)]).int()
+  d = ops.dispatch(idx, torch.ones(t, k, device="cuda"), e, want_order=False)
+  a = ops.quantize_mxfp8_rows(x, d.group_sizes, d.token_idx)
+  b = ops.quantize_mxfp8_scatter(x, d.group_sizes, d.slot_pos, k)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  gs = d.group_sizes.cpu().numpy()
+  prow = padded_rows_of(gs)
+  m_pad = a.q.shape[0]
+  assert b.q.shape == a.q.shape
+  assert np.array_equal(b.q.cpu().numpy()[prow], a.q.cpu().numpy()[prow])
+  assert np.array_equal(sf_bytes_at(b.sf.cpu().numpy(), prow, dim, m_pad),
+                        sf_bytes_at(a.sf.cpu().numpy(), prow, dim, m_pad))
+  # and the slot positions moved to the padded rows address the token's row
+  pp = ops.mxfp8_pad_positions(d.slot_pos, d.group_sizes).cpu().numpy().reshape(t, k)
+  qb = b.q.cpu().numpy()
+  for tok in (0, t // 2, t - 1):
+    for r in pp[tok]:
+      assert np.array_equal(qb[r], qb[pp[tok][0]])

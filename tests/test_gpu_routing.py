@@ -167,6 +167,36 @@ def test_gather_rows_bit_exact(lm):
   assert torch.equal(out.cpu(), ref)
 
 
+@pytest.mark.parametrize("t,k,e,dim,to_f16", [(300, 8, 64, 2048, False), (1000, 16, 896, 2048, True),
+                                              (5, 3, 4, 8, False), (2, 1, 2, 4104, True)])
+def test_scatter_rows_equals_gather(lm, t, k, e, dim, to_f16):
+  """The token-order gather (each row read once, stored k times) writes the
+  rows of the sorted-order gather bit for bit for a dropless dispatch,
+  including rows longer than one 4 KB pass and the bf16 -> f16 conversion."""
+  g = torch.Generator(device="cuda").manual_seed(t * k)
+  x = torch.randn(t, dim, generator=g, device="cuda").to(torch.bfloat16)
+  idx = torch.stack([torch.randperm(e, generator=g, device="cuda")[:k] for _ in range(t)]).int()
+  d = lm.dispatch(idx, None, e, want_order=False)
+  ref = lm.gather_rows(x, d.token_idx, to_f16=to_f16)
+  got = lm.ops.scatter_rows(x, d.slot_pos, k, to_f16=to_f16)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+
+
+def test_scatter_rows_bounds(lm):
+  """A slot position past the output is skipped and reported."""
+  x = torch.ones(4, 64, dtype=torch.bfloat16, device="cuda")
+  pos = torch.tensor([0, 1, 2, 3, 4, 5, 6, 100], dtype=torch.int32, device="cuda")
+  out = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+  lm.ops.scatter_rows(x, pos, 2, out=out)
+  torch.cuda.synchronize()
+  with pytest.raises(lm._native.LmoeError):
+    lm.check_device_status()
+  assert torch.equal(out[:7], torch.ones(7, 64, dtype=torch.bfloat16, device="cuda"))
+  assert torch.equal(out[7], torch.zeros(64, dtype=torch.bfloat16, device="cuda"))
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "fp32"])
 def test_combine_rmsnorm(lm, dtype):
   rng = np.random.default_rng(31)

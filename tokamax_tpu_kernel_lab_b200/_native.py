@@ -58,6 +58,7 @@ SIGNATURES = {
     "lmoe_dispatch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p, _p, _p, _p, _p,
                              _p, _p, _sz, _p]),
     "lmoe_gather_rows": (_i32, [_p, _i64, _p, _p, _i64, _i64, _i32, _p, _p]),
+    "lmoe_scatter_rows": (_i32, [_p, _p, _i64, _i64, _p, _i64, _i64, _i32, _p, _p]),
     "lmoe_combine_rmsnorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _f32, _i32, _p, _p, _p]),
     "lmoe_combine_scatter_add": (_i32, [_p, _p, _p, _p, _i64, _i64, _i64, _i32, _p]),
     "lmoe_ep_reorder": (_i32, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
@@ -65,6 +66,8 @@ SIGNATURES = {
     "lmoe_mxfp4_repack_blockscaled": (_i32, [_p, _p, _i64, _i64, _i64, _i32, _p, _p, _p]),
     "lmoe_mxfp8_quantize_rows": (_i32, [_p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p, _p, _i64,
                                         _p, _p]),
+    "lmoe_mxfp8_quantize_scatter": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
+                                           _i64, _p, _p]),
     "lmoe_mxfp8_pad_positions": (_i32, [_p, _i64, _p, _i64, _p, _p]),
     "lmoe_mxfp8_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32,
                                              _f32, _f32, _i32, _i32, _p, _p]),

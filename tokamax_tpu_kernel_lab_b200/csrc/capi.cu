@@ -152,6 +152,13 @@ int lmoe_gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, vo
                            S(stream));
 }
 
+int lmoe_scatter_rows(const void* x, const int32_t* slot_pos, int64_t num_tokens, int64_t top_k,
+                      void* out, int64_t out_rows, int64_t row_bytes, int convert,
+                      int32_t* dev_status, void* stream) {
+  return lmoe::scatter_rows(x, slot_pos, num_tokens, top_k, out, out_rows, row_bytes, convert,
+                            dev_status, S(stream));
+}
+
 int lmoe_combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,
                          const void* norm_scale, int64_t num_tokens, int64_t top_k,
                          int64_t latent, float eps, int bf16, void* routed_out, void* normed_out,

@@ -88,6 +88,9 @@ size_t dispatch_workspace_bytes(int64_t n_ext, int64_t num_keys);
 int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64_t top_k,
                   int64_t start, int64_t num_keys, int64_t m_out, int pad_bucket, DispatchOut o,
                   void* workspace, size_t ws_bytes, cudaStream_t stream);
+int scatter_rows(const void* x, const int32_t* slot_pos, int64_t T, int64_t k, void* out,
+                 int64_t out_rows, int64_t row_bytes, int convert, int32_t* status,
+                 cudaStream_t stream);
 int gather_rows(const void* x, int64_t x_rows, const int32_t* token_idx, void* out, int64_t rows,
                 int64_t row_bytes, int convert, int32_t* status, cudaStream_t stream);
 int combine_rmsnorm(const void* expert_out, const int32_t* slot_pos, const float* topk_w,

@@ -751,6 +751,106 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
 }
 
 // positions[i] -> padded positions (the combine's slot positions)
+// The quantising gather in token order: warp w takes token t = w, quantises
+// its row once (lane l: blocks l and l + 32 of 32 values, K <= 2048 per pass)
+// and stores the codes and scale bytes at the padded position of each of its
+// k sorted positions slot_pos[t*k + s] -- the rows quantize_mxfp8 writes for
+// a dropless dispatch, each source row read and quantised once instead of k
+// times.  Positions past sum(group_sizes) or outside the capacity are
+// skipped (the latter records LMOE_DEVICE_BOUNDS).
+template <bool F16>
+__global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
+    const uint16_t* __restrict__ x, const int32_t* __restrict__ slot_pos, int64_t T, int k,
+    const int32_t* __restrict__ gs, int G, int K, int64_t m_pad_cap, uint8_t* __restrict__ q,
+    uint8_t* __restrict__ sf, int32_t* status) {
+  extern __shared__ int32_t sh[];
+  int32_t* start = sh;
+  int32_t* pad_off = sh + G + 1;
+  mx_group_offsets(gs, G, start, pad_off);
+  const int lane = threadIdx.x & 31;
+  const int nblk = K / 32;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  bool bad = false;
+  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < T;
+       t += nwarps) {
+    // lane s < k: the padded destination row of slot s (-1: none)
+    int64_t my_dst = -1;
+    if (lane < k) {
+      const int32_t p = slot_pos[t * k + lane];
+      if (p >= 0 && p < start[G]) {
+        my_dst = p + pad_off[mx_group_of(start, G, p)];
+        if (my_dst >= m_pad_cap) {
+          bad = true;
+          my_dst = -1;
+        }
+      }
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * K);
+    for (int b0 = lane; b0 < nblk; b0 += 64) {
+      uint4 raw[2][4];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          raw[u][c] = b0 + 32 * u < nblk ? __ldg(src + (b0 + 32 * u) * 4 + c) : make_uint4(0, 0, 0, 0);
+      uint4 codes[2][2];
+      uint8_t ebyte[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t ws[4] = {raw[u][c].x, raw[u][c].y, raw[u][c].z, raw[u][c].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float2 f;
+            if (F16)
+              f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+            else
+              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+            v[c * 8 + i * 2] = f.x;
+            v[c * 8 + i * 2 + 1] = f.y;
+          }
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        const int e = mx_scale_exp(amax);
+        const float inv = mx_inv_scale(e);
+        uint32_t packed[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint16_t lo, hi;
+          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
+          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
+          packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+        }
+        codes[u][0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        codes[u][1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        ebyte[u] = static_cast<uint8_t>(e + 127);
+      }
+      for (int s = 0; s < k; ++s) {
+        const int64_t dst = __shfl_sync(0xffffffffu, my_dst, s);
+        if (dst < 0) continue;
+        uint8_t* qrow = q + dst * K;
+        const int r = static_cast<int>(dst % 128);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int b = b0 + 32 * u;
+          if (b >= nblk) break;
+          uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
+          __stcs(qd, codes[u][0]);
+          __stcs(qd + 1, codes[u][1]);
+          // atom (K group, row block), byte r0*16 + r1*4 + kb
+          const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
+          sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = ebyte[u];
+        }
+      }
+    }
+  }
+  if (lane == 0 && __any_sync(0xffffffffu, bad)) record_status(status, kDeviceBounds);
+}
+
 __global__ void mx_pad_positions_kernel(const int32_t* __restrict__ pos, int64_t n,
                                         const int32_t* __restrict__ gs, int G,
                                         int32_t* __restrict__ out) {
@@ -829,6 +929,37 @@ int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16, const int
         static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
         (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
         dev_status);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+int lmoe_mxfp8_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                int64_t num_tokens, int64_t top_k, int64_t k,
+                                const int32_t* group_sizes, int64_t num_groups, void* out_q,
+                                void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                void* stream) {
+  using namespace lmoe;
+  if (num_tokens < 0 || top_k <= 0 || top_k > 32 || k <= 0 || k % 128 || m_pad_capacity < 0 ||
+      m_pad_capacity % 128)
+    return LMOE_BAD_SHAPE;
+  if (group_sizes == nullptr || slot_pos == nullptr || num_groups <= 0 || num_groups > 4096)
+    return LMOE_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
+    return LMOE_UNSUPPORTED;
+  if (num_tokens == 0) return LMOE_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t want = (num_tokens * 32 + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
+  const size_t sh = static_cast<size_t>(2 * (num_groups + 1)) * 4;
+  if (x_f16)
+    mx_quantize_scatter_kernel<true><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
+        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
+        static_cast<uint8_t*>(out_sf), dev_status);
+  else
+    mx_quantize_scatter_kernel<false><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
+        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
+        static_cast<uint8_t*>(out_sf), dev_status);
   return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
 }
 

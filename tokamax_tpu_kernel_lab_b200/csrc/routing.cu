@@ -449,6 +449,86 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const uint4* __restric
   if (CONVERT && out_of_range && lane == 0) record_status(status, kF16Range);
 }
 
+// The same copy in token order: warp w takes token t = w, reads its row once
+// (8 x 16 bytes per lane in flight) and stores it at the k sorted positions
+// slot_pos[t*k + s].  For a dropless dispatch every output row is some
+// (token, slot)'s position, so this writes exactly gather_rows' output while
+// reading each source row once instead of k times (and converts it and
+// checks its f16 range once).  Rows no slot points at are left untouched.
+template <bool CONVERT>
+__global__ void __launch_bounds__(256) scatter_rows_kernel(const uint4* __restrict__ x,
+                                                           const int32_t* __restrict__ slot_pos,
+                                                           int64_t T, int k,
+                                                           uint4* __restrict__ out, int64_t out_rows,
+                                                           int vec_per_row, int32_t* status) {
+  const int64_t warp = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  bool out_of_range = false, bad_pos = false;
+  for (int64_t t = warp; t < T; t += nwarps) {
+    // lane s < k holds slot s's position
+    const int32_t my_pos = lane < k ? slot_pos[t * k + lane] : -1;
+    const uint4* src = x + t * vec_per_row;
+    float peak = 0.f;
+    for (int v0 = 0; v0 < vec_per_row; v0 += 256) {
+      uint4 a[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int v = v0 + lane + 32 * i;
+        a[i] = v < vec_per_row ? __ldg(src + v) : make_uint4(0, 0, 0, 0);
+        if (CONVERT) {
+          peak = fmaxf(peak, bf16x8_peak(a[i]));
+          a[i] = bf16x8_to_f16x8(a[i]);
+        }
+      }
+      for (int s = 0; s < k; ++s) {
+        const int32_t p = __shfl_sync(0xffffffffu, my_pos, s);
+        if (p < 0) continue;
+        if (p >= out_rows) {
+          bad_pos = true;
+          continue;
+        }
+        uint4* dst = out + static_cast<int64_t>(p) * vec_per_row;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int v = v0 + lane + 32 * i;
+          if (v < vec_per_row) __stcs(dst + v, a[i]);
+        }
+      }
+    }
+    if (CONVERT) {
+      const float rp = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(peak)));
+      out_of_range |= rp > kF16Max || (rp > 0.f && rp < kF16RunMin);
+    }
+  }
+  if (lane == 0 && bad_pos) record_status(status, kDeviceBounds);
+  if (CONVERT && out_of_range && lane == 0) record_status(status, kF16Range);
+}
+
+int scatter_rows(const void* x, const int32_t* slot_pos, int64_t T, int64_t k, void* out,
+                 int64_t out_rows, int64_t row_bytes, int convert, int32_t* status,
+                 cudaStream_t stream) {
+  if (T < 0 || k <= 0 || k > 32 || out_rows < 0 || row_bytes <= 0 || row_bytes % 16 != 0)
+    return kBadShape;
+  if (row_bytes / 16 >= (1ll << 31) || convert < 0 || convert > 1) return kBadShape;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15) return kUnsupported;
+  if (T == 0) return kOk;
+  const int threads = 256;
+  const int64_t want = (T * 32 + threads - 1) / threads;
+  const int blocks =
+      static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(num_sms(current_device())) * 16));
+  const int vpr = static_cast<int>(row_bytes / 16);
+  if (convert)
+    scatter_rows_kernel<true><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint4*>(x), slot_pos, T, static_cast<int>(k), static_cast<uint4*>(out),
+        out_rows, vpr, status);
+  else
+    scatter_rows_kernel<false><<<blocks, threads, 0, stream>>>(
+        static_cast<const uint4*>(x), slot_pos, T, static_cast<int>(k), static_cast<uint4*>(out),
+        out_rows, vpr, status);
+  return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
 size_t dispatch_workspace_bytes(int64_t n_ext, int64_t num_keys) {
   const int64_t nchunks = (n_ext + kDispChunk - 1) / kDispChunk;
   const int64_t bins = num_keys + 1;

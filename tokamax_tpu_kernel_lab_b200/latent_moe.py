@@ -291,14 +291,14 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
     act, down, slot_pos = mxfp8_expert_ffn(x, d.token_idx, d.group_sizes, d.slot_pos, pw, c,
                                            mark)
   elif pw.expert_gu_mx is not None:
-    act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c, mark)
+    act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c, mark, d.slot_pos)
   elif pw.dtype == torch.bfloat16:
-    sorted_tokens = ops.gather_rows(x, d.token_idx)
+    sorted_tokens = ops.scatter_rows(x, d.slot_pos, c.top_k)
     act = ops.fused_gateup_situ(sorted_tokens, pw.expert_gu, d.group_sizes, beta=beta,
                                 linear_beta=lbeta, round_gate_up=True, rhs_layout="gnk")
     down = ops.ragged_dot(act, pw.expert_down, d.group_sizes, rhs_layout="gnk")
   else:
-    sorted_tokens = ops.gather_rows(x, d.token_idx)
+    sorted_tokens = ops.scatter_rows(x, d.slot_pos, c.top_k)
     gate = ops.ragged_dot(sorted_tokens, pw.expert_gate, d.group_sizes, rhs_layout="gnk")
     up = ops.ragged_dot(sorted_tokens, pw.expert_up, d.group_sizes, rhs_layout="gnk")
     act = ops.situ_and_mul(gate, up, beta, lbeta)
@@ -344,16 +344,18 @@ def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "auto") -> bool:
 
 
 def mxfp4_expert_ffn(x, token_idx, group_sizes, pw: PreparedWeights, c: LatentMoEConfig,
-                     mark=None):
+                     mark=None, slot_pos=None):
   """Routed-expert FFN on MXFP4 weights: row gather into expert-sorted order,
   fused gate/up + SiTU-GLU, down GEMM.  x is f16 on the f16-operand path (see
-  mxfp4_f16_path), bf16 otherwise.  (The gather can also run inside the
-  gate/up kernel's operand load, `row_index=`; at these sizes the one-row TMA
-  gathers feed the tensor cores ~2.5x slower than a separate gather kernel
-  plus contiguous tile loads, so the forward gathers first.)
-  Returns (activation, down output bf16)."""
+  mxfp4_f16_path), bf16 otherwise.  With slot_pos (a dropless dispatch's) the
+  gather runs in token order (each row read once, stored top_k times).  (The
+  gather can also run inside the gate/up kernel's operand load, `row_index=`;
+  at these sizes the one-row TMA gathers feed the tensor cores ~2.5x slower
+  than a separate gather kernel plus contiguous tile loads, so the forward
+  gathers first.)  Returns (activation, down output bf16)."""
   mark = mark or (lambda name: None)
-  rows = ops.gather_rows(x, token_idx)
+  rows = (ops.gather_rows(x, token_idx) if slot_pos is None else
+          ops.scatter_rows(x, slot_pos, c.top_k, out_rows=token_idx.shape[0]))
   mark("gather")
   act = ops.mxfp4_fused_gateup_situ(rows, pw.expert_gu_mx, group_sizes,
                                     beta=c.activation_situ_beta,
@@ -377,12 +379,13 @@ def mxfp8_expert_ffn(x, token_idx, group_sizes, slot_pos, pw: PreparedWeights,
                      c: LatentMoEConfig, mark=None):
   """Routed-expert FFN on the block-scaled tensor core: the gather quantises
   the latent rows to MXFP8 into the padded layout (every expert's rows start
-  at a multiple of 128), gate/up + SiTU-GLU, the activations quantised again,
+  at a multiple of 128; in token order, each row quantised once and stored
+  top_k times), gate/up + SiTU-GLU, the activations quantised again,
   the down GEMM; the slot positions are moved to the padded rows for the
   combine.  Returns (activation, down output, padded slot positions)."""
   mark = mark or (lambda name: None)
   gu, dn = blockscaled_experts(pw)
-  rows = ops.quantize_mxfp8_rows(x, group_sizes, token_idx)
+  rows = ops.quantize_mxfp8_scatter(x, group_sizes, slot_pos, c.top_k)
   mark("gather")
   act = ops.mxfp8_mxfp4_gateup_situ(rows, gu, beta=c.activation_situ_beta,
                                     linear_beta=c.activation_situ_linear_beta,

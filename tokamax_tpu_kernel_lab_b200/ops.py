@@ -528,6 +528,27 @@ def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | No
   return res
 
 
+def scatter_rows(x: torch.Tensor, slot_pos: torch.Tensor, top_k: int, out_rows: int | None = None,
+                 out: torch.Tensor | None = None, to_f16: bool = False):
+  """The dropless gather in token order: out[slot_pos[t*k + s]] = x[t].  Each
+  source row is read (and converted, to_f16 as in gather_rows) once; for a
+  dropless dispatch the result equals gather_rows(x, token_idx) bit for bit.
+  Rows no slot points at are left as they were (uninitialised when `out` is
+  allocated here)."""
+  _need_cuda(x, slot_pos)
+  x = x.contiguous()
+  t = x.shape[0]
+  rows = t * top_k if out_rows is None else int(out_rows)
+  if to_f16 and x.dtype != torch.bfloat16:
+    raise ValueError("to_f16 converts bf16 rows")
+  dt = torch.float16 if to_f16 else x.dtype
+  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=dt, device=x.device)
+  _native.call("lmoe_scatter_rows", _ptr(x), _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k,
+               _ptr(res), res.shape[0], x.shape[1] * x.element_size(), int(to_f16),
+               _ptr(device_status(x.device)), _stream())
+  return res
+
+
 def shard_m_padded(num_tokens, top_k, num_experts, local_num_experts, capacity_factor, tile_size):
   """kimi_k3_latent_moe_reference.py:825-826."""
   expected_total = num_tokens * top_k * local_num_experts / num_experts
@@ -657,6 +678,28 @@ def quantize_mxfp8_rows(x: torch.Tensor, group_sizes: torch.Tensor,
                int(x.dtype == torch.float16), _ptr(ti), None if padded_input else _ptr(gs), g,
                rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)),
                _stream())
+  return out
+
+
+def quantize_mxfp8_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos: torch.Tensor,
+                           top_k: int, *, out: MXFP8Rows | None = None) -> MXFP8Rows:
+  """quantize_mxfp8_rows(x, group_sizes, token_idx) of a dropless dispatch,
+  in token order: each token's row is quantised once and stored at the padded
+  positions of its top_k sorted positions (the same bits; padding rows are
+  left untouched)."""
+  _need_cuda(x, group_sizes, slot_pos)
+  t, k = x.shape
+  g = group_sizes.shape[0]
+  if out is None:
+    m_pad = mxfp8_padded_rows(t * top_k, g)
+    out = MXFP8Rows(torch.empty(m_pad, k, dtype=torch.uint8, device=x.device),
+                    torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=x.device),
+                    group_sizes)
+  gs = group_sizes.to(torch.int32).contiguous()
+  out.group_sizes = gs
+  _native.call("lmoe_mxfp8_quantize_scatter", _ptr(x.contiguous()), int(x.dtype == torch.float16),
+               _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k, k, _ptr(gs), g, _ptr(out.q),
+               _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)), _stream())
   return out
 
 
