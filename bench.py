@@ -55,13 +55,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "LatentMoE layer tokens/s"
 UNIT = "tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-# dram bytes (read + write) per launch of the dominant kernel: an ncu capture
-# (`--metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:mxfp4_swap_kernel`)
-# at 8192 tokens (131072 routed rows) measured 746.5 MB read + 246.5 MB
-# written; scaled by the routed rows to the 16384-token launch (the weight
-# bytes, about a fifth of it, do not grow with the rows, so this overstates
-# by at most ~12%)
-DOMINANT_TRAFFIC_BYTES = int((746.5e6 + 246.5e6) * 2)
+# dram bytes (read + write) per launch of the dominant kernel, from one ncu
+# capture at this configuration (16384 tokens, 262144 routed rows; metrics
+# dram__bytes_read.sum / dram__bytes_write.sum, the first gate/up launch):
+# 1287.9 MB read + 512.4 MB written
+DOMINANT_TRAFFIC_BYTES = int(1287.9e6 + 512.4e6)
 
 
 def parse_args():
