@@ -80,6 +80,8 @@ def parse_args():
                  help="skip the standalone-kernel and token-sweep measurements (N=1)")
   p.add_argument("--phases", action="store_true",
                  help="print per-phase device times of eager forwards instead of the bench line")
+  p.add_argument("--config2", action="store_true",
+                 help="time only benchmark configuration 2 (bf16 ragged_dot) and print its line")
   p.add_argument("--routing", action="store_true",
                  help="time only the routing-phase kernels (router, dispatch, gather, combine) "
                       "at configuration-5 shapes with --tokens tokens and print their line")
@@ -457,6 +459,28 @@ def gpu_routing_kernels(args, lm, ops, dev, peaks, peak_src, tokens: int) -> dic
   return out
 
 
+def gpu_config2(args, ops, dev, peaks, peak_src, iters: int) -> dict:
+  """Benchmark configuration 2 alone: ragged_dot, lhs (8192, 2048), rhs
+  (128, 2048, 1536) in the reference's (G, K, N) layout, Zipf(1.1) group
+  sizes with empty groups."""
+  import numpy as np
+  import torch
+
+  gen = torch.Generator(device=dev).manual_seed(args.seed)
+  m, k, n, g = 8192, 2048, 1536, 128
+  gs = zipf_group_sizes(np.random.default_rng(1), m, g)
+  lhs = (torch.randn(m, k, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
+  rhs = (torch.randn(g, k, n, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
+  gsd = torch.from_numpy(gs).to(dev)
+  res = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+  ms = time_launches(lambda: ops.ragged_dot(lhs, rhs, gsd, out=res), iters)
+  nz = int((gs > 0).sum())
+  entry = roofline_entry(ms, 2.0 * m * k * n, m * k * 2 + nz * k * n * 2 + m * n * 2, peaks,
+                         peak_src)
+  entry["nonempty_groups"] = nz
+  return entry
+
+
 def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
   """Standalone kernels of benchmark configurations 2, 3 and 4 at full size."""
   import numpy as np
@@ -466,20 +490,7 @@ def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
   out = {}
   gen = torch.Generator(device=dev).manual_seed(args.seed)
 
-  # configuration 2: ragged_dot, lhs (8192, 2048), rhs (128, 2048, 1536) in the
-  # reference's (G, K, N) layout, Zipf(1.1) group sizes with empty groups
-  m, k, n, g = 8192, 2048, 1536, 128
-  gs = zipf_group_sizes(np.random.default_rng(1), m, g)
-  lhs = (torch.randn(m, k, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
-  rhs = (torch.randn(g, k, n, generator=gen, device=dev) / k ** 0.5).to(torch.bfloat16)
-  gsd = torch.from_numpy(gs).to(dev)
-  res = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-  ms = time_launches(lambda: ops.ragged_dot(lhs, rhs, gsd, out=res), iters)
-  nz = int((gs > 0).sum())
-  out["config2_ragged_dot_bf16"] = roofline_entry(
-      ms, 2.0 * m * k * n, m * k * 2 + nz * k * n * 2 + m * n * 2, peaks, peak_src)
-  out["config2_ragged_dot_bf16"]["nonempty_groups"] = nz
-  del lhs, rhs, res
+  out["config2_ragged_dot_bf16"] = gpu_config2(args, ops, dev, peaks, peak_src, iters)
 
   # configuration 3: 4096 tokens x top-16 over 896 experts (router bias
   # N(0, 0.5^2)), latent 2048, intermediate 1024, bf16 weights
@@ -687,6 +698,17 @@ def main():
   E = cfg.num_experts
   n_local = E // world
   t_local = args.tokens // world
+  if args.config2:
+    if rank == 0:
+      peaks, peak_src = load_peaks()
+      res = gpu_config2(args, ops, dev, peaks, peak_src, max(3, min(args.steps, 20)))
+      print(json.dumps({"config2_ragged_dot_bf16": res,
+                        "launch": "alone, back-to-back launches between CUDA events"}), flush=True)
+    if world > 1:
+      dist.barrier()
+      dist.destroy_process_group()
+    return
+
   if args.routing:
     if rank == 0:
       peaks, peak_src = load_peaks()
