@@ -246,3 +246,34 @@ def test_token_major_kernels_repeat_bit_exactly(lm):
   gs_fp8 = groups(m // 2, 32, 0.5)
   repeats((m // 2, k), torch.bfloat16,
           lambda o: lm.fp8_ragged_dot(x[:m // 2], q, gs_fp8, scale, out=o))
+
+
+@pytest.mark.parametrize("kind", ["bf16", "f32", "f16", "add", "situ"])
+def test_narrow_tiles_equal_wide_tiles(lm, kind):
+  """A dense GEMM with few token rows takes 128-wide weight tiles (more CTAs,
+  a deeper ring); one with many rows, 256-wide tiles.  Rows present in both
+  must come out bit-identical (each output element sums its K products in
+  the same order either way), for every epilogue the layer's dense
+  projections use; the narrow result also matches the oracle."""
+  from tokamax_tpu_kernel_lab_b200 import ops
+  g = torch.Generator(device="cuda").manual_seed(12)
+  m_small, m_big, k, n = 200, 5120, 1024, 2048
+  a = (torch.randn(m_big, k, generator=g, device="cuda") / k ** 0.5).to(torch.bfloat16)
+  if kind == "situ":
+    w = (torch.randn(2 * n, k, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    run = lambda x: ops.fused_gateup_situ(x, w, None, rhs_layout="gnk")
+  else:
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    add = torch.randn(m_big, n, generator=g, device="cuda").to(torch.bfloat16)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16,
+          "add": torch.bfloat16}[kind]
+    run = lambda x: ops.gemm(x, w, out_dtype=dt,
+                             addend=add[:x.shape[0]].contiguous() if kind == "add" else None)
+  wide = run(a)      # 40 token blocks x 8 (or 16) tiles: 256-wide tiles
+  narrow = run(a[:m_small].contiguous())  # 2 token blocks: 128-wide tiles
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  assert torch.equal(narrow.view(torch.uint8), wide[:m_small].contiguous().view(torch.uint8))
+  if kind == "bf16":
+    ref = to_np(a[:m_small]) @ to_np(w).T
+    assert_gemm_close(ref, to_np(narrow), "narrow-tile gemm")

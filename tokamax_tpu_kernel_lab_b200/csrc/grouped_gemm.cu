@@ -609,6 +609,27 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
 constexpr int kStagesBf16 = 4;
 constexpr int kStagesMx = 5;
 constexpr int kStagesFp8 = 4;
+// Narrow tiles for dense GEMMs too small to fill the GPU (a few token blocks):
+// 128-wide weight tiles give twice the CTAs, and their 32 KB stages fit a
+// ring six deep in the same shared memory.  With few CTAs each one streams its
+// weights from HBM and the ring's depth sets the rate (a ring microbenchmark:
+// the round trip of a TMA copy from HBM is ~2700 clk, so four 512-clk stages
+// leave the tensor pipe waiting).  Every output element sums its K products in
+// the same order as with 256-wide tiles, so the results are the same bits.
+constexpr int kNarrowBN = 128;
+constexpr int kStagesNarrow = 6;
+
+int launch_epi_narrow(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                      int max_tiles, cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: return launch_gemm<kNarrowBN, kStagesNarrow, B_KMAJOR, EPI_BF16>(ta, tb, a, max_tiles, s);
+    case EPI_F32: return launch_gemm<kNarrowBN, kStagesNarrow, B_KMAJOR, EPI_F32>(ta, tb, a, max_tiles, s);
+    case EPI_BF16_ADD:
+      return launch_gemm<kNarrowBN, kStagesNarrow, B_KMAJOR, EPI_BF16_ADD>(ta, tb, a, max_tiles, s);
+    case EPI_SITU: return launch_gemm<kNarrowBN, kStagesNarrow, B_KMAJOR, EPI_SITU>(ta, tb, a, max_tiles, s);
+    default: return kBadShape;
+  }
+}
 
 template <int EPI>
 int dispatch_format(int bf, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
@@ -732,6 +753,18 @@ int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_siz
   a.a_rows = a_rows;
   a.a_src_rows = static_cast<int>(a_src_rows);
   a.out_f16 = (epi == EPI_BF16 || epi == EPI_SITU) ? out_f16 : 0;
+  // a dense K-major GEMM whose 256-wide tiles would leave SMs idle takes the
+  // narrow tiles (one group, no row gather: the tile count is exact)
+  const int64_t m_blocks = (M + kBM - 1) / kBM;
+  if (!b_mn && group_sizes == nullptr && a_rows == nullptr &&
+      m_blocks * a.n_tiles < num_sms(current_device())) {
+    // dims {K, N, G}, box {64, 64, 1}: each half of a 128-wide tile
+    if (!encode_tmap_bf16_3d(&tb, rhs, K, n_weight, G, K * 2, n_weight * K * 2, kBK, kNarrowBN / 2))
+      return kLaunchFailed;
+    const int out_tile = (epi == EPI_SITU) ? kNarrowBN / 2 : kNarrowBN;
+    a.n_tiles = static_cast<int>((N_out + out_tile - 1) / out_tile);
+    return launch_epi_narrow(epi, ta, tb, a, static_cast<int>(m_blocks * a.n_tiles), stream);
+  }
   return launch_epi(epi, b_mn ? B_NMAJOR : B_KMAJOR, ta, tb, a, max_tiles_of(a), stream);
 }
 
