@@ -258,13 +258,30 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   # stream beside the routing, dispatch and gather kernels (which leave most of
   # the tensor cores idle) and joins before the output sum, computed as
   # bf16(bf16(normed @ W_up) + shared) -- the same bits as the other order.
+  # The down-projection depends only on h too.  When it is small (its 128 x
+  # 128 tiles would fill at most half the SMs: a few hundred tokens) it runs on
+  # a second side stream beside the router and the dispatch sort, which then
+  # use few SMs as well, and joins before the gather.  With more tokens each
+  # of these GEMMs fills the GPU and running them at the same time only slows
+  # both (measured: 16384 tokens 5.66 -> 6.12 ms), so they stay in order.
   overlap = pw.dtype == torch.bfloat16 and not return_intermediates
+  x_dtype = torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else torch.bfloat16
+  down_tiles = -(-t // 128) * -(-pw.down.shape[0] // 128)
+  overlap_x = overlap and 2 * down_tiles <= torch.cuda.get_device_properties(
+      h.device).multi_processor_count
   if overlap:
     main = torch.cuda.current_stream(h.device)
     side = ops.side_stream(h.device)
     shared_act = torch.empty(t, pw.shared_gu.shape[0] // 2, dtype=h.dtype, device=h.device)
     shared_out = torch.empty(t, pw.shared_down.shape[0], dtype=h.dtype, device=h.device)
     side.wait_stream(main)
+  if overlap_x:
+    side_x = ops.side_stream(h.device, 1)
+    x = torch.empty(t, pw.down.shape[0], dtype=x_dtype, device=h.device)
+    side_x.wait_stream(main)
+    with torch.cuda.stream(side_x):
+      ops.gemm(h, pw.down, rhs_layout="nk", out=x)
+  if overlap:
     with torch.cuda.stream(side):
       ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
                             round_gate_up=True, rhs_layout="gnk", out=shared_act)
@@ -282,10 +299,14 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                                              renormalize=c.moe_renormalize,
                                              routed_scaling_factor=c.routed_scaling_factor)
   mark("route")
-  x = _dense(h, pw.down, out_dtype=torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else None)
-  mark("down-projection")
+  if not overlap_x:
+    x = _dense(h, pw.down, out_dtype=None if x_dtype == torch.bfloat16 else x_dtype)
+    mark("down-projection")
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
   mark("dispatch sort")
+  if overlap_x:
+    main.wait_stream(side_x)
+    mark("down-projection")
   slot_pos = d.slot_pos
   if pw.expert_gu_mx is not None and mxfp4_operand == "mxfp8":
     act, down, slot_pos = mxfp8_expert_ffn(x, d.token_idx, d.group_sizes, d.slot_pos, pw, c,

@@ -66,16 +66,17 @@ def check_device_status(device=None, reset: bool = True) -> None:
     raise _native.LmoeError("device status", code)
 
 
-_side_streams: dict[int, torch.cuda.Stream] = {}
+_side_streams: dict[tuple[int, int], torch.cuda.Stream] = {}
 
 
-def side_stream(device: torch.device | None = None) -> torch.cuda.Stream:
-  """A second stream per device, for work that runs beside the main path."""
+def side_stream(device: torch.device | None = None, which: int = 0) -> torch.cuda.Stream:
+  """Extra streams per device (`which` = 0, 1, ...), for work that runs beside
+  the main path."""
   idx = (device.index if device is not None and device.index is not None
          else torch.cuda.current_device())
-  if idx not in _side_streams:
-    _side_streams[idx] = torch.cuda.Stream(device=idx)
-  return _side_streams[idx]
+  if (idx, which) not in _side_streams:
+    _side_streams[(idx, which)] = torch.cuda.Stream(device=idx)
+  return _side_streams[(idx, which)]
 
 
 def _check_impl(implementation):
