@@ -82,6 +82,9 @@ def parse_args():
                  help="print per-phase device times of eager forwards instead of the bench line")
   p.add_argument("--config2", action="store_true",
                  help="time only benchmark configuration 2 (bf16 ragged_dot) and print its line")
+  p.add_argument("--config4", action="store_true",
+                 help="time only benchmark configuration 4 (MXFP4 ragged_dot: exact and "
+                      "block-scaled paths) and print its line")
   p.add_argument("--routing", action="store_true",
                  help="time only the routing-phase kernels (router, dispatch, gather, combine) "
                       "at configuration-5 shapes with --tokens tokens and print their line")
@@ -481,6 +484,67 @@ def gpu_config2(args, ops, dev, peaks, peak_src, iters: int) -> dict:
   return entry
 
 
+def gpu_config4(args, lm, ops, dev, peaks, peak_src, iters: int, exact: bool = True,
+                blockscaled: bool = True) -> dict:
+  """Benchmark configuration 4 alone: MXFP4 experts (128 x N 2048 x K 4096;
+  codes uniform over all 16, scale exponents uniform in [-6, 2]), x (16384,
+  4096) N(0, 1), uniform-random group sizes.  The exact path runs with bf16
+  and with f16 operands; the block-scaled path (x quantised to MXFP8,
+  kind::mxf8f6f4) is timed as the GEMM alone and with the quantisation, its
+  peak twice the measured bf16 burst."""
+  import numpy as np
+  import torch
+
+  g4, k4, n4, m4 = 128, 4096, 2048, 16384
+  gen = torch.Generator(device=dev).manual_seed(args.seed + 4)
+  w4 = lm.random_mxfp4(g4, n4, k4, seed=3, device=dev, scale_exp=(-6, 2))
+  x4 = torch.randn(m4, k4, generator=gen, device=dev).to(torch.bfloat16)
+  gs4 = torch.from_numpy(np.random.default_rng(3).multinomial(m4, np.full(g4, 1 / g4)).astype(
+      np.int32)).to(dev)
+  o4 = torch.empty(m4, n4, dtype=torch.bfloat16, device=dev)
+  flops = 2.0 * m4 * k4 * n4
+  w_bytes = g4 * n4 * (k4 // 2 + k4 // 32)
+  out = {}
+  if exact:
+    byt = m4 * k4 * 2 + w_bytes + m4 * n4 * 2
+    ms = time_launches(lambda: ops.mxfp4_ragged_dot(x4, w4, gs4, out=o4), iters)
+    out["config4_mxfp4_bf16_operands"] = roofline_entry(ms, flops, byt, peaks, peak_src)
+    x4h = x4.to(torch.float16)
+    ms = time_launches(lambda: ops.mxfp4_ragged_dot(x4h, w4, gs4, out=o4), iters)
+    out["config4_mxfp4_f16_operands"] = roofline_entry(ms, flops, byt, peaks, peak_src)
+    del x4h
+  if blockscaled:
+    fp8_peak = dict(peaks, bf16_tflops=2 * peaks["bf16_tflops"])
+    src = f"{peak_src} (fp8 = 2 x bf16 burst)"
+    wb = ops.prepare_mxfp4_blockscaled(w4)
+    a4 = ops.quantize_mxfp8_rows(x4, gs4)
+    ops.mxfp8_mxfp4_ragged_dot(a4, wb, out=o4)
+    ms = time_launches(lambda: ops.mxfp8_mxfp4_ragged_dot(a4, wb, out=o4), iters)
+    out["config4_blockscaled_gemm"] = roofline_entry(
+        ms, flops, m4 * k4 * (1 + 1 / 32) + w_bytes + m4 * n4 * 2, fp8_peak, src)
+    ms = time_launches(lambda: (ops.quantize_mxfp8_rows(x4, gs4, out=a4),
+                                ops.mxfp8_mxfp4_ragged_dot(a4, wb, out=o4)), iters)
+    out["config4_blockscaled_with_quantize"] = roofline_entry(
+        ms, flops, m4 * k4 * 2 + w_bytes + m4 * n4 * 2, fp8_peak, src)
+    # MXFP4 activations (kind::mxf4): its MMA runs at four times the bf16 rate
+    fp4_peak = dict(peaks, bf16_tflops=4 * peaks["bf16_tflops"])
+    src4 = f"{peak_src} (fp4 = 4 x bf16 burst)"
+    a4f = ops.quantize_mxfp4_rows(x4, gs4)
+    ops.mxfp4_mxfp4_ragged_dot(a4f, wb, out=o4)
+    ms = time_launches(lambda: ops.mxfp4_mxfp4_ragged_dot(a4f, wb, out=o4), iters)
+    out["config4_mxf4_gemm"] = roofline_entry(
+        ms, flops, m4 * k4 * (0.5 + 1 / 32) + w_bytes + m4 * n4 * 2, fp4_peak, src4)
+    ms = time_launches(lambda: (ops.quantize_mxfp4_rows(x4, gs4, out=a4f),
+                                ops.mxfp4_mxfp4_ragged_dot(a4f, wb, out=o4)), iters)
+    out["config4_mxf4_with_quantize"] = roofline_entry(
+        ms, flops, m4 * k4 * 2 + w_bytes + m4 * n4 * 2, fp4_peak, src4)
+    del wb, a4, a4f
+  del w4, x4, o4
+  torch.cuda.synchronize()
+  torch.cuda.empty_cache()
+  return out
+
+
 def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
   """Standalone kernels of benchmark configurations 2, 3 and 4 at full size."""
   import numpy as np
@@ -523,24 +587,7 @@ def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
   out["config3_gateup_situ_bf16"]["nonempty_groups"] = nz
   del x, w_gu, w_dn, act, dn, rows
 
-  # configuration 4: MXFP4 (128 experts, K 4096, N 2048; codes uniform over
-  # all 16, scale exponents uniform in [-6, 2]), bf16 x (16384, 4096),
-  # uniform-random group sizes
-  g4, k4, n4, m4 = 128, 4096, 2048, 16384
-  w4 = lm.random_mxfp4(g4, n4, k4, seed=3, device=dev, scale_exp=(-6, 2))
-  x4 = torch.randn(m4, k4, generator=gen, device=dev).to(torch.bfloat16)
-  gs4 = torch.from_numpy(np.random.default_rng(3).multinomial(m4, np.full(g4, 1 / g4)).astype(
-      np.int32)).to(dev)
-  o4 = torch.empty(m4, n4, dtype=torch.bfloat16, device=dev)
-  ms4 = time_launches(lambda: ops.mxfp4_ragged_dot(x4, w4, gs4, out=o4), iters)
-  byt = m4 * k4 * 2 + g4 * n4 * (k4 // 2 + k4 // 32) + m4 * n4 * 2
-  out["config4_mxfp4_bf16_operands"] = roofline_entry(ms4, 2.0 * m4 * k4 * n4, byt, peaks,
-                                                      peak_src)
-  x4h = x4.to(torch.float16)
-  ms4h = time_launches(lambda: ops.mxfp4_ragged_dot(x4h, w4, gs4, out=o4), iters)
-  out["config4_mxfp4_f16_operands"] = roofline_entry(ms4h, 2.0 * m4 * k4 * n4, byt, peaks,
-                                                     peak_src)
-  del w4, x4, x4h, o4
+  out.update(gpu_config4(args, lm, ops, dev, peaks, peak_src, iters, blockscaled=False))
   torch.cuda.synchronize()
   torch.cuda.empty_cache()
   return out
@@ -549,10 +596,10 @@ def gpu_config_extras(args, lm, ops, dev, peaks, peak_src) -> dict:
 def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
   """The opt-in block-scaled path (MXFP8 activations x MXFP4 weights on
   kind::mxf8f6f4): the configuration-5 layer forward with
-  mxfp4_operand="mxfp8", its two routed GEMMs and the quantising gather
-  standalone, and configuration 4 on it.  Its MMA runs at twice the bf16
-  rate, so its roofline peak here is twice the measured bf16 burst."""
-  import numpy as np
+  mxfp4_operand="mxfp8" (and with "mxfp4": MXFP4 activations on kind::mxf4),
+  its two routed GEMMs and the quantising gather standalone, and
+  configuration 4 on it.  Its MMA runs at twice the bf16 rate, so its
+  roofline peak here is twice the measured bf16 burst."""
   import torch
 
   iters = max(3, min(args.steps, 10))
@@ -567,6 +614,16 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
     lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp8")
   ms = time_launches(graph.replay, max(5, args.steps))
   out["layer"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
+  del graph
+  # the same layer with MXFP4 activations (kind::mxf4)
+  for _ in range(2):
+    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp4")
+  torch.cuda.synchronize()
+  graph = torch.cuda.CUDAGraph()
+  with torch.cuda.graph(graph):
+    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp4")
+  ms = time_launches(graph.replay, max(5, args.steps))
+  out["layer_mxfp4_activations"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
   del graph
   _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True, mxfp4_operand="mxfp8")
   gs, tix = inter["group_sizes"], inter["token_idx"]
@@ -588,23 +645,11 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
                                       fp8_peak, src)
   out["down"] = roofline_entry(ms_dn, 2.0 * M * I * L,
                                M * I * (1 + 1 / 32) + nz * L * I * 0.53 + M * L * 2, fp8_peak, src)
-  # configuration 4 (bf16 x quantised to MXFP8 first; the quantisation is
-  # timed with the GEMM)
-  g4, k4, n4, m4 = 128, 4096, 2048, 16384
-  gen = torch.Generator(device=dev).manual_seed(args.seed + 4)
-  w4 = ops.prepare_mxfp4_blockscaled(lm.random_mxfp4(g4, n4, k4, seed=3, device=dev,
-                                                     scale_exp=(-6, 2)))
-  x4 = torch.randn(m4, k4, generator=gen, device=dev).to(torch.bfloat16)
-  gs4 = torch.from_numpy(np.random.default_rng(3).multinomial(m4, np.full(g4, 1 / g4)).astype(
-      np.int32)).to(dev)
-  a4 = ops.quantize_mxfp8_rows(x4, gs4)
-  o4 = ops.mxfp8_mxfp4_ragged_dot(a4, w4)
-  ms4 = time_launches(lambda: (ops.quantize_mxfp8_rows(x4, gs4, out=a4),
-                               ops.mxfp8_mxfp4_ragged_dot(a4, w4, out=o4)), iters)
-  out["config4"] = roofline_entry(ms4, 2.0 * m4 * k4 * n4,
-                                  m4 * k4 * 2 + g4 * n4 * (k4 // 2 + k4 // 32) + m4 * n4 * 2,
-                                  fp8_peak, src)
-  del w4, x4, a4, o4
+  c4 = gpu_config4(args, lm, ops, dev, peaks, peak_src, iters, exact=False)
+  out["config4"] = c4["config4_blockscaled_with_quantize"]
+  out["config4_gemm"] = c4["config4_blockscaled_gemm"]
+  out["config4_mxf4_gemm"] = c4["config4_mxf4_gemm"]
+  out["config4_mxf4_with_quantize"] = c4["config4_mxf4_with_quantize"]
   torch.cuda.synchronize()
   torch.cuda.empty_cache()
   return out
@@ -703,6 +748,17 @@ def main():
       peaks, peak_src = load_peaks()
       res = gpu_config2(args, ops, dev, peaks, peak_src, max(3, min(args.steps, 20)))
       print(json.dumps({"config2_ragged_dot_bf16": res,
+                        "launch": "alone, back-to-back launches between CUDA events"}), flush=True)
+    if world > 1:
+      dist.barrier()
+      dist.destroy_process_group()
+    return
+
+  if args.config4:
+    if rank == 0:
+      peaks, peak_src = load_peaks()
+      res = gpu_config4(args, lm, ops, dev, peaks, peak_src, max(3, min(args.steps, 20)))
+      print(json.dumps({"config4": res,
                         "launch": "alone, back-to-back launches between CUDA events"}), flush=True)
     if world > 1:
       dist.barrier()

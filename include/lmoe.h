@@ -460,6 +460,34 @@ LMOE_API int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf
                                            float beta, float linear_beta, int round_gate_up,
                                            int out_dtype, int32_t* dev_status, void* stream);
 
+/* The MXFP4-activation form of the same path (kind::mxf4 on the tensor core,
+ * both operands e2m1, twice the MMA rate of the MXFP8 form and half its
+ * activation bytes, at a larger rounding error: ~10% normwise on N(0,1) rows).
+ * Rows are quantised to MXFP4: e2m1 values (two per byte, the even K index in
+ * the low nibble, out_q m_pad_capacity x k/2 bytes), one E8M0 scale per 32 K
+ * values, the smallest power of two 2^e with amax <= 6 * 2^e, values rounded
+ * to nearest even; the padded layout and the scale atoms are those of the
+ * MXFP8 functions.  Same arguments and errors as lmoe_mxfp8_quantize_rows /
+ * lmoe_mxfp8_quantize_scatter. */
+LMOE_API int lmoe_mxfp4_quantize_rows(const void* x, int64_t x_rows, int x_f16,
+                                      const int32_t* token_idx, const int32_t* group_sizes,
+                                      int64_t num_groups, int64_t rows, int64_t k, void* out_q,
+                                      void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                      void* stream);
+LMOE_API int lmoe_mxfp4_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                         int64_t num_tokens, int64_t top_k, int64_t k,
+                                         const int32_t* group_sizes, int64_t num_groups,
+                                         void* out_q, void* out_sf, int64_t m_pad_capacity,
+                                         int32_t* dev_status, void* stream);
+/* Grouped GEMM of padded MXFP4 rows against prepared MXFP4 weights; arguments
+ * as lmoe_mxfp8_mxfp4_grouped_gemm, k a multiple of 256. */
+LMOE_API int lmoe_mxfp4_mxfp4_grouped_gemm(const void* act_q, const void* act_sf,
+                                           const void* w_packed, const void* w_sf,
+                                           const int32_t* group_sizes, void* out, int64_t m_pad,
+                                           int64_t k, int64_t n_out, int64_t g, int epi,
+                                           float beta, float linear_beta, int round_gate_up,
+                                           int out_dtype, int32_t* dev_status, void* stream);
+
 /* Scatter-add combine of one expert shard:
  *   routed[idx[p]] += dtype(shard_out[p] * w[p])   for idx[p] >= 0
  * Replaces _combine_shard_contribution

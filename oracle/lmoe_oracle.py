@@ -301,12 +301,13 @@ def combine_full(outs: np.ndarray, order: np.ndarray, topk_weight: np.ndarray, d
 
 def latent_moe_forward(hidden_states: np.ndarray, w: Weights, cfg: LatentMoEConfig,
                        dtype: str = "fp32", router_activation: str = "sigmoid",
-                       return_intermediates: bool = False, quantize_activations: bool = False):
+                       return_intermediates: bool = False, quantize_activations=False):
   """Restates `latent_moe_forward` (KR:330-435) with the 18 staged
   intermediates of the golden bundles (06_.../generate_pytorch_golden.py).
-  quantize_activations=True models the block-scaled fast path: the expert
-  FFN's two activation operands (the dispatched latent rows and the SiTU
-  output) are rounded to MXFP8 (quantize_mxfp8) before their matmuls."""
+  quantize_activations=True (or "mxfp8") models the block-scaled fast path:
+  the expert FFN's two activation operands (the dispatched latent rows and
+  the SiTU output) are rounded to MXFP8 (quantize_mxfp8) before their
+  matmuls; "mxfp4" rounds them to MXFP4 (quantize_mxfp4_act) instead."""
   inter = {}
   h = to_dtype(hidden_states, dtype)
   logits, scores, sfc, topk_idx, topk_weight = router_gate(
@@ -320,7 +321,12 @@ def latent_moe_forward(hidden_states: np.ndarray, w: Weights, cfg: LatentMoEConf
   inter["sorted_token_indices"] = order
   inter["group_sizes"] = group_sizes
   sorted_tokens = x[sorted_token_idx]
-  mx = (lambda a: dequantize_mxfp8(*quantize_mxfp8(a))) if quantize_activations else (lambda a: a)
+  if quantize_activations == "mxfp4":
+    mx = lambda a: dequantize_mxfp8(*quantize_mxfp4_act(a))  # values * 2^(byte - 127)
+  elif quantize_activations:
+    mx = lambda a: dequantize_mxfp8(*quantize_mxfp8(a))
+  else:
+    mx = lambda a: a
   gate = ragged_dot(mx(sorted_tokens), w.expert_gate, group_sizes, dtype)
   up = ragged_dot(mx(sorted_tokens), w.expert_up, group_sizes, dtype)
   situ = situ_and_mul(gate, up, cfg.activation_situ_beta, cfg.activation_situ_linear_beta, dtype)
@@ -611,6 +617,52 @@ def dequantize_mxfp8(q: np.ndarray, sf: np.ndarray, block: int = 32) -> np.ndarr
   return (q.reshape(r, k // block, block) * scale[:, :, None]).reshape(r, k).astype(np.float32)
 
 
+# MXFP4 activations (kind::mxf4): the same blocks and scale rule with e2m1
+# elements -- the smallest 2^e with amax <= 6 * 2^e (e2m1's largest finite is
+# 6 = 1.5 * 2^2), values rounded to nearest even on the e2m1 grid; a row of K
+# values is stored as K/2 bytes, the even K index in the low nibble (the
+# packing of the MXFP4 weights, MXD:29-40).
+
+FP4_E2M1_MAX = 6.0
+
+
+def mxfp4_act_scale_exponent(amax: np.ndarray) -> np.ndarray:
+  """Per-block exponent e (int32) with amax <= 6 * 2^e, the smallest such:
+  with amax = f * 2^E (f in [1, 2)), e = E - 2, or E - 1 when f > 1.5.
+  amax == 0 gives -127 (E8M0 byte 0).  Clamped to [-127, 127]."""
+  a = np.asarray(amax, np.float32)
+  bits = a.view(np.uint32)
+  E = ((bits >> 23) & 0xFF).astype(np.int32) - 127
+  mant = (bits & 0x7FFFFF).astype(np.int64)
+  e = E - 2 + (mant > 0x400000).astype(np.int32)
+  e = np.where(a == 0, -127, e)
+  return np.clip(e, -127, 127).astype(np.int32)
+
+
+def e2m1_round(x: np.ndarray) -> np.ndarray:
+  """float32 -> e2m1 (round to nearest even; the sign of a value rounded to
+  zero is kept) -> float32."""
+  return np.asarray(x, np.float32).astype(ml_dtypes.float4_e2m1fn).astype(np.float32)
+
+
+def quantize_mxfp4_act(x: np.ndarray, block: int = 32):
+  """(rows, K) float32 -> (e2m1 values as float32 (rows, K), E8M0 bytes
+  (rows, K / block) uint8); x ~= values * 2^(byte - 127) blockwise."""
+  x = np.asarray(x, np.float32)
+  r, k = x.shape
+  xb = x.reshape(r, k // block, block)
+  e = mxfp4_act_scale_exponent(np.abs(xb).max(axis=2))
+  q = e2m1_round(xb * np.ldexp(np.float32(1.0), -e)[:, :, None].astype(np.float32))
+  return q.reshape(r, k), (e + 127).astype(np.uint8)
+
+
+def pack_e2m1(values: np.ndarray) -> np.ndarray:
+  """(rows, K) e2m1 values (float32) -> (rows, K/2) bytes: code = sign bit 3
+  | grid index (FP4_E2M1_TABLE), the even K index in the low nibble."""
+  codes = np.asarray(values, np.float32).astype(ml_dtypes.float4_e2m1fn).view(np.uint8) & 0x0F
+  return (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+
+
 def mxfp8_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_sizes):
   """f32 result of the block-scaled grouped matmul: the dequantised MXFP8
   rows times the dequantised MXFP4 weights (every product is exact in f32;
@@ -618,6 +670,12 @@ def mxfp8_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_siz
   K/32) scales in the checkpoint's (out, in) layout."""
   lhs = dequantize_mxfp8(lhs_q, lhs_sf)
   return ragged_dot(lhs, LazyMXFP4Experts(weight_packed, weight_scale), group_sizes, dtype="fp32")
+
+
+def mxfp4_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_sizes):
+  """The same for MXFP4 activation rows (e2m1 values as float32, E8M0 bytes):
+  every product is again exact in f32."""
+  return mxfp8_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_sizes)
 
 
 # ----------------------------------------------------------------------------

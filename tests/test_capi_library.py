@@ -65,3 +65,15 @@ def test_peer_wait_limit_is_a_runtime_setting():
   finally:
     assert lib.lmoe_set_peer_wait_timeout_ns(0) == _native.LMOE_OK
   assert int(lib.lmoe_peer_wait_timeout_ns()) == default
+
+
+def test_mxf4_gemm_checks_k_before_any_launch():
+  """The MXFP4-activation grouped GEMM needs k a multiple of 256 (one 256-K
+  stage of 128-byte rows); the host check answers before touching a device."""
+  from tokamax_tpu_kernel_lab_b200 import _native
+  lib = _native.load()
+  rc = lib.lmoe_mxfp4_mxfp4_grouped_gemm(None, None, None, None, None, None, 128, 384, 128, 1, 0,
+                                         0.0, 0.0, 0, 0, None, None)
+  assert rc == _native.LMOE_BAD_SHAPE
+  rc = lib.lmoe_mxfp4_quantize_rows(None, 0, 0, None, None, 1, 4, 200, None, None, 128, None, None)
+  assert rc == _native.LMOE_BAD_SHAPE

@@ -71,6 +71,12 @@ SIGNATURES = {
     "lmoe_mxfp8_pad_positions": (_i32, [_p, _i64, _p, _i64, _p, _p]),
     "lmoe_mxfp8_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32,
                                              _f32, _f32, _i32, _i32, _p, _p]),
+    "lmoe_mxfp4_quantize_rows": (_i32, [_p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p, _p, _i64,
+                                        _p, _p]),
+    "lmoe_mxfp4_quantize_scatter": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
+                                           _i64, _p, _p]),
+    "lmoe_mxfp4_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32,
+                                             _f32, _f32, _i32, _i32, _p, _p]),
     "lmoe_dispatch_static_scratch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p,
                                             _p, _p, _p, _p, _p, _p]),
     "lmoe_ep_buffer_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),

@@ -67,9 +67,9 @@ bool encode_tmap_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
-                       uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
-                       uint32_t box1) {
+static bool encode_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                         uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                         uint32_t box1, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[3] = {d0, d1, d2};
@@ -77,8 +77,22 @@ bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t
   cuuint32_t box[3] = {box0, box1, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+                       uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
+                       uint32_t box1) {
+  return encode_u8_3d(map, base, d0, d1, d2, stride1_bytes, stride2_bytes, box0, box1,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+bool encode_tmap_u8_3d_sw128(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t box0, uint32_t box1) {
+  return encode_u8_3d(map, base, d0, d1, d2, stride1_bytes, stride2_bytes, box0, box1,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 bool encode_tmap_u8_2d_sw128(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,

@@ -29,6 +29,11 @@ bool encode_tmap_fp4_unpacked_3d(CUtensorMap* map, const void* base, uint64_t k,
 bool encode_tmap_u8_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                        uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0,
                        uint32_t box1);
+// The same with 128-byte swizzle (box0 = 128 bytes): packed e2m1 operand rows
+// for the kind::mxf4 MMA.
+bool encode_tmap_u8_3d_sw128(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t box0, uint32_t box1);
 
 int grouped_gemm_bf16(const void* lhs, const void* rhs, const int32_t* group_sizes, void* out,
                       int64_t M, int64_t K, int64_t N_out, int64_t G, int rhs_layout, int epi,

@@ -64,7 +64,7 @@ namespace lmoe {
 
 namespace {
 
-constexpr int kMxBK = 128;     // K elements per stage (4 MMAs of K 32)
+constexpr int kMxRowBytes = 128;  // bytes of an operand row per stage (one 128-byte swizzle row)
 constexpr int kMxRows = 128;   // weight rows per tile (UMMA M)
 constexpr int kMxTok = 192;    // token rows per tile (UMMA N at most)
 constexpr int kMxStages = 4;
@@ -73,17 +73,32 @@ constexpr int kMxMaxGroups = 1024;
 constexpr int kMxThreads = 32 * 7;
 constexpr int kMxTokWarp = 6;
 
+// MMA kinds of this kernel:
+//   KIND_F8F6F4  kind::mxf8f6f4, A e2m1 (the TMA unpacks 64 bytes of codes to a
+//                128-byte row), B e4m3; K 128 per stage = 4 MMAs of K 32; one
+//                E8M0 scale byte per operand row per MMA (scale_vec::1X)
+//   KIND_F4      kind::mxf4, A and B e2m1, both packed (a 128-byte row holds
+//                256 codes, low nibble first); K 256 per stage = 4 MMAs of K 64
+//                at twice the rate of the former; two scale bytes per row per
+//                MMA (scale_vec::2X, selected by scale id 0 or 2)
+enum { KIND_F8F6F4 = 0, KIND_F4 = 1 };
+
+template <int KIND>
 struct MxCfg {
-  static constexpr int kABytes = kMxRows * kMxBK;        // 16 KB in shared memory
-  static constexpr int kATx = kMxRows * kMxBK / 2;       // 8 KB moved (4-bit codes)
+  static constexpr int kBK = KIND == KIND_F4 ? 256 : 128;  // K elements per stage
+  static constexpr int kQuads = kBK / 128;                   // scale atoms (4 K blocks) per row block
+  static constexpr int kABytes = kMxRows * kMxRowBytes;      // 16 KB in shared memory
+  static constexpr int kATx = KIND == KIND_F4 ? kABytes : kABytes / 2;  // bytes moved
   static constexpr int kBoxRows = 64;
-  static constexpr int kBoxBytes = kBoxRows * kMxBK;     // 8 KB
-  static constexpr int kBBytes = 3 * kBoxBytes;          // up to 192 token rows of e4m3
+  static constexpr int kBoxBytes = kBoxRows * kMxRowBytes;  // 8 KB
+  static constexpr int kBBytes = 3 * kBoxBytes;             // up to 192 token rows
   static constexpr int kSfBytes = 512;
-  static constexpr int kSfbAtoms = 2;                    // 192 rows from a 0- or 64-row offset
-  // 41.5 KB of operands, padded so every stage starts 1024-byte aligned
+  static constexpr int kSfbAtoms = 2;                       // 192 rows from a 0- or 64-row offset
+  static constexpr int kSfaOff = kABytes + kBBytes;         // kQuads weight-scale atoms
+  static constexpr int kSfbOff = kSfaOff + kQuads * kSfBytes;  // kQuads x kSfbAtoms token-scale atoms
+  // 41.5 (KIND_F8F6F4) or 43 KB (KIND_F4) of operands, every stage 1024-byte aligned
   static constexpr int kStageBytes =
-      (kABytes + kBBytes + (1 + kSfbAtoms) * kSfBytes + 1023) / 1024 * 1024;
+      (kSfbOff + kQuads * kSfbAtoms * kSfBytes + 1023) / 1024 * 1024;
   static constexpr int kWarpStage = 1024;
   static constexpr int kOutStageBytes = 4 * kWarpStage;
   static constexpr int kSchedBytes = 3 * (kMxMaxGroups + 1) * 4;
@@ -92,9 +107,11 @@ struct MxCfg {
                                   kSchedBytes + 16 + 8 * kNumBars + 16;
   static constexpr int kTmemCols = 512;  // accumulators at columns 0 and 256 (192 wide)
   static constexpr int kAccStride = 256;
-  static constexpr int kSfaCol = kMxTok;          // scales in the gap after accumulator 0
-  static constexpr int kSfbCol = kMxTok + 4;
-  static_assert(kSfbCol + 4 * kSfbAtoms <= kAccStride, "scale columns in the gap");
+  // scales in the gap after accumulator 0: 4 columns per atom, weight atoms
+  // of the stage's quads first, then each quad's (up to) two token atoms
+  static constexpr int kSfaCol = kMxTok;
+  static constexpr int kSfbCol = kMxTok + 4 * kQuads;
+  static_assert(kSfbCol + 4 * kSfbAtoms * kQuads <= kAccStride, "scale columns in the gap");
   static_assert(kStageBytes % 1024 == 0, "1024-byte aligned stages");
   static_assert(kOutStageBytes >= 2 * kMxThreads * 4, "scan scratch");
   static_assert(kSmem <= 232448, "shared memory");
@@ -102,17 +119,29 @@ struct MxCfg {
 
 // ------------------------------------------------------------------ PTX
 // D (+)= A x B with per-32-K E8M0 scales of A rows and B columns read from
-// tensor memory; A = e2m1 weights, B = e4m3 tokens (formats in idesc).
+// tensor memory; A = e2m1 weights, B = e4m3 (KIND_F8F6F4) or e2m1 (KIND_F4)
+// tokens (formats in idesc).
+template <int KIND>
 __device__ __forceinline__ void umma_mx(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                         uint32_t idesc, uint32_t sfa, uint32_t sfb,
                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
-          "r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
-      : "memory");
+  if constexpr (KIND == KIND_F4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
+            "r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}" ::
+            "r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(sfa), "r"(sfb), "r"(accumulate)
+        : "memory");
+  }
 }
 
 // 32 rows x 16 bytes of shared memory -> tensor-memory lanes 0-31 of every
@@ -143,12 +172,15 @@ __device__ __forceinline__ uint64_t sf_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::mxf8f6f4 with block scales: A e2m1 (5), B
-// e4m3 (0), both K-major, E8M0 scales (bit 23), M, N; the scale byte of each
-// operand's TMEM word (the K block of this MMA) goes in bits 29-30 (A) and
-// 4-5 (B).
+// Instruction descriptor with block scales: A format in bits 7-9, B format in
+// bits 10-12 (kind::mxf8f6f4: e2m1 = 5, e4m3 = 0; kind::mxf4: e2m1 = 1), both
+// K-major, N >> 3 in bits 17-22, E8M0 scales (bit 23), M >> 4 in bits 24-28,
+// bit 31 clear (dense K: 32 for mxf8f6f4, 64 for mxf4); the first scale byte
+// of each operand's TMEM word this MMA reads goes in bits 29-30 (A) and 4-5 (B).
+template <int KIND>
 __host__ __device__ constexpr uint32_t idesc_mx(uint32_t m, uint32_t n) {
-  return (5u << 7) | (0u << 10) | ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
+  return (KIND == KIND_F4 ? (1u << 7) | (1u << 10) : (5u << 7) | (0u << 10)) |
+         ((n >> 3) << 17) | (1u << 23) | ((m >> 4) << 24);
 }
 
 struct MxArgs {
@@ -255,11 +287,11 @@ __device__ __forceinline__ int mx_swz(int row) {
   return kChunks == 4 ? ((row >> 1) & 3) : (row & 7);
 }
 
-template <int EPI>
+template <int EPI, int KIND>
 __global__ void __launch_bounds__(kMxThreads, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmT,
                    const __grid_constant__ CUtensorMap tmT64, const MxArgs args) {
-  using C = MxCfg;
+  using C = MxCfg<KIND>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* stages = smem;
@@ -308,8 +340,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_kb = args.K / kMxBK;
-  const int64_t w_sf_per_g = static_cast<int64_t>(args.n_weight / kMxRows) * num_kb * C::kSfBytes;
+  const int num_kb = args.K / C::kBK;
+  const int num_kq = args.K / 128;  // scale atoms along K per row block
+  const int64_t w_sf_per_g = static_cast<int64_t>(args.n_weight / kMxRows) * num_kq * C::kSfBytes;
 
   if (warp == 0 || warp == kMxTokWarp) {
     // ------------------------------------------------------------ producers
@@ -322,7 +355,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
         const int n_box = (tc.rows + C::kBoxRows - 1) / C::kBoxRows;
         const uint8_t* wsf = args.w_sf + tc.g * w_sf_per_g +
-                             static_cast<int64_t>(tc.n_tile) * num_kb * C::kSfBytes;
+                             static_cast<int64_t>(tc.n_tile) * num_kq * C::kSfBytes;
         // token-scale atoms from the one holding row0 through the tile's last row
         const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
         const int64_t rb0 = tc.row0 / kMxAlign;
@@ -333,25 +366,31 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           }
           const uint32_t fb = smem_u32(full + stage);
           const uint32_t base = smem_u32(stages + stage * C::kStageBytes);
+          // x coordinate of the stage's 128-byte rows: 128 per stage in both
+          // kinds (codes of the unpacking weight map, bytes of the others)
+          const int x0 = kb * kMxRowBytes;
           if (!tok) {
-            mbar_arrive_expect_tx(fb, C::kATx + C::kSfBytes);
-            tma_load_3d(base, &tmW, fb, kb * kMxBK, tc.n_tile * kMxRows, tc.g);
-            bulk_load(base + C::kABytes + C::kBBytes, wsf + kb * C::kSfBytes, C::kSfBytes, fb);
+            // the weight-scale atoms of the stage's quads are consecutive
+            mbar_arrive_expect_tx(fb, C::kATx + C::kQuads * C::kSfBytes);
+            tma_load_3d(base, &tmW, fb, x0, tc.n_tile * kMxRows, tc.g);
+            bulk_load(base + C::kSfaOff, wsf + kb * C::kQuads * C::kSfBytes,
+                      C::kQuads * C::kSfBytes, fb);
           } else {
             const uint32_t b_dst = base + C::kABytes;
             if (tc.rows == kMxTok) {
-              mbar_arrive_expect_tx(fb, C::kBBytes + n_atoms * C::kSfBytes);
-              tma_load_2d(b_dst, &tmT, fb, kb * kMxBK, tc.row0);
+              mbar_arrive_expect_tx(fb, C::kBBytes + C::kQuads * n_atoms * C::kSfBytes);
+              tma_load_2d(b_dst, &tmT, fb, x0, tc.row0);
             } else {
-              mbar_arrive_expect_tx(fb, n_box * C::kBoxBytes + n_atoms * C::kSfBytes);
+              mbar_arrive_expect_tx(fb, n_box * C::kBoxBytes + C::kQuads * n_atoms * C::kSfBytes);
               for (int i = 0; i < n_box; ++i)
-                tma_load_2d(b_dst + i * C::kBoxBytes, &tmT64, fb, kb * kMxBK,
-                            tc.row0 + i * C::kBoxRows);
+                tma_load_2d(b_dst + i * C::kBoxBytes, &tmT64, fb, x0, tc.row0 + i * C::kBoxRows);
             }
-            // the tile's token-scale atoms of this K step are consecutive
-            bulk_load(base + C::kABytes + C::kBBytes + C::kSfBytes,
-                      args.act_sf + (static_cast<int64_t>(kb) * row_blocks + rb0) * C::kSfBytes,
-                      n_atoms * C::kSfBytes, fb);
+            // per quad, the tile's token-scale atoms are consecutive
+            for (int q = 0; q < C::kQuads; ++q)
+              bulk_load(base + C::kSfbOff + q * C::kSfbAtoms * C::kSfBytes,
+                        args.act_sf +
+                            (static_cast<int64_t>(kb * C::kQuads + q) * row_blocks + rb0) * C::kSfBytes,
+                        n_atoms * C::kSfBytes, fb);
           }
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
@@ -376,7 +415,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
         const uint32_t n_mma = (tc.rows + 15) & ~15;
-        const uint32_t idesc = idesc_mx(kMxRows, n_mma);
+        const uint32_t idesc = idesc_mx<KIND>(kMxRows, n_mma);
         const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
         // token n's scales sit in column (row0 % 128 + n) / 32 of the copied
         // atoms; row0 % 128 is 0 or 64 (tiles of 192 from 128-aligned group starts)
@@ -396,16 +435,25 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const uint32_t base = smem_u32(stages + stage * C::kStageBytes);
           // this stage's scales into tensor memory; the tensor pipe runs them
           // in order, after the previous stage's MMAs and before these
-          tmem_cp_sf(sfa_t, sf_desc(base + C::kABytes + C::kBBytes));
-          for (int i = 0; i < n_atoms; ++i)
-            tmem_cp_sf(sfb_t + 4 * i, sf_desc(base + C::kABytes + C::kBBytes + (1 + i) * C::kSfBytes));
 #pragma unroll
-          for (int k = 0; k < kMxBK / 32; ++k) {
+          for (int q = 0; q < C::kQuads; ++q) {
+            tmem_cp_sf(sfa_t + 4 * q, sf_desc(base + C::kSfaOff + q * C::kSfBytes));
+            for (int i = 0; i < n_atoms; ++i)
+              tmem_cp_sf(sfb_t + 4 * (q * C::kSfbAtoms + i),
+                         sf_desc(base + C::kSfbOff + (q * C::kSfbAtoms + i) * C::kSfBytes));
+          }
+          // 4 MMAs of 32 bytes of each operand row: K 32 (one scale byte,
+          // id k) or K 64 (two scale bytes of quad k/2, id 0 or 2)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
             const uint64_t adesc = smem_desc_sw128(base + k * 32, 16, 1024);
             const uint64_t bdesc = smem_desc_sw128(base + C::kABytes + k * 32, 16, 1024);
-            const uint32_t kk = static_cast<uint32_t>(k);
-            umma_mx(d_tmem, adesc, bdesc, idesc | (kk << 29) | (kk << 4), sfa_t | (kk << 30),
-                    sfb_mma | (kk << 30), (kb | k) != 0 ? 1u : 0u);
+            const uint32_t q = KIND == KIND_F4 ? static_cast<uint32_t>(k >> 1) : 0u;
+            const uint32_t id = KIND == KIND_F4 ? static_cast<uint32_t>((k & 1) << 1)
+                                                : static_cast<uint32_t>(k);
+            umma_mx<KIND>(d_tmem, adesc, bdesc, idesc | (id << 29) | (id << 4),
+                          (sfa_t + 4 * q) | (id << 30),
+                          (sfb_mma + 4 * C::kSfbAtoms * q) | (id << 30), (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(smem_u32(empty + stage));
           if (++stage == kMxStages) {
@@ -517,10 +565,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   }
 }
 
-template <int EPI>
+template <int EPI, int KIND>
 int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const CUtensorMap& tt64,
               const MxArgs& a, int max_tiles, cudaStream_t stream) {
-  auto kern = mx_gemm_kernel<EPI>;
+  auto kern = mx_gemm_kernel<EPI, KIND>;
+  using C = MxCfg<KIND>;
   const int dev = current_device();
   static std::mutex mu;
   static uint64_t configured = 0;
@@ -528,13 +577,13 @@ int launch_mx(const CUtensorMap& tw, const CUtensorMap& tt, const CUtensorMap& t
     std::lock_guard<std::mutex> lock(mu);
     if (!(configured & (1ull << dev))) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(MxCfg::kSmem)) != cudaSuccess)
+                               static_cast<int>(C::kSmem)) != cudaSuccess)
         return kLaunchFailed;
       configured |= 1ull << dev;
     }
   }
   const int grid = max(1, min(num_sms(dev), max_tiles));
-  kern<<<grid, kMxThreads, MxCfg::kSmem, stream>>>(tw, tt, tt64, a);
+  kern<<<grid, kMxThreads, C::kSmem, stream>>>(tw, tt, tt64, a);
   return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
@@ -586,15 +635,60 @@ __global__ void mx_repack_rows_kernel(const uint8_t* __restrict__ packed, int G,
 }
 
 // ------------------------------------------------------------------ quantise
+// Element formats of the quantised activation rows: MX_E4M3 (one byte per
+// value, MXFP8) or MX_E2M1 (two values per byte, low nibble first, MXFP4).
+enum { MX_E4M3 = 0, MX_E2M1 = 1 };
+
 // Exponent e of a block with absolute maximum `amax`: the smallest with
-// amax <= 448 * 2^e (e4m3's largest finite is 448 = 1.75 * 2^8), E8M0 byte
+// amax <= emax * 2^e, where emax is the format's largest finite value (e4m3:
+// 448 = 1.75 * 2^8; e2m1: 6 = 1.5 * 2^2), so no element saturates; E8M0 byte
 // e + 127, clamped to [0, 254]; 0 for an all-zero block.
+template <int FMT>
 __device__ __forceinline__ int mx_scale_exp(float amax) {
   if (!(amax > 0.f)) return -127;
   const uint32_t b = __float_as_uint(amax);
   const int E = static_cast<int>((b >> 23) & 0xFF) - 127;
-  int e = E - 8 + ((b & 0x7FFFFF) > 0x600000 ? 1 : 0);
+  const int e = FMT == MX_E2M1 ? E - 2 + ((b & 0x7FFFFF) > 0x400000 ? 1 : 0)
+                               : E - 8 + ((b & 0x7FFFFF) > 0x600000 ? 1 : 0);
   return max(-127, min(127, e));
+}
+
+// Bytes of one 32-value block in the quantised row
+template <int FMT>
+constexpr int mx_block_bytes() {
+  return FMT == MX_E2M1 ? 16 : 32;
+}
+
+// A block of 32 values times `inv` (the inverse block scale) rounded to
+// nearest even: e4m3 into w[0..7], or e2m1 pairs into w[0..3] (value 2i in
+// the low nibble of byte i).
+template <int FMT>
+__device__ __forceinline__ void mx_encode_block(const float (&v)[32], float inv, uint32_t (&w)[8]) {
+  if constexpr (FMT == MX_E2M1) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float* x = v + 8 * i;
+      asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+          "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+          : "=r"(w[i])
+          : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv),
+            "f"(x[4] * inv), "f"(x[5] * inv), "f"(x[6] * inv), "f"(x[7] * inv));
+    }
+#pragma unroll
+    for (int i = 4; i < 8; ++i) w[i] = 0;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint16_t lo, hi;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
+      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+    }
+  }
 }
 
 // 2^-e as a float for e in [-127, 127] (exact powers of two; 2^-127 is subnormal)
@@ -664,9 +758,9 @@ __device__ __forceinline__ int mx_group_of(const int32_t* start, int G, int p) {
   return lo;
 }
 
-// One warp per row: gather (optional), quantise to MXFP8, store the row at its
-// padded position and its scales in the atom layout.
-template <bool F16>
+// One warp per row: gather (optional), quantise to MXFP8 or MXFP4 (FMT),
+// store the row at its padded position and its scales in the atom layout.
+template <bool F16, int FMT>
 __global__ void __launch_bounds__(256) mx_quantize_kernel(
     const uint16_t* __restrict__ x, int64_t x_rows, const int32_t* __restrict__ token_idx,
     const int32_t* __restrict__ gs, int G, int64_t rows, int K, int64_t m_pad_cap,
@@ -692,7 +786,7 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
     const int64_t src_row = token_idx != nullptr ? token_idx[p] : p;
     const bool zero = src_row < 0 || src_row >= x_rows;
     const uint4* src = reinterpret_cast<const uint4*>(x + (zero ? 0 : src_row) * K);
-    uint8_t* qrow = q + dst * K;
+    uint8_t* qrow = q + dst * (nblk * mx_block_bytes<FMT>());
     // the lane's blocks two at a time, the second block's loads issued with
     // the first's (nblk is a multiple of 4)
     for (int b0 = lane; b0 < nblk; b0 += 64) {
@@ -726,21 +820,15 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const int e = mx_scale_exp(amax);
+        const int e = mx_scale_exp<FMT>(amax);
         const float inv = mx_inv_scale(e);
         uint32_t packed[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint16_t lo, hi;
-          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
-          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
-          packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-        }
+        mx_encode_block<FMT>(v, inv, packed);
         // evict-first stores: the source rows are re-read k times across the
         // whole output and must stay in L2
-        uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
+        uint4* qd = reinterpret_cast<uint4*>(qrow + b * mx_block_bytes<FMT>());
         __stcs(qd, make_uint4(packed[0], packed[1], packed[2], packed[3]));
-        __stcs(qd + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
+        if (FMT == MX_E4M3) __stcs(qd + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
         // atom (K group, row block), byte r0*16 + r1*4 + kb
         const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
         const int r = static_cast<int>(dst % 128);
@@ -758,7 +846,7 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
 // a dropless dispatch, each source row read and quantised once instead of k
 // times.  Positions past sum(group_sizes) or outside the capacity are
 // skipped (the latter records LMOE_DEVICE_BOUNDS).
-template <bool F16>
+template <bool F16, int FMT>
 __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
     const uint16_t* __restrict__ x, const int32_t* __restrict__ slot_pos, int64_t T, int k,
     const int32_t* __restrict__ gs, int G, int K, int64_t m_pad_cap, uint8_t* __restrict__ q,
@@ -815,16 +903,10 @@ __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const int e = mx_scale_exp(amax);
+        const int e = mx_scale_exp<FMT>(amax);
         const float inv = mx_inv_scale(e);
         uint32_t packed[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          uint16_t lo, hi;
-          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
-          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
-          packed[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-        }
+        mx_encode_block<FMT>(v, inv, packed);
         codes[u][0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
         codes[u][1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
         ebyte[u] = static_cast<uint8_t>(e + 127);
@@ -832,15 +914,15 @@ __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
       for (int s = 0; s < k; ++s) {
         const int64_t dst = __shfl_sync(0xffffffffu, my_dst, s);
         if (dst < 0) continue;
-        uint8_t* qrow = q + dst * K;
+        uint8_t* qrow = q + dst * (nblk * mx_block_bytes<FMT>());
         const int r = static_cast<int>(dst % 128);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int b = b0 + 32 * u;
           if (b >= nblk) break;
-          uint4* qd = reinterpret_cast<uint4*>(qrow + b * 32);
+          uint4* qd = reinterpret_cast<uint4*>(qrow + b * mx_block_bytes<FMT>());
           __stcs(qd, codes[u][0]);
-          __stcs(qd + 1, codes[u][1]);
+          if (FMT == MX_E4M3) __stcs(qd + 1, codes[u][1]);
           // atom (K group, row block), byte r0*16 + r1*4 + kb
           const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
           sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = ebyte[u];
@@ -863,6 +945,142 @@ __global__ void mx_pad_positions_kernel(const int32_t* __restrict__ pos, int64_t
     const int p = pos[i];
     out[i] = (p < 0 || p >= start[G]) ? -1 : p + pad_off[mx_group_of(start, G, p)];
   }
+}
+
+// Quantising row gathers (the C entry points below): validation, launch.
+template <int FMT>
+int mx_quantize_rows_host(const void* x, int64_t x_rows, int x_f16, const int32_t* token_idx,
+                             const int32_t* group_sizes, int64_t num_groups, int64_t rows,
+                             int64_t k, void* out_q, void* out_sf, int64_t m_pad_capacity,
+                             int32_t* dev_status, void* stream) {
+  if (rows < 0 || k <= 0 || k % 128 || m_pad_capacity < 0 || m_pad_capacity % 128) return LMOE_BAD_SHAPE;
+  if (group_sizes != nullptr && (num_groups <= 0 || num_groups > 4096)) return LMOE_BAD_SHAPE;
+  if (group_sizes == nullptr && rows > m_pad_capacity) return LMOE_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
+    return LMOE_UNSUPPORTED;
+  if (rows == 0) return LMOE_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t want = (rows * 32 + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
+  const size_t sh = group_sizes != nullptr ? static_cast<size_t>(2 * (num_groups + 1)) * 4 : 0;
+  if (x_f16)
+    mx_quantize_kernel<true, FMT><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
+        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
+        dev_status);
+  else
+    mx_quantize_kernel<false, FMT><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
+        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
+        dev_status);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+template <int FMT>
+int mx_quantize_scatter_host(const void* x, int x_f16, const int32_t* slot_pos,
+                                int64_t num_tokens, int64_t top_k, int64_t k,
+                                const int32_t* group_sizes, int64_t num_groups, void* out_q,
+                                void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                void* stream) {
+  if (num_tokens < 0 || top_k <= 0 || top_k > 32 || k <= 0 || k % 128 || m_pad_capacity < 0 ||
+      m_pad_capacity % 128)
+    return LMOE_BAD_SHAPE;
+  if (group_sizes == nullptr || slot_pos == nullptr || num_groups <= 0 || num_groups > 4096)
+    return LMOE_BAD_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
+    return LMOE_UNSUPPORTED;
+  if (num_tokens == 0) return LMOE_OK;
+  auto s = static_cast<cudaStream_t>(stream);
+  const int64_t want = (num_tokens * 32 + 255) / 256;
+  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
+  const size_t sh = static_cast<size_t>(2 * (num_groups + 1)) * 4;
+  if (x_f16)
+    mx_quantize_scatter_kernel<true, FMT><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
+        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
+        static_cast<uint8_t*>(out_sf), dev_status);
+  else
+    mx_quantize_scatter_kernel<false, FMT><<<blocks, 256, sh, s>>>(
+        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
+        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
+        static_cast<uint8_t*>(out_sf), dev_status);
+  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+}
+
+// Grouped GEMM of padded block-scaled rows against prepared MXFP4 weights
+// (the C entry points below): validation, tensor maps, launch.
+template <int KIND>
+int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed, const void* w_sf,
+                    const int32_t* group_sizes, void* out, int64_t m_pad, int64_t k, int64_t n_out,
+                    int64_t g, int epi, float beta, float linear_beta, int round_gate_up,
+                    int out_dtype, int32_t* dev_status, void* stream) {
+  // epi: 0 plain (out_dtype 0 bf16, 1 f32, 2 f16), 3 SiTU-GLU over interleaved
+  // gate/up rows (n_out = intermediate; out_dtype 0 bf16, 2 f16)
+  using C = MxCfg<KIND>;
+  if (g <= 0 || g > kMxMaxGroups || m_pad < 0 || m_pad % 128 || k <= 0 || k % C::kBK ||
+      n_out <= 0)
+    return LMOE_BAD_SHAPE;
+  if (epi != EPI_BF16 && epi != EPI_SITU) return LMOE_BAD_SHAPE;
+  if (out_dtype < 0 || out_dtype > 2 || (epi == EPI_SITU && out_dtype == 1)) return LMOE_BAD_SHAPE;
+  const int64_t n_weight = epi == EPI_SITU ? 2 * n_out : n_out;
+  if (n_weight % 128 || (epi == EPI_SITU ? n_out % 16 : n_out % 8)) return LMOE_UNSUPPORTED;
+  if ((reinterpret_cast<uintptr_t>(w_packed) & 31) ||
+      ((reinterpret_cast<uintptr_t>(act_q) | reinterpret_cast<uintptr_t>(out) |
+        reinterpret_cast<uintptr_t>(act_sf) | reinterpret_cast<uintptr_t>(w_sf)) & 15))
+    return LMOE_UNSUPPORTED;
+  if (m_pad == 0) return LMOE_OK;
+  if (m_pad >= (1ll << 31) || k >= (1 << 20)) return LMOE_BAD_SHAPE;
+  MxArgs a{};
+  a.group_sizes = group_sizes;
+  a.status = dev_status;
+  a.out = out;
+  a.w_sf = static_cast<const uint8_t*>(w_sf);
+  a.act_sf = static_cast<const uint8_t*>(act_sf);
+  a.ldo = n_out;
+  a.M_pad = static_cast<int>(m_pad);
+  a.N = static_cast<int>(n_out);
+  a.K = static_cast<int>(k);
+  a.G = static_cast<int>(g);
+  a.n_weight = static_cast<int>(n_weight);
+  a.n_tiles = static_cast<int>(n_weight / kMxRows);
+  a.beta = beta;
+  a.linear_beta = linear_beta;
+  a.inv_beta = beta != 0.f ? 1.f / beta : 0.f;
+  a.inv_linear_beta = linear_beta != 0.f ? 1.f / linear_beta : 0.f;
+  a.round_gate_up = round_gate_up;
+  a.out_f16 = out_dtype == 2;
+  CUtensorMap tw, tt, tt64;
+  // activation row pitch in bytes: e4m3 (KIND_F8F6F4) or packed e2m1 (KIND_F4)
+  const uint64_t act_pitch = KIND == KIND_F4 ? static_cast<uint64_t>(k / 2) : static_cast<uint64_t>(k);
+  if (KIND == KIND_F4) {
+    // packed codes as bytes, 128-byte rows of 256 codes, 128-byte swizzle
+    const uint64_t kh = static_cast<uint64_t>(k / 2);
+    if (!encode_tmap_u8_3d_sw128(&tw, w_packed, kh, static_cast<uint64_t>(n_weight),
+                                 static_cast<uint64_t>(g), kh, static_cast<uint64_t>(n_weight) * kh,
+                                 kMxRowBytes, kMxRows))
+      return LMOE_LAUNCH_FAILED;
+  } else if (!encode_tmap_fp4_unpacked_3d(&tw, w_packed, static_cast<uint64_t>(k),
+                                          static_cast<uint64_t>(n_weight),
+                                          static_cast<uint64_t>(g))) {
+    return LMOE_LAUNCH_FAILED;
+  }
+  // token rows: one box of a full tile, or boxes of 64 rows for a partial one
+  if (!encode_tmap_u8_2d_sw128(&tt, act_q, act_pitch, static_cast<uint64_t>(m_pad), act_pitch,
+                               kMxRowBytes, kMxTok) ||
+      !encode_tmap_u8_2d_sw128(&tt64, act_q, act_pitch, static_cast<uint64_t>(m_pad), act_pitch,
+                               kMxRowBytes, C::kBoxRows))
+    return LMOE_LAUNCH_FAILED;
+  const int64_t tiles = (m_pad / kMxTok + g) * a.n_tiles;
+  const int max_tiles = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
+  auto s = static_cast<cudaStream_t>(stream);
+  int rc;
+  if (epi == EPI_SITU)
+    rc = launch_mx<EPI_SITU, KIND>(tw, tt, tt64, a, max_tiles, s);
+  else if (out_dtype == 1)
+    rc = launch_mx<EPI_F32, KIND>(tw, tt, tt64, a, max_tiles, s);
+  else
+    rc = launch_mx<EPI_BF16, KIND>(tw, tt, tt64, a, max_tiles, s);
+  return rc;
 }
 
 }  // namespace
@@ -908,28 +1126,18 @@ int lmoe_mxfp8_quantize_rows(const void* x, int64_t x_rows, int x_f16, const int
                              const int32_t* group_sizes, int64_t num_groups, int64_t rows,
                              int64_t k, void* out_q, void* out_sf, int64_t m_pad_capacity,
                              int32_t* dev_status, void* stream) {
-  using namespace lmoe;
-  if (rows < 0 || k <= 0 || k % 128 || m_pad_capacity < 0 || m_pad_capacity % 128) return LMOE_BAD_SHAPE;
-  if (group_sizes != nullptr && (num_groups <= 0 || num_groups > 4096)) return LMOE_BAD_SHAPE;
-  if (group_sizes == nullptr && rows > m_pad_capacity) return LMOE_BAD_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
-    return LMOE_UNSUPPORTED;
-  if (rows == 0) return LMOE_OK;
-  auto s = static_cast<cudaStream_t>(stream);
-  const int64_t want = (rows * 32 + 255) / 256;
-  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
-  const size_t sh = group_sizes != nullptr ? static_cast<size_t>(2 * (num_groups + 1)) * 4 : 0;
-  if (x_f16)
-    mx_quantize_kernel<true><<<blocks, 256, sh, s>>>(
-        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
-        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
-        dev_status);
-  else
-    mx_quantize_kernel<false><<<blocks, 256, sh, s>>>(
-        static_cast<const uint16_t*>(x), x_rows, token_idx, group_sizes, (int)num_groups, rows,
-        (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q), static_cast<uint8_t*>(out_sf),
-        dev_status);
-  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+  return lmoe::mx_quantize_rows_host<lmoe::MX_E4M3>(x, x_rows, x_f16, token_idx, group_sizes,
+                                                    num_groups, rows, k, out_q, out_sf,
+                                                    m_pad_capacity, dev_status, stream);
+}
+
+int lmoe_mxfp4_quantize_rows(const void* x, int64_t x_rows, int x_f16, const int32_t* token_idx,
+                             const int32_t* group_sizes, int64_t num_groups, int64_t rows,
+                             int64_t k, void* out_q, void* out_sf, int64_t m_pad_capacity,
+                             int32_t* dev_status, void* stream) {
+  return lmoe::mx_quantize_rows_host<lmoe::MX_E2M1>(x, x_rows, x_f16, token_idx, group_sizes,
+                                                    num_groups, rows, k, out_q, out_sf,
+                                                    m_pad_capacity, dev_status, stream);
 }
 
 int lmoe_mxfp8_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
@@ -937,30 +1145,19 @@ int lmoe_mxfp8_quantize_scatter(const void* x, int x_f16, const int32_t* slot_po
                                 const int32_t* group_sizes, int64_t num_groups, void* out_q,
                                 void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
                                 void* stream) {
-  using namespace lmoe;
-  if (num_tokens < 0 || top_k <= 0 || top_k > 32 || k <= 0 || k % 128 || m_pad_capacity < 0 ||
-      m_pad_capacity % 128)
-    return LMOE_BAD_SHAPE;
-  if (group_sizes == nullptr || slot_pos == nullptr || num_groups <= 0 || num_groups > 4096)
-    return LMOE_BAD_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out_q)) & 15)
-    return LMOE_UNSUPPORTED;
-  if (num_tokens == 0) return LMOE_OK;
-  auto s = static_cast<cudaStream_t>(stream);
-  const int64_t want = (num_tokens * 32 + 255) / 256;
-  const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
-  const size_t sh = static_cast<size_t>(2 * (num_groups + 1)) * 4;
-  if (x_f16)
-    mx_quantize_scatter_kernel<true><<<blocks, 256, sh, s>>>(
-        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
-        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
-        static_cast<uint8_t*>(out_sf), dev_status);
-  else
-    mx_quantize_scatter_kernel<false><<<blocks, 256, sh, s>>>(
-        static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
-        (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
-        static_cast<uint8_t*>(out_sf), dev_status);
-  return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
+  return lmoe::mx_quantize_scatter_host<lmoe::MX_E4M3>(x, x_f16, slot_pos, num_tokens, top_k, k,
+                                                       group_sizes, num_groups, out_q, out_sf,
+                                                       m_pad_capacity, dev_status, stream);
+}
+
+int lmoe_mxfp4_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                int64_t num_tokens, int64_t top_k, int64_t k,
+                                const int32_t* group_sizes, int64_t num_groups, void* out_q,
+                                void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                void* stream) {
+  return lmoe::mx_quantize_scatter_host<lmoe::MX_E2M1>(x, x_f16, slot_pos, num_tokens, top_k, k,
+                                                       group_sizes, num_groups, out_q, out_sf,
+                                                       m_pad_capacity, dev_status, stream);
 }
 
 int lmoe_mxfp8_pad_positions(const int32_t* positions, int64_t n, const int32_t* group_sizes,
@@ -980,62 +1177,19 @@ int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const v
                                   int64_t m_pad, int64_t k, int64_t n_out, int64_t g, int epi,
                                   float beta, float linear_beta, int round_gate_up, int out_dtype,
                                   int32_t* dev_status, void* stream) {
-  using namespace lmoe;
-  // epi: 0 plain (out_dtype 0 bf16, 1 f32, 2 f16), 3 SiTU-GLU over interleaved
-  // gate/up rows (n_out = intermediate; out_dtype 0 bf16, 2 f16)
-  if (g <= 0 || g > kMxMaxGroups || m_pad < 0 || m_pad % 128 || k <= 0 || k % 128 || n_out <= 0)
-    return LMOE_BAD_SHAPE;
-  if (epi != EPI_BF16 && epi != EPI_SITU) return LMOE_BAD_SHAPE;
-  if (out_dtype < 0 || out_dtype > 2 || (epi == EPI_SITU && out_dtype == 1)) return LMOE_BAD_SHAPE;
-  const int64_t n_weight = epi == EPI_SITU ? 2 * n_out : n_out;
-  if (n_weight % 128 || (epi == EPI_SITU ? n_out % 16 : n_out % 8)) return LMOE_UNSUPPORTED;
-  if ((reinterpret_cast<uintptr_t>(w_packed) & 31) ||
-      ((reinterpret_cast<uintptr_t>(act_q) | reinterpret_cast<uintptr_t>(out) |
-        reinterpret_cast<uintptr_t>(act_sf) | reinterpret_cast<uintptr_t>(w_sf)) & 15))
-    return LMOE_UNSUPPORTED;
-  if (m_pad == 0) return LMOE_OK;
-  if (m_pad >= (1ll << 31) || k >= (1 << 20)) return LMOE_BAD_SHAPE;
-  MxArgs a{};
-  a.group_sizes = group_sizes;
-  a.status = dev_status;
-  a.out = out;
-  a.w_sf = static_cast<const uint8_t*>(w_sf);
-  a.act_sf = static_cast<const uint8_t*>(act_sf);
-  a.ldo = n_out;
-  a.M_pad = static_cast<int>(m_pad);
-  a.N = static_cast<int>(n_out);
-  a.K = static_cast<int>(k);
-  a.G = static_cast<int>(g);
-  a.n_weight = static_cast<int>(n_weight);
-  a.n_tiles = static_cast<int>(n_weight / kMxRows);
-  a.beta = beta;
-  a.linear_beta = linear_beta;
-  a.inv_beta = beta != 0.f ? 1.f / beta : 0.f;
-  a.inv_linear_beta = linear_beta != 0.f ? 1.f / linear_beta : 0.f;
-  a.round_gate_up = round_gate_up;
-  a.out_f16 = out_dtype == 2;
-  CUtensorMap tw, tt, tt64;
-  if (!encode_tmap_fp4_unpacked_3d(&tw, w_packed, static_cast<uint64_t>(k),
-                                   static_cast<uint64_t>(n_weight), static_cast<uint64_t>(g)))
-    return LMOE_LAUNCH_FAILED;
-  // token rows: one box of a full tile, or boxes of 64 rows for a partial one
-  if (!encode_tmap_u8_2d_sw128(&tt, act_q, static_cast<uint64_t>(k), static_cast<uint64_t>(m_pad),
-                               static_cast<uint64_t>(k), kMxBK, kMxTok) ||
-      !encode_tmap_u8_2d_sw128(&tt64, act_q, static_cast<uint64_t>(k),
-                               static_cast<uint64_t>(m_pad), static_cast<uint64_t>(k), kMxBK,
-                               MxCfg::kBoxRows))
-    return LMOE_LAUNCH_FAILED;
-  const int64_t tiles = (m_pad / kMxTok + g) * a.n_tiles;
-  const int max_tiles = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
-  auto s = static_cast<cudaStream_t>(stream);
-  int rc;
-  if (epi == EPI_SITU)
-    rc = launch_mx<EPI_SITU>(tw, tt, tt64, a, max_tiles, s);
-  else if (out_dtype == 1)
-    rc = launch_mx<EPI_F32>(tw, tt, tt64, a, max_tiles, s);
-  else
-    rc = launch_mx<EPI_BF16>(tw, tt, tt64, a, max_tiles, s);
-  return rc;
+  return lmoe::mx_grouped_gemm<lmoe::KIND_F8F6F4>(act_q, act_sf, w_packed, w_sf, group_sizes, out,
+                                                 m_pad, k, n_out, g, epi, beta, linear_beta,
+                                                 round_gate_up, out_dtype, dev_status, stream);
+}
+
+int lmoe_mxfp4_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
+                                  const void* w_sf, const int32_t* group_sizes, void* out,
+                                  int64_t m_pad, int64_t k, int64_t n_out, int64_t g, int epi,
+                                  float beta, float linear_beta, int round_gate_up, int out_dtype,
+                                  int32_t* dev_status, void* stream) {
+  return lmoe::mx_grouped_gemm<lmoe::KIND_F4>(act_q, act_sf, w_packed, w_sf, group_sizes, out,
+                                             m_pad, k, n_out, g, epi, beta, linear_beta,
+                                             round_gate_up, out_dtype, dev_status, stream);
 }
 
 }  // extern "C"

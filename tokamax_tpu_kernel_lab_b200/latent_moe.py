@@ -243,7 +243,9 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   path: the latent rows and the SiTU activations are rounded to MXFP8 (e4m3,
   one E8M0 scale per 32 values) and the MXFP4 experts run on the
   block-scaled tensor core (kind::mxf8f6f4); the activation rounding adds
-  ~3% normwise error against the exact forward.
+  ~3% normwise error against the exact forward.  "mxfp4" rounds them to
+  MXFP4 instead (e2m1, one E8M0 scale per 32 values) and runs kind::mxf4, at
+  twice the MMA rate and a larger error (~10% normwise).
 
   `mark(name)` (optional) is called on the host after each phase of the main
   stream is enqueued, e.g. to record CUDA events for a phase timeline."""
@@ -308,9 +310,10 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
     main.wait_stream(side_x)
     mark("down-projection")
   slot_pos = d.slot_pos
-  if pw.expert_gu_mx is not None and mxfp4_operand == "mxfp8":
+  if pw.expert_gu_mx is not None and mxfp4_operand in ("mxfp8", "mxfp4"):
+    fmt = "e4m3" if mxfp4_operand == "mxfp8" else "e2m1"
     act, down, slot_pos = mxfp8_expert_ffn(x, d.token_idx, d.group_sizes, d.slot_pos, pw, c,
-                                           mark)
+                                           mark, fmt=fmt)
   elif pw.expert_gu_mx is not None:
     act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c, mark, d.slot_pos)
   elif pw.dtype == torch.bfloat16:
@@ -358,8 +361,8 @@ def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "auto") -> bool:
   """True when the MXFP4 experts run the f16-operand kernels: mxfp4_operand
   is "auto" and every scale byte lies in their exact range.  The latent
   activations then travel as f16 (the same bf16-rounded values)."""
-  if mxfp4_operand not in ("auto", "bf16", "mxfp8"):
-    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto', 'bf16' or 'mxfp8'")
+  if mxfp4_operand not in ("auto", "bf16", "mxfp8", "mxfp4"):
+    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto', 'bf16', 'mxfp8' or 'mxfp4'")
   return (mxfp4_operand == "auto" and pw.expert_gu_mx is not None and
           pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok)
 
@@ -397,21 +400,26 @@ def blockscaled_experts(pw: PreparedWeights):
 
 
 def mxfp8_expert_ffn(x, token_idx, group_sizes, slot_pos, pw: PreparedWeights,
-                     c: LatentMoEConfig, mark=None):
+                     c: LatentMoEConfig, mark=None, fmt: str = "e4m3"):
   """Routed-expert FFN on the block-scaled tensor core: the gather quantises
-  the latent rows to MXFP8 into the padded layout (every expert's rows start
-  at a multiple of 128; in token order, each row quantised once and stored
-  top_k times), gate/up + SiTU-GLU, the activations quantised again,
-  the down GEMM; the slot positions are moved to the padded rows for the
-  combine.  Returns (activation, down output, padded slot positions)."""
+  the latent rows to MXFP8 (fmt "e4m3") or MXFP4 ("e2m1") into the padded
+  layout (every expert's rows start at a multiple of 128; in token order,
+  each row quantised once and stored top_k times), gate/up + SiTU-GLU, the
+  activations quantised again, the down GEMM; the slot positions are moved
+  to the padded rows for the combine.  Returns (activation, down output,
+  padded slot positions)."""
   mark = mark or (lambda name: None)
   gu, dn = blockscaled_experts(pw)
-  rows = ops.quantize_mxfp8_scatter(x, group_sizes, slot_pos, c.top_k)
+  if fmt == "e4m3":
+    quantize_scatter, quantize_rows = ops.quantize_mxfp8_scatter, ops.quantize_mxfp8_rows
+  else:
+    quantize_scatter, quantize_rows = ops.quantize_mxfp4_scatter, ops.quantize_mxfp4_rows
+  rows = quantize_scatter(x, group_sizes, slot_pos, c.top_k)
   mark("gather")
   act = ops.mxfp8_mxfp4_gateup_situ(rows, gu, beta=c.activation_situ_beta,
                                     linear_beta=c.activation_situ_linear_beta,
                                     round_gate_up=True)
-  act_q = ops.quantize_mxfp8_rows(act, group_sizes, padded_input=True)
+  act_q = quantize_rows(act, group_sizes, padded_input=True)
   mark("expert gate/up")
   down = ops.mxfp8_mxfp4_ragged_dot(act_q, dn)
   mark("expert down")

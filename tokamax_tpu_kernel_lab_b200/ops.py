@@ -651,8 +651,64 @@ class MXFP8Rows:
   group_sizes: torch.Tensor
 
 
+@dataclasses.dataclass
+class MXFP4Rows:
+  """Activation rows quantised to MXFP4 in the same padded layout: q (M_pad,
+  K/2) bytes of e2m1 pairs (the even K index in the low nibble), sf and
+  group_sizes as in MXFP8Rows."""
+
+  q: torch.Tensor
+  sf: torch.Tensor
+  group_sizes: torch.Tensor
+
+
+_MX_FORMATS = {  # element format -> (rows class, K values per byte, quantising C entry points)
+    "e4m3": (MXFP8Rows, 1, "lmoe_mxfp8_quantize_rows", "lmoe_mxfp8_quantize_scatter"),
+    "e2m1": (MXFP4Rows, 2, "lmoe_mxfp4_quantize_rows", "lmoe_mxfp4_quantize_scatter"),
+}
+
+
 def mxfp8_padded_rows(num_rows: int, num_groups: int) -> int:
   return int(_native.load().lmoe_mxfp8_padded_rows(num_rows, num_groups))
+
+
+def _mx_rows(fmt: str, m_pad: int, k: int, group_sizes: torch.Tensor, device):
+  cls, k_per_byte, _, _ = _MX_FORMATS[fmt]
+  return cls(torch.empty(m_pad, k // k_per_byte, dtype=torch.uint8, device=device),
+             torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=device),
+             group_sizes)
+
+
+def _quantize_rows(fmt, x, group_sizes, token_idx, padded_input, out):
+  _need_cuda(x, group_sizes, token_idx)
+  rows = token_idx.shape[0] if token_idx is not None else x.shape[0]
+  k = x.shape[1]
+  g = group_sizes.shape[0]
+  if out is None:
+    m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
+    out = _mx_rows(fmt, m_pad, k, group_sizes, x.device)
+  gs = group_sizes.to(torch.int32).contiguous()
+  out.group_sizes = gs
+  ti = None if token_idx is None else token_idx.to(torch.int32).contiguous()
+  _native.call(_MX_FORMATS[fmt][2], _ptr(x.contiguous()), x.shape[0],
+               int(x.dtype == torch.float16), _ptr(ti), None if padded_input else _ptr(gs), g,
+               rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)),
+               _stream())
+  return out
+
+
+def _quantize_scatter(fmt, x, group_sizes, slot_pos, top_k, out):
+  _need_cuda(x, group_sizes, slot_pos)
+  t, k = x.shape
+  g = group_sizes.shape[0]
+  if out is None:
+    out = _mx_rows(fmt, mxfp8_padded_rows(t * top_k, g), k, group_sizes, x.device)
+  gs = group_sizes.to(torch.int32).contiguous()
+  out.group_sizes = gs
+  _native.call(_MX_FORMATS[fmt][3], _ptr(x.contiguous()), int(x.dtype == torch.float16),
+               _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k, k, _ptr(gs), g, _ptr(out.q),
+               _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)), _stream())
+  return out
 
 
 def quantize_mxfp8_rows(x: torch.Tensor, group_sizes: torch.Tensor,
@@ -663,23 +719,7 @@ def quantize_mxfp8_rows(x: torch.Tensor, group_sizes: torch.Tensor,
   padding in one kernel).  With padded_input=True, x is already in that
   layout (the padded output of an earlier block-scaled GEMM) and every row
   keeps its position.  x bf16 or f16 (K a multiple of 128)."""
-  _need_cuda(x, group_sizes, token_idx)
-  rows = token_idx.shape[0] if token_idx is not None else x.shape[0]
-  k = x.shape[1]
-  g = group_sizes.shape[0]
-  if out is None:
-    m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
-    out = MXFP8Rows(torch.empty(m_pad, k, dtype=torch.uint8, device=x.device),
-                    torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=x.device),
-                    group_sizes)
-  gs = group_sizes.to(torch.int32).contiguous()
-  out.group_sizes = gs
-  ti = None if token_idx is None else token_idx.to(torch.int32).contiguous()
-  _native.call("lmoe_mxfp8_quantize_rows", _ptr(x.contiguous()), x.shape[0],
-               int(x.dtype == torch.float16), _ptr(ti), None if padded_input else _ptr(gs), g,
-               rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)),
-               _stream())
-  return out
+  return _quantize_rows("e4m3", x, group_sizes, token_idx, padded_input, out)
 
 
 def quantize_mxfp8_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos: torch.Tensor,
@@ -688,20 +728,22 @@ def quantize_mxfp8_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos:
   in token order: each token's row is quantised once and stored at the padded
   positions of its top_k sorted positions (the same bits; padding rows are
   left untouched)."""
-  _need_cuda(x, group_sizes, slot_pos)
-  t, k = x.shape
-  g = group_sizes.shape[0]
-  if out is None:
-    m_pad = mxfp8_padded_rows(t * top_k, g)
-    out = MXFP8Rows(torch.empty(m_pad, k, dtype=torch.uint8, device=x.device),
-                    torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=x.device),
-                    group_sizes)
-  gs = group_sizes.to(torch.int32).contiguous()
-  out.group_sizes = gs
-  _native.call("lmoe_mxfp8_quantize_scatter", _ptr(x.contiguous()), int(x.dtype == torch.float16),
-               _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k, k, _ptr(gs), g, _ptr(out.q),
-               _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)), _stream())
-  return out
+  return _quantize_scatter("e4m3", x, group_sizes, slot_pos, top_k, out)
+
+
+def quantize_mxfp4_rows(x: torch.Tensor, group_sizes: torch.Tensor,
+                        token_idx: torch.Tensor | None = None, *, padded_input: bool = False,
+                        out: MXFP4Rows | None = None) -> MXFP4Rows:
+  """quantize_mxfp8_rows with e2m1 elements (MXFP4: scale 2^e, the smallest
+  with amax <= 6 * 2^e per 32 K values; values rounded to nearest even)."""
+  return _quantize_rows("e2m1", x, group_sizes, token_idx, padded_input, out)
+
+
+def quantize_mxfp4_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos: torch.Tensor,
+                           top_k: int, *, out: MXFP4Rows | None = None) -> MXFP4Rows:
+  """quantize_mxfp8_scatter with e2m1 elements (the rows quantize_mxfp4_rows
+  writes for the dispatch's token_idx, bit for bit)."""
+  return _quantize_scatter("e2m1", x, group_sizes, slot_pos, top_k, out)
 
 
 def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> torch.Tensor:
@@ -715,29 +757,38 @@ def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> t
   return out
 
 
-def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows, w: MXFP4BlockScaled,
+def _mx_gemm_entry(a) -> str:
+  if isinstance(a, MXFP8Rows):
+    return "lmoe_mxfp8_mxfp4_grouped_gemm"
+  if isinstance(a, MXFP4Rows):
+    return "lmoe_mxfp4_mxfp4_grouped_gemm"
+  raise TypeError(f"block-scaled rows expected, got {type(a).__name__}")
+
+
+def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows | MXFP4Rows, w: MXFP4BlockScaled,
                            out_dtype: torch.dtype = torch.bfloat16,
                            out: torch.Tensor | None = None) -> torch.Tensor:
-  """Padded MXFP8 rows @ dequant(w[g])^T per group -> (M_pad, N); rows past
-  each group's count are not written."""
+  """Padded block-scaled rows @ dequant(w[g])^T per group -> (M_pad, N); rows
+  past each group's count are not written.  MXFP8 rows run kind::mxf8f6f4,
+  MXFP4 rows (K a multiple of 256) kind::mxf4."""
   g, n, k = w.shape
   if w.gateup:
     raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
   m_pad = a.q.shape[0]
   res = out if out is not None else torch.empty(m_pad, n, dtype=out_dtype, device=a.q.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
-  _native.call("lmoe_mxfp8_mxfp4_grouped_gemm", _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
+  _native.call(_mx_gemm_entry(a), _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
                _ptr(a.group_sizes), _ptr(res), m_pad, k, n, g, 0, 0.0, 0.0, 0, code,
                _ptr(device_status(a.q.device)), _stream())
   return res
 
 
-def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows, w: MXFP4BlockScaled, *, beta: float = 4.0,
+def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows | MXFP4Rows, w: MXFP4BlockScaled, *, beta: float = 4.0,
                             linear_beta: float = 25.0, round_gate_up: bool = True,
                             out_dtype: torch.dtype = torch.bfloat16,
                             out: torch.Tensor | None = None) -> torch.Tensor:
   """SiTU-GLU of the block-scaled grouped matmul against gate/up-interleaved
-  MXFP4 weights -> (M_pad, I) (padded rows)."""
+  MXFP4 weights -> (M_pad, I) (padded rows); MXFP8 or MXFP4 rows."""
   g, two_i, k = w.shape
   if not w.gateup:
     raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
@@ -745,8 +796,13 @@ def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows, w: MXFP4BlockScaled, *, beta: float = 
   res = out if out is not None else torch.empty(m_pad, two_i // 2, dtype=out_dtype,
                                                 device=a.q.device)
   code = {torch.bfloat16: 0, torch.float16: 2}[res.dtype]
-  _native.call("lmoe_mxfp8_mxfp4_grouped_gemm", _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
+  _native.call(_mx_gemm_entry(a), _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
                _ptr(a.group_sizes), _ptr(res), m_pad, k, two_i // 2, g, 3, float(beta),
                float(linear_beta), int(round_gate_up), code, _ptr(device_status(a.q.device)),
                _stream())
   return res
+
+
+# the same functions under the names of the MXFP4-activation form
+mxfp4_mxfp4_ragged_dot = mxfp8_mxfp4_ragged_dot
+mxfp4_mxfp4_gateup_situ = mxfp8_mxfp4_gateup_situ
