@@ -513,6 +513,15 @@ def gpu_config4(args, lm, ops, dev, peaks, peak_src, iters: int, exact: bool = T
     ms = time_launches(lambda: ops.mxfp4_ragged_dot(x4h, w4, gs4, out=o4), iters)
     out["config4_mxfp4_f16_operands"] = roofline_entry(ms, flops, byt, peaks, peak_src)
     del x4h
+    # the same exact matmul on the block-scaled tensor core: the rows split
+    # into two e4m3 planes (the split timed with the GEMM), two MMAs per K
+    # step at the MXFP8 rate, so its peak is the bf16 one
+    wb = ops.prepare_mxfp4_blockscaled(w4)
+    rows = ops.quantize_split_rows(x4, gs4)
+    ms = time_launches(lambda: ops.mxfp4_ragged_dot_blockscaled(x4, wb, gs4, out=o4, rows=rows),
+                       iters)
+    out["config4_exact_split_blockscaled"] = roofline_entry(ms, flops, byt, peaks, peak_src)
+    del wb, rows
   if blockscaled:
     fp8_peak = dict(peaks, bf16_tflops=2 * peaks["bf16_tflops"])
     src = f"{peak_src} (fp8 = 2 x bf16 burst)"
@@ -615,16 +624,18 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
   ms = time_launches(graph.replay, max(5, args.steps))
   out["layer"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
   del graph
-  # the same layer with MXFP4 activations (kind::mxf4)
-  for _ in range(2):
-    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp4")
-  torch.cuda.synchronize()
-  graph = torch.cuda.CUDAGraph()
-  with torch.cuda.graph(graph):
-    lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="mxfp4")
-  ms = time_launches(graph.replay, max(5, args.steps))
-  out["layer_mxfp4_activations"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
-  del graph
+  # the same layer with MXFP4 activations (kind::mxf4), and exact on the
+  # block-scaled tensor core (two e4m3 planes per activation row)
+  for mode, key in (("mxfp4", "layer_mxfp4_activations"), ("split", "layer_exact_split")):
+    for _ in range(2):
+      lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+      lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
+    ms = time_launches(graph.replay, max(5, args.steps))
+    out[key] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
+    del graph
   _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True, mxfp4_operand="mxfp8")
   gs, tix = inter["group_sizes"], inter["token_idx"]
   x = inter["latent_projection"]
@@ -656,21 +667,26 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
 
 
 def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
-  """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay)."""
+  """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay):
+  the default forward, and the exact forward on the block-scaled tensor core
+  (mxfp4_operand="split") as `split_ms`."""
   import torch
   out = {}
   for t in tokens:
     gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + t)
     h = torch.randn(t, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
-    for _ in range(2):
-      lm.latent_moe_forward(h, pw, cfg)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-      lm.latent_moe_forward(h, pw, cfg)
-    ms = time_launches(graph.replay, max(5, args.steps))
-    out[f"T{t}"] = {"ms": ms, "tokens_per_s": t / (ms / 1e3)}
-    del graph
+    res = {}
+    for mode in ("auto", "split"):
+      for _ in range(2):
+        lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
+      torch.cuda.synchronize()
+      graph = torch.cuda.CUDAGraph()
+      with torch.cuda.graph(graph):
+        lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
+      res[mode] = time_launches(graph.replay, max(5, args.steps))
+      del graph
+    out[f"T{t}"] = {"ms": res["auto"], "tokens_per_s": t / (res["auto"] / 1e3),
+                    "split_ms": res["split"]}
   return out
 
 

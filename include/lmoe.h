@@ -479,6 +479,56 @@ LMOE_API int lmoe_mxfp4_quantize_scatter(const void* x, int x_f16, const int32_t
                                          const int32_t* group_sizes, int64_t num_groups,
                                          void* out_q, void* out_sf, int64_t m_pad_capacity,
                                          int32_t* dev_status, void* stream);
+/* The exact MXFP4 matmul on the block-scaled tensor core: bf16/f16 rows split
+ * into two e4m3 planes under one E8M0 scale per 32 K values (the MXFP8 scale
+ * rule): hi = e4m3(x / 2^e), lo = e4m3(x / 2^e - hi), both rounded to nearest
+ * even.  hi + lo holds every bf16 value with |x| >= 2^-2 of its block's scale
+ * unit exactly (smaller ones to within 2^-10 of that unit), so the GEMM below
+ * multiplies the activations themselves: ~1e-6 normwise from the
+ * dequant-then-matmul result, at the MXFP8 MMA rate and with no weight
+ * expansion.  out_q holds 2 x m_pad_capacity x k bytes (plane hi, then lo);
+ * otherwise the arguments, layouts and errors of lmoe_mxfp8_quantize_rows /
+ * lmoe_mxfp8_quantize_scatter. */
+LMOE_API int lmoe_bf16split_quantize_rows(const void* x, int64_t x_rows, int x_f16,
+                                          const int32_t* token_idx, const int32_t* group_sizes,
+                                          int64_t num_groups, int64_t rows, int64_t k,
+                                          void* out_q, void* out_sf, int64_t m_pad_capacity,
+                                          int32_t* dev_status, void* stream);
+LMOE_API int lmoe_bf16split_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                             int64_t num_tokens, int64_t top_k, int64_t k,
+                                             const int32_t* group_sizes, int64_t num_groups,
+                                             void* out_q, void* out_sf, int64_t m_pad_capacity,
+                                             int32_t* dev_status, void* stream);
+/* The block-scaled gate/up + SiTU-GLU GEMM with its activations written
+ * quantised for the down GEMM (no bf16 activation tensor): input rows of
+ * act_kind 0 (MXFP8), 1 (MXFP4, k a multiple of 256) or 2 (split), weights
+ * prepared with interleave_gateup = 1 (n = 2 * inter); the SiTU output of
+ * each padded row (rounded to bf16) is quantised per 32 features to out_fmt 0
+ * (MXFP8), 1 (MXFP4, inter a multiple of 256) or 2 (split; out_q 2 x m_pad x
+ * inter bytes) with the scale rule of the matching quantise function, codes
+ * at the same padded rows of out_q, scale atoms (inter/128, m_pad/128, 512)
+ * to out_sf: the bytes that quantising the bf16 activations would give.
+ * inter a multiple of 128. */
+LMOE_API int lmoe_blockscaled_gateup_situ_quantized(const void* act_q, const void* act_sf,
+                                                    int act_kind, const void* w_packed,
+                                                    const void* w_sf, const int32_t* group_sizes,
+                                                    int64_t m_pad, int64_t k, int64_t inter,
+                                                    int64_t g, float beta, float linear_beta,
+                                                    int round_gate_up, int out_fmt, void* out_q,
+                                                    void* out_sf, int32_t* dev_status,
+                                                    void* stream);
+/* Grouped GEMM of split rows against prepared MXFP4 weights: arguments as
+ * lmoe_mxfp8_mxfp4_grouped_gemm, plus m_out: 0 writes the padded rows (out
+ * has m_pad rows); m_out > 0 writes row r of group g at its unpadded position
+ * (the sum of the earlier groups' sizes + r; out has m_out rows, those at or
+ * past sum(group_sizes) are zeroed) -- the ragged_dot output layout. */
+LMOE_API int lmoe_bf16split_mxfp4_grouped_gemm(const void* act_q, const void* act_sf,
+                                               const void* w_packed, const void* w_sf,
+                                               const int32_t* group_sizes, void* out,
+                                               int64_t m_pad, int64_t k, int64_t n_out, int64_t g,
+                                               int epi, float beta, float linear_beta,
+                                               int round_gate_up, int out_dtype, int64_t m_out,
+                                               int32_t* dev_status, void* stream);
 /* Grouped GEMM of padded MXFP4 rows against prepared MXFP4 weights; arguments
  * as lmoe_mxfp8_mxfp4_grouped_gemm, k a multiple of 256. */
 LMOE_API int lmoe_mxfp4_mxfp4_grouped_gemm(const void* act_q, const void* act_sf,

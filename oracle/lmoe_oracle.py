@@ -663,6 +663,35 @@ def pack_e2m1(values: np.ndarray) -> np.ndarray:
   return (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
 
 
+# The exact form on the same tensor core: each row split into two e4m3 planes
+# under the MXFP8 block scale 2^e -- hi = e4m3(x / 2^e), lo = e4m3(x / 2^e -
+# hi), both rounded to nearest even.  A bf16 value has 8 significant bits;
+# hi takes the top 4 (rounded), and the remainder is a multiple of the value's
+# bf16 spacing no larger than half hi's spacing, so it has at most 4
+# significant bits: e4m3 holds it exactly whenever it is not below e4m3's
+# subnormal step 2^-9, i.e. for |x| >= 2^(e-2).  hi + lo is then x itself, and
+# the GEMM on both planes is the exact product.
+
+
+def split_e4m3(x: np.ndarray, block: int = 32):
+  """(rows, K) float32 -> (hi values (rows, K), lo values (rows, K), E8M0
+  bytes (rows, K / block)) with x ~= (hi + lo) * 2^(byte - 127) blockwise."""
+  x = np.asarray(x, np.float32)
+  r, k = x.shape
+  xb = x.reshape(r, k // block, block)
+  e = mxfp8_scale_exponent(np.abs(xb).max(axis=2))
+  v = (xb * np.ldexp(np.float32(1.0), -e)[:, :, None].astype(np.float32)).astype(np.float32)
+  hi = e4m3_round(v)
+  lo = e4m3_round((v - hi).astype(np.float32))
+  return hi.reshape(r, k), lo.reshape(r, k), (e + 127).astype(np.uint8)
+
+
+def dequantize_split(hi: np.ndarray, lo: np.ndarray, sf: np.ndarray, block: int = 32):
+  """(hi + lo) * 2^(byte - 127) per block, in float32 (exact: hi + lo has at
+  most 8 significant bits)."""
+  return dequantize_mxfp8((hi + lo).astype(np.float32), sf, block)
+
+
 def mxfp8_mxfp4_ragged_dot(lhs_q, lhs_sf, weight_packed, weight_scale, group_sizes):
   """f32 result of the block-scaled grouped matmul: the dequantised MXFP8
   rows times the dequantised MXFP4 weights (every product is exact in f32;

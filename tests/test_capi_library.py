@@ -77,3 +77,11 @@ def test_mxf4_gemm_checks_k_before_any_launch():
   assert rc == _native.LMOE_BAD_SHAPE
   rc = lib.lmoe_mxfp4_quantize_rows(None, 0, 0, None, None, 1, 4, 200, None, None, 128, None, None)
   assert rc == _native.LMOE_BAD_SHAPE
+
+
+def test_split_gemm_checks_m_out_before_any_launch():
+  from tokamax_tpu_kernel_lab_b200 import _native
+  lib = _native.load()
+  rc = lib.lmoe_bf16split_mxfp4_grouped_gemm(None, None, None, None, None, None, 128, 256, 128, 1,
+                                             0, 0.0, 0.0, 0, 0, -1, None, None)
+  assert rc == _native.LMOE_BAD_SHAPE

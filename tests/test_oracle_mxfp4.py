@@ -139,3 +139,24 @@ def test_mxfp4_activation_error_is_the_e2m1_step():
   r4 = float(np.linalg.norm(e4 - x) / np.linalg.norm(x))
   r8 = float(np.linalg.norm(e8 - x) / np.linalg.norm(x))
   assert 0.08 < r4 < 0.16 and 0.015 < r8 < 0.04
+
+
+def test_split_e4m3_holds_the_bf16_value():
+  """Two e4m3 planes under the MXFP8 block scale 2^e (hi, and lo = the
+  rounding remainder) hold every bf16 value with |x| >= 2^(e-2) exactly and
+  the rest to within 2^(e-10): the exact product on the block-scaled MMA."""
+  rng = np.random.default_rng(15)
+  x = O.bf16_round((rng.standard_normal((128, 512)) *
+                    10.0 ** rng.uniform(-6, 6, (128, 1))).astype(np.float32))
+  x[0, :32] = 448.0
+  x[1, :31] = 1e-30
+  x[1, 31] = 1.0
+  hi, lo, sf = O.split_e4m3(x)
+  assert np.array_equal(O.e4m3_round(hi), hi) and np.array_equal(O.e4m3_round(lo), lo)
+  np.testing.assert_array_equal(sf, O.quantize_mxfp8(x)[1])
+  e = np.repeat(sf.astype(np.int32) - 127, 32, axis=1)
+  d = O.dequantize_split(hi, lo, sf)
+  big = np.abs(x) >= np.ldexp(1.0, e - 2)
+  assert big.mean() > 0.99
+  assert np.array_equal(d[big], x[big])
+  assert np.all(np.abs(d - x)[~big] <= np.ldexp(1.0, e - 10)[~big])

@@ -77,6 +77,15 @@ SIGNATURES = {
                                            _i64, _p, _p]),
     "lmoe_mxfp4_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i32,
                                              _f32, _f32, _i32, _i32, _p, _p]),
+    "lmoe_bf16split_quantize_rows": (_i32, [_p, _i64, _i32, _p, _p, _i64, _i64, _i64, _p, _p,
+                                            _i64, _p, _p]),
+    "lmoe_bf16split_quantize_scatter": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
+                                               _i64, _p, _p]),
+    "lmoe_bf16split_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
+                                                 _i32, _f32, _f32, _i32, _i32, _i64, _p, _p]),
+    "lmoe_blockscaled_gateup_situ_quantized": (_i32, [_p, _p, _i32, _p, _p, _p, _i64, _i64, _i64,
+                                                      _i64, _f32, _f32, _i32, _i32, _p, _p, _p,
+                                                      _p]),
     "lmoe_dispatch_static_scratch": (_i32, [_p, _p, _i64, _i64, _i64, _i64, _i64, _i32, _p, _p,
                                             _p, _p, _p, _p, _p, _p]),
     "lmoe_ep_buffer_bytes": (_i64, [_i64, _i64, _i64, _i64, _i64]),

@@ -67,7 +67,6 @@ namespace {
 constexpr int kMxRowBytes = 128;  // bytes of an operand row per stage (one 128-byte swizzle row)
 constexpr int kMxRows = 128;   // weight rows per tile (UMMA M)
 constexpr int kMxTok = 192;    // token rows per tile (UMMA N at most)
-constexpr int kMxStages = 4;
 constexpr int kMxAlign = 128;  // row alignment of every expert's activation rows
 constexpr int kMxMaxGroups = 1024;
 constexpr int kMxThreads = 32 * 7;
@@ -81,30 +80,43 @@ constexpr int kMxTokWarp = 6;
 //                256 codes, low nibble first); K 256 per stage = 4 MMAs of K 64
 //                at twice the rate of the former; two scale bytes per row per
 //                MMA (scale_vec::2X, selected by scale id 0 or 2)
-enum { KIND_F8F6F4 = 0, KIND_F4 = 1 };
+//   KIND_F8_SPLIT  kind::mxf8f6f4 as KIND_F8F6F4, with the token operand in two
+//                e4m3 planes that share the block scale: hi = e4m3(x / 2^e) and
+//                lo = e4m3(x / 2^e - hi).  hi + lo carries all 8 significant
+//                bits of a bf16 value (exactly, for |x| >= 2^-2 of the scale
+//                unit), so two MMAs into one accumulator give the product of
+//                the bf16 activations themselves: the exact MXFP4 matmul on the
+//                block-scaled tensor core, with no weight expansion
+enum { KIND_F8F6F4 = 0, KIND_F4 = 1, KIND_F8_SPLIT = 2 };
 
 template <int KIND>
 struct MxCfg {
   static constexpr int kBK = KIND == KIND_F4 ? 256 : 128;  // K elements per stage
   static constexpr int kQuads = kBK / 128;                   // scale atoms (4 K blocks) per row block
+  static constexpr int kPlanes = KIND == KIND_F8_SPLIT ? 2 : 1;  // token operand planes
+  static constexpr int kStages = KIND == KIND_F8_SPLIT ? 3 : 4;
   static constexpr int kABytes = kMxRows * kMxRowBytes;      // 16 KB in shared memory
   static constexpr int kATx = KIND == KIND_F4 ? kABytes : kABytes / 2;  // bytes moved
   static constexpr int kBoxRows = 64;
   static constexpr int kBoxBytes = kBoxRows * kMxRowBytes;  // 8 KB
-  static constexpr int kBBytes = 3 * kBoxBytes;             // up to 192 token rows
+  static constexpr int kBPlaneBytes = 3 * kBoxBytes;        // up to 192 token rows
+  static constexpr int kBBytes = kPlanes * kBPlaneBytes;
   static constexpr int kSfBytes = 512;
   static constexpr int kSfbAtoms = 2;                       // 192 rows from a 0- or 64-row offset
   static constexpr int kSfaOff = kABytes + kBBytes;         // kQuads weight-scale atoms
   static constexpr int kSfbOff = kSfaOff + kQuads * kSfBytes;  // kQuads x kSfbAtoms token-scale atoms
-  // 41.5 (KIND_F8F6F4) or 43 KB (KIND_F4) of operands, every stage 1024-byte aligned
+  // 41.5 (KIND_F8F6F4), 43 (KIND_F4) or 65.5 KB (KIND_F8_SPLIT) of operands, every
+  // stage 1024-byte aligned
   static constexpr int kStageBytes =
       (kSfbOff + kQuads * kSfbAtoms * kSfBytes + 1023) / 1024 * 1024;
   static constexpr int kWarpStage = 1024;
   static constexpr int kOutStageBytes = 4 * kWarpStage;
+  // the quantising SiTU epilogue's block maxima: 4 warps x 2 slots x 32 tokens
+  static constexpr int kXchgBytes = 4 * 2 * 32 * 4;
   static constexpr int kSchedBytes = 3 * (kMxMaxGroups + 1) * 4;
-  static constexpr int kNumBars = 2 * kMxStages + 5;
-  static constexpr size_t kSmem = 1024 + size_t(kMxStages) * kStageBytes + kOutStageBytes +
-                                  kSchedBytes + 16 + 8 * kNumBars + 16;
+  static constexpr int kNumBars = 2 * kStages + 7;
+  static constexpr size_t kSmem = 1024 + size_t(kStages) * kStageBytes + kOutStageBytes +
+                                  kXchgBytes + kSchedBytes + 16 + 8 * kNumBars + 16;
   static constexpr int kTmemCols = 512;  // accumulators at columns 0 and 256 (192 wide)
   static constexpr int kAccStride = 256;
   // scales in the gap after accumulator 0: 4 columns per atom, weight atoms
@@ -113,7 +125,7 @@ struct MxCfg {
   static constexpr int kSfbCol = kMxTok + 4 * kQuads;
   static_assert(kSfbCol + 4 * kSfbAtoms * kQuads <= kAccStride, "scale columns in the gap");
   static_assert(kStageBytes % 1024 == 0, "1024-byte aligned stages");
-  static_assert(kOutStageBytes >= 2 * kMxThreads * 4, "scan scratch");
+  static_assert(kOutStageBytes >= 3 * kMxThreads * 4, "scan scratch");
   static_assert(kSmem <= 232448, "shared memory");
 };
 
@@ -196,64 +208,239 @@ struct MxArgs {
   float beta, linear_beta, inv_beta, inv_linear_beta;
   int round_gate_up;
   int out_f16;
+  int m_out;  // 0: output rows at the padded positions; > 0: unpadded, m_out rows
+  // EPI_SITU only: with q_out set, the activations are written quantised for
+  // the next block-scaled GEMM instead of to `out` -- format q_fmt (MX_E4M3,
+  // MX_E2M1 or MX_E4M3_SPLIT) at the same padded rows, scale atoms to q_sf
+  uint8_t* q_out;
+  uint8_t* q_sf;
+  int q_fmt;
 };
 
 struct MxTile {
   int g, n_tile, row0, rows;
 };
 
-// Schedule: padded row starts (multiples of 128), true row counts, tile starts.
-__device__ int mx_schedule(const MxArgs& a, int32_t* row_off, int32_t* row_cnt,
-                           int32_t* tile_start, int32_t* scan_rows, int32_t* scan_tiles) {
+// ------------------------------------------------------------------ quantise
+// Element formats of the quantised activation rows: MX_E4M3 (one byte per
+// value, MXFP8), MX_E2M1 (two values per byte, low nibble first, MXFP4) or
+// MX_E4M3_SPLIT (two e4m3 planes under the MXFP8 scale: hi, and lo = the
+// rounding remainder of hi, so hi + lo carries the value's 8 significant bits).
+enum { MX_E4M3 = 0, MX_E2M1 = 1, MX_E4M3_SPLIT = 2 };
+
+// Exponent e of a block with absolute maximum `amax`: the smallest with
+// amax <= emax * 2^e, where emax is the format's largest finite value (e4m3:
+// 448 = 1.75 * 2^8; e2m1: 6 = 1.5 * 2^2), so no element saturates; E8M0 byte
+// e + 127, clamped to [0, 254]; 0 for an all-zero block.
+template <int FMT>
+__device__ __forceinline__ int mx_scale_exp(float amax) {
+  if (!(amax > 0.f)) return -127;
+  const uint32_t b = __float_as_uint(amax);
+  const int E = static_cast<int>((b >> 23) & 0xFF) - 127;
+  const int e = FMT == MX_E2M1 ? E - 2 + ((b & 0x7FFFFF) > 0x400000 ? 1 : 0)
+                               : E - 8 + ((b & 0x7FFFFF) > 0x600000 ? 1 : 0);  // e4m3, both planes
+  return max(-127, min(127, e));
+}
+
+// The quantising gathers give each 32-value block to two lanes: lane l holds
+// values [16 l, 16 l + 16) of each 512-value chunk of a row, so a warp's store
+// of one plane's codes covers 512 contiguous bytes (e4m3; 256 for e2m1), and
+// an 8-lane group holds one K group (4 blocks = one scale word).
+template <int FMT>
+struct MxHalf {
+  uint32_t hi[4];  // 16 e4m3 codes, or 16 e2m1 codes in hi[0..1]
+  uint32_t lo[4];  // MX_E4M3_SPLIT: the lo plane's 16 codes
+  uint32_t sfw;    // scale word of the lane's K group (every lane of the 8-lane group)
+};
+
+// 2^-e as a float for e in [-127, 127] (exact powers of two; 2^-127 is subnormal)
+__device__ __forceinline__ float mx_inv_scale(int e) {
+  const int x = -e;
+  return x >= -126 ? __uint_as_float(static_cast<uint32_t>(x + 127) << 23)
+                   : __uint_as_float(1u << (x + 149));
+}
+
+// 16 bf16 or f16 values (two uint4) as floats.
+template <bool F16>
+__device__ __forceinline__ void mx_unpack16(const uint4 (&raw)[2], float (&v)[16]) {
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint32_t ws[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f;
+      if (F16)
+        f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
+      else
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+      v[i * 2 + c * 8] = f.x;
+      v[i * 2 + c * 8 + 1] = f.y;
+    }
+  }
+}
+
+// The 16 values' codes under the block exponent e, rounded to nearest even:
+// e4m3 pairs, or e2m1 pairs (value 2i in the low nibble of byte i); for
+// MX_E4M3_SPLIT also the remainders x * inv - e4m3(x * inv) (exact in f32)
+// rounded to e4m3.
+template <int FMT>
+__device__ __forceinline__ void mx_encode16(const float (&v)[16], int e, MxHalf<FMT>& o) {
+  const float inv = mx_inv_scale(e);
+  if constexpr (FMT == MX_E2M1) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float* x = v + 8 * i;
+      asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+          "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+          "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+          : "=r"(o.hi[i])
+          : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv),
+            "f"(x[4] * inv), "f"(x[5] * inv), "f"(x[6] * inv), "f"(x[7] * inv));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float x0 = v[i * 4] * inv, x1 = v[i * 4 + 1] * inv;
+      const float x2 = v[i * 4 + 2] * inv, x3 = v[i * 4 + 3] * inv;
+      uint16_t p01, p23;
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p01) : "f"(x1), "f"(x0));
+      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(p23) : "f"(x3), "f"(x2));
+      o.hi[i] = static_cast<uint32_t>(p01) | (static_cast<uint32_t>(p23) << 16);
+      if constexpr (FMT == MX_E4M3_SPLIT) {
+        // the rounded pairs back to f32 (through f16, exact for e4m3)
+        uint32_t h01, h23;
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h01) : "h"(p01));
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h23) : "h"(p23));
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+        uint16_t l01, l23;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(l01) : "f"(x1 - f01.y), "f"(x0 - f01.x));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(l23) : "f"(x3 - f23.y), "f"(x2 - f23.x));
+        o.lo[i] = static_cast<uint32_t>(l01) | (static_cast<uint32_t>(l23) << 16);
+      }
+    }
+  }
+}
+
+// Quantise the lane's 16 values (raw: two uint4 of bf16 or f16; the partner
+// lane l ^ 1 holds the other half of the block).  All 32 lanes must call.
+template <bool F16, int FMT>
+__device__ __forceinline__ void mx_quantize_half(const uint4 (&raw)[2], int lane, MxHalf<FMT>& o) {
+  float v[16];
+  mx_unpack16<F16>(raw, v);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  const int e = mx_scale_exp<FMT>(amax);
+  mx_encode16<FMT>(v, e, o);
+  // the K group's 4 scale bytes (block (lane / 2) % 4 of the group)
+  uint32_t w = static_cast<uint32_t>(e + 127) << (8 * ((lane >> 1) & 3));
+  w |= __shfl_xor_sync(0xffffffffu, w, 2);
+  w |= __shfl_xor_sync(0xffffffffu, w, 4);
+  o.sfw = w;
+}
+
+// Store the lane's codes of value index vi (a multiple of 16) of padded row
+// dst: each plane's codes at its byte offset, the scale word by the first
+// lane of each 8-lane group.
+template <int FMT>
+__device__ __forceinline__ void mx_store_half(const MxHalf<FMT>& o, int lane, int vi, int64_t dst,
+                                              int K, int64_t m_pad_cap, uint8_t* q, uint8_t* sf) {
+  if constexpr (FMT == MX_E2M1) {
+    __stcs(reinterpret_cast<uint2*>(q + dst * (K / 2) + vi / 2), make_uint2(o.hi[0], o.hi[1]));
+  } else {
+    uint8_t* qd = q + dst * K + vi;
+    __stcs(reinterpret_cast<uint4*>(qd), make_uint4(o.hi[0], o.hi[1], o.hi[2], o.hi[3]));
+    if constexpr (FMT == MX_E4M3_SPLIT)  // the lo plane, m_pad_cap rows further
+      __stcs(reinterpret_cast<uint4*>(qd + m_pad_cap * K),
+             make_uint4(o.lo[0], o.lo[1], o.lo[2], o.lo[3]));
+  }
+  if ((lane & 7) == 0) {
+    // atom (K group, row block), bytes r0*16 + r1*4 for row r0 + 32*r1
+    const int rr = static_cast<int>(dst % 128);
+    const int64_t atom = static_cast<int64_t>(vi / 128) * (m_pad_cap / 128) + dst / 128;
+    *reinterpret_cast<uint32_t*>(sf + atom * 512 + (rr & 31) * 16 + (rr >> 5) * 4) = o.sfw;
+  }
+}
+
+// One scale byte (block exponent e) of padded row r, K block blk, in the atom
+// layout of a tensor with m_pad_cap padded rows.
+__device__ __forceinline__ void mx_store_scale_byte(uint8_t* sf, int64_t r, int blk, int e,
+                                                    int64_t m_pad_cap) {
+  const int rr = static_cast<int>(r % 128);
+  const int64_t atom = static_cast<int64_t>(blk / 4) * (m_pad_cap / 128) + r / 128;
+  sf[atom * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (blk & 3)] = static_cast<uint8_t>(e + 127);
+}
+
+// Schedule: padded row starts (multiples of 128), unpadded row starts (the
+// exclusive prefix sums of the group sizes, row_src[G] = their sum), tile
+// starts.  `scan` holds 3 x blockDim.x ints of scratch.
+__device__ int mx_schedule(const MxArgs& a, int32_t* row_off, int32_t* row_src,
+                           int32_t* tile_start, int32_t* scan) {
   const int G = a.G;
   const int nthr = blockDim.x;
+  int32_t* scan_rows = scan;
+  int32_t* scan_src = scan + nthr;
+  int32_t* scan_tiles = scan + 2 * nthr;
   const int per = (G + nthr - 1) / nthr;
   const int g0 = min(G, static_cast<int>(threadIdx.x) * per);
   const int g1 = min(G, g0 + per);
-  long long rows = 0, tiles = 0;
+  long long rows = 0, src = 0, tiles = 0;
   int bad = 0;
   for (int g = g0; g < g1; ++g) {
     const int s = __ldg(a.group_sizes + g);
     if (s < 0) bad = 1;
     const int ss = max(s, 0);
     rows += (ss + kMxAlign - 1) / kMxAlign * kMxAlign;
+    src += ss;
     tiles += static_cast<long long>((ss + kMxTok - 1) / kMxTok) * a.n_tiles;
   }
   scan_rows[threadIdx.x] = bad ? -1 : static_cast<int32_t>(min(rows, (long long)INT32_MAX));
+  scan_src[threadIdx.x] = static_cast<int32_t>(min(src, (long long)INT32_MAX));
   scan_tiles[threadIdx.x] = static_cast<int32_t>(min(tiles, (long long)INT32_MAX));
   __syncthreads();
   __shared__ int s_total;
   if (threadIdx.x == 0) {
-    long long r = 0, t = 0;
+    long long r = 0, u = 0, t = 0;
     int invalid = 0;
     for (int i = 0; i < nthr; ++i) {
       const int rr = scan_rows[i];
+      const int uu = scan_src[i];
       const int tt = scan_tiles[i];
       if (rr < 0) invalid = 1;
       scan_rows[i] = static_cast<int32_t>(r);
+      scan_src[i] = static_cast<int32_t>(u);
       scan_tiles[i] = static_cast<int32_t>(t);
       r += max(rr, 0);
+      u += uu;
       t += tt;
     }
-    if (invalid || r > a.M_pad || t > INT32_MAX) {
+    if (invalid || r > a.M_pad || t > INT32_MAX || (a.m_out > 0 && u > a.m_out)) {
       record_status(a.status, kDeviceBounds);
       s_total = -1;
     } else {
       s_total = static_cast<int>(t);
       row_off[G] = static_cast<int32_t>(r);
+      row_src[G] = static_cast<int32_t>(u);
       tile_start[G] = static_cast<int32_t>(t);
     }
   }
   __syncthreads();
   if (s_total >= 0) {
     int r = scan_rows[threadIdx.x];
+    int u = scan_src[threadIdx.x];
     int t = scan_tiles[threadIdx.x];
     for (int g = g0; g < g1; ++g) {
-      const int s = __ldg(a.group_sizes + g);
+      const int s = max(__ldg(a.group_sizes + g), 0);
       row_off[g] = r;
-      row_cnt[g] = s;
+      row_src[g] = u;
       tile_start[g] = t;
       r += (s + kMxAlign - 1) / kMxAlign * kMxAlign;
+      u += s;
       t += ((s + kMxTok - 1) / kMxTok) * a.n_tiles;
     }
   }
@@ -262,14 +449,14 @@ __device__ int mx_schedule(const MxArgs& a, int32_t* row_off, int32_t* row_cnt,
 }
 
 __device__ __forceinline__ MxTile mx_tile(const int32_t* tile_start, const int32_t* row_off,
-                                          const int32_t* row_cnt, int G, int n_tiles, int t) {
+                                          const int32_t* row_src, int G, int n_tiles, int t) {
   MxTile c;
   c.g = find_group(tile_start, G, t);
   const int local = t - tile_start[c.g];
   const int m_tile = local / n_tiles;
   c.n_tile = local - m_tile * n_tiles;
   c.row0 = row_off[c.g] + m_tile * kMxTok;
-  c.rows = min(kMxTok, row_cnt[c.g] - m_tile * kMxTok);
+  c.rows = min(kMxTok, row_src[c.g + 1] - row_src[c.g] - m_tile * kMxTok);
   return c;
 }
 
@@ -295,18 +482,20 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_align_up<1024>(smem_raw);
   uint8_t* stages = smem;
-  uint8_t* ostage = stages + kMxStages * C::kStageBytes;
-  int32_t* row_off = reinterpret_cast<int32_t*>(ostage + C::kOutStageBytes);
-  int32_t* row_cnt = row_off + (kMxMaxGroups + 1);
-  int32_t* tile_start = row_cnt + (kMxMaxGroups + 1);
+  uint8_t* ostage = stages + C::kStages * C::kStageBytes;
+  const uint32_t xchg = smem_u32(ostage + C::kOutStageBytes);
+  int32_t* row_off = reinterpret_cast<int32_t*>(ostage + C::kOutStageBytes + C::kXchgBytes);
+  int32_t* row_src = row_off + (kMxMaxGroups + 1);
+  int32_t* tile_start = row_src + (kMxMaxGroups + 1);
   // mbarriers need 8-byte alignment (three schedule arrays of 1025 ints end at 4 mod 8)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_align_up<16>(tile_start + (kMxMaxGroups + 1)));
   uint64_t* full = bars;
-  uint64_t* empty = full + kMxStages;
-  uint64_t* acc_full = empty + kMxStages;
+  uint64_t* empty = full + C::kStages;
+  uint64_t* acc_full = empty + C::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* xbar = drain + 1;  // epilogue warps 2 and 3 (4 and 5) exchange block maxima
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -314,11 +503,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   const int G = args.G;
   if (threadIdx.x == 0) *abort_flag = 0;
   int32_t* scan = reinterpret_cast<int32_t*>(ostage);
-  const int total = mx_schedule(args, row_off, row_cnt, tile_start, scan, scan + kMxThreads);
+  const int total = mx_schedule(args, row_off, row_src, tile_start, scan);
   if (total < 0) return;  // uniform across the CTA; nothing allocated yet
 
   if (warp == 0 && lane == 0) {
-    for (int s = 0; s < kMxStages; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(full + s), 2);  // the weight and the token producer
       mbar_init(smem_u32(empty + s), 1);
     }
@@ -327,6 +516,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       mbar_init(smem_u32(acc_empty + b), 128);
     }
     mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(xbar), 2);
+    mbar_init(smem_u32(xbar + 1), 2);
     fence_mbarrier_init();
     tma_prefetch_desc(&tmW);
     tma_prefetch_desc(&tmT);
@@ -352,7 +543,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       bool ok = true;
       const int64_t row_blocks = args.M_pad / kMxAlign;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+        const MxTile tc = mx_tile(tile_start, row_off, row_src, G, args.n_tiles, t);
         const int n_box = (tc.rows + C::kBoxRows - 1) / C::kBoxRows;
         const uint8_t* wsf = args.w_sf + tc.g * w_sf_per_g +
                              static_cast<int64_t>(tc.n_tile) * num_kq * C::kSfBytes;
@@ -379,11 +570,23 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const uint32_t b_dst = base + C::kABytes;
             if (tc.rows == kMxTok) {
               mbar_arrive_expect_tx(fb, C::kBBytes + C::kQuads * n_atoms * C::kSfBytes);
-              tma_load_2d(b_dst, &tmT, fb, x0, tc.row0);
+              for (int p = 0; p < C::kPlanes; ++p) {
+                if (C::kPlanes > 1)
+                  tma_load_3d(b_dst + p * C::kBPlaneBytes, &tmT, fb, x0, tc.row0, p);
+                else
+                  tma_load_2d(b_dst, &tmT, fb, x0, tc.row0);
+              }
             } else {
-              mbar_arrive_expect_tx(fb, n_box * C::kBoxBytes + C::kQuads * n_atoms * C::kSfBytes);
-              for (int i = 0; i < n_box; ++i)
-                tma_load_2d(b_dst + i * C::kBoxBytes, &tmT64, fb, x0, tc.row0 + i * C::kBoxRows);
+              mbar_arrive_expect_tx(fb, C::kPlanes * n_box * C::kBoxBytes +
+                                            C::kQuads * n_atoms * C::kSfBytes);
+              for (int p = 0; p < C::kPlanes; ++p)
+                for (int i = 0; i < n_box; ++i) {
+                  const uint32_t dst = b_dst + p * C::kBPlaneBytes + i * C::kBoxBytes;
+                  if (C::kPlanes > 1)
+                    tma_load_3d(dst, &tmT64, fb, x0, tc.row0 + i * C::kBoxRows, p);
+                  else
+                    tma_load_2d(dst, &tmT64, fb, x0, tc.row0 + i * C::kBoxRows);
+                }
             }
             // per quad, the tile's token-scale atoms are consecutive
             for (int q = 0; q < C::kQuads; ++q)
@@ -394,14 +597,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           }
           issued |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kMxStages) {
+          if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
       if (!ok) {
-        for (uint32_t s = 0; s < kMxStages; ++s)
+        for (uint32_t s = 0; s < C::kStages; ++s)
           if (issued & (1u << s)) mbar_drain(smem_u32(full + s), (last_parity >> s) & 1u);
       }
     }
@@ -413,7 +616,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       const uint32_t sfa_t = tmem_base + C::kSfaCol;
       const uint32_t sfb_t = tmem_base + C::kSfbCol;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+        const MxTile tc = mx_tile(tile_start, row_off, row_src, G, args.n_tiles, t);
         const uint32_t n_mma = (tc.rows + 15) & ~15;
         const uint32_t idesc = idesc_mx<KIND>(kMxRows, n_mma);
         const int n_atoms = ((tc.row0 % kMxAlign) + tc.rows + kMxAlign - 1) / kMxAlign;
@@ -443,20 +646,26 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                          sf_desc(base + C::kSfbOff + (q * C::kSfbAtoms + i) * C::kSfBytes));
           }
           // 4 MMAs of 32 bytes of each operand row: K 32 (one scale byte,
-          // id k) or K 64 (two scale bytes of quad k/2, id 0 or 2)
+          // id k) or K 64 (two scale bytes of quad k/2, id 0 or 2); with two
+          // token planes, one MMA per plane into the same accumulator
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t adesc = smem_desc_sw128(base + k * 32, 16, 1024);
-            const uint64_t bdesc = smem_desc_sw128(base + C::kABytes + k * 32, 16, 1024);
             const uint32_t q = KIND == KIND_F4 ? static_cast<uint32_t>(k >> 1) : 0u;
             const uint32_t id = KIND == KIND_F4 ? static_cast<uint32_t>((k & 1) << 1)
                                                 : static_cast<uint32_t>(k);
-            umma_mx<KIND>(d_tmem, adesc, bdesc, idesc | (id << 29) | (id << 4),
-                          (sfa_t + 4 * q) | (id << 30),
-                          (sfb_mma + 4 * C::kSfbAtoms * q) | (id << 30), (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int p = 0; p < C::kPlanes; ++p) {
+              const uint64_t bdesc =
+                  smem_desc_sw128(base + C::kABytes + p * C::kBPlaneBytes + k * 32, 16, 1024);
+              umma_mx<KIND>(d_tmem, adesc, bdesc, idesc | (id << 29) | (id << 4),
+                            (sfa_t + 4 * q) | (id << 30),
+                            (sfb_mma + 4 * C::kSfbAtoms * q) | (id << 30),
+                            (kb | k | p) != 0 ? 1u : 0u);
+            }
           }
           umma_commit(smem_u32(empty + stage));
-          if (++stage == kMxStages) {
+          if (++stage == C::kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -477,11 +686,15 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const uint32_t stg = smem_u32(ostage + q * C::kWarpStage);
     constexpr int esize = (EPI == EPI_F32) ? 4 : 2;
     uint32_t acc = 0, acc_phase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const MxTile tc = mx_tile(tile_start, row_off, row_cnt, G, args.n_tiles, t);
+    uint32_t xcount = 0;  // block-maximum exchanges so far (the pair barrier's phases)
+    bool xok = true;
+    for (int t = blockIdx.x; t < total && xok; t += gridDim.x) {
+      const MxTile tc = mx_tile(tile_start, row_off, row_src, G, args.n_tiles, t);
       if (!mbar_wait(smem_u32(acc_full + acc), acc_phase, abort_flag, args.status)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::kAccStride;
+      // padded row -> output row (the unpadded position when m_out > 0)
+      const int64_t out_shift = args.m_out > 0 ? row_src[tc.g] - row_off[tc.g] : 0;
 #pragma unroll 1
       for (int c = 0; c < kMxTok / 32; ++c) {
         if (c * 32 >= tc.rows) break;  // warp-uniform
@@ -510,9 +723,55 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           __syncwarp();
           const int tok = tok0 + lane;
           const int f0 = tc.n_tile * (kMxRows / 2) + q * 16;
-          if (tok < tok_end) {
-            uint16_t* orow =
-                reinterpret_cast<uint16_t*>(args.out) + static_cast<int64_t>(tok) * args.ldo + f0;
+          if (args.q_out != nullptr) {
+            // quantised activations: lane = token, its 16 features (bf16
+            // values); their 32-feature block spans this warp and warp q ^ 1,
+            // which meet through shared memory and a pair barrier
+            const uint4 raw[2] = {lds_v4(stg + lane * 32), lds_v4(stg + lane * 32 + 16)};
+            float fv[16];
+            mx_unpack16<false>(raw, fv);
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(fv[i]));
+            const uint32_t slot = xcount & 1u;
+            sts_u32(xchg + ((q * 2 + slot) * 32 + lane) * 4, __float_as_uint(amax));
+            __syncwarp();
+            const uint32_t xb = smem_u32(xbar + (q >> 1));
+            if (lane == 0) mbar_arrive(xb);
+            if (!mbar_wait(xb, slot, abort_flag, args.status)) {
+              xok = false;
+              break;
+            }
+            amax = fmaxf(amax, lds_f32(xchg + (((q ^ 1) * 2 + slot) * 32 + lane) * 4));
+            ++xcount;
+            if (tok < tok_end) {
+              const int64_t plane = static_cast<int64_t>(args.M_pad) * args.N;
+              if (args.q_fmt == MX_E2M1) {
+                const int e = mx_scale_exp<MX_E2M1>(amax);
+                MxHalf<MX_E2M1> o;
+                mx_encode16<MX_E2M1>(fv, e, o);
+                *reinterpret_cast<uint2*>(args.q_out + static_cast<int64_t>(tok) * (args.N / 2) +
+                                          f0 / 2) = make_uint2(o.hi[0], o.hi[1]);
+                if ((q & 1) == 0) mx_store_scale_byte(args.q_sf, tok, tc.n_tile * 2 + (q >> 1), e, args.M_pad);
+              } else {
+                const int e = mx_scale_exp<MX_E4M3>(amax);
+                uint8_t* qd = args.q_out + static_cast<int64_t>(tok) * args.N + f0;
+                if (args.q_fmt == MX_E4M3_SPLIT) {
+                  MxHalf<MX_E4M3_SPLIT> o;
+                  mx_encode16<MX_E4M3_SPLIT>(fv, e, o);
+                  *reinterpret_cast<uint4*>(qd) = make_uint4(o.hi[0], o.hi[1], o.hi[2], o.hi[3]);
+                  *reinterpret_cast<uint4*>(qd + plane) = make_uint4(o.lo[0], o.lo[1], o.lo[2], o.lo[3]);
+                } else {
+                  MxHalf<MX_E4M3> o;
+                  mx_encode16<MX_E4M3>(fv, e, o);
+                  *reinterpret_cast<uint4*>(qd) = make_uint4(o.hi[0], o.hi[1], o.hi[2], o.hi[3]);
+                }
+                if ((q & 1) == 0) mx_store_scale_byte(args.q_sf, tok, tc.n_tile * 2 + (q >> 1), e, args.M_pad);
+              }
+            }
+          } else if (tok < tok_end) {
+            uint16_t* orow = reinterpret_cast<uint16_t*>(args.out) +
+                             (tok + out_shift) * args.ldo + f0;
             if (f0 + 8 <= args.N) *reinterpret_cast<uint4*>(orow) = lds_v4(stg + lane * 32);
             if (f0 + 16 <= args.N) *reinterpret_cast<uint4*>(orow + 8) = lds_v4(stg + lane * 32 + 16);
           }
@@ -538,7 +797,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const int tok = tok0 + p0 + lane;
             if (lane < kRows && tok < tok_end) {
               uint8_t* orow = reinterpret_cast<uint8_t*>(args.out) +
-                              (static_cast<int64_t>(tok) * args.ldo + f0) * esize;
+                              ((tok + out_shift) * args.ldo + f0) * esize;
 #pragma unroll
               for (int cc = 0; cc < kChunks; ++cc) {
                 if (f0 + (cc + 1) * (16 / esize) <= args.N)
@@ -550,10 +809,27 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           }
         }
       }
+      if (!xok) break;
       tc_fence_before();
       mbar_arrive(smem_u32(acc_empty + acc));
       acc ^= 1u;
       if (acc == 0) acc_phase ^= 1u;
+    }
+    // unpadded output: rows at or past sum(group_sizes) are zero (ragged_dot
+    // semantics), written by the epilogue warps of all CTAs
+    if (args.m_out > 0) {
+      const int64_t row_bytes = static_cast<int64_t>(args.N) * esize;
+      const int64_t chunks_per_row = row_bytes / 16;
+      const int64_t first = row_src[G];
+      const int64_t n_chunks = (args.m_out - first) * chunks_per_row;
+      const int etid = threadIdx.x - 64;  // epilogue warps 2-5
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * 128 + etid; i < n_chunks;
+           i += static_cast<int64_t>(gridDim.x) * 128) {
+        const int64_t rr = first + i / chunks_per_row;
+        const int64_t cc = i % chunks_per_row;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(args.out) +
+                                  (rr * args.ldo) * esize + cc * 16) = make_uint4(0, 0, 0, 0);
+      }
     }
   }
 
@@ -634,70 +910,6 @@ __global__ void mx_repack_rows_kernel(const uint8_t* __restrict__ packed, int G,
   }
 }
 
-// ------------------------------------------------------------------ quantise
-// Element formats of the quantised activation rows: MX_E4M3 (one byte per
-// value, MXFP8) or MX_E2M1 (two values per byte, low nibble first, MXFP4).
-enum { MX_E4M3 = 0, MX_E2M1 = 1 };
-
-// Exponent e of a block with absolute maximum `amax`: the smallest with
-// amax <= emax * 2^e, where emax is the format's largest finite value (e4m3:
-// 448 = 1.75 * 2^8; e2m1: 6 = 1.5 * 2^2), so no element saturates; E8M0 byte
-// e + 127, clamped to [0, 254]; 0 for an all-zero block.
-template <int FMT>
-__device__ __forceinline__ int mx_scale_exp(float amax) {
-  if (!(amax > 0.f)) return -127;
-  const uint32_t b = __float_as_uint(amax);
-  const int E = static_cast<int>((b >> 23) & 0xFF) - 127;
-  const int e = FMT == MX_E2M1 ? E - 2 + ((b & 0x7FFFFF) > 0x400000 ? 1 : 0)
-                               : E - 8 + ((b & 0x7FFFFF) > 0x600000 ? 1 : 0);
-  return max(-127, min(127, e));
-}
-
-// Bytes of one 32-value block in the quantised row
-template <int FMT>
-constexpr int mx_block_bytes() {
-  return FMT == MX_E2M1 ? 16 : 32;
-}
-
-// A block of 32 values times `inv` (the inverse block scale) rounded to
-// nearest even: e4m3 into w[0..7], or e2m1 pairs into w[0..3] (value 2i in
-// the low nibble of byte i).
-template <int FMT>
-__device__ __forceinline__ void mx_encode_block(const float (&v)[32], float inv, uint32_t (&w)[8]) {
-  if constexpr (FMT == MX_E2M1) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float* x = v + 8 * i;
-      asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-          "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
-          "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
-          "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
-          "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
-          "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
-          : "=r"(w[i])
-          : "f"(x[0] * inv), "f"(x[1] * inv), "f"(x[2] * inv), "f"(x[3] * inv),
-            "f"(x[4] * inv), "f"(x[5] * inv), "f"(x[6] * inv), "f"(x[7] * inv));
-    }
-#pragma unroll
-    for (int i = 4; i < 8; ++i) w[i] = 0;
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint16_t lo, hi;
-      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(v[i * 4 + 1] * inv), "f"(v[i * 4] * inv));
-      asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(v[i * 4 + 3] * inv), "f"(v[i * 4 + 2] * inv));
-      w[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
-    }
-  }
-}
-
-// 2^-e as a float for e in [-127, 127] (exact powers of two; 2^-127 is subnormal)
-__device__ __forceinline__ float mx_inv_scale(int e) {
-  const int x = -e;
-  return x >= -126 ? __uint_as_float(static_cast<uint32_t>(x + 127) << 23)
-                   : __uint_as_float(1u << (x + 149));
-}
-
 // Padded start of every group (multiples of 128) from the group sizes, in
 // shared memory: pad_off[g] = padded_start[g] - start[g]; start[g] also kept.
 // start[g] = sum of the counts before group g, pad_off[g] = (the same sum of
@@ -758,10 +970,12 @@ __device__ __forceinline__ int mx_group_of(const int32_t* start, int G, int p) {
   return lo;
 }
 
-// One warp per row: gather (optional), quantise to MXFP8 or MXFP4 (FMT),
-// store the row at its padded position and its scales in the atom layout.
+// One warp per row: gather (optional), quantise (FMT), store the row at its
+// padded position and its scales in the atom layout.  The row is read 1024
+// values (two chunks per lane) at a time; K is a multiple of 128, so an 8-lane
+// group is inside the row or past it as a whole.
 template <bool F16, int FMT>
-__global__ void __launch_bounds__(256) mx_quantize_kernel(
+__global__ void __launch_bounds__(256, 4) mx_quantize_kernel(
     const uint16_t* __restrict__ x, int64_t x_rows, const int32_t* __restrict__ token_idx,
     const int32_t* __restrict__ gs, int G, int64_t rows, int K, int64_t m_pad_cap,
     uint8_t* __restrict__ q, uint8_t* __restrict__ sf, int32_t* status) {
@@ -770,7 +984,6 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
   int32_t* pad_off = sh + G + 1;
   if (gs != nullptr) mx_group_offsets(gs, G, start, pad_off);
   const int lane = threadIdx.x & 31;
-  const int nblk = K / 32;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   for (int64_t p = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; p < rows;
        p += nwarps) {
@@ -786,68 +999,36 @@ __global__ void __launch_bounds__(256) mx_quantize_kernel(
     const int64_t src_row = token_idx != nullptr ? token_idx[p] : p;
     const bool zero = src_row < 0 || src_row >= x_rows;
     const uint4* src = reinterpret_cast<const uint4*>(x + (zero ? 0 : src_row) * K);
-    uint8_t* qrow = q + dst * (nblk * mx_block_bytes<FMT>());
-    // the lane's blocks two at a time, the second block's loads issued with
-    // the first's (nblk is a multiple of 4)
-    for (int b0 = lane; b0 < nblk; b0 += 64) {
-      uint4 raw[2][4];
+    for (int c0 = 0; c0 < K; c0 += 1024) {
+      uint4 raw[2][2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int i = 0; i < 2; ++i) {
+        const int vi = c0 + 512 * i + 16 * lane;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          raw[u][c] = (zero || b0 + 32 * u >= nblk) ? make_uint4(0, 0, 0, 0)
-                                                     : __ldg(src + (b0 + 32 * u) * 4 + c);
+        for (int c = 0; c < 2; ++c)
+          raw[i][c] = (zero || vi >= K) ? make_uint4(0, 0, 0, 0) : __ldg(src + vi / 8 + c);
+      }
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int b = b0 + 32 * u;
-        if (b >= nblk) break;
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 w = raw[u][c];
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float2 f;
-            if (F16)
-              f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
-            else
-              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
-            v[c * 8 + i * 2] = f.x;
-            v[c * 8 + i * 2 + 1] = f.y;
-          }
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const int e = mx_scale_exp<FMT>(amax);
-        const float inv = mx_inv_scale(e);
-        uint32_t packed[8];
-        mx_encode_block<FMT>(v, inv, packed);
-        // evict-first stores: the source rows are re-read k times across the
-        // whole output and must stay in L2
-        uint4* qd = reinterpret_cast<uint4*>(qrow + b * mx_block_bytes<FMT>());
-        __stcs(qd, make_uint4(packed[0], packed[1], packed[2], packed[3]));
-        if (FMT == MX_E4M3) __stcs(qd + 1, make_uint4(packed[4], packed[5], packed[6], packed[7]));
-        // atom (K group, row block), byte r0*16 + r1*4 + kb
-        const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
-        const int r = static_cast<int>(dst % 128);
-        sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = static_cast<uint8_t>(e + 127);
+      for (int i = 0; i < 2; ++i) {
+        const int vi = c0 + 512 * i + 16 * lane;
+        MxHalf<FMT> o;
+        mx_quantize_half<F16, FMT>(raw[i], lane, o);
+        if (vi < K) mx_store_half<FMT>(o, lane, vi, dst, K, m_pad_cap, q, sf);
       }
     }
   }
 }
 
-// positions[i] -> padded positions (the combine's slot positions)
 // The quantising gather in token order: warp w takes token t = w, quantises
-// its row once (lane l: blocks l and l + 32 of 32 values, K <= 2048 per pass)
-// and stores the codes and scale bytes at the padded position of each of its
-// k sorted positions slot_pos[t*k + s] -- the rows quantize_mxfp8 writes for
-// a dropless dispatch, each source row read and quantised once instead of k
-// times.  Positions past sum(group_sizes) or outside the capacity are
-// skipped (the latter records LMOE_DEVICE_BOUNDS).
+// its row once and stores the codes and scale words at the padded position of
+// each of its k sorted positions slot_pos[t*k + s] -- the rows
+// mx_quantize_kernel writes for a dropless dispatch, each source row read and
+// quantised once instead of k times.  The row is taken 1024 values at a time
+// (the codes of both chunks kept in registers across the k stores).
+// Positions past sum(group_sizes) or outside the capacity are skipped (the
+// latter records LMOE_DEVICE_BOUNDS).
 template <bool F16, int FMT>
-__global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
+__global__ void __launch_bounds__(256, 4) mx_quantize_scatter_kernel(
     const uint16_t* __restrict__ x, const int32_t* __restrict__ slot_pos, int64_t T, int k,
     const int32_t* __restrict__ gs, int G, int K, int64_t m_pad_cap, uint8_t* __restrict__ q,
     uint8_t* __restrict__ sf, int32_t* status) {
@@ -856,7 +1037,6 @@ __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
   int32_t* pad_off = sh + G + 1;
   mx_group_offsets(gs, G, start, pad_off);
   const int lane = threadIdx.x & 31;
-  const int nblk = K / 32;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   bool bad = false;
   for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < T;
@@ -874,58 +1054,25 @@ __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
       }
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + t * K);
-    for (int b0 = lane; b0 < nblk; b0 += 64) {
-      uint4 raw[2][4];
+    for (int c0 = 0; c0 < K; c0 += 1024) {
+      uint4 raw[2][2];
 #pragma unroll
-      for (int u = 0; u < 2; ++u)
+      for (int i = 0; i < 2; ++i) {
+        const int vi = c0 + 512 * i + 16 * lane;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          raw[u][c] = b0 + 32 * u < nblk ? __ldg(src + (b0 + 32 * u) * 4 + c) : make_uint4(0, 0, 0, 0);
-      uint4 codes[2][2];
-      uint8_t ebyte[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t ws[4] = {raw[u][c].x, raw[u][c].y, raw[u][c].z, raw[u][c].w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float2 f;
-            if (F16)
-              f = __half22float2(*reinterpret_cast<const __half2*>(&ws[i]));
-            else
-              f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
-            v[c * 8 + i * 2] = f.x;
-            v[c * 8 + i * 2 + 1] = f.y;
-          }
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-        const int e = mx_scale_exp<FMT>(amax);
-        const float inv = mx_inv_scale(e);
-        uint32_t packed[8];
-        mx_encode_block<FMT>(v, inv, packed);
-        codes[u][0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        codes[u][1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-        ebyte[u] = static_cast<uint8_t>(e + 127);
+        for (int c = 0; c < 2; ++c)
+          raw[i][c] = vi < K ? __ldg(src + vi / 8 + c) : make_uint4(0, 0, 0, 0);
       }
+      MxHalf<FMT> o[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) mx_quantize_half<F16, FMT>(raw[i], lane, o[i]);
       for (int s = 0; s < k; ++s) {
         const int64_t dst = __shfl_sync(0xffffffffu, my_dst, s);
         if (dst < 0) continue;
-        uint8_t* qrow = q + dst * (nblk * mx_block_bytes<FMT>());
-        const int r = static_cast<int>(dst % 128);
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int b = b0 + 32 * u;
-          if (b >= nblk) break;
-          uint4* qd = reinterpret_cast<uint4*>(qrow + b * mx_block_bytes<FMT>());
-          __stcs(qd, codes[u][0]);
-          if (FMT == MX_E4M3) __stcs(qd + 1, codes[u][1]);
-          // atom (K group, row block), byte r0*16 + r1*4 + kb
-          const int64_t atom = static_cast<int64_t>(b / 4) * (m_pad_cap / 128) + dst / 128;
-          sf[atom * 512 + (r & 31) * 16 + (r >> 5) * 4 + (b & 3)] = ebyte[u];
+        for (int i = 0; i < 2; ++i) {
+          const int vi = c0 + 512 * i + 16 * lane;
+          if (vi < K) mx_store_half<FMT>(o[i], lane, vi, dst, K, m_pad_cap, q, sf);
         }
       }
     }
@@ -933,6 +1080,7 @@ __global__ void __launch_bounds__(256) mx_quantize_scatter_kernel(
   if (lane == 0 && __any_sync(0xffffffffu, bad)) record_status(status, kDeviceBounds);
 }
 
+// positions[i] -> padded positions (the combine's slot positions)
 __global__ void mx_pad_positions_kernel(const int32_t* __restrict__ pos, int64_t n,
                                         const int32_t* __restrict__ gs, int G,
                                         int32_t* __restrict__ out) {
@@ -1013,7 +1161,8 @@ template <int KIND>
 int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed, const void* w_sf,
                     const int32_t* group_sizes, void* out, int64_t m_pad, int64_t k, int64_t n_out,
                     int64_t g, int epi, float beta, float linear_beta, int round_gate_up,
-                    int out_dtype, int32_t* dev_status, void* stream) {
+                    int out_dtype, int64_t m_out, int32_t* dev_status, void* stream,
+                    void* q_out = nullptr, void* q_sf = nullptr, int q_fmt = MX_E4M3) {
   // epi: 0 plain (out_dtype 0 bf16, 1 f32, 2 f16), 3 SiTU-GLU over interleaved
   // gate/up rows (n_out = intermediate; out_dtype 0 bf16, 2 f16)
   using C = MxCfg<KIND>;
@@ -1028,9 +1177,23 @@ int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
       ((reinterpret_cast<uintptr_t>(act_q) | reinterpret_cast<uintptr_t>(out) |
         reinterpret_cast<uintptr_t>(act_sf) | reinterpret_cast<uintptr_t>(w_sf)) & 15))
     return LMOE_UNSUPPORTED;
+  if (m_out < 0 || m_out >= (1ll << 31)) return LMOE_BAD_SHAPE;
+  if (q_out != nullptr) {
+    // quantised SiTU output: padded rows, bf16 values, the next GEMM's K
+    // (the intermediate size) a multiple of 128 (of 256 for e2m1)
+    if (epi != EPI_SITU || m_out != 0 || out_dtype != 0 || q_sf == nullptr) return LMOE_BAD_SHAPE;
+    if (q_fmt != MX_E4M3 && q_fmt != MX_E2M1 && q_fmt != MX_E4M3_SPLIT) return LMOE_BAD_SHAPE;
+    if (n_out % (q_fmt == MX_E2M1 ? 256 : 128)) return LMOE_BAD_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(q_out) | reinterpret_cast<uintptr_t>(q_sf)) & 15)
+      return LMOE_UNSUPPORTED;
+  }
   if (m_pad == 0) return LMOE_OK;
   if (m_pad >= (1ll << 31) || k >= (1 << 20)) return LMOE_BAD_SHAPE;
   MxArgs a{};
+  a.m_out = static_cast<int>(m_out);
+  a.q_out = static_cast<uint8_t*>(q_out);
+  a.q_sf = static_cast<uint8_t*>(q_sf);
+  a.q_fmt = q_fmt;
   a.group_sizes = group_sizes;
   a.status = dev_status;
   a.out = out;
@@ -1064,12 +1227,21 @@ int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
                                           static_cast<uint64_t>(g))) {
     return LMOE_LAUNCH_FAILED;
   }
-  // token rows: one box of a full tile, or boxes of 64 rows for a partial one
-  if (!encode_tmap_u8_2d_sw128(&tt, act_q, act_pitch, static_cast<uint64_t>(m_pad), act_pitch,
-                               kMxRowBytes, kMxTok) ||
-      !encode_tmap_u8_2d_sw128(&tt64, act_q, act_pitch, static_cast<uint64_t>(m_pad), act_pitch,
-                               kMxRowBytes, C::kBoxRows))
+  // token rows: one box of a full tile, or boxes of 64 rows for a partial one;
+  // the split form's two planes (hi, lo) are the third coordinate
+  if (C::kPlanes > 1) {
+    const uint64_t mp = static_cast<uint64_t>(m_pad);
+    if (!encode_tmap_u8_3d_sw128(&tt, act_q, act_pitch, mp, C::kPlanes, act_pitch,
+                                 mp * act_pitch, kMxRowBytes, kMxTok) ||
+        !encode_tmap_u8_3d_sw128(&tt64, act_q, act_pitch, mp, C::kPlanes, act_pitch,
+                                 mp * act_pitch, kMxRowBytes, C::kBoxRows))
+      return LMOE_LAUNCH_FAILED;
+  } else if (!encode_tmap_u8_2d_sw128(&tt, act_q, act_pitch, static_cast<uint64_t>(m_pad),
+                                      act_pitch, kMxRowBytes, kMxTok) ||
+             !encode_tmap_u8_2d_sw128(&tt64, act_q, act_pitch, static_cast<uint64_t>(m_pad),
+                                      act_pitch, kMxRowBytes, C::kBoxRows)) {
     return LMOE_LAUNCH_FAILED;
+  }
   const int64_t tiles = (m_pad / kMxTok + g) * a.n_tiles;
   const int max_tiles = static_cast<int>(std::min<int64_t>(tiles, 1 << 30));
   auto s = static_cast<cudaStream_t>(stream);
@@ -1160,6 +1332,26 @@ int lmoe_mxfp4_quantize_scatter(const void* x, int x_f16, const int32_t* slot_po
                                                        m_pad_capacity, dev_status, stream);
 }
 
+int lmoe_bf16split_quantize_rows(const void* x, int64_t x_rows, int x_f16,
+                                 const int32_t* token_idx, const int32_t* group_sizes,
+                                 int64_t num_groups, int64_t rows, int64_t k, void* out_q,
+                                 void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                 void* stream) {
+  return lmoe::mx_quantize_rows_host<lmoe::MX_E4M3_SPLIT>(
+      x, x_rows, x_f16, token_idx, group_sizes, num_groups, rows, k, out_q, out_sf,
+      m_pad_capacity, dev_status, stream);
+}
+
+int lmoe_bf16split_quantize_scatter(const void* x, int x_f16, const int32_t* slot_pos,
+                                    int64_t num_tokens, int64_t top_k, int64_t k,
+                                    const int32_t* group_sizes, int64_t num_groups, void* out_q,
+                                    void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
+                                    void* stream) {
+  return lmoe::mx_quantize_scatter_host<lmoe::MX_E4M3_SPLIT>(
+      x, x_f16, slot_pos, num_tokens, top_k, k, group_sizes, num_groups, out_q, out_sf,
+      m_pad_capacity, dev_status, stream);
+}
+
 int lmoe_mxfp8_pad_positions(const int32_t* positions, int64_t n, const int32_t* group_sizes,
                              int64_t num_groups, int32_t* out, void* stream) {
   using namespace lmoe;
@@ -1179,7 +1371,7 @@ int lmoe_mxfp8_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const v
                                   int32_t* dev_status, void* stream) {
   return lmoe::mx_grouped_gemm<lmoe::KIND_F8F6F4>(act_q, act_sf, w_packed, w_sf, group_sizes, out,
                                                  m_pad, k, n_out, g, epi, beta, linear_beta,
-                                                 round_gate_up, out_dtype, dev_status, stream);
+                                                 round_gate_up, out_dtype, 0, dev_status, stream);
 }
 
 int lmoe_mxfp4_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
@@ -1189,7 +1381,48 @@ int lmoe_mxfp4_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const v
                                   int32_t* dev_status, void* stream) {
   return lmoe::mx_grouped_gemm<lmoe::KIND_F4>(act_q, act_sf, w_packed, w_sf, group_sizes, out,
                                              m_pad, k, n_out, g, epi, beta, linear_beta,
-                                             round_gate_up, out_dtype, dev_status, stream);
+                                             round_gate_up, out_dtype, 0, dev_status, stream);
+}
+
+int lmoe_blockscaled_gateup_situ_quantized(const void* act_q, const void* act_sf, int act_kind,
+                                           const void* w_packed, const void* w_sf,
+                                           const int32_t* group_sizes, int64_t m_pad, int64_t k,
+                                           int64_t inter, int64_t g, float beta,
+                                           float linear_beta, int round_gate_up, int out_fmt,
+                                           void* out_q, void* out_sf, int32_t* dev_status,
+                                           void* stream) {
+  using namespace lmoe;
+  if (out_q == nullptr) return LMOE_BAD_SHAPE;
+  switch (act_kind) {
+    case 0:
+      return mx_grouped_gemm<KIND_F8F6F4>(act_q, act_sf, w_packed, w_sf, group_sizes, nullptr,
+                                          m_pad, k, inter, g, EPI_SITU, beta, linear_beta,
+                                          round_gate_up, 0, 0, dev_status, stream, out_q, out_sf,
+                                          out_fmt);
+    case 1:
+      return mx_grouped_gemm<KIND_F4>(act_q, act_sf, w_packed, w_sf, group_sizes, nullptr, m_pad,
+                                      k, inter, g, EPI_SITU, beta, linear_beta, round_gate_up, 0, 0,
+                                      dev_status, stream, out_q, out_sf, out_fmt);
+    case 2:
+      return mx_grouped_gemm<KIND_F8_SPLIT>(act_q, act_sf, w_packed, w_sf, group_sizes, nullptr,
+                                            m_pad, k, inter, g, EPI_SITU, beta, linear_beta,
+                                            round_gate_up, 0, 0, dev_status, stream, out_q, out_sf,
+                                            out_fmt);
+    default:
+      return LMOE_BAD_SHAPE;
+  }
+}
+
+int lmoe_bf16split_mxfp4_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
+                                      const void* w_sf, const int32_t* group_sizes, void* out,
+                                      int64_t m_pad, int64_t k, int64_t n_out, int64_t g, int epi,
+                                      float beta, float linear_beta, int round_gate_up,
+                                      int out_dtype, int64_t m_out, int32_t* dev_status,
+                                      void* stream) {
+  return lmoe::mx_grouped_gemm<lmoe::KIND_F8_SPLIT>(act_q, act_sf, w_packed, w_sf, group_sizes,
+                                                   out, m_pad, k, n_out, g, epi, beta,
+                                                   linear_beta, round_gate_up, out_dtype, m_out,
+                                                   dev_status, stream);
 }
 
 }  // extern "C"

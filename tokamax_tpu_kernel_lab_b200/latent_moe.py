@@ -245,7 +245,11 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   block-scaled tensor core (kind::mxf8f6f4); the activation rounding adds
   ~3% normwise error against the exact forward.  "mxfp4" rounds them to
   MXFP4 instead (e2m1, one E8M0 scale per 32 values) and runs kind::mxf4, at
-  twice the MMA rate and a larger error (~10% normwise).
+  twice the MMA rate and a larger error (~10% normwise).  "split" keeps the
+  exact result on the block-scaled tensor core: each activation row becomes
+  two e4m3 planes under one scale (hi and the rounding remainder lo, which
+  together hold its bf16 value) multiplied into one accumulator (~1e-6
+  normwise from the exact forward).
 
   `mark(name)` (optional) is called on the host after each phase of the main
   stream is enqueued, e.g. to record CUDA events for a phase timeline."""
@@ -310,10 +314,10 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
     main.wait_stream(side_x)
     mark("down-projection")
   slot_pos = d.slot_pos
-  if pw.expert_gu_mx is not None and mxfp4_operand in ("mxfp8", "mxfp4"):
-    fmt = "e4m3" if mxfp4_operand == "mxfp8" else "e2m1"
+  if pw.expert_gu_mx is not None and mxfp4_operand in ("mxfp8", "mxfp4", "split"):
+    fmt = {"mxfp8": "e4m3", "mxfp4": "e2m1", "split": "e4m3x2"}[mxfp4_operand]
     act, down, slot_pos = mxfp8_expert_ffn(x, d.token_idx, d.group_sizes, d.slot_pos, pw, c,
-                                           mark, fmt=fmt)
+                                           mark, fmt=fmt, keep_activation=return_intermediates)
   elif pw.expert_gu_mx is not None:
     act, down = mxfp4_expert_ffn(x, d.token_idx, d.group_sizes, pw, c, mark, d.slot_pos)
   elif pw.dtype == torch.bfloat16:
@@ -361,8 +365,9 @@ def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "auto") -> bool:
   """True when the MXFP4 experts run the f16-operand kernels: mxfp4_operand
   is "auto" and every scale byte lies in their exact range.  The latent
   activations then travel as f16 (the same bf16-rounded values)."""
-  if mxfp4_operand not in ("auto", "bf16", "mxfp8", "mxfp4"):
-    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto', 'bf16', 'mxfp8' or 'mxfp4'")
+  if mxfp4_operand not in ("auto", "bf16", "mxfp8", "mxfp4", "split"):
+    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto', 'bf16', 'mxfp8', 'mxfp4' or "
+                     "'split'")
   return (mxfp4_operand == "auto" and pw.expert_gu_mx is not None and
           pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok)
 
@@ -400,26 +405,36 @@ def blockscaled_experts(pw: PreparedWeights):
 
 
 def mxfp8_expert_ffn(x, token_idx, group_sizes, slot_pos, pw: PreparedWeights,
-                     c: LatentMoEConfig, mark=None, fmt: str = "e4m3"):
+                     c: LatentMoEConfig, mark=None, fmt: str = "e4m3",
+                     keep_activation: bool = True):
   """Routed-expert FFN on the block-scaled tensor core: the gather quantises
-  the latent rows to MXFP8 (fmt "e4m3") or MXFP4 ("e2m1") into the padded
-  layout (every expert's rows start at a multiple of 128; in token order,
-  each row quantised once and stored top_k times), gate/up + SiTU-GLU, the
-  activations quantised again, the down GEMM; the slot positions are moved
-  to the padded rows for the combine.  Returns (activation, down output,
-  padded slot positions)."""
+  the latent rows to MXFP8 (fmt "e4m3"), MXFP4 ("e2m1") or two e4m3 planes
+  ("e4m3x2", the exact split) into the padded layout (every expert's rows
+  start at a multiple of 128; in token order, each row quantised once and
+  stored top_k times), gate/up + SiTU-GLU, the
+  activations quantised again (inside the gate/up kernel's epilogue unless
+  keep_activation asks for the bf16 activations), the down GEMM; the slot
+  positions are moved to the padded rows for the combine.  Returns
+  (activation or None, down output, padded slot positions)."""
   mark = mark or (lambda name: None)
   gu, dn = blockscaled_experts(pw)
-  if fmt == "e4m3":
-    quantize_scatter, quantize_rows = ops.quantize_mxfp8_scatter, ops.quantize_mxfp8_rows
-  else:
-    quantize_scatter, quantize_rows = ops.quantize_mxfp4_scatter, ops.quantize_mxfp4_rows
+  quantize_scatter, quantize_rows = {
+      "e4m3": (ops.quantize_mxfp8_scatter, ops.quantize_mxfp8_rows),
+      "e2m1": (ops.quantize_mxfp4_scatter, ops.quantize_mxfp4_rows),
+      "e4m3x2": (ops.quantize_split_scatter, ops.quantize_split_rows)}[fmt]
   rows = quantize_scatter(x, group_sizes, slot_pos, c.top_k)
   mark("gather")
-  act = ops.mxfp8_mxfp4_gateup_situ(rows, gu, beta=c.activation_situ_beta,
-                                    linear_beta=c.activation_situ_linear_beta,
-                                    round_gate_up=True)
-  act_q = quantize_rows(act, group_sizes, padded_input=True)
+  if keep_activation:
+    act = ops.mxfp8_mxfp4_gateup_situ(rows, gu, beta=c.activation_situ_beta,
+                                      linear_beta=c.activation_situ_linear_beta,
+                                      round_gate_up=True)
+    act_q = quantize_rows(act, group_sizes, padded_input=True)
+  else:
+    # the gate/up kernel writes the down GEMM's quantised rows directly
+    act = None
+    act_q = ops.blockscaled_gateup_situ_quantized(
+        rows, gu, fmt, beta=c.activation_situ_beta, linear_beta=c.activation_situ_linear_beta,
+        round_gate_up=True)
   mark("expert gate/up")
   down = ops.mxfp8_mxfp4_ragged_dot(act_q, dn)
   mark("expert down")

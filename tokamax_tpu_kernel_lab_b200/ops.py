@@ -662,9 +662,22 @@ class MXFP4Rows:
   group_sizes: torch.Tensor
 
 
+@dataclasses.dataclass
+class SplitRows:
+  """bf16/f16 activation rows split into two e4m3 planes under one E8M0 scale
+  per 32 K values, in the padded layout: q (2, M_pad, K) (plane 0 hi =
+  e4m3(x / 2^e), plane 1 lo = e4m3(x / 2^e - hi)), sf and group_sizes as in
+  MXFP8Rows.  hi + lo carries the rows' bf16 values (see quantize_split_rows)."""
+
+  q: torch.Tensor
+  sf: torch.Tensor
+  group_sizes: torch.Tensor
+
+
 _MX_FORMATS = {  # element format -> (rows class, K values per byte, quantising C entry points)
     "e4m3": (MXFP8Rows, 1, "lmoe_mxfp8_quantize_rows", "lmoe_mxfp8_quantize_scatter"),
     "e2m1": (MXFP4Rows, 2, "lmoe_mxfp4_quantize_rows", "lmoe_mxfp4_quantize_scatter"),
+    "e4m3x2": (SplitRows, 1, "lmoe_bf16split_quantize_rows", "lmoe_bf16split_quantize_scatter"),
 }
 
 
@@ -674,7 +687,8 @@ def mxfp8_padded_rows(num_rows: int, num_groups: int) -> int:
 
 def _mx_rows(fmt: str, m_pad: int, k: int, group_sizes: torch.Tensor, device):
   cls, k_per_byte, _, _ = _MX_FORMATS[fmt]
-  return cls(torch.empty(m_pad, k // k_per_byte, dtype=torch.uint8, device=device),
+  planes = (2,) if cls is SplitRows else ()
+  return cls(torch.empty(*planes, m_pad, k // k_per_byte, dtype=torch.uint8, device=device),
              torch.empty(k // 128, m_pad // 128, 512, dtype=torch.uint8, device=device),
              group_sizes)
 
@@ -692,7 +706,7 @@ def _quantize_rows(fmt, x, group_sizes, token_idx, padded_input, out):
   ti = None if token_idx is None else token_idx.to(torch.int32).contiguous()
   _native.call(_MX_FORMATS[fmt][2], _ptr(x.contiguous()), x.shape[0],
                int(x.dtype == torch.float16), _ptr(ti), None if padded_input else _ptr(gs), g,
-               rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)),
+               rows, k, _ptr(out.q), _ptr(out.sf), out.q.shape[-2], _ptr(device_status(x.device)),
                _stream())
   return out
 
@@ -707,7 +721,7 @@ def _quantize_scatter(fmt, x, group_sizes, slot_pos, top_k, out):
   out.group_sizes = gs
   _native.call(_MX_FORMATS[fmt][3], _ptr(x.contiguous()), int(x.dtype == torch.float16),
                _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k, k, _ptr(gs), g, _ptr(out.q),
-               _ptr(out.sf), out.q.shape[0], _ptr(device_status(x.device)), _stream())
+               _ptr(out.sf), out.q.shape[-2], _ptr(device_status(x.device)), _stream())
   return out
 
 
@@ -746,6 +760,22 @@ def quantize_mxfp4_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos:
   return _quantize_scatter("e2m1", x, group_sizes, slot_pos, top_k, out)
 
 
+def quantize_split_rows(x: torch.Tensor, group_sizes: torch.Tensor,
+                        token_idx: torch.Tensor | None = None, *, padded_input: bool = False,
+                        out: SplitRows | None = None) -> SplitRows:
+  """quantize_mxfp8_rows into two e4m3 planes: hi = e4m3(x / 2^e) and lo =
+  e4m3(x / 2^e - hi) under the MXFP8 block scale.  Every bf16 value with
+  |x| >= 2^(e-2) is held exactly by hi + lo (smaller ones to within 2^(e-10)),
+  so a block-scaled GEMM on both planes is the exact product."""
+  return _quantize_rows("e4m3x2", x, group_sizes, token_idx, padded_input, out)
+
+
+def quantize_split_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos: torch.Tensor,
+                           top_k: int, *, out: SplitRows | None = None) -> SplitRows:
+  """quantize_mxfp8_scatter into the two planes of quantize_split_rows."""
+  return _quantize_scatter("e4m3x2", x, group_sizes, slot_pos, top_k, out)
+
+
 def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> torch.Tensor:
   """Sorted-order row positions -> their rows in the padded layout."""
   _need_cuda(positions, group_sizes)
@@ -757,49 +787,100 @@ def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> t
   return out
 
 
-def _mx_gemm_entry(a) -> str:
-  if isinstance(a, MXFP8Rows):
-    return "lmoe_mxfp8_mxfp4_grouped_gemm"
-  if isinstance(a, MXFP4Rows):
-    return "lmoe_mxfp4_mxfp4_grouped_gemm"
-  raise TypeError(f"block-scaled rows expected, got {type(a).__name__}")
+def _mx_gemm(a, w, res, m_pad, k, n, g, epi, beta, linear_beta, round_gate_up, code, m_out=0):
+  common = (_ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf), _ptr(a.group_sizes), _ptr(res),
+            m_pad, k, n, g, epi, float(beta), float(linear_beta), int(round_gate_up), code)
+  tail = (_ptr(device_status(a.q.device)), _stream())
+  if isinstance(a, SplitRows):
+    _native.call("lmoe_bf16split_mxfp4_grouped_gemm", *common, m_out, *tail)
+  elif m_out:
+    raise ValueError("unpadded output rows need split rows")
+  elif isinstance(a, MXFP8Rows):
+    _native.call("lmoe_mxfp8_mxfp4_grouped_gemm", *common, *tail)
+  elif isinstance(a, MXFP4Rows):
+    _native.call("lmoe_mxfp4_mxfp4_grouped_gemm", *common, *tail)
+  else:
+    raise TypeError(f"block-scaled rows expected, got {type(a).__name__}")
 
 
-def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows | MXFP4Rows, w: MXFP4BlockScaled,
+def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockScaled,
                            out_dtype: torch.dtype = torch.bfloat16,
                            out: torch.Tensor | None = None) -> torch.Tensor:
   """Padded block-scaled rows @ dequant(w[g])^T per group -> (M_pad, N); rows
   past each group's count are not written.  MXFP8 rows run kind::mxf8f6f4,
-  MXFP4 rows (K a multiple of 256) kind::mxf4."""
+  MXFP4 rows (K a multiple of 256) kind::mxf4, split rows kind::mxf8f6f4 on
+  both planes (the exact product)."""
   g, n, k = w.shape
   if w.gateup:
     raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
-  m_pad = a.q.shape[0]
+  m_pad = a.q.shape[-2]
   res = out if out is not None else torch.empty(m_pad, n, dtype=out_dtype, device=a.q.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
-  _native.call(_mx_gemm_entry(a), _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
-               _ptr(a.group_sizes), _ptr(res), m_pad, k, n, g, 0, 0.0, 0.0, 0, code,
-               _ptr(device_status(a.q.device)), _stream())
+  _mx_gemm(a, w, res, m_pad, k, n, g, 0, 0.0, 0.0, 0, code)
   return res
 
 
-def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows | MXFP4Rows, w: MXFP4BlockScaled, *, beta: float = 4.0,
-                            linear_beta: float = 25.0, round_gate_up: bool = True,
-                            out_dtype: torch.dtype = torch.bfloat16,
+def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockScaled, *,
+                            beta: float = 4.0, linear_beta: float = 25.0,
+                            round_gate_up: bool = True, out_dtype: torch.dtype = torch.bfloat16,
                             out: torch.Tensor | None = None) -> torch.Tensor:
   """SiTU-GLU of the block-scaled grouped matmul against gate/up-interleaved
-  MXFP4 weights -> (M_pad, I) (padded rows); MXFP8 or MXFP4 rows."""
+  MXFP4 weights -> (M_pad, I) (padded rows); MXFP8, MXFP4 or split rows."""
   g, two_i, k = w.shape
   if not w.gateup:
     raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
-  m_pad = a.q.shape[0]
+  m_pad = a.q.shape[-2]
   res = out if out is not None else torch.empty(m_pad, two_i // 2, dtype=out_dtype,
                                                 device=a.q.device)
   code = {torch.bfloat16: 0, torch.float16: 2}[res.dtype]
-  _native.call(_mx_gemm_entry(a), _ptr(a.q), _ptr(a.sf), _ptr(w.packed), _ptr(w.sf),
-               _ptr(a.group_sizes), _ptr(res), m_pad, k, two_i // 2, g, 3, float(beta),
-               float(linear_beta), int(round_gate_up), code, _ptr(device_status(a.q.device)),
-               _stream())
+  _mx_gemm(a, w, res, m_pad, k, two_i // 2, g, 3, beta, linear_beta, round_gate_up, code)
+  return res
+
+
+def mxfp4_ragged_dot_blockscaled(lhs: torch.Tensor, w: MXFP4BlockScaled,
+                                 group_sizes: torch.Tensor,
+                                 out_dtype: torch.dtype = torch.bfloat16,
+                                 out: torch.Tensor | None = None,
+                                 rows: SplitRows | None = None) -> torch.Tensor:
+  """mxfp4_ragged_dot (the exact MXFP4 grouped matmul, ragged_dot layout:
+  lhs (M, K) bf16/f16 in group order, out (M, N), rows past sum(group_sizes)
+  zero) on the block-scaled tensor core: the rows split into two e4m3 planes
+  (quantize_split_rows), both multiplied into one accumulator, the output
+  written at the unpadded rows.  Within ~1e-6 normwise of the exact kernel.
+  `rows` (optional) is reused as the split buffer."""
+  g, n, k = w.shape
+  if w.gateup:
+    raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
+  m = lhs.shape[0]
+  a = quantize_split_rows(lhs, group_sizes, out=rows)
+  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
+  if m > 0:
+    _mx_gemm(a, w, res, a.q.shape[-2], k, n, g, 0, 0.0, 0.0, 0, code, m_out=m)
+  return res
+
+
+_ROWS_KIND = {MXFP8Rows: 0, MXFP4Rows: 1, SplitRows: 2}
+_FMT_CODE = {"e4m3": 0, "e2m1": 1, "e4m3x2": 2}
+
+
+def blockscaled_gateup_situ_quantized(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockScaled,
+                                      fmt: str, *, beta: float = 4.0, linear_beta: float = 25.0,
+                                      round_gate_up: bool = True, out=None):
+  """mxfp8_mxfp4_gateup_situ with the SiTU activations written straight into
+  block-scaled rows of format `fmt` ("e4m3", "e2m1" or "e4m3x2") for the down
+  GEMM: the same bytes as quantising the bf16 output (padded_input=True), with
+  no bf16 activation tensor in between."""
+  g, two_i, k = w.shape
+  if not w.gateup:
+    raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
+  m_pad = a.q.shape[-2]
+  res = out if out is not None else _mx_rows(fmt, m_pad, two_i // 2, a.group_sizes, a.q.device)
+  res.group_sizes = a.group_sizes
+  _native.call("lmoe_blockscaled_gateup_situ_quantized", _ptr(a.q), _ptr(a.sf),
+               _ROWS_KIND[type(a)], _ptr(w.packed), _ptr(w.sf), _ptr(a.group_sizes), m_pad, k,
+               two_i // 2, g, float(beta), float(linear_beta), int(round_gate_up), _FMT_CODE[fmt],
+               _ptr(res.q), _ptr(res.sf), _ptr(device_status(a.q.device)), _stream())
   return res
 
 
