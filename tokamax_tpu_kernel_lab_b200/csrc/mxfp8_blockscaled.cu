@@ -1,18 +1,23 @@
-// Block-scaled fast path: MXFP8 activations x MXFP4 weights on the
-// block-scaled tensor core (tcgen05.mma kind::mxf8f6f4.block_scale).
+// Block-scaled paths: MXFP4 weights on the block-scaled tensor core
+// (tcgen05.mma kind::mxf8f6f4.block_scale / kind::mxf4.block_scale).
 //
 // The exact MXFP4 kernels (mxfp4_swap.cu) expand every weight tile to f16 or
-// bf16 in shared memory and multiply on kind::f16.  This path instead feeds
-// the e2m1 codes to the tensor core as they are -- the TMA unpacks each group
-// of 16 codes into the 16-byte-per-16-element shared-memory form the MMA
-// reads -- with their E8M0 block scales in tensor memory, and quantises the
-// activations to MXFP8 (e4m3 elements, one E8M0 scale per 32 K values; the
-// scale rule is the smallest power of two that fits the block's absolute
-// maximum under 448, so no element saturates).  No expansion work at all,
-// and each MMA instruction covers K = 32 instead of 16.  The price is the
-// activation rounding: this is an opt-in path with a measured error, not a
-// replacement for the exact one.  The reference's operator carries the hook
-// for this (`maybe_quantize_lhs`,
+// bf16 in shared memory and multiply on kind::f16.  These kernels instead
+// feed the e2m1 codes to the tensor core as they are, with their E8M0 block
+// scales in tensor memory, against activations quantised per 32 K values
+// under one E8M0 scale each (the MMA kinds below):
+//   MXFP8 rows   e4m3 (scale: the smallest power of two that fits the block's
+//                absolute maximum under 448, so no element saturates);
+//                kind::mxf8f6f4, the codes unpacked by the TMA (16 codes into
+//                16 bytes); an opt-in path with a measured error (~3%)
+//   MXFP4 rows   e2m1 (amax <= 6 * 2^e); kind::mxf4, both operands packed, at
+//                twice the MMA rate; opt-in, ~12% error
+//   split rows   the bf16 activations as two e4m3 planes under the MXFP8
+//                scale (hi and the rounding remainder lo, which together hold
+//                the bf16 value), two kind::mxf8f6f4 MMAs per K slice: the
+//                exact product, with no weight expansion
+// The reference's operator carries the hook for quantising the activations
+// (`maybe_quantize_lhs`,
 // 05_ragged_dot_on_tpu/kimi_k3_latent_moe_ragged_dot.py:257-263) but never
 // exercises it.
 //
@@ -26,28 +31,30 @@
 //               the layout tcgen05.cp 32x128b.warpx4 copies to tensor memory
 //               (row r's scales for the MMA's 4 K blocks land in TMEM column
 //               r/32 of every lane quarter, byte kb)
-//   activations e4m3 rows (M_pad, K); every expert's rows start at a multiple
-//               of 128 (rows past an expert's count up to that boundary are
-//               padding nobody reads), so a 128-row tile owns whole atoms
+//   activations rows (M_pad, K) e4m3, (M_pad, K/2) e2m1 pairs or (2, M_pad, K)
+//               e4m3 planes; every expert's rows start at a multiple of 128
+//               (rows past an expert's count up to that boundary are padding
+//               nobody reads), so a 128-row tile owns whole atoms
 //   act SF      (K/128, M_pad/128) atoms, the same byte layout per 128 rows,
 //               K-step major so a tile's consecutive row blocks are one copy
 //
 // GEMM tile: 128 weight rows (UMMA M) x 192 token rows (UMMA N, or the tile's
-// row count rounded up to 16), K step 128 = 4 MMAs of K 32.  Two 192-column
+// row count rounded up to 16), 128-byte operand rows per ring stage (K 128 =
+// 4 MMAs of K 32, or K 256 = 4 MMAs of K 64 for kind::mxf4).  Two 192-column
 // accumulators (at columns 0 and 256) leave room for the scale columns, and
 // every tile of a group starts 64-row aligned inside its 128-aligned group, so
 // the tokens' scales for the tile are whole atoms starting 0 or 2 columns in
-// (64 rows = 2 columns).  Per ring stage: weights 16 KB (8 KB moved), tokens
-// up to 192 rows (24 KB), one weight-scale atom and up to two token-scale
-// atoms.
-//   warp 0     weight producer: TMA (codes) and the weight-scale atom
-//   warp 6     token producer: TMA (e4m3 rows; one 192-row box for a full
-//              tile) and the token-scale atoms (one bulk copy)
+// (64 rows = 2 columns).
+//   warp 0     weight producer: TMA (codes) and the weight-scale atoms
+//   warp 6     token producer: TMA (one 192-row box per plane for a full
+//              tile) and the token-scale atoms (one bulk copy per quad)
 //              (one thread issues a copy only every few hundred cycles, so
 //              the copies of a step are split over two threads and kept few)
 //   warp 1     TMEM owner and MMA issuer; copies each stage's scale atoms into
 //              tensor memory (tcgen05.cp) ahead of its MMAs
-//   warps 2-5  epilogue (tensor-memory lane = weight row, column = token)
+//   warps 2-5  epilogue (tensor-memory lane = weight row, column = token);
+//              the SiTU epilogue can write its activations already quantised
+//              for the next GEMM
 #include <cuda.h>
 
 #include <algorithm>
