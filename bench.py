@@ -57,9 +57,10 @@ UNIT = "tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 # dram bytes (read + write) per launch of the dominant kernel, from one ncu
 # capture at this configuration (16384 tokens, 262144 routed rows; metrics
-# dram__bytes_read.sum / dram__bytes_write.sum, the first gate/up launch):
-# 1287.9 MB read + 512.4 MB written
-DOMINANT_TRAFFIC_BYTES = int(1287.9e6 + 512.4e6)
+# dram__bytes_read.sum / dram__bytes_write.sum, the first gate/up launch of the
+# default forward: the block-scaled gate/up + SiTU kernel on split rows):
+# 1319.6 MB read + 520.5 MB written
+DOMINANT_TRAFFIC_BYTES = int(1319579904 + 520499456)
 
 
 def parse_args():
@@ -527,6 +528,9 @@ def gpu_config4(args, lm, ops, dev, peaks, peak_src, iters: int, exact: bool = T
     src = f"{peak_src} (fp8 = 2 x bf16 burst)"
     wb = ops.prepare_mxfp4_blockscaled(w4)
     a4 = ops.quantize_mxfp8_rows(x4, gs4)
+    # these GEMMs write the padded row layout: every group starts at a
+    # multiple of 128 rows, so their output has the padded row count
+    o4 = torch.empty(a4.q.shape[-2], n4, dtype=torch.bfloat16, device=dev)
     ops.mxfp8_mxfp4_ragged_dot(a4, wb, out=o4)
     ms = time_launches(lambda: ops.mxfp8_mxfp4_ragged_dot(a4, wb, out=o4), iters)
     out["config4_blockscaled_gemm"] = roofline_entry(
@@ -625,8 +629,8 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
   out["layer"] = {"ms": ms, "tokens_per_s": h.shape[0] / (ms / 1e3)}
   del graph
   # the same layer with MXFP4 activations (kind::mxf4), and exact on the
-  # block-scaled tensor core (two e4m3 planes per activation row)
-  for mode, key in (("mxfp4", "layer_mxfp4_activations"), ("split", "layer_exact_split")):
+  # weights-major kernels (codes expanded to f16 tiles, kind::f16)
+  for mode, key in (("mxfp4", "layer_mxfp4_activations"), ("f16", "layer_exact_weights_major")):
     for _ in range(2):
       lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
     torch.cuda.synchronize()
@@ -668,15 +672,16 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
 
 def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
   """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay):
-  the default forward, and the exact forward on the block-scaled tensor core
-  (mxfp4_operand="split") as `split_ms`."""
+  the default forward (the exact product on the block-scaled tensor core),
+  and the weights-major f16-operand kernels (mxfp4_operand="f16") as
+  `f16_ms`."""
   import torch
   out = {}
   for t in tokens:
     gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + t)
     h = torch.randn(t, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
     res = {}
-    for mode in ("auto", "split"):
+    for mode in ("auto", "f16"):
       for _ in range(2):
         lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
       torch.cuda.synchronize()
@@ -686,7 +691,7 @@ def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
       res[mode] = time_launches(graph.replay, max(5, args.steps))
       del graph
     out[f"T{t}"] = {"ms": res["auto"], "tokens_per_s": t / (res["auto"] / 1e3),
-                    "split_ms": res["split"]}
+                    "f16_ms": res["f16"]}
   return out
 
 
@@ -924,13 +929,27 @@ def main():
          "pipelining": "upload, forward and download of neighbouring steps overlap"}
 
   # ---------------------------------------------------------------- dominant kernel
-  # the MXFP4 fused gate/up grouped GEMM on this rank's routed rows (already
-  # gathered into expert order, as the forward feeds it), timed alone
+  # The routed gate/up + SiTU-GLU grouped GEMM on this rank's routed rows, fed
+  # as the forward feeds it, timed alone.  One GPU: the default forward's
+  # kernel -- the block-scaled MMA (kind::mxf8f6f4) on the e2m1 weight codes
+  # and the latent rows split into two e4m3 planes (hi + remainder), two MMAs
+  # per 32-wide K slice, i.e. the exact product at the FP8 instruction rate
+  # twice over = the bf16 rate; it writes the down GEMM's split rows.
+  # Several GPUs: the expert-parallel path's weights-major kernel (codes
+  # expanded to f16 tiles in shared memory, kind::f16).
   rows = t_local * cfg.top_k
   if world == 1:
     _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True)
     gs = inter["group_sizes"]
-    xs = ops.gather_rows(inter["latent_projection"], inter["token_idx"])
+    gu_bs, _ = lm.latent_moe.blockscaled_experts(pw)
+    xs = ops.quantize_split_scatter(inter["latent_projection"], gs, inter["slot_pos"],
+                                    cfg.top_k)
+    act = ops.blockscaled_gateup_situ_quantized(xs, gu_bs, "e4m3x2")
+    gateup = lambda: ops.blockscaled_gateup_situ_quantized(xs, gu_bs, "e4m3x2", out=act)
+    dom_kernel = ("mxfp4 fused gate/up + SiTU-GLU grouped GEMM, block-scaled tcgen05 "
+                  "kind::mxf8f6f4 on split (hi + lo e4m3) activation rows: the exact product")
+    traffic = DOMINANT_TRAFFIC_BYTES
+    del inter
   else:
     # stand-in for the expert-major rows this rank receives: the local share of
     # the routed rows spread evenly over the local experts
@@ -938,8 +957,10 @@ def main():
     gs[0] += rows - int(gs.sum().item())
     xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(
         torch.float16 if lm.latent_moe.mxfp4_f16_path(pw) else torch.bfloat16)
-  act = torch.empty(rows, cfg.intermediate_size, dtype=xs.dtype, device=dev)
-  gateup = lambda: ops.mxfp4_fused_gateup_situ(xs, pw.expert_gu_mx, gs, out=act)
+    act = torch.empty(rows, cfg.intermediate_size, dtype=xs.dtype, device=dev)
+    gateup = lambda: ops.mxfp4_fused_gateup_situ(xs, pw.expert_gu_mx, gs, out=act)
+    dom_kernel = "mxfp4 fused gate/up + SiTU-GLU grouped GEMM, weights-major (tcgen05 kind::f16)"
+    traffic = None  # the one-GPU capture does not cover this rank's row count
   flops = 2.0 * rows * cfg.latent_size * 2 * cfg.intermediate_size
   peaks, peak_src = load_peaks()
   # (1) alone on an idle GPU, at its boost clock: the condition of the burst
@@ -958,11 +979,11 @@ def main():
     k_ms_hot = time_launches(gateup, max(args.steps, 10), warmup=0)
   achieved = flops / (k_ms / 1e3) / 1e12
   achieved_hot = flops / (k_ms_hot / 1e3) / 1e12
-  roofline = {"kernel": "mxfp4 fused gate/up + SiTU-GLU grouped GEMM (tcgen05)",
+  roofline = {"kernel": dom_kernel,
               "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
               "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
               "peak_source": f"{peak_src} dense bf16 burst (the kernel is timed alone, from idle)",
-              "traffic": DOMINANT_TRAFFIC_BYTES, "ms_per_launch": k_ms,
+              "traffic": traffic, "ms_per_launch": k_ms,
               "flops_per_launch": flops, "clocks": dclk.summary(),
               "weight_bytes_per_launch": int(pw.expert_gu_mx.packed.numel() +
                                              pw.expert_gu_mx.scale.numel()),

@@ -75,7 +75,8 @@ def _worker(rank, world, port, results, mode="nccl"):
       results[rank] = [o.cpu() for o in outs] + [o.cpu() for o in replays]
       if rank == 0:
         full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
-        results["ref"] = [lm.latent_moe_forward(x, full, cfg).cpu() for x in hs]
+        results["ref"] = [lm.latent_moe_forward(x, full, cfg, mxfp4_operand="f16").cpu()
+                          for x in hs]
       dist.barrier()
       return
     stats = EPStats([], [])
@@ -86,7 +87,7 @@ def _worker(rank, world, port, results, mode="nccl"):
     results[rank] = (out.cpu(), stats.send_rows, stats.recv_rows)
     if rank == 0:
       full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
-      results["ref"] = lm.latent_moe_forward(h, full, cfg).cpu()
+      results["ref"] = lm.latent_moe_forward(h, full, cfg, mxfp4_operand="f16").cpu()
     dist.barrier()
   finally:
     dist.destroy_process_group()

@@ -157,7 +157,7 @@ def test_peer_exchange_emulated_ranks_bit_exact(lm, world, fused_return):
   backends = [GpuBackend(shard_experts(pw, r, world), cfg) for r in range(world)]
   for epoch in (1, 2):
     h = torch.randn(t, cfg.hidden_size, generator=gen, device="cuda").to(torch.bfloat16)
-    ref = lm.latent_moe_forward(h, pw, cfg)
+    ref = lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="f16")
     hs = [h[r * t_local:(r + 1) * t_local].contiguous() for r in range(world)]
     out = emulated_forward(lm, ranks, backends, hs, cfg, epoch, fused_return)
     torch.cuda.synchronize()

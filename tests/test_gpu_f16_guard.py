@@ -7,7 +7,9 @@ lose precision in the f16 subnormals.  The kernels that write f16 operands
 (the dense GEMM's f16 output, the converting row gather) record
 LMOE_F16_RANGE in the device status word in both cases, and the layer
 forward has a bf16-operand mode (`mxfp4_operand="bf16"`) that carries such
-rows exactly.  Reference: the latent x is held in the compute dtype, bf16
+rows exactly.  The default mode (`"auto"` = `"split"`, the block-scaled
+kernels on two e4m3 planes under a per-32-value power-of-two scale) has no
+such range: it matches the bf16 mode on the same inputs and records nothing.  Reference: the latent x is held in the compute dtype, bf16
 (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:365)."""
 
 import numpy as np
@@ -126,6 +128,17 @@ def _oracle_forward(cfg, pw, h):
                               return_intermediates=True)
 
 
+def _assert_default_mode_matches(lm, h, pw, cfg, exact):
+  """The default (split) forward on the same inputs records nothing and
+  matches the bf16-operand forward `exact` at the bf16 tolerance, on the
+  scale of each token's own output."""
+  _clear(lm)
+  got = to_np(lm.latent_moe_forward(h, pw, cfg))
+  assert _status(lm) == 0
+  scale = np.abs(exact).max(axis=1, keepdims=True)
+  assert_bf16_close(exact / scale, got / scale, "default (split) mode, per-token scale")
+
+
 def test_layer_with_huge_latent_values_flags_and_bf16_mode_is_exact(lm):
   """Token 0's hidden state is scaled so its latent row reaches ~1e5: the
   default (f16) path records LMOE_F16_RANGE; mxfp4_operand="bf16" runs the
@@ -138,7 +151,7 @@ def test_layer_with_huge_latent_values_flags_and_bf16_mode_is_exact(lm):
   h[0] *= 40000.0
   h = h.to(torch.bfloat16)
   _clear(lm)
-  lm.latent_moe_forward(h, pw, cfg)
+  lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="f16")
   assert _status(lm) == _native.LMOE_F16_RANGE
   _clear(lm)
   final, inter = lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="bf16",
@@ -158,6 +171,7 @@ def test_layer_with_huge_latent_values_flags_and_bf16_mode_is_exact(lm):
   rest = same.copy()
   rest[0] = False
   assert_bf16_close(ref[rest], got[rest], "bf16-operand layer, other tokens")
+  _assert_default_mode_matches(lm, h, pw, cfg, got)
 
 
 def test_layer_with_tiny_rows_flags_and_bf16_mode_is_exact(lm):
@@ -170,7 +184,7 @@ def test_layer_with_tiny_rows_flags_and_bf16_mode_is_exact(lm):
   gen = torch.Generator(device="cuda").manual_seed(13)
   h = (torch.randn(256, cfg.hidden_size, generator=gen, device="cuda") * 3e-3).to(torch.bfloat16)
   _clear(lm)
-  lm.latent_moe_forward(h, pw, cfg)
+  lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="f16")
   assert _status(lm) == _native.LMOE_F16_RANGE
   _clear(lm)
   final, inter = lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="bf16",
@@ -181,6 +195,7 @@ def test_layer_with_tiny_rows_flags_and_bf16_mode_is_exact(lm):
                            rinter["router_scores_for_choice"], rinter["topk_indices"])
   s0 = float(np.abs(ref).max())  # outputs ~1e-4: compared on their own scale
   assert_bf16_close(ref[same] / s0, to_np(final)[same] / s0, "bf16-operand layer, tiny rows")
+  _assert_default_mode_matches(lm, h, pw, cfg, to_np(final))
 
 
 def test_layer_with_small_latent_values_matches_oracle(lm):
@@ -192,7 +207,8 @@ def test_layer_with_small_latent_values_matches_oracle(lm):
   gen = torch.Generator(device="cuda").manual_seed(14)
   h = torch.randn(256, cfg.hidden_size, generator=gen, device="cuda").to(torch.bfloat16)
   _clear(lm)
-  final, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True)
+  final, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True,
+                                       mxfp4_operand="f16")
   assert _status(lm) == 0
   x, act = inter["latent_projection"], inter["situ_output"]
   assert x.dtype == torch.float16 and act.dtype == torch.float16

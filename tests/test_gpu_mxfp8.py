@@ -294,3 +294,39 @@ def test_quantize_scatter_equals_row_order(lm, t, k, e, dim, f16):
   for tok in (0, t // 2, t - 1):
     for r in pp[tok]:
       assert np.array_equal(qb[r], qb[pp[tok][0]])
+
+
+def test_output_buffers_are_checked_before_any_launch(lm):
+  """An `out=` buffer must have exactly the shape the kernel writes: the
+  block-scaled GEMMs write the padded row layout (every group starting at a
+  multiple of 128), so an (M, N) buffer for M routed rows is too short and
+  is refused with ValueError before anything is launched; the same holds for
+  the bf16 ragged_dot and for block-scaled row buffers."""
+  ops = _ops()
+  rng = np.random.default_rng(41)
+  g, n, k = 4, 256, 256
+  gs = np.array([100, 3, 0, 60], np.int32)
+  m = int(gs.sum())
+  codes = rng.integers(0, 256, (g, n, k // 2), dtype=np.uint8)
+  scales = rng.integers(120, 126, (g, n, k // 32), dtype=np.uint8)
+  wb = ops.prepare_mxfp4_blockscaled(ops.MXFP4Weights(to_dev(codes), to_dev(scales)))
+  x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+  gs_d = to_dev(gs)
+  rows = ops.quantize_mxfp8_rows(x, gs_d)
+  m_pad = rows.q.shape[-2]
+  assert m_pad > m
+  with pytest.raises(ValueError):
+    ops.mxfp8_mxfp4_ragged_dot(rows, wb, out=torch.empty(m, n, dtype=torch.bfloat16,
+                                                         device="cuda"))
+  good = ops.mxfp8_mxfp4_ragged_dot(rows, wb, out=torch.empty(m_pad, n, dtype=torch.bfloat16,
+                                                              device="cuda"))
+  assert good.shape == (m_pad, n)
+  with pytest.raises(ValueError):
+    ops.quantize_split_rows(x, gs_d, out=ops.quantize_mxfp8_rows(x, gs_d))
+  rhs = torch.randn(g, k, n, device="cuda").to(torch.bfloat16)
+  with pytest.raises(ValueError):
+    ops.ragged_dot(x, rhs, gs_d, out=torch.empty(m - 1, n, dtype=torch.bfloat16, device="cuda"))
+  with pytest.raises(ValueError):
+    ops.ragged_dot(x, rhs, gs_d, out=torch.empty(n, m, dtype=torch.bfloat16, device="cuda").t())
+  torch.cuda.synchronize()
+  lm.check_device_status()

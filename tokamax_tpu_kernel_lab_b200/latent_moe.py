@@ -149,8 +149,8 @@ class PreparedWeights:
   shared_down: torch.Tensor
   expert_gu_mx: ops.MXFP4Weights | None = None     # (E, 2I, L/2) codes: [w1 gate | w3 up]
   expert_down_mx: ops.MXFP4Weights | None = None   # (E, L, I/2) codes: w2
-  # the same experts prepared for the block-scaled MMA (built on first use of
-  # mxfp4_operand="mxfp8", then kept)
+  # the same experts prepared for the block-scaled MMA (built on the first
+  # forward that uses it -- the default "split" mode among them -- then kept)
   expert_gu_bs: ops.MXFP4BlockScaled | None = None
   expert_down_bs: ops.MXFP4BlockScaled | None = None
 
@@ -231,25 +231,27 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   """The 8-step LatentMoE forward (kimi_k3_latent_moe_reference.py:330-435).
   `weights` is a LatentMoEWeights (prepared on the fly) or PreparedWeights.
 
-  mxfp4_operand (MXFP4 experts only): "auto" runs the f16-operand kernels
-  when every weight scale allows it (see mxfp4_f16_path): the latent rows
-  then travel as f16 carrying their bf16-rounded values.  That is exact for
-  magnitudes up to 65504 (bf16 values below 2^-17 lose low bits as f16
-  subnormals, an absolute error below 2^-25); a larger latent value would
-  become inf, so the kernel that writes the f16 rows records LMOE_F16_RANGE
-  in the device status word (check_device_status raises it).  "bf16" keeps
-  the latent rows in bf16 and runs the bf16-operand kernels: the same result
-  without the range limit, somewhat slower.  "mxfp8" is the opt-in fast
-  path: the latent rows and the SiTU activations are rounded to MXFP8 (e4m3,
-  one E8M0 scale per 32 values) and the MXFP4 experts run on the
-  block-scaled tensor core (kind::mxf8f6f4); the activation rounding adds
-  ~3% normwise error against the exact forward.  "mxfp4" rounds them to
-  MXFP4 instead (e2m1, one E8M0 scale per 32 values) and runs kind::mxf4, at
-  twice the MMA rate and a larger error (~10% normwise).  "split" keeps the
-  exact result on the block-scaled tensor core: each activation row becomes
-  two e4m3 planes under one scale (hi and the rounding remainder lo, which
-  together hold its bf16 value) multiplied into one accumulator (~1e-6
-  normwise from the exact forward).
+  mxfp4_operand (MXFP4 experts only): "auto" (the default) is "split": the
+  exact product on the block-scaled tensor core -- each latent or SiTU
+  activation row becomes two e4m3 planes under one E8M0 scale per 32 values
+  (hi and the rounding remainder lo, which together hold its bf16 value for
+  every |x| >= 2^-2 of the block scale, and within 2^-10 of it below), both
+  multiplied into one f32 accumulator by kind::mxf8f6f4 MMAs that read the
+  e2m1 weight codes as stored (~1e-6 normwise from the dequant-then-matmul
+  product).  "f16" runs the weights-major kernels, which expand the codes
+  into f16 tiles in shared memory, when every weight scale allows it (see
+  mxfp4_f16_path; otherwise their bf16 form): the latent rows then travel as
+  f16 carrying their bf16-rounded values, exact up to 65504 in magnitude (a
+  larger value would become inf, so the kernel that writes the f16 rows
+  records LMOE_F16_RANGE in the device status word, which
+  check_device_status raises).  "bf16" runs the weights-major kernels on
+  bf16 operands without that range limit.  "mxfp8" is the opt-in fast path:
+  the latent rows and the SiTU activations are rounded to MXFP8 (e4m3, one
+  E8M0 scale per 32 values) and run one kind::mxf8f6f4 MMA per K slice; the
+  activation rounding adds ~3% normwise error against the exact forward.
+  "mxfp4" rounds them to MXFP4 instead (e2m1, one E8M0 scale per 32 values)
+  and runs kind::mxf4, at twice the MMA rate and a larger error (~10%
+  normwise).
 
   `mark(name)` (optional) is called on the host after each phase of the main
   stream is enqueued, e.g. to record CUDA events for a phase timeline."""
@@ -271,6 +273,7 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   # of these GEMMs fills the GPU and running them at the same time only slows
   # both (measured: 16384 tokens 5.66 -> 6.12 ms), so they stay in order.
   overlap = pw.dtype == torch.bfloat16 and not return_intermediates
+  mxfp4_operand = resolve_mxfp4_operand(pw, mxfp4_operand)
   x_dtype = torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else torch.bfloat16
   down_tiles = -(-t // 128) * -(-pw.down.shape[0] // 128)
   overlap_x = overlap and 2 * down_tiles <= torch.cuda.get_device_properties(
@@ -361,14 +364,26 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   return final
 
 
-def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "auto") -> bool:
-  """True when the MXFP4 experts run the f16-operand kernels: mxfp4_operand
-  is "auto" and every scale byte lies in their exact range.  The latent
-  activations then travel as f16 (the same bf16-rounded values)."""
-  if mxfp4_operand not in ("auto", "bf16", "mxfp8", "mxfp4", "split"):
-    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'auto', 'bf16', 'mxfp8', 'mxfp4' or "
-                     "'split'")
-  return (mxfp4_operand == "auto" and pw.expert_gu_mx is not None and
+MXFP4_OPERANDS = ("auto", "split", "f16", "bf16", "mxfp8", "mxfp4")
+
+
+def resolve_mxfp4_operand(pw: PreparedWeights, mxfp4_operand: str = "auto") -> str:
+  """The MXFP4 expert mode a forward runs: "auto" is "split" (the exact
+  product on the block-scaled tensor core) when the experts are MXFP4."""
+  if mxfp4_operand not in MXFP4_OPERANDS:
+    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: one of {', '.join(MXFP4_OPERANDS)}")
+  if mxfp4_operand == "auto" and pw.expert_gu_mx is not None:
+    return "split"
+  return mxfp4_operand
+
+
+def mxfp4_f16_path(pw: PreparedWeights, mxfp4_operand: str = "f16") -> bool:
+  """True when the MXFP4 experts run the weights-major f16-operand kernels:
+  mxfp4_operand is "f16" and every scale byte lies in their exact range.
+  The latent activations then travel as f16 (the same bf16-rounded values)."""
+  if mxfp4_operand not in MXFP4_OPERANDS:
+    raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: one of {', '.join(MXFP4_OPERANDS)}")
+  return (mxfp4_operand == "f16" and pw.expert_gu_mx is not None and
           pw.expert_gu_mx.f16_operand_ok and pw.expert_down_mx.f16_operand_ok)
 
 

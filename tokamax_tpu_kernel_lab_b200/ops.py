@@ -88,6 +88,21 @@ def _check_impl(implementation):
 # ----------------------------------------------------------------------------- GEMMs
 
 
+def _out(out: torch.Tensor | None, shape: tuple, dtype: torch.dtype, device) -> torch.Tensor:
+  """The output tensor of an op: `out` when the caller passes one, else a new
+  tensor.  The kernels write a dense row-major block of exactly `shape`, so
+  a given `out` must be contiguous, have that shape and sit on the inputs'
+  device (its dtype selects the output format where an op offers several);
+  anything else raises ValueError before a kernel could write past it."""
+  if out is None:
+    return torch.empty(shape, dtype=dtype, device=device)
+  shape = tuple(int(d) for d in shape)
+  if tuple(out.shape) != shape or not out.is_contiguous() or out.device != torch.device(device):
+    raise ValueError(f"out: expected a contiguous {shape} tensor on {device}, got "
+                     f"{tuple(out.shape)} (contiguous={out.is_contiguous()}) on {out.device}")
+  return out
+
+
 def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, *,
                implementation: str | None = None, precision=None,
                preferred_element_type: torch.dtype | None = None, rhs_layout: str = "gkn",
@@ -119,7 +134,7 @@ def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, 
   if lhs.dtype == torch.float32:
     if rhs.dtype != torch.float32:
       raise ValueError("f32 lhs needs f32 rhs")
-    res = out if out is not None else torch.empty(m, n, dtype=torch.float32, device=lhs.device)
+    res = _out(out, (m, n), torch.float32, lhs.device)
     _native.call("lmoe_ragged_dot_f32", _ptr(lhs), _ptr(rhs), _ptr(gs), _ptr(res), m, k, n, g,
                  layout, _ptr(status), _stream())
     return res
@@ -128,7 +143,7 @@ def ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tensor, 
   out_dtype = preferred_element_type or torch.bfloat16
   if out_dtype not in (torch.bfloat16, torch.float32):
     raise NotImplementedError(f"preferred_element_type={out_dtype}")
-  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, n), out_dtype, lhs.device)
   _native.call("lmoe_ragged_dot_bf16", _ptr(lhs), _ptr(rhs), _ptr(gs), _ptr(res), m, k, n, g,
                layout, int(out_dtype == torch.float32), int(zero_tail), _ptr(status),
                _stream())
@@ -146,7 +161,7 @@ def gemm(lhs: torch.Tensor, rhs: torch.Tensor, *, addend: torch.Tensor | None = 
   layout = {"kn": 0, "nk": 1}[rhs_layout]
   m, k = lhs.shape
   n = rhs.shape[1] if layout == 0 else rhs.shape[0]
-  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, n), out_dtype, lhs.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
   _native.call("lmoe_gemm_bf16", _ptr(lhs), _ptr(rhs), _ptr(addend), _ptr(res), m, k, n, layout,
                code, _ptr(device_status(lhs.device)), _stream())
@@ -187,7 +202,7 @@ def fused_gateup_situ(lhs: torch.Tensor, w_gateup: torch.Tensor, group_sizes: to
     raise ValueError("group_sizes must have one entry per weight group")
   gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
   ri = None if row_index is None else row_index.to(torch.int32).contiguous()
-  res = out if out is not None else torch.empty(m, inter, dtype=torch.bfloat16, device=lhs.device)
+  res = _out(out, (m, inter), torch.bfloat16, lhs.device)
   _native.call("lmoe_gateup_situ_bf16", _ptr(lhs.contiguous()), _ptr(w.contiguous()), _ptr(gs),
                _ptr(res), m, k, inter, g, layout, float(beta), float(linear_beta),
                int(round_gate_up), _ptr(ri), src_rows, int(zero_tail),
@@ -238,7 +253,7 @@ def mxfp4_ragged_dot(lhs: torch.Tensor, w: MXFP4Weights, group_sizes: torch.Tens
   if lhs_f16 and not w.f16_operand_ok:
     raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
   out_dtype = preferred_element_type or torch.bfloat16
-  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, n), out_dtype, lhs.device)
   _native.call("lmoe_mxfp4_ragged_dot", _ptr(lhs.contiguous()), _ptr(w.packed), _ptr(w.scale),
                _ptr(group_sizes.to(torch.int32).contiguous()), _ptr(res), m, k, n, g,
                int(lhs_f16), int(out_dtype == torch.float32), int(zero_tail),
@@ -286,7 +301,7 @@ def mxfp4_fused_gateup_situ(lhs: torch.Tensor, w_gateup: MXFP4Weights,
     raise NotImplementedError("f16 lhs needs MXFP4 scale bytes in [104, 140]")
   gs = None if group_sizes is None else group_sizes.to(torch.int32).contiguous()
   ri = None if row_index is None else row_index.to(torch.int32).contiguous()
-  res = out if out is not None else torch.empty(m, inter, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, inter), out_dtype, lhs.device)
   _native.call("lmoe_mxfp4_gateup_situ", _ptr(lhs.contiguous()), _ptr(w_gateup.packed),
                _ptr(w_gateup.scale), _ptr(gs), _ptr(res), m, k, inter, g, float(beta),
                float(linear_beta), int(round_gate_up), int(lhs_f16),
@@ -319,7 +334,7 @@ def fp8_ragged_dot(lhs: torch.Tensor, rhs: torch.Tensor, group_sizes: torch.Tens
     raise NotImplementedError("rhs_scale must be float32")
   block = k // scale.shape[1]
   out_dtype = preferred_element_type or torch.bfloat16
-  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, n), out_dtype, lhs.device)
   _native.call("lmoe_fp8_ragged_dot", _ptr(lhs.contiguous()), _ptr(rhs.contiguous()),
                _ptr(scale.contiguous()), _ptr(group_sizes.to(torch.int32).contiguous()),
                _ptr(res), m, k, n, g, block, int(res.dtype == torch.float32), int(zero_tail),
@@ -522,7 +537,7 @@ def gather_rows(x: torch.Tensor, token_idx: torch.Tensor, out: torch.Tensor | No
   if to_f16 and x.dtype != torch.bfloat16:
     raise ValueError("to_f16 converts bf16 rows")
   dt = torch.float16 if to_f16 else x.dtype
-  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=dt, device=x.device)
+  res = _out(out, (rows, x.shape[1]), dt, x.device)
   _native.call("lmoe_gather_rows", _ptr(x), x.shape[0], _ptr(token_idx.to(torch.int32)),
                _ptr(res), rows, x.shape[1] * x.element_size(), int(to_f16),
                _ptr(device_status(x.device)), _stream())
@@ -543,7 +558,7 @@ def scatter_rows(x: torch.Tensor, slot_pos: torch.Tensor, top_k: int, out_rows: 
   if to_f16 and x.dtype != torch.bfloat16:
     raise ValueError("to_f16 converts bf16 rows")
   dt = torch.float16 if to_f16 else x.dtype
-  res = out if out is not None else torch.empty(rows, x.shape[1], dtype=dt, device=x.device)
+  res = _out(out, (rows, x.shape[1]), dt, x.device)
   _native.call("lmoe_scatter_rows", _ptr(x), _ptr(slot_pos.to(torch.int32).contiguous()), t, top_k,
                _ptr(res), res.shape[0], x.shape[1] * x.element_size(), int(to_f16),
                _ptr(device_status(x.device)), _stream())
@@ -693,14 +708,29 @@ def _mx_rows(fmt: str, m_pad: int, k: int, group_sizes: torch.Tensor, device):
              group_sizes)
 
 
+def _check_mx_rows(out, fmt: str, m_pad: int, k: int):
+  """A caller's block-scaled row buffer must be the one _mx_rows(fmt, m_pad,
+  k, ...) would allocate (codes and scale atoms of exactly those shapes), so
+  no kernel writes past it."""
+  cls, k_per_byte, _, _ = _MX_FORMATS[fmt]
+  planes = (2,) if cls is SplitRows else ()
+  want_q, want_sf = (*planes, m_pad, k // k_per_byte), (k // 128, m_pad // 128, 512)
+  if (type(out) is not cls or tuple(out.q.shape) != want_q or tuple(out.sf.shape) != want_sf or
+      not out.q.is_contiguous() or not out.sf.is_contiguous()):
+    raise ValueError(f"out: expected {cls.__name__} with codes {want_q} and scale atoms {want_sf}, "
+                     f"got {type(out).__name__} {tuple(out.q.shape)} / {tuple(out.sf.shape)}")
+
+
 def _quantize_rows(fmt, x, group_sizes, token_idx, padded_input, out):
   _need_cuda(x, group_sizes, token_idx)
   rows = token_idx.shape[0] if token_idx is not None else x.shape[0]
   k = x.shape[1]
   g = group_sizes.shape[0]
+  m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
   if out is None:
-    m_pad = x.shape[0] if padded_input else mxfp8_padded_rows(rows, g)
     out = _mx_rows(fmt, m_pad, k, group_sizes, x.device)
+  else:
+    _check_mx_rows(out, fmt, m_pad, k)
   gs = group_sizes.to(torch.int32).contiguous()
   out.group_sizes = gs
   ti = None if token_idx is None else token_idx.to(torch.int32).contiguous()
@@ -717,6 +747,8 @@ def _quantize_scatter(fmt, x, group_sizes, slot_pos, top_k, out):
   g = group_sizes.shape[0]
   if out is None:
     out = _mx_rows(fmt, mxfp8_padded_rows(t * top_k, g), k, group_sizes, x.device)
+  else:
+    _check_mx_rows(out, fmt, mxfp8_padded_rows(t * top_k, g), k)
   gs = group_sizes.to(torch.int32).contiguous()
   out.group_sizes = gs
   _native.call(_MX_FORMATS[fmt][3], _ptr(x.contiguous()), int(x.dtype == torch.float16),
@@ -814,7 +846,7 @@ def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockSc
   if w.gateup:
     raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
   m_pad = a.q.shape[-2]
-  res = out if out is not None else torch.empty(m_pad, n, dtype=out_dtype, device=a.q.device)
+  res = _out(out, (m_pad, n), out_dtype, a.q.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
   _mx_gemm(a, w, res, m_pad, k, n, g, 0, 0.0, 0.0, 0, code)
   return res
@@ -830,8 +862,7 @@ def mxfp8_mxfp4_gateup_situ(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockS
   if not w.gateup:
     raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
   m_pad = a.q.shape[-2]
-  res = out if out is not None else torch.empty(m_pad, two_i // 2, dtype=out_dtype,
-                                                device=a.q.device)
+  res = _out(out, (m_pad, two_i // 2), out_dtype, a.q.device)
   code = {torch.bfloat16: 0, torch.float16: 2}[res.dtype]
   _mx_gemm(a, w, res, m_pad, k, two_i // 2, g, 3, beta, linear_beta, round_gate_up, code)
   return res
@@ -853,7 +884,7 @@ def mxfp4_ragged_dot_blockscaled(lhs: torch.Tensor, w: MXFP4BlockScaled,
     raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
   m = lhs.shape[0]
   a = quantize_split_rows(lhs, group_sizes, out=rows)
-  res = out if out is not None else torch.empty(m, n, dtype=out_dtype, device=lhs.device)
+  res = _out(out, (m, n), out_dtype, lhs.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
   if m > 0:
     _mx_gemm(a, w, res, a.q.shape[-2], k, n, g, 0, 0.0, 0.0, 0, code, m_out=m)
@@ -875,7 +906,11 @@ def blockscaled_gateup_situ_quantized(a: MXFP8Rows | MXFP4Rows | SplitRows, w: M
   if not w.gateup:
     raise ValueError("prepare the fused weight with prepare_mxfp4_blockscaled(..., gateup=True)")
   m_pad = a.q.shape[-2]
-  res = out if out is not None else _mx_rows(fmt, m_pad, two_i // 2, a.group_sizes, a.q.device)
+  if out is None:
+    res = _mx_rows(fmt, m_pad, two_i // 2, a.group_sizes, a.q.device)
+  else:
+    _check_mx_rows(out, fmt, m_pad, two_i // 2)
+    res = out
   res.group_sizes = a.group_sizes
   _native.call("lmoe_blockscaled_gateup_situ_quantized", _ptr(a.q), _ptr(a.sf),
                _ROWS_KIND[type(a)], _ptr(w.packed), _ptr(w.sf), _ptr(a.group_sizes), m_pad, k,
