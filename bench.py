@@ -672,26 +672,33 @@ def gpu_mxfp8_extras(args, lm, ops, pw, cfg, h, dev, peaks, peak_src) -> dict:
 
 def gpu_token_sweep(args, lm, pw, cfg, dev, tokens=(128, 1024, 4096)) -> dict:
   """Configuration 5 at smaller token counts (one GPU, CUDA-graph replay):
-  the default forward (the exact product on the block-scaled tensor core),
-  and the weights-major f16-operand kernels (mxfp4_operand="f16") as
-  `f16_ms`."""
+  the default forward (the exact product on the block-scaled tensor core,
+  and at token counts whose dense projections would not fill the SMs, the
+  split-K phase kernels for them), the weights-major f16-operand kernels
+  (mxfp4_operand="f16") as `f16_ms`, and, where the default takes the phase
+  kernels, the same forward without them as `no_dense_phases_ms`."""
   import torch
   out = {}
   for t in tokens:
     gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + t)
     h = torch.randn(t, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
+    variants = {"auto": {}, "f16": {"mxfp4_operand": "f16"}}
+    if lm.latent_moe._use_dense_phases(None, pw, cfg, t, h, torch.bfloat16, False):
+      variants["no_dense_phases"] = {"dense_phases": False}
     res = {}
-    for mode in ("auto", "f16"):
+    for name, kw in variants.items():
       for _ in range(2):
-        lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
+        lm.latent_moe_forward(h, pw, cfg, **kw)
       torch.cuda.synchronize()
       graph = torch.cuda.CUDAGraph()
       with torch.cuda.graph(graph):
-        lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode)
-      res[mode] = time_launches(graph.replay, max(5, args.steps))
+        lm.latent_moe_forward(h, pw, cfg, **kw)
+      res[name] = time_launches(graph.replay, max(5, args.steps))
       del graph
     out[f"T{t}"] = {"ms": res["auto"], "tokens_per_s": t / (res["auto"] / 1e3),
                     "f16_ms": res["f16"]}
+    if "no_dense_phases" in res:
+      out[f"T{t}"]["no_dense_phases_ms"] = res["no_dense_phases"]
   return out
 
 

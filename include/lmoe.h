@@ -214,6 +214,59 @@ LMOE_API int lmoe_router_fused_bf16(const void* hidden, const void* router_weigh
                            int32_t* topk_idx, float* topk_w, void* workspace,
                            size_t workspace_bytes, int32_t* dev_status, void* stream);
 
+/* Workspace bytes lmoe_dense_input_phase needs (0 for unsupported shapes). */
+LMOE_API size_t lmoe_dense_input_workspace_size(int64_t num_tokens, int64_t hidden_size,
+                                                int64_t num_experts, int64_t latent_size,
+                                                int64_t shared_intermediate);
+
+/* The input phase of the layer for small token counts, one persistent split-K
+ * kernel: the three projections of the hidden states in one launch --
+ *   logits     = h @ W_router^T                       (T, E) f32
+ *   latent_out = bf16(h @ W_down^T)                   (T, L) bf16
+ *   shared_act = bf16(situ(bf16(h @ W_g^T), bf16(h @ W_u^T)))   (T, Is) bf16
+ *                (round_gate_up 0: g and u unrounded)
+ * with the SiTU-GLU of lmoe_gateup_situ_bf16 (beta, linear_beta).  hidden
+ * (T, d) bf16; router_w (E, d), down_w (L, d) and shared_gu_w (2*Is, d) =
+ * [gate rows | up rows] are bf16 with d contiguous (the nn.Linear layout).
+ * The K steps of each 128-column tile are split over the SMs (a split count
+ * that depends on the weight shapes and the SM count, not on T, so each
+ * token's result is independent of T); the CTA that finishes a tile's last
+ * split sums the f32 partials in split order.  d % 64 == 0, E % 4 == 0,
+ * L and Is % 8 == 0, 16-byte aligned pointers (LMOE_UNSUPPORTED otherwise).
+ * workspace: device scratch of lmoe_dense_input_workspace_size bytes,
+ * 256-byte aligned (LMOE_SCRATCH_TOO_SMALL otherwise); calls that share a
+ * workspace must not overlap on the GPU.  Replaces the router gate, the
+ * down-projection and the shared expert's gate/up of latent_moe_forward
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:347-365, 428-433). */
+LMOE_API int lmoe_dense_input_phase(const void* hidden, const void* router_w, const void* down_w,
+                                    const void* shared_gu_w, float* logits, void* latent_out,
+                                    void* shared_act, int64_t num_tokens, int64_t hidden_size,
+                                    int64_t num_experts, int64_t latent_size,
+                                    int64_t shared_intermediate, float beta, float linear_beta,
+                                    int round_gate_up, void* workspace, size_t workspace_bytes,
+                                    int32_t* dev_status, void* stream);
+
+/* Workspace bytes lmoe_dense_output_phase needs (0 for unsupported shapes). */
+LMOE_API size_t lmoe_dense_output_workspace_size(int64_t num_tokens, int64_t latent_size,
+                                                 int64_t shared_intermediate, int64_t hidden_size);
+
+/* The output phase of the layer for small token counts, one persistent split-K
+ * kernel over two K segments:
+ *   out = bf16(normed @ W_up^T + shared_act @ W_sd^T)       (T, d) bf16
+ * i.e. the up-projection, the shared expert's down projection and the output
+ * sum with one rounding of the f32 sum (the reference rounds each branch to
+ * bf16 before adding: the results differ by at most about one bf16 spacing of
+ * the output).  normed (T, L), shared_act (T, Is) bf16; up_w (d, L) and
+ * shared_down_w (d, Is) bf16 with K contiguous.  L and Is % 64 == 0,
+ * d % 8 == 0, 16-byte aligned pointers; workspace as for the input phase.
+ * Replaces the up-projection, the shared expert's output and the sum of
+ * latent_moe_forward (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:419-435). */
+LMOE_API int lmoe_dense_output_phase(const void* normed, const void* up_w, const void* shared_act,
+                                     const void* shared_down_w, void* out, int64_t num_tokens,
+                                     int64_t latent_size, int64_t shared_intermediate,
+                                     int64_t hidden_size, void* workspace, size_t workspace_bytes,
+                                     int32_t* dev_status, void* stream);
+
 /* Workspace bytes lmoe_dispatch needs for max(num_tokens*top_k, m_out) entries. */
 LMOE_API size_t lmoe_dispatch_workspace_size(int64_t num_entries, int64_t num_local_experts);
 

@@ -206,11 +206,12 @@ def test_layer_split_mode_matches_the_exact_forward(lm):
   st = torch.cuda.Stream()
   st.wait_stream(torch.cuda.current_stream())
   with torch.cuda.stream(st):
-    lm.latent_moe_forward(static_h, pw, cfg, mxfp4_operand="split")
+    lm.latent_moe_forward(static_h, pw, cfg, mxfp4_operand="split", dense_phases=False)
   torch.cuda.current_stream().wait_stream(st)
   graph = torch.cuda.CUDAGraph()
   with torch.cuda.graph(graph):
-    out = lm.latent_moe_forward(static_h, pw, cfg, mxfp4_operand="split")
+    # the forward with intermediates runs the dense projections unfused
+    out = lm.latent_moe_forward(static_h, pw, cfg, mxfp4_operand="split", dense_phases=False)
   graph.replay()
   torch.cuda.synchronize()
   assert torch.equal(out, final)

@@ -100,6 +100,12 @@ SIGNATURES = {
     "lmoe_ep_dispatch_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64, _p,
                                     _p]),
     "lmoe_ep_return_put": (_i32, [_p, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64, _p, _p]),
+    "lmoe_dense_input_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "lmoe_dense_input_phase": (_i32, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                      _f32, _f32, _i32, _p, _sz, _p, _p]),
+    "lmoe_dense_output_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "lmoe_dense_output_phase": (_i32, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _sz, _p,
+                                       _p]),
 }
 
 # kernels launched by one call of each entry point (for the bench's launch count)

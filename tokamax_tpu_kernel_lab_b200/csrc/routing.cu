@@ -156,12 +156,112 @@ __global__ void __launch_bounds__(256, 3) router_topk_kernel(
   }
 }
 
+// The same selection for few tokens (sigmoid scores): one 256-thread CTA
+// per token instead of one warp, so a token's k rounds run on 256 lanes
+// (E <= 1024: at most 4 experts per thread, expert threadIdx.x + 256 j).
+// Each round every thread offers its best remaining (key, id), the warps
+// reduce them with the same order-preserving unsigned max / lowest-id min as
+// router_topk_kernel, and the eight warp winners meet in shared memory.  The
+// winners, their order and the weight arithmetic (scores summed in selection
+// order by one thread, w / (sum + 1e-20) when k > 1 and renormalize, times
+// rsf) equal router_topk_kernel's, bit for bit; with one warp per token that
+// kernel runs its k rounds serially per token, which at a few hundred tokens
+// leaves most SMs idle and takes ~20 us.
+constexpr int kTopkBlockThreads = 256;
+constexpr int64_t kTopkBlockMaxTokens = 1024;
+
+__global__ void __launch_bounds__(kTopkBlockThreads) router_topk_block_kernel(
+    const float* __restrict__ logits, const float* __restrict__ bias, int E, int k,
+    int renormalize, float rsf, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
+  __shared__ uint32_t s_key[kTopkBlockThreads / 32];
+  __shared__ int s_id[kTopkBlockThreads / 32];
+  __shared__ float s_score[32];
+  __shared__ int s_win[32];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const float* row = logits + static_cast<int64_t>(blockIdx.x) * E;
+  float key[4], sc[4];
+  bool live[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int e = tid + kTopkBlockThreads * j;
+    live[j] = e < E;
+    sc[j] = live[j] ? router_sigmoid(row[e]) : 0.f;
+    key[j] = live[j] ? sc[j] + (bias ? bias[e] : 0.f) : -FLT_MAX;
+    live[j] = live[j] && key[j] == key[j];  // a NaN key never wins
+  }
+  for (int s = 0; s < k; ++s) {
+    // this thread's best remaining entry (ids increase with j)
+    float bv = -FLT_MAX;
+    int be = INT_MAX;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (live[j] && sel_before(key[j], tid + kTopkBlockThreads * j, bv, be)) {
+        bv = key[j];
+        be = tid + kTopkBlockThreads * j;
+      }
+    const uint32_t fb = __float_as_uint(bv);
+    const uint32_t ku = fb ^ ((fb & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, ku);
+    const uint32_t emin =
+        __reduce_min_sync(0xffffffffu, ku == kmax ? static_cast<uint32_t>(be) : 0xFFFFFFFFu);
+    if (lane == 0) {
+      s_key[warp] = kmax;
+      s_id[warp] = static_cast<int>(emin);
+    }
+    __syncthreads();
+    uint32_t wk = s_key[0];
+    int we = s_id[0];
+#pragma unroll
+    for (int w = 1; w < kTopkBlockThreads / 32; ++w) {
+      const uint32_t kw = s_key[w];
+      const int ew = s_id[w];
+      if (kw > wk || (kw == wk && ew < we)) {
+        wk = kw;
+        we = ew;
+      }
+    }
+    if (we == INT_MAX && tid == 0) {  // fewer than k selectable experts (NaN keys)
+      s_score[s] = 0.f;
+      s_win[s] = -1;
+    }
+    if (we % kTopkBlockThreads == tid && we != INT_MAX) {
+      const int j = we / kTopkBlockThreads;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        if (jj == j) {
+          live[jj] = false;
+          s_score[s] = sc[jj];
+        }
+      s_win[s] = we;
+    }
+    __syncthreads();  // s_key/s_id are rewritten next round; s_score/s_win are complete
+  }
+  if (tid == 0) {
+    float wsum = 0.f;
+    for (int s = 0; s < k; ++s) wsum += s_score[s];
+    for (int s = 0; s < k; ++s) {
+      float w = s_score[s];
+      if (k > 1 && renormalize) w = w / (wsum + 1e-20f);
+      w = w * rsf;
+      topk_idx[static_cast<int64_t>(blockIdx.x) * k + s] = s_win[s];
+      topk_w[static_cast<int64_t>(blockIdx.x) * k + s] = w;
+    }
+  }
+}
+
 int router_topk(const float* logits, const float* bias, int64_t T, int64_t E, int64_t k,
                 int activation, int renormalize, float rsf, int32_t* topk_idx, float* topk_w,
                 cudaStream_t stream) {
   if (T < 0 || E <= 0 || E > 1024 || k <= 0 || k > 32 || k > E) return kBadShape;
   if (activation != 0 && activation != 1) return kBadShape;
   if (T == 0) return kOk;
+  if (activation == 0 && T <= kTopkBlockMaxTokens) {
+    router_topk_block_kernel<<<static_cast<int>(T), kTopkBlockThreads, 0, stream>>>(
+        logits, bias, static_cast<int>(E), static_cast<int>(k), renormalize, rsf, topk_idx,
+        topk_w);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  }
   const int threads = 256;
   const int blocks = static_cast<int>((T * 32 + threads - 1) / threads);
   const int per = static_cast<int>((E + 31) / 32);

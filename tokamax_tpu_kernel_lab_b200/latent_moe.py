@@ -227,7 +227,7 @@ def prepare_weights(w: LatentMoEWeights, dtype: torch.dtype | None = None) -> Pr
 def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoEConfig, *,
                        router_activation: str = "sigmoid",
                        return_intermediates: bool = False, mxfp4_operand: str = "auto",
-                       mark=None):
+                       dense_phases: bool | None = None, mark=None):
   """The 8-step LatentMoE forward (kimi_k3_latent_moe_reference.py:330-435).
   `weights` is a LatentMoEWeights (prepared on the fly) or PreparedWeights.
 
@@ -253,6 +253,17 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   and runs kind::mxf4, at twice the MMA rate and a larger error (~10%
   normwise).
 
+  dense_phases (bf16 dense weights with a shared expert): the dense
+  projections run as two persistent split-K kernels, one per phase -- the
+  router logits, the down-projection and the shared expert's gate/up in one
+  launch over the hidden states (then the top-k from the logits), the
+  up-projection, the shared expert's down projection and the output sum in
+  another (the sum of the two branches rounded once to bf16 instead of each
+  branch first: within about one bf16 spacing of the output).  None (the
+  default) takes them when their output tiles would not fill the SMs (a few
+  hundred tokens or fewer on one GPU); False never; True whenever the shapes
+  allow.  Not with return_intermediates.
+
   `mark(name)` (optional) is called on the host after each phase of the main
   stream is enqueued, e.g. to record CUDA events for a phase timeline."""
   mark = mark or (lambda name: None)
@@ -272,9 +283,10 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   # use few SMs as well, and joins before the gather.  With more tokens each
   # of these GEMMs fills the GPU and running them at the same time only slows
   # both (measured: 16384 tokens 5.66 -> 6.12 ms), so they stay in order.
-  overlap = pw.dtype == torch.bfloat16 and not return_intermediates
   mxfp4_operand = resolve_mxfp4_operand(pw, mxfp4_operand)
   x_dtype = torch.float16 if mxfp4_f16_path(pw, mxfp4_operand) else torch.bfloat16
+  phases = _use_dense_phases(dense_phases, pw, c, t, h, x_dtype, return_intermediates)
+  overlap = pw.dtype == torch.bfloat16 and not return_intermediates and not phases
   down_tiles = -(-t // 128) * -(-pw.down.shape[0] // 128)
   overlap_x = overlap and 2 * down_tiles <= torch.cuda.get_device_properties(
       h.device).multi_processor_count
@@ -295,8 +307,14 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
       ops.fused_gateup_situ(h, pw.shared_gu, None, beta=beta, linear_beta=lbeta,
                             round_gate_up=True, rhs_layout="gnk", out=shared_act)
       ops.gemm(shared_act, pw.shared_down, rhs_layout="nk", out=shared_out)
-  if return_intermediates or not ops.router_fused_supported(h, pw.router, c.top_k,
-                                                             router_activation):
+  if phases:
+    logits, x, shared_act = ops.dense_input_phase(h, pw.router, pw.down, pw.shared_gu, beta=beta,
+                                                  linear_beta=lbeta, round_gate_up=True)
+    topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
+                                       routed_scaling_factor=c.routed_scaling_factor,
+                                       activation=router_activation)
+  elif return_intermediates or not ops.router_fused_supported(h, pw.router, c.top_k,
+                                                               router_activation):
     logits = ops.router_logits(h, pw.router)
     topk_idx, topk_w = ops.router_topk(logits, pw.bias, c.top_k, renormalize=c.moe_renormalize,
                                        routed_scaling_factor=c.routed_scaling_factor,
@@ -308,7 +326,7 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                                              renormalize=c.moe_renormalize,
                                              routed_scaling_factor=c.routed_scaling_factor)
   mark("route")
-  if not overlap_x:
+  if not overlap_x and not phases:
     x = _dense(h, pw.down, out_dtype=None if x_dtype == torch.bfloat16 else x_dtype)
     mark("down-projection")
   d = ops.dispatch(topk_idx, topk_w, c.num_experts, want_order=return_intermediates)
@@ -339,6 +357,10 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
   routed, normed = ops.combine_rmsnorm(down, slot_pos, topk_w, pw.norm_scale, c.rms_norm_eps,
                                        want_routed=True)
   mark("combine")
+  if phases:
+    out = ops.dense_output_phase(normed, pw.up, shared_act, pw.shared_down)
+    mark("tail")
+    return out
   if overlap:
     main.wait_stream(side)
     out = _dense(normed, pw.up, addend=shared_out)
@@ -362,6 +384,25 @@ def latent_moe_forward(hidden_states: torch.Tensor, weights, config: LatentMoECo
                  slot_pos=d.slot_pos, token_idx=d.token_idx)
     return final, inter
   return final
+
+
+def _use_dense_phases(dense_phases, pw: "PreparedWeights", c: LatentMoEConfig, t: int, h,
+                      x_dtype, return_intermediates: bool) -> bool:
+  """Whether latent_moe_forward runs the dense projections as the split-K
+  phase kernels (see its `dense_phases` argument)."""
+  if dense_phases is False or return_intermediates or t == 0:
+    return False
+  si = pw.shared_gu.shape[0] // 2 if pw.shared_gu is not None else 0
+  supported = (pw.dtype == torch.bfloat16 and x_dtype == torch.bfloat16 and si > 0 and
+               pw.shared_down is not None and
+               ops._native.load().lmoe_dense_input_workspace_size(
+                   t, c.hidden_size, c.num_experts, pw.down.shape[0], si) > 0 and
+               ops._native.load().lmoe_dense_output_workspace_size(
+                   t, pw.down.shape[0], si, pw.up.shape[0]) > 0)
+  if not supported:
+    return False
+  return dense_phases is True or ops.dense_phases_pay_off(t, c.num_experts, pw.down.shape[0], si,
+                                                          h.device)
 
 
 MXFP4_OPERANDS = ("auto", "split", "f16", "bf16", "mxfp8", "mxfp4")

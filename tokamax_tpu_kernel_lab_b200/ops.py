@@ -457,6 +457,80 @@ def router_gate_fused(hidden_states: torch.Tensor, router_weight_nk: torch.Tenso
   return idx, tw
 
 
+def dense_phases_pay_off(num_tokens: int, num_experts: int, latent_size: int,
+                         shared_intermediate: int, device=None) -> bool:
+  """True when the layer's dense projections should run as the split-K phase
+  kernels: their output tiles (128 tokens x 128 columns) would not fill the
+  SMs, so an ordinary GEMM would leave most of them idle."""
+  sms = torch.cuda.get_device_properties(device).multi_processor_count
+  m_tiles = -(-num_tokens // 128)
+  n_tiles = -(-num_experts // 128) + -(-latent_size // 128) + -(-shared_intermediate // 64)
+  return 0 < m_tiles * n_tiles < sms
+
+
+def dense_input_phase(hidden_states: torch.Tensor, router_weight_nk: torch.Tensor,
+                      down_weight_nk: torch.Tensor, shared_gu_nk: torch.Tensor, *,
+                      beta: float = 4.0, linear_beta: float = 25.0, round_gate_up: bool = True,
+                      workspace: torch.Tensor | None = None):
+  """The layer's input phase in one persistent split-K kernel
+  (kimi_k3_latent_moe_reference.py:347-365, 428-433): router logits
+  h @ Wr^T (f32), the latent rows bf16(h @ Wd^T) and the shared expert's
+  SiTU-GLU activation from the fused [gate | up] weight (2 Is, d).  Weights
+  are (N, K) with K contiguous.  Returns (logits, latent, shared_act)."""
+  _need_cuda(hidden_states, router_weight_nk, down_weight_nk, shared_gu_nk)
+  h = hidden_states.contiguous()
+  if h.dtype != torch.bfloat16:
+    raise NotImplementedError("the dense phase kernels take bf16 hidden states")
+  t, d = h.shape
+  e, latent, si = router_weight_nk.shape[0], down_weight_nk.shape[0], shared_gu_nk.shape[0] // 2
+  for w in (router_weight_nk, down_weight_nk, shared_gu_nk):
+    if w.dim() != 2 or w.shape[1] != d or w.dtype != torch.bfloat16:
+      raise ValueError("weights must be bf16 (N, d) matrices")
+  logits = torch.empty(t, e, dtype=torch.float32, device=h.device)
+  x = torch.empty(t, latent, dtype=torch.bfloat16, device=h.device)
+  act = torch.empty(t, si, dtype=torch.bfloat16, device=h.device)
+  ws = int(_native.load().lmoe_dense_input_workspace_size(t, d, e, latent, si))
+  if ws == 0:
+    raise NotImplementedError(f"dense input phase: unsupported shape t={t} d={d} e={e} "
+                              f"latent={latent} shared={si}")
+  if workspace is None or workspace.numel() < ws:
+    workspace = torch.empty(ws, dtype=torch.uint8, device=h.device)
+  _native.call("lmoe_dense_input_phase", _ptr(h), _ptr(router_weight_nk.contiguous()),
+               _ptr(down_weight_nk.contiguous()), _ptr(shared_gu_nk.contiguous()), _ptr(logits),
+               _ptr(x), _ptr(act), t, d, e, latent, si, float(beta), float(linear_beta),
+               int(round_gate_up), _ptr(workspace), workspace.numel(),
+               _ptr(device_status(h.device)), _stream())
+  return logits, x, act
+
+
+def dense_output_phase(normed: torch.Tensor, up_weight_nk: torch.Tensor, shared_act: torch.Tensor,
+                       shared_down_nk: torch.Tensor, *, workspace: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+  """The layer's output phase in one persistent split-K kernel
+  (kimi_k3_latent_moe_reference.py:419-435): bf16(normed @ Wup^T +
+  shared_act @ Wsd^T), the up-projection, the shared expert's down
+  projection and the output sum, the f32 sum rounded once."""
+  _need_cuda(normed, up_weight_nk, shared_act, shared_down_nk)
+  a0, a1 = normed.contiguous(), shared_act.contiguous()
+  t, latent = a0.shape
+  si = a1.shape[1]
+  d = up_weight_nk.shape[0]
+  if (a1.shape[0] != t or up_weight_nk.shape != (d, latent) or
+      tuple(shared_down_nk.shape) != (d, si)):
+    raise ValueError("shape mismatch in the dense output phase")
+  res = _out(out, (t, d), torch.bfloat16, a0.device)
+  ws = int(_native.load().lmoe_dense_output_workspace_size(t, latent, si, d))
+  if ws == 0:
+    raise NotImplementedError(f"dense output phase: unsupported shape t={t} latent={latent} "
+                              f"shared={si} d={d}")
+  if workspace is None or workspace.numel() < ws:
+    workspace = torch.empty(ws, dtype=torch.uint8, device=a0.device)
+  _native.call("lmoe_dense_output_phase", _ptr(a0), _ptr(up_weight_nk.contiguous()), _ptr(a1),
+               _ptr(shared_down_nk.contiguous()), _ptr(res), t, latent, si, d, _ptr(workspace),
+               workspace.numel(), _ptr(device_status(a0.device)), _stream())
+  return res
+
+
 def router_gate(hidden_states, router_weight_nk, bias, top_k, *, renormalize=True,
                 routed_scaling_factor=1.0, activation="sigmoid", fused: bool | None = None):
   """(topk_idx, topk_weight f32) on the original hidden states.  fused=None
