@@ -574,7 +574,10 @@ LMOE_API int lmoe_blockscaled_gateup_situ_quantized(const void* act_q, const voi
  * lmoe_mxfp8_mxfp4_grouped_gemm, plus m_out: 0 writes the padded rows (out
  * has m_pad rows); m_out > 0 writes row r of group g at its unpadded position
  * (the sum of the earlier groups' sizes + r; out has m_out rows, those at or
- * past sum(group_sizes) are zeroed) -- the ragged_dot output layout. */
+ * past sum(group_sizes) are zeroed) -- the ragged_dot output layout.  m_out < 0:
+ * the same with -m_out rows and the rows past sum(group_sizes) left
+ * unwritten (an output sized by capacity, such as an expert-parallel receive
+ * region). */
 LMOE_API int lmoe_bf16split_mxfp4_grouped_gemm(const void* act_q, const void* act_sf,
                                                const void* w_packed, const void* w_sf,
                                                const int32_t* group_sizes, void* out,

@@ -80,8 +80,11 @@ def test_mxf4_gemm_checks_k_before_any_launch():
 
 
 def test_split_gemm_checks_m_out_before_any_launch():
+  """|m_out| must fit 31 bits (m_out < 0 asks for the unpadded layout without
+  zeroing the rows past sum(group_sizes))."""
   from tokamax_tpu_kernel_lab_b200 import _native
   lib = _native.load()
-  rc = lib.lmoe_bf16split_mxfp4_grouped_gemm(None, None, None, None, None, None, 128, 256, 128, 1,
-                                             0, 0.0, 0.0, 0, 0, -1, None, None)
-  assert rc == _native.LMOE_BAD_SHAPE
+  for m_out in (1 << 31, -(1 << 31)):
+    rc = lib.lmoe_bf16split_mxfp4_grouped_gemm(None, None, None, None, None, None, 128, 256, 128,
+                                               1, 0, 0.0, 0.0, 0, 0, m_out, None, None)
+    assert rc == _native.LMOE_BAD_SHAPE

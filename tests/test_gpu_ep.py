@@ -70,13 +70,22 @@ def _worker(rank, world, port, results, mode="nccl"):
         torch.cuda.synchronize()
         lm.check_device_status()
         del graph
+        # the routed experts on the block-scaled tensor core (split rows)
+        split = GpuBackend(pw, cfg, mxfp4_operand="split")
+        outs_split = [ep_forward_peer(x[rank * t:(rank + 1) * t].contiguous(), split, cfg, xchg)
+                      for x in hs[:2]]
+        torch.cuda.synchronize()
+        lm.check_device_status()
       finally:
         xchg.close()
-      results[rank] = [o.cpu() for o in outs] + [o.cpu() for o in replays]
+      results[rank] = ([o.cpu() for o in outs] + [o.cpu() for o in replays] +
+                       [o.cpu() for o in outs_split])
       if rank == 0:
         full = lm.init_prepared_mxfp4(cfg, seed=21, device=dev, bias_std=0.5)
         results["ref"] = [lm.latent_moe_forward(x, full, cfg, mxfp4_operand="f16").cpu()
                           for x in hs]
+        results["ref_split"] = [lm.latent_moe_forward(x, full, cfg, mxfp4_operand="split",
+                                                      dense_phases=False).cpu() for x in hs[:2]]
       dist.barrier()
       return
     stats = EPStats([], [])
@@ -116,7 +125,8 @@ def test_ep_forward_peer_bit_exact_vs_single_gpu(world):
   mgr = mp.get_context("spawn").Manager()
   results = mgr.dict()
   mp.spawn(_worker, args=(world, _free_port(), results, "peer"), nprocs=world, join=True)
-  refs = list(results["ref"]) + list(results["ref"])[:2]  # eager x3, then graph replays x2
+  # eager x3, graph replays x2 (fused return), then the split-row experts x2
+  refs = list(results["ref"]) + list(results["ref"])[:2] + list(results["ref_split"])
   for i, ref in enumerate(refs):
     got = torch.cat([results[r][i] for r in range(world)])
     assert torch.equal(got, ref), f"forward {i}"

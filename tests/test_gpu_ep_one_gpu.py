@@ -143,8 +143,12 @@ def emulated_forward(lm, ranks, backends, hs, cfg, epoch, fused_return):
 
 
 @pytest.mark.parametrize("world", [2, 4])
-@pytest.mark.parametrize("fused_return", [False, True])
-def test_peer_exchange_emulated_ranks_bit_exact(lm, world, fused_return):
+@pytest.mark.parametrize("fused_return,mode", [(False, "f16"), (True, "f16"), (False, "split")])
+def test_peer_exchange_emulated_ranks_bit_exact(lm, world, fused_return, mode):
+  """Both expert forms: the weights-major f16-operand kernels (with and
+  without the fused return) and the block-scaled kernels on split rows, each
+  bit-exact against the one-GPU forward in the same mode (its dense
+  projections as separate GEMMs, as the expert-parallel path runs them)."""
   from tokamax_tpu_kernel_lab_b200.expert_parallel import GpuBackend, shard_experts
   cfg = lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
   pw = lm.init_prepared_mxfp4(cfg, seed=23, bias_std=0.5)
@@ -154,10 +158,11 @@ def test_peer_exchange_emulated_ranks_bit_exact(lm, world, fused_return):
   nbytes = buffer_bytes(lm, cfg, world, t_local)
   bufs = [torch.zeros(nbytes, dtype=torch.uint8, device="cuda") for _ in range(world)]
   ranks = [EmulatedRank(lm, cfg, r, world, t_local, bufs) for r in range(world)]
-  backends = [GpuBackend(shard_experts(pw, r, world), cfg) for r in range(world)]
+  backends = [GpuBackend(shard_experts(pw, r, world), cfg, mxfp4_operand=mode)
+              for r in range(world)]
   for epoch in (1, 2):
     h = torch.randn(t, cfg.hidden_size, generator=gen, device="cuda").to(torch.bfloat16)
-    ref = lm.latent_moe_forward(h, pw, cfg, mxfp4_operand="f16")
+    ref = lm.latent_moe_forward(h, pw, cfg, mxfp4_operand=mode, dense_phases=False)
     hs = [h[r * t_local:(r + 1) * t_local].contiguous() for r in range(world)]
     out = emulated_forward(lm, ranks, backends, hs, cfg, epoch, fused_return)
     torch.cuda.synchronize()

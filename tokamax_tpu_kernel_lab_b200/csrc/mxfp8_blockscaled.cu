@@ -216,6 +216,7 @@ struct MxArgs {
   int round_gate_up;
   int out_f16;
   int m_out;  // 0: output rows at the padded positions; > 0: unpadded, m_out rows
+  int zero_tail;  // unpadded output: rows at or past sum(group_sizes) are zeroed
   // EPI_SITU only: with q_out set, the activations are written quantised for
   // the next block-scaled GEMM instead of to `out` -- format q_fmt (MX_E4M3,
   // MX_E2M1 or MX_E4M3_SPLIT) at the same padded rows, scale atoms to q_sf
@@ -824,7 +825,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     }
     // unpadded output: rows at or past sum(group_sizes) are zero (ragged_dot
     // semantics), written by the epilogue warps of all CTAs
-    if (args.m_out > 0) {
+    if (args.m_out > 0 && args.zero_tail) {
       const int64_t row_bytes = static_cast<int64_t>(args.N) * esize;
       const int64_t chunks_per_row = row_bytes / 16;
       const int64_t first = row_src[G];
@@ -1184,7 +1185,11 @@ int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
       ((reinterpret_cast<uintptr_t>(act_q) | reinterpret_cast<uintptr_t>(out) |
         reinterpret_cast<uintptr_t>(act_sf) | reinterpret_cast<uintptr_t>(w_sf)) & 15))
     return LMOE_UNSUPPORTED;
-  if (m_out < 0 || m_out >= (1ll << 31)) return LMOE_BAD_SHAPE;
+  // m_out < 0: unpadded output of -m_out rows whose tail past sum(group_sizes)
+  // is left as it is (a buffer sized by capacity)
+  const bool zero_tail = m_out > 0;
+  if (m_out < 0) m_out = -m_out;
+  if (m_out >= (1ll << 31)) return LMOE_BAD_SHAPE;
   if (q_out != nullptr) {
     // quantised SiTU output: padded rows, bf16 values, the next GEMM's K
     // (the intermediate size) a multiple of 128 (of 256 for e2m1)
@@ -1198,6 +1203,7 @@ int mx_grouped_gemm(const void* act_q, const void* act_sf, const void* w_packed,
   if (m_pad >= (1ll << 31) || k >= (1 << 20)) return LMOE_BAD_SHAPE;
   MxArgs a{};
   a.m_out = static_cast<int>(m_out);
+  a.zero_tail = zero_tail ? 1 : 0;
   a.q_out = static_cast<uint8_t*>(q_out);
   a.q_sf = static_cast<uint8_t*>(q_sf);
   a.q_fmt = q_fmt;

@@ -43,14 +43,25 @@ import torch
 import torch.distributed as dist
 
 from . import _native, ops
-from .latent_moe import LatentMoEConfig, PreparedWeights, _dense, mxfp4_f16_path
+from .latent_moe import (LatentMoEConfig, PreparedWeights, _dense, blockscaled_experts,
+                         mxfp4_f16_path)
 
 
 class GpuBackend:
-  """The sm_100a kernels."""
+  """The sm_100a kernels.  mxfp4_operand (MXFP4 experts): "f16" runs the
+  routed experts on the weights-major kernels with f16 operands (bf16 when
+  the weight scales do not allow f16), "split" on the block-scaled tensor
+  core with the rows split into two e4m3 planes -- the same results as
+  latent_moe_forward with that mode.  The fused return
+  (ep_forward_peer(..., fused_return=True)) runs the weights-major kernels."""
 
-  def __init__(self, pw: PreparedWeights, cfg: LatentMoEConfig):
+  def __init__(self, pw: PreparedWeights, cfg: LatentMoEConfig, mxfp4_operand: str = "f16"):
+    if mxfp4_operand not in ("f16", "split"):
+      raise ValueError(f"mxfp4_operand={mxfp4_operand!r}: 'f16' or 'split'")
     self.pw, self.cfg = pw, cfg
+    self.split = mxfp4_operand == "split" and pw.expert_gu_mx is not None
+    if self.split:
+      blockscaled_experts(pw)  # the one-time repack, outside any graph capture
 
   def route(self, h):
     c = self.cfg
@@ -60,7 +71,21 @@ class GpuBackend:
 
   def down(self, h):
     # f16 latent rows when the MXFP4 f16-operand kernels consume them
-    return _dense(h, self.pw.down, out_dtype=torch.float16 if mxfp4_f16_path(self.pw) else None)
+    f16 = not self.split and mxfp4_f16_path(self.pw)
+    return _dense(h, self.pw.down, out_dtype=torch.float16 if f16 else None)
+
+  def _split_experts(self, rows_in, gs_local, out_rows: int, zero_tail: bool):
+    """Expert FFN on the block-scaled tensor core of rows already in expert
+    order: the split quantisation into the padded layout, gate/up + SiTU-GLU
+    writing the down GEMM's split rows, the down GEMM writing the unpadded
+    (ragged_dot) layout."""
+    c = self.cfg
+    gu, dn = blockscaled_experts(self.pw)
+    rows = ops.quantize_split_rows(rows_in, gs_local)
+    act_q = ops.blockscaled_gateup_situ_quantized(rows, gu, "e4m3x2", beta=c.activation_situ_beta,
+                                                  linear_beta=c.activation_situ_linear_beta,
+                                                  round_gate_up=True)
+    return ops.mxfp8_mxfp4_ragged_dot(act_q, dn, unpadded_rows=out_rows, zero_tail=zero_tail)
 
   def dispatch(self, idx, w):
     d = ops.dispatch(idx, w, self.cfg.num_experts, want_order=False)
@@ -88,6 +113,8 @@ class GpuBackend:
     c, pw = self.cfg, self.pw
     b, lb = c.activation_situ_beta, c.activation_situ_linear_beta
     xe = ops.gather_rows(src, index)
+    if self.split:
+      return self._split_experts(xe, gs_local, xe.shape[0], True)
     if pw.expert_gu_mx is not None:
       act = ops.mxfp4_fused_gateup_situ(xe, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb,
                                         out_dtype=xe.dtype)
@@ -102,6 +129,8 @@ class GpuBackend:
     read nor written)."""
     c, pw = self.cfg, self.pw
     b, lb = c.activation_situ_beta, c.activation_situ_linear_beta
+    if self.split:
+      return self._split_experts(recv, gs_local, recv.shape[0], False)
     if pw.expert_gu_mx is not None:
       act = ops.mxfp4_fused_gateup_situ(recv, pw.expert_gu_mx, gs_local, beta=b, linear_beta=lb,
                                         out_dtype=recv.dtype, zero_tail=False)
@@ -393,7 +422,9 @@ def shard_experts(pw_full: PreparedWeights, rank: int, world: int) -> PreparedWe
        else pw_full.expert_gu.shape[0])
   n = e // world
   sl = slice(rank * n, (rank + 1) * n)
-  out = dataclasses.replace(pw_full)
+  # the block-scaled repack (if the full set has one) covers every expert:
+  # the shard builds its own on first use
+  out = dataclasses.replace(pw_full, expert_gu_bs=None, expert_down_bs=None)
   if pw_full.expert_gu_mx is not None:
     out.expert_gu_mx = ops.MXFP4Weights(pw_full.expert_gu_mx.packed[sl].contiguous(),
                                         pw_full.expert_gu_mx.scale[sl].contiguous())

@@ -911,18 +911,32 @@ def _mx_gemm(a, w, res, m_pad, k, n, g, epi, beta, linear_beta, round_gate_up, c
 
 def mxfp8_mxfp4_ragged_dot(a: MXFP8Rows | MXFP4Rows | SplitRows, w: MXFP4BlockScaled,
                            out_dtype: torch.dtype = torch.bfloat16,
-                           out: torch.Tensor | None = None) -> torch.Tensor:
+                           out: torch.Tensor | None = None, unpadded_rows: int | None = None,
+                           zero_tail: bool = True) -> torch.Tensor:
   """Padded block-scaled rows @ dequant(w[g])^T per group -> (M_pad, N); rows
   past each group's count are not written.  MXFP8 rows run kind::mxf8f6f4,
   MXFP4 rows (K a multiple of 256) kind::mxf4, split rows kind::mxf8f6f4 on
-  both planes (the exact product)."""
+  both planes (the exact product).  With `unpadded_rows` (split rows only)
+  the output is (unpadded_rows, N) in the ragged_dot layout: row r of group g
+  at the sum of the earlier groups' sizes + r, and the rows past
+  sum(group_sizes) zeroed, or left unwritten with zero_tail=False (an output
+  sized by capacity)."""
   g, n, k = w.shape
   if w.gateup:
     raise ValueError("gate/up-interleaved weights go through mxfp8_mxfp4_gateup_situ")
   m_pad = a.q.shape[-2]
-  res = _out(out, (m_pad, n), out_dtype, a.q.device)
+  if unpadded_rows is None:
+    res = _out(out, (m_pad, n), out_dtype, a.q.device)
+    code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
+    _mx_gemm(a, w, res, m_pad, k, n, g, 0, 0.0, 0.0, 0, code)
+    return res
+  if not isinstance(a, SplitRows):
+    raise ValueError("unpadded output rows need split rows")
+  rows = int(unpadded_rows)
+  res = _out(out, (rows, n), out_dtype, a.q.device)
   code = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}[res.dtype]
-  _mx_gemm(a, w, res, m_pad, k, n, g, 0, 0.0, 0.0, 0, code)
+  if rows > 0:
+    _mx_gemm(a, w, res, m_pad, k, n, g, 0, 0.0, 0.0, 0, code, m_out=rows if zero_tail else -rows)
   return res
 
 
