@@ -809,8 +809,12 @@ def main():
                               expert_start=rank * n_local, num_local_experts=n_local)
   gen = torch.Generator(device=dev).manual_seed(args.seed * 7919 + rank)
   h = torch.randn(t_local, cfg.hidden_size, generator=gen, device=dev).to(torch.bfloat16)
-  # the routed experts on the block-scaled tensor core (split rows), as on one GPU
-  backend = GpuBackend(pw, cfg, mxfp4_operand="split")
+  # Several GPUs: the routed experts on the weights-major f16-operand kernels.
+  # The receive region holds the rows unpadded in bf16/f16, so the split path
+  # needs a separate quantising pass there (the one-GPU forward folds it into
+  # the gather); measured at n = 2 the experts phase took 2.00 / 2.24 ms per
+  # rank with it against 1.94 / 2.21 ms on the weights-major kernels.
+  backend = GpuBackend(pw, cfg, mxfp4_operand="f16")
   xchg = PeerExchange(cfg, t_local) if world > 1 and args.exchange == "peer" else None
 
   def forward(x, mark=None):
@@ -943,8 +947,9 @@ def main():
   # and the latent rows split into two e4m3 planes (hi + remainder), two MMAs
   # per 32-wide K slice, i.e. the exact product at the FP8 instruction rate
   # twice over = the bf16 rate; it writes the down GEMM's split rows.
-  # Several GPUs: the same kernel on a stand-in for the rows this rank's
-  # experts receive.
+  # Several GPUs: the expert-parallel path's weights-major kernel (codes
+  # expanded to f16 tiles in shared memory, kind::f16) on a stand-in for the
+  # rows this rank's experts receive.
   rows = t_local * cfg.top_k
   if world == 1:
     _, inter = lm.latent_moe_forward(h, pw, cfg, return_intermediates=True)
@@ -964,13 +969,12 @@ def main():
     # the routed rows spread evenly over the local experts
     gs = torch.full((n_local,), rows // n_local, dtype=torch.int32, device=dev)
     gs[0] += rows - int(gs.sum().item())
-    gu_bs, _ = lm.latent_moe.blockscaled_experts(pw)
-    xs = ops.quantize_split_rows(
-        torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(torch.bfloat16), gs)
-    act = ops.blockscaled_gateup_situ_quantized(xs, gu_bs, "e4m3x2")
-    gateup = lambda: ops.blockscaled_gateup_situ_quantized(xs, gu_bs, "e4m3x2", out=act)
-    dom_kernel = ("mxfp4 fused gate/up + SiTU-GLU grouped GEMM, block-scaled tcgen05 "
-                  "kind::mxf8f6f4 on split activation rows (this rank's experts)")
+    xs = torch.randn(rows, cfg.latent_size, generator=gen, device=dev).to(
+        torch.float16 if lm.latent_moe.mxfp4_f16_path(pw) else torch.bfloat16)
+    act = torch.empty(rows, cfg.intermediate_size, dtype=xs.dtype, device=dev)
+    gateup = lambda: ops.mxfp4_fused_gateup_situ(xs, pw.expert_gu_mx, gs, out=act)
+    dom_kernel = ("mxfp4 fused gate/up + SiTU-GLU grouped GEMM, weights-major (tcgen05 "
+                  "kind::f16), this rank's experts")
     traffic = None  # the one-GPU capture does not cover this rank's row count
   flops = 2.0 * rows * cfg.latent_size * 2 * cfg.intermediate_size
   peaks, peak_src = load_peaks()
