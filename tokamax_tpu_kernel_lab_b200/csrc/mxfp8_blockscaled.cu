@@ -1027,12 +1027,12 @@ __global__ void __launch_bounds__(256, 4) mx_quantize_kernel(
   }
 }
 
-// The quantising gather in token order: warp w takes token t = w, quantises
-// its row once and stores the codes and scale words at the padded position of
-// each of its k sorted positions slot_pos[t*k + s] -- the rows
-// mx_quantize_kernel writes for a dropless dispatch, each source row read and
-// quantised once instead of k times.  The row is taken 1024 values at a time
-// (the codes of both chunks kept in registers across the k stores).
+// The quantising gather in token order: a warp takes one 1024-value chunk of
+// token t's row, quantises it once and stores the codes and scale words at
+// the padded position of each of t's k sorted positions slot_pos[t*k + s] --
+// the rows mx_quantize_kernel writes for a dropless dispatch, each source row
+// read and quantised once instead of k times (the codes of the chunk's two
+// halves kept in registers across the k stores).
 // Positions past sum(group_sizes) or outside the capacity are skipped (the
 // latter records LMOE_DEVICE_BOUNDS).
 template <bool F16, int FMT>
@@ -1047,8 +1047,14 @@ __global__ void __launch_bounds__(256, 4) mx_quantize_scatter_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
   bool bad = false;
-  for (int64_t t = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; t < T;
-       t += nwarps) {
+  // a work item is one token's 1024-value chunk, so a few hundred tokens
+  // still spread over many warps
+  const int nchunks = (K + 1023) / 1024;
+  const int64_t items = T * nchunks;
+  for (int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; w < items;
+       w += nwarps) {
+    const int64_t t = w / nchunks;
+    const int c0 = static_cast<int>(w % nchunks) * 1024;
     // lane s < k: the padded destination row of slot s (-1: none)
     int64_t my_dst = -1;
     if (lane < k) {
@@ -1062,7 +1068,7 @@ __global__ void __launch_bounds__(256, 4) mx_quantize_scatter_kernel(
       }
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + t * K);
-    for (int c0 = 0; c0 < K; c0 += 1024) {
+    {
       uint4 raw[2][2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
@@ -1147,7 +1153,7 @@ int mx_quantize_scatter_host(const void* x, int x_f16, const int32_t* slot_pos,
     return LMOE_UNSUPPORTED;
   if (num_tokens == 0) return LMOE_OK;
   auto s = static_cast<cudaStream_t>(stream);
-  const int64_t want = (num_tokens * 32 + 255) / 256;
+  const int64_t want = (num_tokens * ((k + 1023) / 1024) * 32 + 255) / 256;
   const int blocks = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms(current_device())) * 8));
   const size_t sh = static_cast<size_t>(2 * (num_groups + 1)) * 4;
   if (x_f16)
