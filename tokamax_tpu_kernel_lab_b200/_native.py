@@ -152,15 +152,17 @@ def load() -> ctypes.CDLL:
     return lib
 
 
-def call(name: str, *args) -> int:
-  """Invoke an entry point; raise on a non-OK host status.
+def call(name: str, *args, kernels: int | None = None) -> int:
+  """Invoke an entry point; raise on a non-OK host status.  `kernels` (the
+  launch count of this call, when it depends on the arguments) overrides
+  KERNELS_PER_CALL.
 
   LMOE_UNSUPPORTED maps to NotImplementedError (the reference's error class for
   shapes an implementation does not support), LMOE_BAD_SHAPE to ValueError."""
   global launch_count
   rc = getattr(load(), name)(*args)
   if rc == LMOE_OK:
-    launch_count += KERNELS_PER_CALL.get(name, 1)
+    launch_count += KERNELS_PER_CALL.get(name, 1) if kernels is None else kernels
     return rc
   if rc == LMOE_UNSUPPORTED:
     raise NotImplementedError(f"{name}: unsupported shape or alignment (status {rc})")

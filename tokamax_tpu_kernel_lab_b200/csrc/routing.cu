@@ -460,6 +460,120 @@ __global__ void __launch_bounds__(kDispThreads) dispatch_scatter_kernel(
   }
 }
 
+// All three steps in one block for dispatches of at most one chunk
+// (n_ext <= kDispChunk: a few hundred tokens): the in-chunk ranks of kernel 1,
+// the bin totals kept in shared memory (with one chunk, kernel 2's per-chunk
+// prefix is zero) and kernel 3's bin starts, group sizes and scatter.  The
+// same positions, bit for bit, with one launch and no workspace round trips:
+// at 2048 entries the three kernels were latency chains of ~10-15 us each.
+__global__ void __launch_bounds__(kDispThreads) dispatch_single_chunk_kernel(
+    const int32_t* __restrict__ flat_ids, const float* __restrict__ flat_w, int64_t S,
+    int64_t n_ext, int start, int num_keys, int top_k, int64_t m_out, int pad_bucket,
+    DispatchOut o) {
+  extern __shared__ uint16_t whist[];  // [8 warps][bins], then int32 totals / starts
+  const int bins = num_keys + 1;
+  int32_t* totals = reinterpret_cast<int32_t*>(whist + ((8 * bins + 1) & ~1));
+  int32_t* bin_start = totals + bins;
+  __shared__ int warp_sums[kDispThreads / 32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 8 * bins; i += blockDim.x) whist[i] = 0;
+  __syncthreads();
+  // kernel 1's ranks: warp w owns entries [w * 32 * kDispItems, ...), 32 at a time
+  uint16_t* h = whist + warp * bins;
+  const int64_t base = static_cast<int64_t>(warp) * 32 * kDispItems;
+  int keys[kDispItems];
+  int ranks[kDispItems];
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int it = 0; it < kDispItems; ++it) {
+    const int64_t i = base + it * 32 + lane;
+    const bool live = i < n_ext;
+    const int key = live ? entry_key(flat_ids, i, S, start, num_keys) : -1 - lane;
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int before = __popc(peers & lt);
+    const int leader = __ffs(peers) - 1;
+    int r = 0;
+    if (live) r = h[key] + before;
+    __syncwarp();
+    if (live && lane == leader) h[key] = static_cast<uint16_t>(h[key] + __popc(peers));
+    __syncwarp();
+    keys[it] = key;
+    ranks[it] = r;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < bins; b += blockDim.x) {
+    int run = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const int c = whist[w * bins + b];
+      whist[w * bins + b] = static_cast<uint16_t>(run);
+      run += c;
+    }
+    totals[b] = run;
+  }
+  __syncthreads();
+  // kernel 3's bin starts: exclusive scan of the totals
+  const int per = (bins + kDispThreads - 1) / kDispThreads;
+  const int b0 = min(bins, static_cast<int>(threadIdx.x) * per), b1 = min(bins, b0 + per);
+  int local = 0;
+  for (int b = b0; b < b1; ++b) local += totals[b];
+  int incl = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  int wbase = 0;
+  for (int w = 0; w < warp; ++w) wbase += warp_sums[w];
+  int run = wbase + incl - local;
+  for (int b = b0; b < b1; ++b) {
+    bin_start[b] = run;
+    run += totals[b];
+  }
+  __syncthreads();
+  // group sizes: kept counts after the m_out cap, plus the padding bucket
+  int kept_local = 0;
+  for (int b = threadIdx.x; b < num_keys; b += blockDim.x) {
+    const int64_t s0 = bin_start[b];
+    const int64_t room = m_out - s0;
+    const int64_t tb = totals[b];
+    const int64_t kept = room <= 0 ? 0 : (tb < room ? tb : room);
+    o.group_sizes[b] = static_cast<int32_t>(kept);
+    if (o.per_expert_counts) o.per_expert_counts[b] = static_cast<int32_t>(kept);
+    kept_local += static_cast<int>(kept);
+  }
+  if (pad_bucket) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) kept_local += __shfl_xor_sync(0xffffffffu, kept_local, off);
+    __syncthreads();  // warp_sums is reused
+    if (lane == 0) warp_sums[warp] = kept_local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int tot = 0;
+      for (int w = 0; w < kDispThreads / 32; ++w) tot += warp_sums[w];
+      o.group_sizes[num_keys] = static_cast<int32_t>(m_out - tot);
+    }
+  }
+  // the scatter, from this warp's own entries and ranks
+#pragma unroll
+  for (int it = 0; it < kDispItems; ++it) {
+    const int64_t i = base + it * 32 + lane;
+    if (i >= n_ext) continue;
+    const int key = keys[it];
+    const int64_t pos = static_cast<int64_t>(bin_start[key]) + whist[warp * bins + key] + ranks[it];
+    const bool in_range = pos < m_out;
+    if (i < S && o.slot_pos) o.slot_pos[i] = (in_range && key < num_keys) ? static_cast<int32_t>(pos) : -1;
+    if (!in_range) continue;
+    const bool valid = key < num_keys;
+    if (o.order) o.order[pos] = static_cast<int32_t>(i);
+    o.token_idx[pos] = valid ? static_cast<int32_t>(i / top_k) : -1;
+    if (o.weight) o.weight[pos] = (valid && flat_w) ? flat_w[i] : 0.f;
+    if (o.valid) o.valid[pos] = valid ? 1 : 0;
+  }
+}
+
 // 8 bf16 -> 8 f16 (exact for magnitudes in f16's normal range)
 __device__ __forceinline__ uint4 bf16x8_to_f16x8(uint4 v) {
   uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -663,6 +777,20 @@ int dispatch_sort(const int32_t* flat_ids, const float* flat_w, int64_t S, int64
   ws.totals = reinterpret_cast<int32_t*>(p);
   p += al(bins * 4);
   ws.rank = reinterpret_cast<int32_t*>(p);
+  if (n_ext <= kDispChunk) {
+    // one chunk: the fused single-block form
+    const size_t sh1 = static_cast<size_t>((8 * bins + 1) & ~1) * sizeof(uint16_t) +
+                       static_cast<size_t>(2 * bins) * sizeof(int32_t);
+    if (sh1 > 48 * 1024 &&
+        cudaFuncSetAttribute(dispatch_single_chunk_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(sh1)) != cudaSuccess)
+      return kLaunchFailed;
+    dispatch_single_chunk_kernel<<<1, kDispThreads, sh1, stream>>>(
+        flat_ids, flat_w, S, n_ext, static_cast<int>(start), static_cast<int>(num_keys),
+        static_cast<int>(top_k), m_out, pad_bucket, o);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+  }
   const size_t sh = static_cast<size_t>(8) * bins * sizeof(uint16_t);
   if (sh > 48 * 1024) {
     if (cudaFuncSetAttribute(dispatch_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -598,7 +598,8 @@ def dispatch(topk_idx: torch.Tensor, topk_weight: torch.Tensor | None, num_local
   _native.call("lmoe_dispatch", _ptr(ids), _ptr(w), t, k, expert_start, num_local_experts, m_out,
                int(pad_bucket), _ptr(res.order), _ptr(res.token_idx), _ptr(res.weight),
                _ptr(res.slot_pos), _ptr(res.group_sizes), _ptr(res.per_expert_counts),
-               _ptr(res.valid), _ptr(workspace), workspace.numel(), _stream())
+               _ptr(res.valid), _ptr(workspace), workspace.numel(), _stream(),
+               kernels=0 if n_ext == 0 else (1 if n_ext <= 2048 else 3))  # fused: one chunk
   if res.valid is not None:
     res.valid = res.valid.view(torch.bool)
   return res
