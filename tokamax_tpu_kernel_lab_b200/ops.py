@@ -458,7 +458,7 @@ def router_gate_fused(hidden_states: torch.Tensor, router_weight_nk: torch.Tenso
 
 
 def dense_phases_pay_off(num_tokens: int, num_experts: int, latent_size: int,
-                         shared_intermediate: int, device=None) -> bool:
+                         shared_intermediate: int, device=None, sms: int | None = None) -> bool:
   """True when the layer's dense projections should run as the split-K phase
   kernels: their output tiles (128 tokens x 128 columns) would fill the SMs
   at most twice over, so the separate GEMMs (and the fused router, whose
@@ -466,7 +466,8 @@ def dense_phases_pay_off(num_tokens: int, num_experts: int, latent_size: int,
   long serial K loops.  Measured at configuration 5 (graph replay): 128
   tokens 0.253 vs 0.284 ms, 512 tokens 0.390 vs 0.396 ms, and at 1024 tokens
   (above the rule) 0.569 vs 0.542 ms."""
-  sms = torch.cuda.get_device_properties(device).multi_processor_count
+  if sms is None:
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
   m_tiles = -(-num_tokens // 128)
   n_tiles = -(-num_experts // 128) + -(-latent_size // 128) + -(-shared_intermediate // 64)
   return 0 < m_tiles * n_tiles <= 2 * sms
