@@ -19,7 +19,9 @@ resident in HBM, device-timed with CUDA events (max over ranks); `e2e` = the
 same through the public API with every step's input copied from pinned host
 memory and its output copied back inside the timed region (the copies of
 neighbouring steps overlap the forward, on their own streams); `roofline` for the dominant
-kernel (the MXFP4 fused gate/up grouped GEMM); `cpu_baseline` = the CPU
+kernel (the MXFP4 fused gate/up + SiTU-GLU grouped GEMM: on one GPU the default
+forward's block-scaled kernel on split activation rows, under expert parallelism
+the weights-major kernel the exchange runs); `cpu_baseline` = the CPU
 restatement of the reference forward on a token sample; `clocks` sampled
 with nvidia-smi during the timed region.
 
