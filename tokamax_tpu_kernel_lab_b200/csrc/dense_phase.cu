@@ -40,7 +40,6 @@
 #include <cuda.h>
 
 #include <algorithm>
-#include <cudaTypedefs.h>
 #include <mutex>
 
 #include "../../include/lmoe.h"
@@ -433,7 +432,6 @@ struct PhasePlan {
 // T.
 void choose_splits(PhaseArgs& a, int sms) {
   int best_cost = 1 << 30;
-  const int kb_total = a.seg_kb[0] + a.seg_kb[1];
   for (int s0 = 1; s0 <= std::min(a.seg_kb[0], 32); ++s0) {
     int s1 = 0;
     if (a.seg_kb[1] > 0)
@@ -454,7 +452,6 @@ void choose_splits(PhaseArgs& a, int sms) {
     }
   }
   a.splits = a.seg_splits[0] + a.seg_splits[1];
-  (void)kb_total;
 }
 
 PhasePlan make_plan(int64_t T, int n_tiles, int64_t k0, int64_t k1) {
