@@ -552,6 +552,22 @@ LMOE_API int lmoe_bf16split_quantize_scatter(const void* x, int x_f16, const int
                                              const int32_t* group_sizes, int64_t num_groups,
                                              void* out_q, void* out_sf, int64_t m_pad_capacity,
                                              int32_t* dev_status, void* stream);
+/* lmoe_bf16split_quantize_scatter that also writes, for every slot s of every
+ * token t, padded_slot_pos[t * top_k + s] = the slot's row in the padded
+ * layout (-1 where the slot has none): the output of lmoe_mxfp8_pad_positions
+ * on slot_pos, produced by the gather that already computes it, so the combine
+ * after the padded GEMMs needs no separate kernel.  padded_slot_pos: device
+ * int32 [num_tokens * top_k].  Replaces, with the split rows' GEMMs, the
+ * gather and scatter-back positions of latent_moe_forward
+ * (05_ragged_dot_on_tpu/kimi_k3_latent_moe_reference.py:370-378, 413). */
+LMOE_API int lmoe_bf16split_quantize_scatter_positions(const void* x, int x_f16,
+                                                       const int32_t* slot_pos,
+                                                       int64_t num_tokens, int64_t top_k,
+                                                       int64_t k, const int32_t* group_sizes,
+                                                       int64_t num_groups, void* out_q,
+                                                       void* out_sf, int64_t m_pad_capacity,
+                                                       int32_t* padded_slot_pos,
+                                                       int32_t* dev_status, void* stream);
 /* The block-scaled gate/up + SiTU-GLU GEMM with its activations written
  * quantised for the down GEMM (no bf16 activation tensor): input rows of
  * act_kind 0 (MXFP8), 1 (MXFP4, k a multiple of 256) or 2 (split), weights

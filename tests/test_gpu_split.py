@@ -252,3 +252,34 @@ def test_quantising_gateup_epilogue_equals_quantising_the_activations(lm, kind, 
     assert np.array_equal(gq[prow], wq[prow])
   assert np.array_equal(sf_bytes_at(got.sf.cpu().numpy(), prow, inter, m_pad),
                         sf_bytes_at(want.sf.cpu().numpy(), prow, inter, m_pad))
+
+
+def test_split_scatter_writes_the_padded_positions(lm):
+  """lmoe_bf16split_quantize_scatter_positions: the same split rows as the
+  plain token-order gather, and the slot positions of lmoe_mxfp8_pad_positions,
+  bit for bit (a dropless dispatch of 700 tokens, top-8 over 96 experts)."""
+  from tokamax_tpu_kernel_lab_b200 import ops
+  rng = np.random.default_rng(71)
+  t, k, e, dim = 700, 8, 96, 512
+  ids = np.stack([rng.choice(e, size=k, replace=False) for _ in range(t)]).astype(np.int32)
+  w = rng.random((t, k), dtype=np.float32)
+  d = ops.dispatch(torch.from_numpy(ids).cuda(), torch.from_numpy(w).cuda(), e)
+  x = torch.randn(t, dim, device="cuda").to(torch.bfloat16)
+  rows, pos = ops.quantize_split_scatter_with_positions(x, d.group_sizes, d.slot_pos, k)
+  ref = ops.quantize_split_scatter(x, d.group_sizes, d.slot_pos, k)
+  ref_pos = ops.mxfp8_pad_positions(d.slot_pos, d.group_sizes)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  assert torch.equal(pos, ref_pos)
+  live = to_np(ref_pos) >= 0
+  used = np.unique(to_np(ref_pos)[live].astype(np.int64))
+  assert torch.equal(rows.q[:, used], ref.q[:, used])
+  # the scale bytes of the written rows (atoms (K/128, M_pad/128, 512 B): byte
+  # (r % 32) * 16 + ((r % 128) // 32) * 4 + kb % 4 of atom (kb // 4, r // 128))
+  m_pad = rows.q.shape[-2]
+  kb = np.arange(dim // 32)
+  atom = (kb[None, :] // 4) * (m_pad // 128) + used[:, None] // 128
+  byte = (used[:, None] % 32) * 16 + ((used[:, None] % 128) // 32) * 4 + kb[None, :] % 4
+  idx = atom * 512 + byte
+  a, b = rows.sf.reshape(-1).cpu().numpy(), ref.sf.reshape(-1).cpu().numpy()
+  assert np.array_equal(a[idx], b[idx])

@@ -81,6 +81,8 @@ SIGNATURES = {
                                             _i64, _p, _p]),
     "lmoe_bf16split_quantize_scatter": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64, _p, _p,
                                                _i64, _p, _p]),
+    "lmoe_bf16split_quantize_scatter_positions": (_i32, [_p, _i32, _p, _i64, _i64, _i64, _p, _i64,
+                                                         _p, _p, _i64, _p, _p, _p]),
     "lmoe_bf16split_mxfp4_grouped_gemm": (_i32, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64,
                                                  _i32, _f32, _f32, _i32, _i32, _i64, _p, _p]),
     "lmoe_blockscaled_gateup_situ_quantized": (_i32, [_p, _p, _i32, _p, _p, _p, _i64, _i64, _i64,

@@ -1039,7 +1039,7 @@ template <bool F16, int FMT>
 __global__ void __launch_bounds__(256, 4) mx_quantize_scatter_kernel(
     const uint16_t* __restrict__ x, const int32_t* __restrict__ slot_pos, int64_t T, int k,
     const int32_t* __restrict__ gs, int G, int K, int64_t m_pad_cap, uint8_t* __restrict__ q,
-    uint8_t* __restrict__ sf, int32_t* status) {
+    uint8_t* __restrict__ sf, int32_t* __restrict__ padded_pos, int32_t* status) {
   extern __shared__ int32_t sh[];
   int32_t* start = sh;
   int32_t* pad_off = sh + G + 1;
@@ -1066,6 +1066,9 @@ __global__ void __launch_bounds__(256, 4) mx_quantize_scatter_kernel(
           my_dst = -1;
         }
       }
+      // the padded position of each slot (lmoe_mxfp8_pad_positions' output),
+      // written once per token by the warp of its first chunk
+      if (padded_pos != nullptr && c0 == 0) padded_pos[t * k + lane] = static_cast<int32_t>(my_dst);
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + t * K);
     {
@@ -1143,7 +1146,7 @@ int mx_quantize_scatter_host(const void* x, int x_f16, const int32_t* slot_pos,
                                 int64_t num_tokens, int64_t top_k, int64_t k,
                                 const int32_t* group_sizes, int64_t num_groups, void* out_q,
                                 void* out_sf, int64_t m_pad_capacity, int32_t* dev_status,
-                                void* stream) {
+                                void* stream, int32_t* padded_pos = nullptr) {
   if (num_tokens < 0 || top_k <= 0 || top_k > 32 || k <= 0 || k % 128 || m_pad_capacity < 0 ||
       m_pad_capacity % 128)
     return LMOE_BAD_SHAPE;
@@ -1160,12 +1163,12 @@ int mx_quantize_scatter_host(const void* x, int x_f16, const int32_t* slot_pos,
     mx_quantize_scatter_kernel<true, FMT><<<blocks, 256, sh, s>>>(
         static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
         (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
-        static_cast<uint8_t*>(out_sf), dev_status);
+        static_cast<uint8_t*>(out_sf), padded_pos, dev_status);
   else
     mx_quantize_scatter_kernel<false, FMT><<<blocks, 256, sh, s>>>(
         static_cast<const uint16_t*>(x), slot_pos, num_tokens, (int)top_k, group_sizes,
         (int)num_groups, (int)k, m_pad_capacity, static_cast<uint8_t*>(out_q),
-        static_cast<uint8_t*>(out_sf), dev_status);
+        static_cast<uint8_t*>(out_sf), padded_pos, dev_status);
   return cudaGetLastError() == cudaSuccess ? LMOE_OK : LMOE_LAUNCH_FAILED;
 }
 
@@ -1369,6 +1372,18 @@ int lmoe_bf16split_quantize_scatter(const void* x, int x_f16, const int32_t* slo
   return lmoe::mx_quantize_scatter_host<lmoe::MX_E4M3_SPLIT>(
       x, x_f16, slot_pos, num_tokens, top_k, k, group_sizes, num_groups, out_q, out_sf,
       m_pad_capacity, dev_status, stream);
+}
+
+int lmoe_bf16split_quantize_scatter_positions(const void* x, int x_f16, const int32_t* slot_pos,
+                                              int64_t num_tokens, int64_t top_k, int64_t k,
+                                              const int32_t* group_sizes, int64_t num_groups,
+                                              void* out_q, void* out_sf, int64_t m_pad_capacity,
+                                              int32_t* padded_slot_pos, int32_t* dev_status,
+                                              void* stream) {
+  if (padded_slot_pos == nullptr) return LMOE_BAD_SHAPE;
+  return lmoe::mx_quantize_scatter_host<lmoe::MX_E4M3_SPLIT>(
+      x, x_f16, slot_pos, num_tokens, top_k, k, group_sizes, num_groups, out_q, out_sf,
+      m_pad_capacity, dev_status, stream, padded_slot_pos);
 }
 
 int lmoe_mxfp8_pad_positions(const int32_t* positions, int64_t n, const int32_t* group_sizes,

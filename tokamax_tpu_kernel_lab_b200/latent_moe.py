@@ -478,7 +478,12 @@ def mxfp8_expert_ffn(x, token_idx, group_sizes, slot_pos, pw: PreparedWeights,
       "e4m3": (ops.quantize_mxfp8_scatter, ops.quantize_mxfp8_rows),
       "e2m1": (ops.quantize_mxfp4_scatter, ops.quantize_mxfp4_rows),
       "e4m3x2": (ops.quantize_split_scatter, ops.quantize_split_rows)}[fmt]
-  rows = quantize_scatter(x, group_sizes, slot_pos, c.top_k)
+  padded_pos = None
+  if fmt == "e4m3x2":
+    # the gather also writes the slot positions moved to the padded rows
+    rows, padded_pos = ops.quantize_split_scatter_with_positions(x, group_sizes, slot_pos, c.top_k)
+  else:
+    rows = quantize_scatter(x, group_sizes, slot_pos, c.top_k)
   mark("gather")
   if keep_activation:
     act = ops.mxfp8_mxfp4_gateup_situ(rows, gu, beta=c.activation_situ_beta,
@@ -494,7 +499,9 @@ def mxfp8_expert_ffn(x, token_idx, group_sizes, slot_pos, pw: PreparedWeights,
   mark("expert gate/up")
   down = ops.mxfp8_mxfp4_ragged_dot(act_q, dn)
   mark("expert down")
-  return act, down, ops.mxfp8_pad_positions(slot_pos, group_sizes)
+  if padded_pos is None:
+    padded_pos = ops.mxfp8_pad_positions(slot_pos, group_sizes)
+  return act, down, padded_pos
 
 
 def _dense(a: torch.Tensor, w_nk: torch.Tensor, addend: torch.Tensor | None = None,

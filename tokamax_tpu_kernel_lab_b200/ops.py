@@ -888,6 +888,26 @@ def quantize_split_scatter(x: torch.Tensor, group_sizes: torch.Tensor, slot_pos:
   return _quantize_scatter("e4m3x2", x, group_sizes, slot_pos, top_k, out)
 
 
+def quantize_split_scatter_with_positions(x: torch.Tensor, group_sizes: torch.Tensor,
+                                          slot_pos: torch.Tensor, top_k: int
+                                          ) -> tuple[SplitRows, torch.Tensor]:
+  """quantize_split_scatter that also returns the slot positions moved to
+  the padded rows (mxfp8_pad_positions(slot_pos, group_sizes)), written by
+  the same kernel."""
+  _need_cuda(x, group_sizes, slot_pos)
+  t, k = x.shape
+  g = group_sizes.shape[0]
+  out = _mx_rows("e4m3x2", mxfp8_padded_rows(t * top_k, g), k, group_sizes, x.device)
+  gs = group_sizes.to(torch.int32).contiguous()
+  out.group_sizes = gs
+  pos = torch.empty(t * top_k, dtype=torch.int32, device=x.device)
+  _native.call("lmoe_bf16split_quantize_scatter_positions", _ptr(x.contiguous()),
+               int(x.dtype == torch.float16), _ptr(slot_pos.to(torch.int32).contiguous()), t,
+               top_k, k, _ptr(gs), g, _ptr(out.q), _ptr(out.sf), out.q.shape[-2], _ptr(pos),
+               _ptr(device_status(x.device)), _stream())
+  return out, pos
+
+
 def mxfp8_pad_positions(positions: torch.Tensor, group_sizes: torch.Tensor) -> torch.Tensor:
   """Sorted-order row positions -> their rows in the padded layout."""
   _need_cuda(positions, group_sizes)
