@@ -189,3 +189,26 @@ def test_config5_small_batch_with_phases(lm):
   err = float(np.abs(g - u).max() / np.abs(u).max())
   assert err <= 1e-2, f"normwise {err:.2e}"
   assert np.all(np.abs(g - u) <= 2e-2 + 1e-2 * np.abs(u))
+
+
+def test_bf16_expert_layer_with_phases_matches_oracle(lm):
+  """bf16 routed experts (not MXFP4) with the dense phase kernels: the layer
+  against the oracle forward on the same weights, routing compared up to
+  near-ties."""
+  cfg = lm.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+  w = lm.init_weights(cfg, seed=35, bias_std=0.5)
+  pw = lm.prepare_weights(w)
+  gen = torch.Generator(device="cuda").manual_seed(35)
+  h = torch.randn(96, cfg.hidden_size, generator=gen, device="cuda").to(torch.bfloat16)
+  assert lm.latent_moe._use_dense_phases(None, pw, cfg, 96, h, torch.bfloat16, False)
+  got = lm.latent_moe_forward(h, pw, cfg)
+  idx = _routing(_ops(), pw, cfg, h, True)
+  torch.cuda.synchronize()
+  lm.check_device_status()
+  npw = {k: (to_np(v) if isinstance(v, torch.Tensor) else v) for k, v in vars(w).items()}
+  ow = O.Weights(**{k: npw[k] for k in O.Weights.__dataclass_fields__})
+  ocfg = O.LatentMoEConfig(1024, 512, 256, 64, 8, 2)
+  ref, rinter = O.latent_moe_forward(to_np(h), ow, ocfg, dtype="bf16", return_intermediates=True)
+  same = routing_agreement(idx.cpu().numpy(), rinter["router_scores_for_choice"],
+                           rinter["topk_indices"])
+  assert_bf16_close(ref[same], to_np(got)[same], "bf16-expert layer with dense phases")
